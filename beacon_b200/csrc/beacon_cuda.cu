@@ -1,0 +1,606 @@
+// beacon_cuda.cu -- libbeacon_cuda.so: the extern "C" boundary (include/beacon_cuda.h)
+// over the sm_100a kernels.  One translation unit so every kernel shares the
+// device fault words in sm100.cuh.
+//
+// Host-side responsibilities: argument validation (mirroring LaunchParams::validate,
+// crates/beacon-cuda/src/launch.rs:78-97, plus shape/alignment checks), TMA tensor-map
+// encoding, tile-shape selection, workspace management and error mapping onto
+// LaunchError (crates/beacon-cuda/src/error.rs:4-13).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/beacon_cuda.h"
+#include "attention.cuh"
+#include "elementwise.cuh"
+#include "gemm.cuh"
+#include "sm100.cuh"
+
+using namespace beacon;
+using bf16 = __nv_bfloat16;
+
+// ===========================================================================
+// errors
+// ===========================================================================
+namespace {
+
+thread_local std::string t_last_error;
+thread_local int t_last_status = BEACON_OK;
+std::atomic<uint64_t> g_launches{0};
+
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  t_last_status = status;
+  return status;
+}
+
+int check_launch(const char* what) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(BEACON_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return BEACON_OK;
+}
+
+#define BEACON_TRY(expr)             \
+  do {                               \
+    int _rc = (expr);                \
+    if (_rc != BEACON_OK) return _rc; \
+  } while (0)
+
+// ===========================================================================
+// devices
+// ===========================================================================
+struct DeviceInfo {
+  int sms = 0;
+  int major = 0, minor = 0;
+  bool init = false;
+};
+std::mutex g_dev_mu;
+DeviceInfo g_dev[64];
+
+int current_device(int* dev, DeviceInfo** info) {
+  int d = 0;
+  cudaError_t e = cudaGetDevice(&d);
+  if (e != cudaSuccess) return fail(BEACON_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (d < 0 || d >= 64) return fail(BEACON_ERR_CUDA, "device ordinal %d out of range", d);
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceInfo& di = g_dev[d];
+  if (!di.init) {
+    cudaDeviceGetAttribute(&di.sms, cudaDevAttrMultiProcessorCount, d);
+    cudaDeviceGetAttribute(&di.major, cudaDevAttrComputeCapabilityMajor, d);
+    cudaDeviceGetAttribute(&di.minor, cudaDevAttrComputeCapabilityMinor, d);
+    di.init = true;
+  }
+  if (di.major != 10 || di.minor != 0)
+    return fail(BEACON_ERR_MODULE_LOAD, "device %d is sm_%d%d; this library is built for sm_100a only", d, di.major,
+                di.minor);
+  *dev = d;
+  *info = &di;
+  return BEACON_OK;
+}
+
+// ===========================================================================
+// TMA tensor maps
+// ===========================================================================
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// bf16 tensor of `rank` dims (dims[0] innermost, contiguous), 128-byte swizzle.
+int make_map(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+             const uint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(BEACON_ERR_MODULE_LOAD, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t d[5], s[4];
+  cuuint32_t b[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    es[i] = 1;
+  }
+  for (int i = 0; i + 1 < rank; ++i) s[i] = strides_bytes[i];
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void*>(base), d, s, b, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return BEACON_OK;
+}
+
+int make_map_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t ld_elems,
+                uint32_t box_inner, uint32_t box_outer) {
+  const uint64_t dims[2] = {inner, outer};
+  const uint64_t strides[1] = {ld_elems * 2};
+  const uint32_t box[2] = {box_inner, box_outer};
+  return make_map(m, base, 2, dims, strides, box);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ===========================================================================
+// workspace: grow-only, one per device
+// ===========================================================================
+struct Workspace {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+std::mutex g_ws_mu;
+Workspace g_ws[64];
+
+int get_workspace(int dev, size_t need, void* user, size_t user_bytes, void** out) {
+  if (need == 0) {
+    *out = user;
+    return BEACON_OK;
+  }
+  if (user != nullptr) {
+    if (user_bytes < need)
+      return fail(BEACON_ERR_OUT_OF_MEMORY, "workspace of %zu bytes given, %zu needed", user_bytes, need);
+    *out = user;
+    return BEACON_OK;
+  }
+  std::lock_guard<std::mutex> lk(g_ws_mu);
+  Workspace& w = g_ws[dev];
+  if (w.bytes < need) {
+    if (w.ptr) {
+      cudaDeviceSynchronize();
+      cudaFree(w.ptr);
+      w.ptr = nullptr;
+      w.bytes = 0;
+    }
+    cudaError_t e = cudaMalloc(&w.ptr, need);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      size_t fr = 0, tot = 0;
+      cudaMemGetInfo(&fr, &tot);
+      t_last_error = "workspace allocation failed";
+      t_last_status = BEACON_ERR_OUT_OF_MEMORY;
+      return fail(BEACON_ERR_OUT_OF_MEMORY, "out of device memory: requested %zu bytes, %zu available", need, fr);
+    }
+    w.bytes = need;
+  }
+  *out = w.ptr;
+  return BEACON_OK;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// ===========================================================================
+// GEMM dispatch
+// ===========================================================================
+struct Operand {
+  const void* ptr;
+  bool mn_major;  // A: [K][M] storage (else [M][K]);  B: [K][N] storage (else [N][K])
+  int64_t ld;     // elements between consecutive storage rows
+};
+
+template <int BN, bool A_MN, bool B_MN>
+int launch_gemm_tc_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb2, const GemmParams& p,
+                     int sms, cudaStream_t st) {
+  using Cfg = GemmCfg<BN>;
+  auto kern = k_gemm_bf16_tc<BN, A_MN, B_MN>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return fail(BEACON_ERR_CUDA, "gemm smem attribute: %s", cudaGetErrorString(e));
+    attr_set[dev] = true;
+  }
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int grid = tiles < sms ? tiles : sms;
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tb2, p);
+  return check_launch("k_gemm_bf16_tc");
+}
+
+template <int BN>
+int launch_gemm_tc_bn(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb2,
+                      const GemmParams& p, int sms, cudaStream_t st) {
+  if (!a_mn && b_mn) return launch_gemm_tc_t<BN, false, true>(ta, tb, tb2, p, sms, st);
+  if (!a_mn && !b_mn) return launch_gemm_tc_t<BN, false, false>(ta, tb, tb2, p, sms, st);
+  if (a_mn && b_mn) return launch_gemm_tc_t<BN, true, true>(ta, tb, tb2, p, sms, st);
+  return launch_gemm_tc_t<BN, true, false>(ta, tb, tb2, p, sms, st);
+}
+
+// Pick the N tile: the widest tile keeps shared-memory traffic per FLOP lowest,
+// narrower tiles win back idle SMs when the tile count is a poor multiple of the SM count.
+int choose_bn(int64_t M, int64_t Nout, bool swiglu, int sms) {
+  const int cands[3] = {256, 128, 64};
+  const double cost[3] = {1.0, 0.93, 0.80};
+  int best = 256;
+  double best_score = -1.0;
+  for (int i = 0; i < 3; ++i) {
+    const int bn = cands[i];
+    if (swiglu && bn < 128) continue;
+    const int64_t cols = swiglu ? bn / 2 : bn;
+    const int64_t tiles = ((M + 127) / 128) * ((Nout + cols - 1) / cols);
+    const int64_t waves = (tiles + sms - 1) / sms;
+    const double eff = (double)tiles / (double)(waves * sms);
+    const double score = eff * cost[i];
+    if (score > best_score + 1e-9) {
+      best_score = score;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+// C[M,N] = A . B (+ epilogue) with bf16 operands.  `B2` is the up-projection for kEpiSwiglu.
+int gemm_bf16(const Operand& A, const Operand& B, const Operand* B2, GemmParams p, cudaStream_t st, int force_bn = 0) {
+  int dev;
+  DeviceInfo* di;
+  BEACON_TRY(current_device(&dev, &di));
+  if (p.M == 0 || p.N == 0) return BEACON_OK;
+  const bool swiglu = p.epi == kEpiSwiglu;
+  const bool tma_ok = aligned16(A.ptr) && aligned16(B.ptr) && (A.ld % 8 == 0) && (B.ld % 8 == 0) &&
+                      (!swiglu || (aligned16(B2->ptr) && B2->ld % 8 == 0)) && p.K > 0;
+  if (!tma_ok) {
+    if (swiglu) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "swiglu GEMM needs 16-byte aligned rows");
+    // exact SIMT path for shapes TMA cannot describe
+    const long long sam = A.mn_major ? 1 : A.ld, sak = A.mn_major ? A.ld : 1;
+    const long long sbk = B.mn_major ? B.ld : 1, sbn = B.mn_major ? 1 : B.ld;
+    dim3 grid((unsigned)((p.N + 63) / 64), (unsigned)((p.M + 63) / 64));
+    k_gemm_simt<bf16><<<grid, 256, 0, st>>>(reinterpret_cast<const bf16*>(A.ptr), sam, sak,
+                                            reinterpret_cast<const bf16*>(B.ptr), sbk, sbn, p);
+    return check_launch("k_gemm_simt<bf16>");
+  }
+  const int bn = force_bn ? force_bn : choose_bn(p.M, p.N, swiglu, di->sms);
+  const int cols = swiglu ? bn / 2 : bn;
+  p.tiles_m = (p.M + 127) / 128;
+  p.tiles_n = (p.N + cols - 1) / cols;
+  CUtensorMap ta, tb, tb2;
+  // A logical [M,K]
+  if (!A.mn_major)
+    BEACON_TRY(make_map_2d(&ta, A.ptr, (uint64_t)p.K, (uint64_t)p.M, (uint64_t)A.ld, 64, 128));
+  else
+    BEACON_TRY(make_map_2d(&ta, A.ptr, (uint64_t)p.M, (uint64_t)p.K, (uint64_t)A.ld, 64, 64));
+  // B logical [K,N]; for SwiGLU the tensor's N is the hidden width F
+  auto map_b = [&](CUtensorMap* m, const Operand& op) -> int {
+    if (op.mn_major) return make_map_2d(m, op.ptr, (uint64_t)p.N, (uint64_t)p.K, (uint64_t)op.ld, 64, 64);
+    return make_map_2d(m, op.ptr, (uint64_t)p.K, (uint64_t)p.N, (uint64_t)op.ld, 64, (uint32_t)cols);
+  };
+  BEACON_TRY(map_b(&tb, B));
+  if (swiglu) {
+    if (B2->mn_major != B.mn_major) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "swiglu operands differ in major");
+    BEACON_TRY(map_b(&tb2, *B2));
+  } else {
+    tb2 = tb;
+  }
+  switch (bn) {
+    case 256: return launch_gemm_tc_bn<256>(A.mn_major, B.mn_major, ta, tb, tb2, p, di->sms, st);
+    case 128: return launch_gemm_tc_bn<128>(A.mn_major, B.mn_major, ta, tb, tb2, p, di->sms, st);
+    default: return launch_gemm_tc_bn<64>(A.mn_major, B.mn_major, ta, tb, tb2, p, di->sms, st);
+  }
+}
+
+int gemm_f32(const Operand& A, const Operand& B, GemmParams p, cudaStream_t st) {
+  if (p.M == 0 || p.N == 0) return BEACON_OK;
+  const long long sam = A.mn_major ? 1 : A.ld, sak = A.mn_major ? A.ld : 1;
+  const long long sbk = B.mn_major ? B.ld : 1, sbn = B.mn_major ? 1 : B.ld;
+  dim3 grid((unsigned)((p.N + 63) / 64), (unsigned)((p.M + 63) / 64));
+  k_gemm_simt<float><<<grid, 256, 0, st>>>(reinterpret_cast<const float*>(A.ptr), sam, sak,
+                                           reinterpret_cast<const float*>(B.ptr), sbk, sbn, p);
+  return check_launch("k_gemm_simt<f32>");
+}
+
+GemmParams gemm_params(int64_t M, int64_t N, int64_t K, void* out, int64_t ldo, bool out_f32) {
+  GemmParams p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.out = out;
+  p.ldo = ldo;
+  p.out_f32 = out_f32 ? 1 : 0;
+  p.epi = kEpiStore;
+  p.aux_f32 = out_f32 ? 1 : 0;
+  return p;
+}
+
+int check_dtype_gemm(int dtype) {
+  if (dtype != BEACON_BF16 && dtype != BEACON_F32)
+    return fail(BEACON_ERR_UNIMPLEMENTED, "dtype %d: the GEMM family supports f32 and bf16", dtype);
+  return BEACON_OK;
+}
+
+int check_dims(const char* what, int64_t a, int64_t b, int64_t c) {
+  if (a < 0 || b < 0 || c < 0) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "%s: negative dimension", what);
+  if (a > INT32_MAX || b > INT32_MAX || c > INT32_MAX)
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "%s: dimension exceeds 2^31-1", what);
+  return BEACON_OK;
+}
+
+int zero_fill(void* p, size_t bytes, cudaStream_t st) {
+  if (!p || bytes == 0) return BEACON_OK;
+  cudaError_t e = cudaMemsetAsync(p, 0, bytes, st);
+  if (e != cudaSuccess) return fail(BEACON_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+  return BEACON_OK;
+}
+
+// One logical C = A.B with the given storage of A and B, dtype-dispatched.
+int gemm_any(int dtype, const Operand& A, const Operand& B, GemmParams p, cudaStream_t st) {
+  if (p.K == 0) {  // empty reduction: out = epilogue(0)
+    const size_t es = p.out_f32 ? 4 : 2;
+    if (p.epi == kEpiStore || (p.epi == kEpiBias && p.bias == nullptr)) {
+      if ((int64_t)p.ldo == p.N) return zero_fill(p.out, (size_t)p.M * p.N * es, st);
+    }
+  }
+  if (dtype == BEACON_F32) return gemm_f32(A, B, p, st);
+  return gemm_bf16(A, B, nullptr, p, st);
+}
+
+cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+int grid_for(int64_t work, int threads, int sms) {
+  int64_t g = (work + threads - 1) / threads;
+  const int64_t cap = (int64_t)sms * 8;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return (int)g;
+}
+
+}  // namespace
+
+// ===========================================================================
+// library
+// ===========================================================================
+extern "C" int beacon_version(void) { return 100; }
+
+extern "C" int beacon_last_error(char* buf, size_t len) {
+  if (buf && len) {
+    strncpy(buf, t_last_error.c_str(), len - 1);
+    buf[len - 1] = '\0';
+  }
+  return t_last_status;
+}
+
+extern "C" uint64_t beacon_launch_count(void) { return g_launches.load(); }
+
+extern "C" int beacon_device_status(int device, unsigned int out[3]) {
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return fail(BEACON_ERR_CUDA, "cudaSetDevice(%d): %s", device, cudaGetErrorString(e));
+  e = cudaDeviceSynchronize();
+  unsigned int w[4] = {0, 0, 0, 0};
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(w, g_beacon_status, sizeof(w));
+  const unsigned int zero[4] = {0, 0, 0, 0};
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_beacon_status, zero, sizeof(zero));
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return fail(BEACON_ERR_CUDA, "device status: %s", cudaGetErrorString(e));
+  if (out) {
+    out[0] = w[0];
+    out[1] = w[1];
+    out[2] = w[2];
+  }
+  if (w[0] != 0) return fail(BEACON_ERR_CUDA, "device fault code %u at site 0x%x (%u faults)", w[0], w[1], w[2]);
+  return BEACON_OK;
+}
+
+// ===========================================================================
+// matmul / linear
+// ===========================================================================
+extern "C" int beacon_matmul_fwd(void* out, const void* lhs, const void* rhs, int64_t m, int64_t k, int64_t n,
+                                 int dtype, void* stream) {
+  BEACON_TRY(check_dtype_gemm(dtype));
+  BEACON_TRY(check_dims("matmul_fwd", m, k, n));
+  if (m && n && (!out || (k && (!lhs || !rhs))))
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "matmul_fwd: null pointer");
+  GemmParams p = gemm_params(m, n, k, out, n, dtype == BEACON_F32);
+  return gemm_any(dtype, Operand{lhs, false, k}, Operand{rhs, true, n}, p, as_stream(stream));
+}
+
+extern "C" int beacon_matmul_bwd(void* dlhs, void* drhs, const void* dout, const void* lhs, const void* rhs,
+                                 int64_t m, int64_t k, int64_t n, int dtype, void* stream) {
+  BEACON_TRY(check_dtype_gemm(dtype));
+  BEACON_TRY(check_dims("matmul_bwd", m, k, n));
+  cudaStream_t st = as_stream(stream);
+  const bool f32 = dtype == BEACON_F32;
+  if (dlhs) {  // dlhs[m,k] = dout[m,n] . rhs[k,n]^T   (B stored [N=k][K=n]: K-major)
+    GemmParams p = gemm_params(m, k, n, dlhs, k, f32);
+    BEACON_TRY(gemm_any(dtype, Operand{dout, false, n}, Operand{rhs, false, n}, p, st));
+  }
+  if (drhs) {  // drhs[k,n] = lhs[m,k]^T . dout[m,n]  (A stored [K=m][M=k]: MN-major; B [K=m][N=n]: MN-major)
+    GemmParams p = gemm_params(k, n, m, drhs, n, f32);
+    BEACON_TRY(gemm_any(dtype, Operand{lhs, true, k}, Operand{dout, true, n}, p, st));
+  }
+  return BEACON_OK;
+}
+
+extern "C" int beacon_linear_fwd(void* out, const void* x, const void* weight, const void* bias, int64_t m,
+                                 int64_t k, int64_t n, int dtype, void* stream) {
+  BEACON_TRY(check_dtype_gemm(dtype));
+  BEACON_TRY(check_dims("linear_fwd", m, k, n));
+  GemmParams p = gemm_params(m, n, k, out, n, dtype == BEACON_F32);
+  if (bias) {
+    p.epi = kEpiBias;
+    p.bias = bias;
+  }
+  return gemm_any(dtype, Operand{x, false, k}, Operand{weight, true, n}, p, as_stream(stream));
+}
+
+extern "C" int beacon_linear_bwd(void* dx, void* dweight, void* dbias, const void* dout, const void* x,
+                                 const void* weight, int64_t m, int64_t k, int64_t n, int dtype, void* stream) {
+  BEACON_TRY(check_dtype_gemm(dtype));
+  BEACON_TRY(check_dims("linear_bwd", m, k, n));
+  BEACON_TRY(beacon_matmul_bwd(dx, dweight, dout, x, weight, m, k, n, dtype, stream));
+  if (dbias && n > 0) {
+    int dev;
+    DeviceInfo* di;
+    BEACON_TRY(current_device(&dev, &di));
+    cudaStream_t st = as_stream(stream);
+    const int parts = (int)std::min<int64_t>(std::max<int64_t>(m, 1), (int64_t)di->sms * 2);
+    void* ws = nullptr;
+    BEACON_TRY(get_workspace(dev, (size_t)parts * n * 4, nullptr, 0, &ws));
+    float* part = reinterpret_cast<float*>(ws);
+    if (dtype == BEACON_F32) {
+      k_colsum_partial<float><<<parts, 256, 0, st>>>(part, reinterpret_cast<const float*>(dout), m, (int)n);
+      BEACON_TRY(check_launch("k_colsum_partial"));
+      k_colsum<float><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(reinterpret_cast<float*>(dbias), part, parts,
+                                                                     (int)n);
+    } else {
+      k_colsum_partial<bf16><<<parts, 256, 0, st>>>(part, reinterpret_cast<const bf16*>(dout), m, (int)n);
+      BEACON_TRY(check_launch("k_colsum_partial"));
+      k_colsum<bf16><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(reinterpret_cast<bf16*>(dbias), part, parts,
+                                                                    (int)n);
+    }
+    BEACON_TRY(check_launch("k_colsum"));
+  }
+  return BEACON_OK;
+}
+
+// ===========================================================================
+// elementwise
+// ===========================================================================
+extern "C" int beacon_residual_add_fwd(void* out, const void* a, const void* b, int64_t n, int dtype,
+                                       void* stream) {
+  if (n < 0) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "residual_add: negative n");
+  if (n == 0) return BEACON_OK;
+  int dev;
+  DeviceInfo* di;
+  BEACON_TRY(current_device(&dev, &di));
+  cudaStream_t st = as_stream(stream);
+  const bool vec_ok = aligned16(out) && aligned16(a) && aligned16(b);
+  if (dtype == BEACON_BF16) {
+    if (!vec_ok) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "residual_add: pointers must be 16-byte aligned");
+    k_add_bf16<<<grid_for(n / 8 + 1, 256, di->sms), 256, 0, st>>>(
+        reinterpret_cast<bf16*>(out), reinterpret_cast<const bf16*>(a), reinterpret_cast<const bf16*>(b), n);
+  } else if (dtype == BEACON_F32) {
+    if (!vec_ok) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "residual_add: pointers must be 16-byte aligned");
+    k_add_f32<<<grid_for(n / 4 + 1, 256, di->sms), 256, 0, st>>>(
+        reinterpret_cast<float*>(out), reinterpret_cast<const float*>(a), reinterpret_cast<const float*>(b), n);
+  } else {
+    return fail(BEACON_ERR_UNIMPLEMENTED, "residual_add: dtype %d", dtype);
+  }
+  return check_launch("residual_add_fwd");
+}
+
+extern "C" int beacon_residual_add_bwd(void* d_a, void* d_b, const void* d_out, int64_t n, int dtype,
+                                       void* stream) {
+  if (n < 0) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "residual_add_bwd: negative n");
+  if (n == 0) return BEACON_OK;
+  if (dtype < 0 || dtype > 3) return fail(BEACON_ERR_UNIMPLEMENTED, "residual_add_bwd: dtype %d", dtype);
+  const int es[4] = {4, 2, 2, 1};
+  int dev;
+  DeviceInfo* di;
+  BEACON_TRY(current_device(&dev, &di));
+  if (!aligned16(d_out) || (d_a && !aligned16(d_a)) || (d_b && !aligned16(d_b)))
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "residual_add_bwd: pointers must be 16-byte aligned");
+  const long long nbytes = n * es[dtype];
+  k_fanout2<<<grid_for(nbytes / 16 + 1, 256, di->sms), 256, 0, as_stream(stream)>>>(
+      reinterpret_cast<uint8_t*>(d_a), reinterpret_cast<uint8_t*>(d_b), reinterpret_cast<const uint8_t*>(d_out),
+      nbytes);
+  return check_launch("residual_add_bwd");
+}
+
+extern "C" int beacon_cast(void* dst, const void* src, int64_t n, int kind, void* stream) {
+  if (n < 0) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "cast: negative n");
+  if (kind < 0 || kind > 3) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "cast: unknown kind %d", kind);
+  if (n == 0) return BEACON_OK;
+  int dev;
+  DeviceInfo* di;
+  BEACON_TRY(current_device(&dev, &di));
+  k_cast<<<grid_for(n, 256, di->sms), 256, 0, as_stream(stream)>>>(dst, src, n, kind);
+  return check_launch("cast");
+}
+
+// ===========================================================================
+// RMSNorm
+// ===========================================================================
+extern "C" int beacon_rmsnorm_adjoint_fwd(void* out, const void* x, const void* weight, float* rms,
+                                          int64_t tokens, int64_t dim, float eps, int dtype, void* stream) {
+  if (tokens < 0 || dim <= 0 || dim > INT32_MAX)
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "rmsnorm_fwd: bad shape tokens=%lld dim=%lld",
+                (long long)tokens, (long long)dim);
+  if (tokens == 0) return BEACON_OK;
+  int dev;
+  DeviceInfo* di;
+  BEACON_TRY(current_device(&dev, &di));
+  cudaStream_t st = as_stream(stream);
+  const int grid = (int)std::min<int64_t>(tokens, (int64_t)di->sms * 16);
+  const bool vec = aligned16(out) && aligned16(x) && aligned16(weight) && dim % 8 == 0;
+  const int d = (int)dim;
+#define RMS_FWD(T, V) \
+  k_rmsnorm_fwd<T, V><<<grid, 256, 0, st>>>((T*)out, rms, (const T*)x, (const T*)weight, tokens, d, eps)
+  if (dtype == BEACON_BF16) {
+    if (vec && dim <= 256 * 8 * 1) RMS_FWD(bf16, 1);
+    else if (vec && dim <= 256 * 8 * 2) RMS_FWD(bf16, 2);
+    else if (vec && dim <= 256 * 8 * 4) RMS_FWD(bf16, 4);
+    else if (vec && dim <= 256 * 8 * 8) RMS_FWD(bf16, 8);
+    else k_rmsnorm_fwd_any<bf16><<<grid, 256, 0, st>>>((bf16*)out, rms, (const bf16*)x, (const bf16*)weight, tokens, d, eps);
+  } else if (dtype == BEACON_F32) {
+    if (vec && dim <= 256 * 8 * 1) RMS_FWD(float, 1);
+    else if (vec && dim <= 256 * 8 * 2) RMS_FWD(float, 2);
+    else if (vec && dim <= 256 * 8 * 4) RMS_FWD(float, 4);
+    else k_rmsnorm_fwd_any<float><<<grid, 256, 0, st>>>((float*)out, rms, (const float*)x, (const float*)weight, tokens, d, eps);
+  } else {
+    return fail(BEACON_ERR_UNIMPLEMENTED, "rmsnorm_fwd: dtype %d", dtype);
+  }
+#undef RMS_FWD
+  return check_launch("rmsnorm_fwd");
+}
+
+extern "C" int beacon_rmsnorm_adjoint_bwd(void* dx, void* dweight, const void* dy, const void* x, const float* rms,
+                                          const void* weight, int64_t tokens, int64_t dim, int dtype,
+                                          void* workspace, size_t workspace_bytes, void* stream) {
+  if (tokens < 0 || dim <= 0 || dim > INT32_MAX)
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "rmsnorm_bwd: bad shape");
+  if (dtype != BEACON_BF16 && dtype != BEACON_F32) return fail(BEACON_ERR_UNIMPLEMENTED, "rmsnorm_bwd: dtype %d", dtype);
+  int dev;
+  DeviceInfo* di;
+  BEACON_TRY(current_device(&dev, &di));
+  cudaStream_t st = as_stream(stream);
+  const int es = dtype == BEACON_F32 ? 4 : 2;
+  if (tokens == 0) {
+    if (dweight) return zero_fill(dweight, (size_t)dim * es, st);
+    return BEACON_OK;
+  }
+  const bool vec = aligned16(dx) && aligned16(x) && aligned16(dy) && aligned16(weight);
+  if (!vec) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "rmsnorm_bwd: pointers must be 16-byte aligned");
+  const int grid = (int)std::min<int64_t>(tokens, (int64_t)di->sms * 4);
+  float* part = nullptr;
+  if (dweight) {
+    void* ws = nullptr;
+    BEACON_TRY(get_workspace(dev, (size_t)grid * dim * 4, workspace, workspace_bytes, &ws));
+    part = reinterpret_cast<float*>(ws);
+  }
+  if (dtype == BEACON_BF16) {
+    k_rmsnorm_bwd<bf16><<<grid, 256, 0, st>>>((bf16*)dx, part, (const bf16*)dy, (const bf16*)x, rms,
+                                              (const bf16*)weight, tokens, (int)dim);
+    BEACON_TRY(check_launch("rmsnorm_bwd"));
+    if (dweight) k_colsum<bf16><<<(unsigned)((dim + 255) / 256), 256, 0, st>>>((bf16*)dweight, part, grid, (int)dim);
+  } else {
+    k_rmsnorm_bwd<float><<<grid, 256, 0, st>>>((float*)dx, part, (const float*)dy, (const float*)x, rms,
+                                               (const float*)weight, tokens, (int)dim);
+    BEACON_TRY(check_launch("rmsnorm_bwd"));
+    if (dweight) k_colsum<float><<<(unsigned)((dim + 255) / 256), 256, 0, st>>>((float*)dweight, part, grid, (int)dim);
+  }
+  if (dweight) BEACON_TRY(check_launch("rmsnorm_bwd colsum"));
+  return BEACON_OK;
+}
+
+#include "abi_attention.inc"
+#include "abi_swiglu.inc"
+#include "abi_arena.inc"

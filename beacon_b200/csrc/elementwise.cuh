@@ -1,0 +1,372 @@
+// elementwise.cuh -- residual add, casts, RMSNorm forward/backward.
+//
+// All HBM-bound: 128-bit vectorised, coalesced loads and stores, fp32 math,
+// warp-shuffle reductions.  The dtype codecs restate the reference's bit-level
+// rules (crates/beacon-core/src/dtype.rs) so casts are bit-exact with it.
+#pragma once
+
+#include "sm100.cuh"
+
+namespace beacon {
+
+// ---------------------------------------------------------------------------
+// dtype codecs (device), dtype.rs:58-66 (bf16) and dtype.rs:138-209 (fp8 e4m3)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint16_t bf16_bits_from_f32(float x) {
+  const uint32_t bits = __float_as_uint(x);
+  if ((bits & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((bits >> 16) | 0x0040u);
+  const uint32_t bias = 0x7fffu + ((bits >> 16) & 1u);
+  return (uint16_t)((bits + bias) >> 16);
+}
+
+// Rust f32::round is half-away-from-zero; ties are detected inside an
+// f32::EPSILON window and sent to the even neighbour (dtype.rs:197-209).
+__device__ __forceinline__ float round_half_even_window(float x) {
+  const float r = roundf(x);
+  if (fabsf(x - floorf(x) - 0.5f) < 1.1920929e-7f) {
+    const float down = floorf(x);
+    return ((((long long)down) % 2) == 0) ? down : down + 1.0f;
+  }
+  return r;
+}
+
+__device__ __forceinline__ uint8_t fp8e4m3_from_f32(float x) {
+  if (isnan(x)) return 0xff;
+  const uint8_t sign_bit = signbit(x) ? 0x80 : 0x00;
+  const float ax = fabsf(x);
+  if (ax == 0.0f) return sign_bit;
+  if (ax >= 448.0f) return (uint8_t)(sign_bit | 0x7e);
+  if (ax < 0.015625f) {  // below 2^-6, the smallest normal: multiples of 2^-9
+    float m = round_half_even_window(ax * 512.0f);
+    if (m > 7.0f) m = 7.0f;
+    return (uint8_t)(sign_bit | (uint8_t)m);
+  }
+  // floor(log2(ax)) of a normal float is its unbiased exponent; where a rounded
+  // log2 would land on the next integer the mantissa rounds up to 8 below and
+  // the exponent is bumped, giving the same code.
+  int exp = (int)((__float_as_uint(ax) >> 23) & 0xff) - 127;
+  if (exp < -6) exp = -6;
+  const float frac = ax * __uint_as_float((uint32_t)(127 - exp) << 23) - 1.0f;  // ax / 2^exp, exact
+  int mant = (int)round_half_even_window(frac * 8.0f);
+  int biased = exp + 7;
+  if (mant == 8) {
+    mant = 0;
+    biased += 1;
+  }
+  if (biased >= 0x0f && mant >= 0x07) return (uint8_t)(sign_bit | 0x7e);
+  return (uint8_t)(sign_bit | (uint8_t)(biased << 3) | (uint8_t)mant);
+}
+
+__device__ __forceinline__ float fp8e4m3_to_f32(uint8_t b) {
+  const float sign = (b & 0x80) ? -1.0f : 1.0f;
+  const int exp = (b >> 3) & 0x0f;
+  const int mant = b & 0x07;
+  if (exp == 0x0f && mant == 0x07) return __uint_as_float(0x7fc00000u);
+  if (exp == 0) return sign * (float)mant * 0.001953125f;  // 2^-9
+  return sign * (1.0f + (float)mant * 0.125f) * __uint_as_float((uint32_t)(exp - 7 + 127) << 23);
+}
+
+// ---------------------------------------------------------------------------
+// residual add / backward / casts: grid-stride, 16-byte vectors + scalar tail
+// ---------------------------------------------------------------------------
+__global__ void k_add_bf16(__nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ a,
+                           const __nv_bfloat16* __restrict__ b, long long n) {
+  const long long nvec = n / 8;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+    const uint4 va = reinterpret_cast<const uint4*>(a)[i];
+    const uint4 vb = reinterpret_cast<const uint4*>(b)[i];
+    const __nv_bfloat162* pa = reinterpret_cast<const __nv_bfloat162*>(&va);
+    const __nv_bfloat162* pb = reinterpret_cast<const __nv_bfloat162*>(&vb);
+    uint4 vo;
+    __nv_bfloat162* po = reinterpret_cast<__nv_bfloat162*>(&vo);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 fa = __bfloat1622float2(pa[j]), fb = __bfloat1622float2(pb[j]);
+      po[j] = __floats2bfloat162_rn(fa.x + fb.x, fa.y + fb.y);
+    }
+    reinterpret_cast<uint4*>(out)[i] = vo;
+  }
+  for (long long i = nvec * 8 + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    out[i] = __float2bfloat16_rn(__bfloat162float(a[i]) + __bfloat162float(b[i]));
+}
+
+__global__ void k_add_f32(float* __restrict__ out, const float* __restrict__ a, const float* __restrict__ b,
+                          long long n) {
+  const long long nvec = n / 4;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+    const float4 va = reinterpret_cast<const float4*>(a)[i];
+    const float4 vb = reinterpret_cast<const float4*>(b)[i];
+    reinterpret_cast<float4*>(out)[i] = make_float4(va.x + vb.x, va.y + vb.y, va.z + vb.z, va.w + vb.w);
+  }
+  for (long long i = nvec * 4 + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    out[i] = a[i] + b[i];
+}
+
+// d_a = d_b = d_out, for any element size: copy 16-byte vectors then bytes.
+__global__ void k_fanout2(uint8_t* __restrict__ da, uint8_t* __restrict__ db, const uint8_t* __restrict__ src,
+                          long long nbytes) {
+  const long long nvec = nbytes / 16;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+    const uint4 v = reinterpret_cast<const uint4*>(src)[i];
+    if (da) reinterpret_cast<uint4*>(da)[i] = v;
+    if (db) reinterpret_cast<uint4*>(db)[i] = v;
+  }
+  for (long long i = nvec * 16 + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nbytes; i += stride) {
+    if (da) da[i] = src[i];
+    if (db) db[i] = src[i];
+  }
+}
+
+// kind: 0 f32->fp8, 1 fp8->f32, 2 f32->bf16, 3 bf16->f32 (CastKind order)
+__global__ void k_cast(void* __restrict__ dst, const void* __restrict__ src, long long n, int kind) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    switch (kind) {
+      case 0:
+        reinterpret_cast<uint8_t*>(dst)[i] = fp8e4m3_from_f32(reinterpret_cast<const float*>(src)[i]);
+        break;
+      case 1:
+        reinterpret_cast<float*>(dst)[i] = fp8e4m3_to_f32(reinterpret_cast<const uint8_t*>(src)[i]);
+        break;
+      case 2:
+        reinterpret_cast<uint16_t*>(dst)[i] = bf16_bits_from_f32(reinterpret_cast<const float*>(src)[i]);
+        break;
+      default:
+        reinterpret_cast<float*>(dst)[i] =
+            __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(src)[i] << 16);
+        break;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// RMSNorm
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = __bfloat1622float2(h[j]);
+    v[2 * j] = f.x;
+    v[2 * j + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&v)[8]) {
+  uint4 u;
+  u.x = pack_bf16x2(v[0], v[1]);
+  u.y = pack_bf16x2(v[2], v[3]);
+  u.z = pack_bf16x2(v[4], v[5]);
+  u.w = pack_bf16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+__device__ __forceinline__ void store8(float* p, const float (&v)[8]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+__device__ __forceinline__ float ldf(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+__device__ __forceinline__ float ldf(const float* p) { return *p; }
+__device__ __forceinline__ void stf(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+__device__ __forceinline__ void stf(float* p, float v) { *p = v; }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide sum for blockDim.x == 256; `red` holds 8 floats of shared memory.
+__device__ __forceinline__ float block_sum_256(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = (l < 8) ? red[l] : 0.0f;
+  t = warp_sum(t);
+  return t;
+}
+
+// One CTA of 256 threads per row (norm.rs:5-9 `rowwise`), grid-stride over rows.
+// VEC: 8-element vectors per thread held in registers (dim <= 256*8*VEC).
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) k_rmsnorm_fwd(T* __restrict__ y, float* __restrict__ rms,
+                                                     const T* __restrict__ x, const T* __restrict__ w,
+                                                     long long rows, int dim, float eps) {
+  __shared__ float red[8];
+  const int nvec = dim / 8;
+  for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
+    const T* xr = x + r * dim;
+    float v[VEC][8];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const int vi = threadIdx.x + i * 256;
+      if (vi < nvec) {
+        load8(xr + vi * 8, v[i]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss = fmaf(v[i][j], v[i][j], ss);
+      }
+    }
+    for (int e = nvec * 8 + threadIdx.x; e < dim; e += 256) {  // dim % 8 tail
+      const float t = ldf(xr + e);
+      ss = fmaf(t, t, ss);
+    }
+    ss = block_sum_256(ss, red);
+    const float rr = sqrtf(ss / (float)dim + eps);
+    const float inv = 1.0f / rr;
+    if (threadIdx.x == 0) rms[r] = rr;
+    T* yr = y + r * dim;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const int vi = threadIdx.x + i * 256;
+      if (vi < nvec) {
+        float g[8], o[8];
+        load8(w + vi * 8, g);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = v[i][j] * inv * g[j];
+        store8(yr + vi * 8, o);
+      }
+    }
+    for (int e = nvec * 8 + threadIdx.x; e < dim; e += 256) stf(yr + e, ldf(xr + e) * inv * ldf(w + e));
+  }
+}
+
+// Generic fallback for any dim (two passes over the row, second from L1/L2).
+template <typename T>
+__global__ void __launch_bounds__(256) k_rmsnorm_fwd_any(T* __restrict__ y, float* __restrict__ rms,
+                                                         const T* __restrict__ x, const T* __restrict__ w,
+                                                         long long rows, int dim, float eps) {
+  __shared__ float red[8];
+  for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
+    const T* xr = x + r * dim;
+    float ss = 0.0f;
+    for (int e = threadIdx.x; e < dim; e += 256) {
+      const float t = ldf(xr + e);
+      ss = fmaf(t, t, ss);
+    }
+    ss = block_sum_256(ss, red);
+    const float rr = sqrtf(ss / (float)dim + eps);
+    const float inv = 1.0f / rr;
+    if (threadIdx.x == 0) rms[r] = rr;
+    for (int e = threadIdx.x; e < dim; e += 256) stf(y + r * dim + e, ldf(xr + e) * inv * ldf(w + e));
+  }
+}
+
+// Backward: dx per row; dweight partial sums per CTA into part[blockIdx.x, dim] (fp32).
+template <typename T>
+__global__ void __launch_bounds__(256) k_rmsnorm_bwd(T* __restrict__ dx, float* __restrict__ part,
+                                                     const T* __restrict__ dy, const T* __restrict__ x,
+                                                     const float* __restrict__ rms, const T* __restrict__ w,
+                                                     long long rows, int dim) {
+  __shared__ float red[8];
+  const bool vec = (dim % 8) == 0;
+  float* pr = part ? part + (long long)blockIdx.x * dim : nullptr;
+  // zero this CTA's partial row
+  if (pr)
+    for (int e = threadIdx.x; e < dim; e += 256) pr[e] = 0.0f;
+  __syncthreads();
+  for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
+    const T* xr = x + r * dim;
+    const T* dyr = dy + r * dim;
+    const float rr = rms[r];
+    const float inv = 1.0f / rr;
+    float dot = 0.0f;
+    if (vec) {
+      for (int vi = threadIdx.x; vi < dim / 8; vi += 256) {
+        float a[8], b[8], g[8];
+        load8(xr + vi * 8, a);
+        load8(dyr + vi * 8, b);
+        load8(w + vi * 8, g);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dot = fmaf(g[j] * b[j], a[j], dot);
+      }
+    } else {
+      for (int e = threadIdx.x; e < dim; e += 256) dot = fmaf(ldf(w + e) * ldf(dyr + e), ldf(xr + e), dot);
+    }
+    dot = block_sum_256(dot, red);
+    const float c = dot * inv * inv * inv / (float)dim;
+    T* dxr = dx + r * dim;
+    if (vec) {
+      for (int vi = threadIdx.x; vi < dim / 8; vi += 256) {
+        float a[8], b[8], g[8], o[8];
+        load8(xr + vi * 8, a);
+        load8(dyr + vi * 8, b);
+        load8(w + vi * 8, g);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = g[j] * b[j] * inv - a[j] * c;
+        store8(dxr + vi * 8, o);
+        if (pr) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) pr[vi * 8 + j] += b[j] * a[j] * inv;
+        }
+      }
+    } else {
+      for (int e = threadIdx.x; e < dim; e += 256) {
+        const float a = ldf(xr + e), b = ldf(dyr + e);
+        stf(dxr + e, ldf(w + e) * b * inv - a * c);
+        if (pr) pr[e] += b * a * inv;
+      }
+    }
+  }
+}
+
+// dweight[d] = sum over CTAs of part[cta, d]
+template <typename T>
+__global__ void k_colsum(T* __restrict__ out, const float* __restrict__ part, int nparts, int dim) {
+  const int d = blockIdx.x * blockDim.x + threadIdx.x;
+  if (d >= dim) return;
+  float s = 0.0f;
+  for (int i = 0; i < nparts; ++i) s += part[(long long)i * dim + d];
+  stf(out + d, s);
+}
+
+// dbias[n] = sum_rows dout[m, n]: CTA-partial column sums (fp32) then k_colsum.
+template <typename T>
+__global__ void __launch_bounds__(256) k_colsum_partial(float* __restrict__ part, const T* __restrict__ src,
+                                                        long long rows, int cols) {
+  for (int c = threadIdx.x; c < cols; c += 256) {
+    float s = 0.0f;
+    for (long long r = blockIdx.x; r < rows; r += gridDim.x) s += ldf(src + r * cols + c);
+    part[(long long)blockIdx.x * cols + c] = s;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// SwiGLU elementwise pieces (mlp.rs:12-52); silu(z) = z * sigmoid(z)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float sigmoid_f(float z) { return 1.0f / (1.0f + expf(-z)); }
+
+// h = silu(gate) * up
+template <typename T>
+__global__ void k_swiglu_h(T* __restrict__ h, const T* __restrict__ gate, const T* __restrict__ up, long long n) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const float g = ldf(gate + i), u = ldf(up + i);
+    stf(h + i, g * sigmoid_f(g) * u);
+  }
+}
+
+// In place: gate <- dgate = dh * up * s * (1 + g (1 - s)),  up <- dup = dh * silu(g),  s = sigmoid(g).
+// Optionally also writes h = silu(g) * up first (for dWd).
+template <typename T>
+__global__ void k_swiglu_bwd_elem(T* __restrict__ gate, T* __restrict__ up, const T* __restrict__ dh, long long n) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const float g = ldf(gate + i), u = ldf(up + i), d = ldf(dh + i);
+    const float s = sigmoid_f(g);
+    stf(gate + i, d * u * s * (1.0f + g * (1.0f - s)));
+    stf(up + i, d * g * s);
+  }
+}
+
+}  // namespace beacon

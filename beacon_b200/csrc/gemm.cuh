@@ -1,0 +1,393 @@
+// gemm.cuh -- bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// C[M,N] = A[M,K] . B[K,N] (+ fused epilogue), fp32 accumulation in TMEM.
+// Either operand may be K-major or MN-major in HBM, so one kernel serves
+// matmul_fwd (A K-major, B MN-major), dlhs = dout . rhs^T (B K-major) and
+// drhs = lhs^T . dout (A and B MN-major) without any transpose pass.
+//
+// Persistent, warp-specialised CTA of 6 warps, one CTA per SM:
+//   warp 0      TMA producer: STAGES-deep ring of (A 128x64, B BNx64) bf16 tiles,
+//               128-byte swizzle, one mbarrier "full" and "empty" per stage.
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16).
+//   warps 2-5   epilogue: tcgen05.ld of the fp32 accumulator (one TMEM lane per
+//               thread), fused bias / row-scale / residual / SwiGLU, bf16 or f32 store.
+// The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
+// of tile i overlaps the main loop of tile i+1.
+#pragma once
+
+#include "sm100.cuh"
+
+namespace beacon {
+
+enum GemmEpilogue : int {
+  kEpiStore = 0,     // out = acc
+  kEpiBias = 1,      // out = acc + bias[col]
+  kEpiRowScale = 2,  // out = acc * row_scale[row] (+ bias[col] when bias != null)
+  kEpiResidual = 3,  // out = acc + residual[row, col]
+  kEpiSwiglu = 4,    // out[:, j] = silu(acc_gate[:, j]) * acc_up[:, j]; B = [Wg | Wu] per tile
+};
+
+struct GemmParams {
+  int M, N, K;            // N: output columns (SwiGLU: F, the hidden width)
+  int tiles_m, tiles_n;
+  void* out;
+  long long ldo;          // output row stride, elements
+  int out_f32;            // 1: float32 output, 0: bf16 output
+  int epi;
+  int aux_f32;            // 1: bias / residual are float32, 0: bf16
+  const void* bias;       // [N]
+  const float* row_scale; // [M]
+  const void* residual;   // [M, ldr]
+  long long ldr;
+};
+
+__device__ __forceinline__ float gemm_aux(const void* base, long long idx, int is_f32) {
+  return is_f32 ? reinterpret_cast<const float*>(base)[idx]
+                : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[idx]);
+}
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int BM = 128;
+  static constexpr int BK = 64;  // one 128-byte swizzle row of bf16
+  static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr uint32_t A_BYTES = BM * BK * 2;
+  static constexpr uint32_t B_BYTES = BN * BK * 2;
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;  // power of two: 512 / 256 / 128
+  static constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+  static constexpr int THREADS = 192;
+};
+
+__device__ __forceinline__ float silu_f(float z) { return z / (1.0f + __expf(-z)); }
+
+// Apply the epilogue to 32 consecutive columns [col0, col0+32) of one row and store.
+__device__ __forceinline__ void gemm_store_chunk(const GemmParams& p, int row, int col0, float (&v)[32]) {
+  if (row >= p.M) return;
+  if (p.epi == kEpiRowScale) {
+    const float s = p.row_scale[row];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] *= s;
+  }
+  if ((p.epi == kEpiBias || p.epi == kEpiRowScale) && p.bias != nullptr) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j < p.N) v[j] += gemm_aux(p.bias, col0 + j, p.aux_f32);
+  }
+  if (p.epi == kEpiResidual) {
+    const long long rbase = (long long)row * p.ldr;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j < p.N) v[j] += gemm_aux(p.residual, rbase + col0 + j, p.aux_f32);
+  }
+  const bool full = (col0 + 32 <= p.N);
+  if (p.out_f32) {
+    float* o = reinterpret_cast<float*>(p.out) + (long long)row * p.ldo + col0;
+    if (full && ((p.ldo & 3) == 0)) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    } else {
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < p.N) o[j] = v[j];
+    }
+  } else {
+    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + (long long)row * p.ldo + col0;
+    if (full && ((p.ldo & 7) == 0)) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        uint4 w;
+        w.x = pack_bf16x2(v[j + 0], v[j + 1]);
+        w.y = pack_bf16x2(v[j + 2], v[j + 3]);
+        w.z = pack_bf16x2(v[j + 4], v[j + 5]);
+        w.w = pack_bf16x2(v[j + 6], v[j + 7]);
+        *reinterpret_cast<uint4*>(o + j) = w;
+      }
+    } else {
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < p.N) o[j] = __float2bfloat16_rn(v[j]);
+    }
+  }
+}
+
+// Fault-site codes (g_beacon_status[1]) for the GEMM's waits.
+enum : unsigned int {
+  kSiteGemmEmpty = 0x101,
+  kSiteGemmTmemEmpty = 0x102,
+  kSiteGemmFull = 0x103,
+  kSiteGemmTmemFull = 0x104,
+  kSiteGemmDrain = 0x105,
+};
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(192, 1)
+    k_gemm_bf16_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmB2, const GemmParams p) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int BM = Cfg::BM, BK = Cfg::BK, STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;  // [2]
+  uint64_t* tempty = tfull + 2;      // [2]
+  uint64_t* drain = tempty + 2;      // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t warp = warp_id(), lane = lane_id();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);  // one arrive per epilogue warp
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (p.epi == kEpiSwiglu) tma_prefetch_desc(&tmB2);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_tiles = p.tiles_m * p.tiles_n;
+  const int ktiles = (p.K + BK - 1) / BK;
+  const bool swiglu = (p.epi == kEpiSwiglu);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0, issued_parity = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int tm = tile / p.tiles_n, tn = tile % p.tiles_n;
+        for (int kt = 0; kt < ktiles; ++kt) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteGemmEmpty)) {
+            ok = false;
+            break;
+          }
+          uint64_t* fb = &full[stage];
+          mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
+          uint8_t* a = sA + stage * Cfg::A_BYTES;
+          uint8_t* b = sB + stage * Cfg::B_BYTES;
+          const int k0 = kt * BK;
+          if constexpr (!A_MN) {
+            tma_load_2d(a, &tmA, fb, k0, tm * BM);
+          } else {
+            tma_load_2d(a, &tmA, fb, tm * BM, k0);
+            tma_load_2d(a + 64 * BK * 2, &tmA, fb, tm * BM + 64, k0);
+          }
+          if (!swiglu) {
+            if constexpr (!B_MN) {
+              tma_load_2d(b, &tmB, fb, k0, tn * BN);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j) tma_load_2d(b + j * 64 * BK * 2, &tmB, fb, tn * BN + j * 64, k0);
+            }
+          } else {
+            const int n0 = tn * (BN / 2);
+            if constexpr (!B_MN) {
+              tma_load_2d(b, &tmB, fb, k0, n0);
+              tma_load_2d(b + (BN / 2) * 128, &tmB2, fb, k0, n0);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BN / 128; ++j) {
+                tma_load_2d(b + j * 64 * BK * 2, &tmB, fb, n0 + j * 64, k0);
+                tma_load_2d(b + (j + BN / 128) * 64 * BK * 2, &tmB2, fb, n0 + j * 64, k0);
+              }
+            }
+          }
+          issued |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Let every TMA copy already in flight land before the CTA can exit.
+        volatile int no_abort = 0;
+        for (int s = 0; s < STAGES; ++s)
+          if (issued & (1u << s)) mbar_wait(&full[s], (issued_parity >> s) & 1u, &no_abort, kSiteGemmDrain);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_f16(BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, kSiteGemmTmemEmpty)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+        for (int kt = 0; kt < ktiles; ++kt) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, kSiteGemmFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * Cfg::A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * Cfg::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = A_MN ? make_sdesc_sw128(a_addr + kk * 2048, 64 * BK * 2, 1024)
+                                     : make_sdesc_sw128(a_addr + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? make_sdesc_sw128(b_addr + kk * 2048, 64 * BK * 2, 1024)
+                                     : make_sdesc_sw128(b_addr + kk * 32, 16, 1024);
+            umma_f16_ss(d, ad, bd, idesc, (kt | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);  // frees the smem stage once these MMAs have read it
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);  // accumulator ready for the epilogue
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      // Drain: every MMA this thread issued has finished before TMEM is freed.
+      umma_commit(drain);
+      volatile int no_abort = 0;
+      mbar_wait(drain, 0, &no_abort, kSiteGemmDrain);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5)
+    const uint32_t q = warp & 3u;  // TMEM lane quarter this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int tm = tile / p.tiles_n, tn = tile % p.tiles_n;
+      const bool got = mbar_wait(&tfull[acc], acc_phase, abort_flag, kSiteGemmTmemFull);
+      if (!__all_sync(0xffffffffu, got)) break;  // warp-uniform: tcgen05.ld below is warp-collective
+      tc_fence_after();
+      const int row = tm * BM + (int)(q * 32 + lane);
+      const uint32_t tbase = tmem_base + ((q * 32u) << 16) + (uint32_t)(acc * BN);
+      if (!swiglu) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c * 32, r);
+          tmem_wait_ld();
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          const int col0 = tn * BN + c * 32;
+          if (col0 < p.N) gemm_store_chunk(p, row, col0, v);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          uint32_t g[32], u[32];
+          tmem_ld32(tbase + c * 32, g);
+          tmem_ld32(tbase + BN / 2 + c * 32, u);
+          tmem_wait_ld();
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = silu_f(__uint_as_float(g[j])) * __uint_as_float(u[j]);
+          const int col0 = tn * (BN / 2) + c * 32;
+          if (col0 < p.N) gemm_store_chunk(p, row, col0, v);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Exact-FP32 SIMT GEMM (FFMA only, no TF32) for f32 operands and for bf16 shapes
+// the TMA path cannot describe (row strides not a multiple of 16 bytes).
+// A(m,k) = A[m*sam + k*sak], B(k,n) = B[k*sbk + n*sbn]; 64x64 tile, 4x4 per thread.
+// ---------------------------------------------------------------------------
+template <typename TIn>
+__device__ __forceinline__ float to_f(TIn x);
+template <>
+__device__ __forceinline__ float to_f<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+template <typename TIn>
+__global__ void __launch_bounds__(256)
+    k_gemm_simt(const TIn* __restrict__ A, long long sam, long long sak, const TIn* __restrict__ B, long long sbk,
+                long long sbn, const GemmParams p) {
+  __shared__ float As[16][64 + 1];
+  __shared__ float Bs[16][64 + 1];
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < p.K; k0 += 16) {
+    for (int e = threadIdx.x; e < 16 * 64; e += 256) {
+      const int kk = e / 64, mm = e % 64;
+      const int m = m0 + mm, k = k0 + kk;
+      As[kk][mm] = (m < p.M && k < p.K) ? to_f(A[m * sam + k * sak]) : 0.0f;
+      const int n = n0 + mm;
+      Bs[kk][mm] = (n < p.N && k < p.K) ? to_f(B[k * sbk + n * sbn]) : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+  for (int i = 0; i < 4; ++i) {
+    const int m = m0 + ty * 4 + i;
+    if (m >= p.M) continue;
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + tx * 4 + j;
+      if (n >= p.N) continue;
+      float v = acc[i][j];
+      if (p.epi == kEpiRowScale) v *= p.row_scale[m];
+      if ((p.epi == kEpiBias || p.epi == kEpiRowScale) && p.bias) v += gemm_aux(p.bias, n, p.aux_f32);
+      if (p.epi == kEpiResidual) v += gemm_aux(p.residual, m * p.ldr + n, p.aux_f32);
+      if (p.out_f32)
+        reinterpret_cast<float*>(p.out)[m * p.ldo + n] = v;
+      else
+        reinterpret_cast<__nv_bfloat16*>(p.out)[m * p.ldo + n] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+}  // namespace beacon

@@ -1,0 +1,235 @@
+"""Tensor-level front end over the C ABI (torch tensors for device memory and streams).
+
+Every function checks its operands, calls one ``beacon_*`` entry point on the
+current torch stream, and raises a :mod:`beacon_b200.errors` variant on failure.
+Operands must be contiguous CUDA tensors: there is no CPU path.
+
+Shapes follow the reference's launcher traits (crates/beacon-cuda/src/*.rs):
+matrices are row-major ``[rows, cols]``, attention tensors ``[B, H, S, D]``.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from .errors import InvalidLaunchConfig, check
+
+_DT = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16}
+
+
+def _p(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _dtype(*ts) -> int:
+    t0 = ts[0]
+    if t0.dtype not in _DT:
+        raise InvalidLaunchConfig(f"dtype {t0.dtype} not supported (float32, bfloat16)")
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise InvalidLaunchConfig("operands must be CUDA tensors (no CPU path)")
+        if not t.is_contiguous():
+            raise InvalidLaunchConfig("operands must be contiguous")
+        if t.dtype != t0.dtype:
+            raise InvalidLaunchConfig(f"mixed dtypes {t0.dtype} / {t.dtype}")
+    return _DT[t0.dtype]
+
+
+# ---------------------------------------------------------------- matmul / linear
+
+def matmul_fwd(lhs, rhs, out=None):
+    """out[m,n] = lhs[m,k] . rhs[k,n]  (matmul.rs:18-29)."""
+    m, k = lhs.shape
+    k2, n = rhs.shape
+    if k != k2:
+        raise InvalidLaunchConfig(f"matmul_fwd: inner dims {k} vs {k2}")
+    dt = _dtype(lhs, rhs)
+    if out is None:
+        out = torch.empty(m, n, dtype=lhs.dtype, device=lhs.device)
+    check(_lib.lib().beacon_matmul_fwd(_p(out), _p(lhs), _p(rhs), m, k, n, dt, _stream()))
+    return out
+
+
+def matmul_bwd(dout, lhs, rhs, need_dlhs=True, need_drhs=True):
+    """(dlhs, drhs) = (dout . rhs^T, lhs^T . dout)  (matmul.rs:31-44)."""
+    m, k = lhs.shape
+    n = rhs.shape[1]
+    dt = _dtype(dout, lhs, rhs)
+    dl = torch.empty(m, k, dtype=lhs.dtype, device=lhs.device) if need_dlhs else None
+    dr = torch.empty(k, n, dtype=lhs.dtype, device=lhs.device) if need_drhs else None
+    check(_lib.lib().beacon_matmul_bwd(_p(dl), _p(dr), _p(dout), _p(lhs), _p(rhs), m, k, n, dt, _stream()))
+    return dl, dr
+
+
+def linear_fwd(x, weight, bias=None, out=None):
+    """out = x . weight + bias, weight [k, n]  (matmul.rs:46-58)."""
+    m, k = x.shape
+    n = weight.shape[1]
+    dt = _dtype(x, weight, bias)
+    if out is None:
+        out = torch.empty(m, n, dtype=x.dtype, device=x.device)
+    check(_lib.lib().beacon_linear_fwd(_p(out), _p(x), _p(weight), _p(bias), m, k, n, dt, _stream()))
+    return out
+
+
+def linear_bwd(dout, x, weight, need_dbias=True):
+    """(dx, dweight, dbias)  (matmul.rs:60-78)."""
+    m, k = x.shape
+    n = weight.shape[1]
+    dt = _dtype(dout, x, weight)
+    dx = torch.empty_like(x)
+    dw = torch.empty_like(weight)
+    db = torch.empty(n, dtype=x.dtype, device=x.device) if need_dbias else None
+    check(_lib.lib().beacon_linear_bwd(_p(dx), _p(dw), _p(db), _p(dout), _p(x), _p(weight), m, k, n, dt,
+                                       _stream()))
+    return dx, dw, db
+
+
+# ---------------------------------------------------------------- attention
+
+def attention_fwd(q, k, v, causal=True, out=None, lse=None):
+    """(out, lse) for q [B,Hq,S,D], k/v [B,Hkv,S,D]  (attention.rs:21-40; GQA when Hkv < Hq)."""
+    B, Hq, S, D = q.shape
+    Hkv = k.shape[1]
+    dt = _dtype(q, k, v)
+    if out is None:
+        out = torch.empty_like(q)
+    if lse is None:
+        lse = torch.empty(B, Hq, S, dtype=torch.float32, device=q.device)
+    L = _lib.lib()
+    if Hkv == Hq:
+        rc = L.beacon_attention_adjoint_fwd(_p(out), _p(q), _p(k), _p(v), _p(lse), B, Hq, S, D, int(causal), dt,
+                                            _stream())
+    else:
+        rc = L.beacon_attention_gqa_fwd(_p(out), _p(q), _p(k), _p(v), _p(lse), B, Hq, Hkv, S, D, int(causal), dt,
+                                        _stream())
+    check(rc)
+    return out, lse
+
+
+def attention_bwd(dout, q, k, v, lse, causal=True, out=None, workspace=None):
+    """(dq, dk, dv)  (attention.rs:42-64).  Passing the forward `out` skips its recompute."""
+    B, Hq, S, D = q.shape
+    Hkv = k.shape[1]
+    dt = _dtype(dout, q, k, v, out)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    ws = _p(workspace)
+    wsb = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    L = _lib.lib()
+    if out is not None:
+        rc = L.beacon_attention_bwd_with_out(_p(dq), _p(dk), _p(dv), _p(dout), _p(q), _p(k), _p(v), _p(out),
+                                             _p(lse), B, Hq, Hkv, S, D, int(causal), dt, ws, wsb, _stream())
+    elif Hkv == Hq:
+        rc = L.beacon_attention_adjoint_bwd(_p(dq), _p(dk), _p(dv), _p(dout), _p(q), _p(k), _p(v), _p(lse), B, Hq,
+                                            S, D, int(causal), dt, ws, wsb, _stream())
+    else:
+        rc = L.beacon_attention_gqa_bwd(_p(dq), _p(dk), _p(dv), _p(dout), _p(q), _p(k), _p(v), _p(lse), B, Hq,
+                                        Hkv, S, D, int(causal), dt, ws, wsb, _stream())
+    check(rc)
+    return dq, dk, dv
+
+
+def attention_bwd_workspace_bytes(B, Hq, S, D, dtype=torch.bfloat16) -> int:
+    return int(_lib.lib().beacon_attention_bwd_workspace_size(B, Hq, S, D, _DT[dtype]))
+
+
+# ---------------------------------------------------------------- RMSNorm
+
+def rmsnorm_fwd(x, weight, eps=1e-5):
+    """(out, rms) with rms[t] = sqrt(mean(x[t]^2) + eps)  (norm.rs:20-31)."""
+    T, dim = x.shape
+    dt = _dtype(x, weight)
+    out = torch.empty_like(x)
+    rms = torch.empty(T, dtype=torch.float32, device=x.device)
+    check(_lib.lib().beacon_rmsnorm_adjoint_fwd(_p(out), _p(x), _p(weight), _p(rms), T, dim, eps, dt, _stream()))
+    return out, rms
+
+
+def rmsnorm_bwd(dy, x, rms, weight):
+    """(dx, dweight)  (norm.rs:33-50)."""
+    T, dim = x.shape
+    dt = _dtype(dy, x, weight)
+    dx = torch.empty_like(x)
+    dw = torch.empty_like(weight)
+    check(_lib.lib().beacon_rmsnorm_adjoint_bwd(_p(dx), _p(dw), _p(dy), _p(x), _p(rms), _p(weight), T, dim, dt,
+                                                None, 0, _stream()))
+    return dx, dw
+
+
+# ---------------------------------------------------------------- SwiGLU MLP
+
+def swiglu_fwd(x, gate_proj, up_proj, down_proj):
+    """out = (silu(x Wg) * (x Wu)) Wd  (mlp.rs:12-29)."""
+    T, dm = x.shape
+    F = gate_proj.shape[1]
+    dt = _dtype(x, gate_proj, up_proj, down_proj)
+    out = torch.empty(T, dm, dtype=x.dtype, device=x.device)
+    check(_lib.lib().beacon_swiglu_adjoint_fwd(_p(out), _p(x), _p(gate_proj), _p(up_proj), _p(down_proj), T, dm, F,
+                                               dt, None, 0, _stream()))
+    return out
+
+
+def swiglu_bwd(dy, x, gate_proj, up_proj, down_proj):
+    """(dx, dgate_proj, dup_proj, ddown_proj)  (mlp.rs:31-52)."""
+    T, dm = x.shape
+    F = gate_proj.shape[1]
+    dt = _dtype(dy, x, gate_proj, up_proj, down_proj)
+    dx = torch.empty_like(x)
+    dg, du, dd = torch.empty_like(gate_proj), torch.empty_like(up_proj), torch.empty_like(down_proj)
+    check(_lib.lib().beacon_swiglu_adjoint_bwd(_p(dx), _p(dg), _p(du), _p(dd), _p(dy), _p(x), _p(gate_proj),
+                                               _p(up_proj), _p(down_proj), T, dm, F, dt, None, 0, _stream()))
+    return dx, dg, du, dd
+
+
+# ---------------------------------------------------------------- elementwise
+
+def residual_add(a, b):
+    """a + b  (elementwise.rs:47-55)."""
+    dt = _dtype(a, b)
+    out = torch.empty_like(a)
+    check(_lib.lib().beacon_residual_add_fwd(_p(out), _p(a), _p(b), a.numel(), dt, _stream()))
+    return out
+
+
+def residual_add_bwd(dout):
+    """(d_a, d_b) = (dout, dout)  (elementwise.rs:57-65)."""
+    dt = _dtype(dout)
+    da, db = torch.empty_like(dout), torch.empty_like(dout)
+    check(_lib.lib().beacon_residual_add_bwd(_p(da), _p(db), _p(dout), dout.numel(), dt, _stream()))
+    return da, db
+
+
+CAST_F32_TO_FP8E4M3, CAST_FP8E4M3_TO_F32, CAST_F32_TO_BF16, CAST_BF16_TO_F32 = 0, 1, 2, 3
+
+
+def cast(src, kind: int):
+    """CastKind conversions with the reference's rounding (elementwise.rs:120-128)."""
+    if not src.is_cuda or not src.is_contiguous():
+        raise InvalidLaunchConfig("cast: operand must be a contiguous CUDA tensor")
+    out_dt = {0: torch.uint8, 1: torch.float32, 2: torch.bfloat16, 3: torch.float32}[kind]
+    in_dt = {0: torch.float32, 1: torch.uint8, 2: torch.float32, 3: torch.bfloat16}[kind]
+    if src.dtype != in_dt:
+        raise InvalidLaunchConfig(f"cast kind {kind} expects {in_dt}, got {src.dtype}")
+    out = torch.empty(src.shape, dtype=out_dt, device=src.device)
+    check(_lib.lib().beacon_cast(_p(out), _p(src), src.numel(), kind, _stream()))
+    return out
+
+
+def device_status(device: int = 0):
+    """(code, site, count) of device-side faults since the last call; raises Cuda on a fault."""
+    arr = (ctypes.c_uint * 3)()
+    rc = _lib.lib().beacon_device_status(device, arr)
+    check(rc)
+    return tuple(arr)
+
+
+def launch_count() -> int:
+    return int(_lib.lib().beacon_launch_count())

@@ -1,0 +1,214 @@
+/*
+ * beacon_cuda.h -- C ABI of libbeacon_cuda.so, the B200 (sm_100a) kernels behind
+ * beacon's launcher traits.
+ *
+ * One entry point per kernel ID of crates/beacon-cuda (the IDs equal the
+ * launcher strings of crates/beacon-adjoint-table/src/lib.rs:53-116).  Each takes
+ * plain device pointers, explicit shapes, a dtype and a CUDA stream, because the
+ * reference's typed traits drop the shapes before KernelLauncher::launch
+ * (e.g. `let _ = (m, k, n)` at crates/beacon-cuda/src/matmul.rs:27).
+ *
+ * Conventions
+ *  - Row-major contiguous tensors: matrices [rows, cols]; attention tensors
+ *    [B, H, S, D]; LSE [B, H, S] float32; RMSNorm statistic rms [tokens] float32.
+ *  - `dtype` is a beacon_dtype (crates/beacon-core/src/dtype.rs:1-6 order).
+ *    BEACON_BF16: bf16 operands, fp32 accumulation on tcgen05 tensor cores.
+ *    BEACON_F32 : exact fp32 FFMA (no TF32) -- the 1e-5 parity path.
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream).  Every call is
+ *    asynchronous on that stream and never synchronises the device, except
+ *    where a comment says it may grow the library's internal workspace.
+ *  - Return value: a beacon_status that maps 1:1 onto beacon-cuda's LaunchError
+ *    variants (crates/beacon-cuda/src/error.rs:4-13); 0 is Ok.  The message of
+ *    the last error on the calling thread is available from beacon_last_error().
+ *  - No entry point falls back to the CPU.  A device without sm_100 support
+ *    fails with BEACON_ERR_MODULE_LOAD.
+ */
+#ifndef BEACON_CUDA_H
+#define BEACON_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* LaunchError variants, crates/beacon-cuda/src/error.rs:4-13 */
+typedef enum beacon_status {
+    BEACON_OK = 0,
+    BEACON_ERR_UNIMPLEMENTED = 1,
+    BEACON_ERR_INVALID_LAUNCH_CONFIG = 2,
+    BEACON_ERR_MODULE_LOAD = 3,
+    BEACON_ERR_FUNCTION_NOT_FOUND = 4,
+    BEACON_ERR_CUDA = 5,
+    BEACON_ERR_CUBLAS = 6,
+    BEACON_ERR_OUT_OF_MEMORY = 7,
+    BEACON_ERR_SHAPE_MISMATCH = 8
+} beacon_status;
+
+/* DType, crates/beacon-core/src/dtype.rs:1-7 */
+typedef enum beacon_dtype {
+    BEACON_F32 = 0,
+    BEACON_F16 = 1,
+    BEACON_BF16 = 2,
+    BEACON_FP8E4M3 = 3
+} beacon_dtype;
+
+/* CastKind, crates/beacon-cuda/src/elementwise.rs:27-44 */
+typedef enum beacon_cast_kind {
+    BEACON_CAST_F32_TO_FP8E4M3 = 0,
+    BEACON_CAST_FP8E4M3_TO_F32 = 1,
+    BEACON_CAST_F32_TO_BF16 = 2,
+    BEACON_CAST_BF16_TO_F32 = 3
+} beacon_cast_kind;
+
+/* ---- library / errors ----------------------------------------------------- */
+
+/* Library ABI version (major * 10000 + minor * 100 + patch). */
+int beacon_version(void);
+
+/* Copies the calling thread's last error message into buf (NUL-terminated,
+ * truncated to len) and returns the status that produced it. */
+int beacon_last_error(char* buf, size_t len);
+
+/* Reads and clears the device-side fault words of `device`:
+ * out[0] fault code (0 none, 1 a bounded wait timed out), out[1] site,
+ * out[2] number of faults since the last read.  Synchronises the device.
+ * Replaces the kernel-completion check of crates/beacon-cuda/src/device.rs:72-74. */
+int beacon_device_status(int device, unsigned int out[3]);
+
+/* Number of kernels launched by this library since load (all devices, all threads). */
+uint64_t beacon_launch_count(void);
+
+/* ---- matmul / linear: crates/beacon-cuda/src/matmul.rs ---------------------- */
+
+/* matmul_fwd (matmul.rs:18-29): out[m,n] = lhs[m,k] . rhs[k,n] */
+int beacon_matmul_fwd(void* out, const void* lhs, const void* rhs, int64_t m, int64_t k, int64_t n,
+                      int dtype, void* stream);
+
+/* matmul_bwd (matmul.rs:31-44): dlhs[m,k] = dout . rhs^T ; drhs[k,n] = lhs^T . dout.
+ * Either gradient pointer may be NULL to skip it. */
+int beacon_matmul_bwd(void* dlhs, void* drhs, const void* dout, const void* lhs, const void* rhs,
+                      int64_t m, int64_t k, int64_t n, int dtype, void* stream);
+
+/* linear_fwd (matmul.rs:46-58): out[m,n] = x[m,k] . weight[k,n] + bias[n] (bias may be NULL). */
+int beacon_linear_fwd(void* out, const void* x, const void* weight, const void* bias, int64_t m, int64_t k,
+                      int64_t n, int dtype, void* stream);
+
+/* linear_bwd (matmul.rs:60-78): dx = dout . weight^T ; dweight = x^T . dout ; dbias = sum_rows dout.
+ * Any gradient pointer may be NULL to skip it. */
+int beacon_linear_bwd(void* dx, void* dweight, void* dbias, const void* dout, const void* x, const void* weight,
+                      int64_t m, int64_t k, int64_t n, int dtype, void* stream);
+
+/* ---- attention: crates/beacon-cuda/src/attention.rs ------------------------ */
+
+/* attention_fwd (attention.rs:21-40), kernel `attention_adjoint_fwd`:
+ * out = softmax(Q K^T / sqrt(head_dim) + causal mask) V, lse = natural-log logsumexp
+ * per query row (float32).  q, k, v, out: [batch, heads, seqlen, head_dim]. */
+int beacon_attention_adjoint_fwd(void* out, const void* q, const void* k, const void* v, float* lse,
+                                 int64_t batch, int64_t heads, int64_t seqlen, int64_t head_dim, int causal,
+                                 int dtype, void* stream);
+
+/* attention_bwd (attention.rs:42-64), kernel `attention_adjoint_bwd`; adjoint entry
+ * crates/beacon-adjoint-table/src/lib.rs:86-99 (saved q, k, v, lse; scores recomputed).
+ * The forward output is not an argument, so the kernel recomputes it to form
+ * rowsum(dO * O).  Scratch: `workspace` of at least
+ * beacon_attention_bwd_workspace_size(...) bytes, or NULL to use the library's
+ * per-device workspace (grown with cudaMalloc on first use; the growth synchronises
+ * the device). */
+int beacon_attention_adjoint_bwd(void* dq, void* dk, void* dv, const void* dout, const void* q, const void* k,
+                                 const void* v, const float* lse, int64_t batch, int64_t heads, int64_t seqlen,
+                                 int64_t head_dim, int causal, int dtype, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
+size_t beacon_attention_bwd_workspace_size(int64_t batch, int64_t q_heads, int64_t seqlen, int64_t head_dim,
+                                           int dtype);
+
+/* Grouped-query variants.  No reference counterpart: attention.rs:28-31 has only
+ * `heads`; these add kv_heads (q_heads % kv_heads == 0; query head h reads KV head
+ * h / (q_heads / kv_heads)).  kv_heads == q_heads is exactly the entry points above.
+ * k, v, dk, dv: [batch, kv_heads, seqlen, head_dim]. */
+int beacon_attention_gqa_fwd(void* out, const void* q, const void* k, const void* v, float* lse, int64_t batch,
+                             int64_t q_heads, int64_t kv_heads, int64_t seqlen, int64_t head_dim, int causal,
+                             int dtype, void* stream);
+int beacon_attention_gqa_bwd(void* dq, void* dk, void* dv, const void* dout, const void* q, const void* k,
+                             const void* v, const float* lse, int64_t batch, int64_t q_heads, int64_t kv_heads,
+                             int64_t seqlen, int64_t head_dim, int causal, int dtype, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
+/* Backward that is also given the forward output `out`, so it skips the
+ * recompute; for callers that keep O resident.  No reference counterpart. */
+int beacon_attention_bwd_with_out(void* dq, void* dk, void* dv, const void* dout, const void* q, const void* k,
+                                  const void* v, const void* out, const float* lse, int64_t batch,
+                                  int64_t q_heads, int64_t kv_heads, int64_t seqlen, int64_t head_dim,
+                                  int causal, int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- RMSNorm: crates/beacon-cuda/src/norm.rs:19-51 -------------------------- */
+
+/* rmsnorm_fwd (norm.rs:20-31): rms[t] = sqrt(mean(x[t]^2) + eps) (float32),
+ * out = x * weight / rms.  The reference signature has no eps; its callers pass 1e-5. */
+int beacon_rmsnorm_adjoint_fwd(void* out, const void* x, const void* weight, float* rms, int64_t tokens,
+                               int64_t dim, float eps, int dtype, void* stream);
+
+/* rmsnorm_bwd (norm.rs:33-50): dx = (w dy)/rms - x sum(w dy x)/(dim rms^3);
+ * dweight = sum_t dy x / rms (NULL to skip).  Workspace as for attention. */
+int beacon_rmsnorm_adjoint_bwd(void* dx, void* dweight, const void* dy, const void* x, const float* rms,
+                               const void* weight, int64_t tokens, int64_t dim, int dtype, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/* ---- SwiGLU MLP: crates/beacon-cuda/src/mlp.rs:12-52 ----------------------- */
+
+/* swiglu_fwd (mlp.rs:12-29): out[t, dm] = (silu(x Wg) * (x Wu)) Wd;
+ * gate_proj, up_proj: [d_model, d_ff]; down_proj: [d_ff, d_model].
+ * The gate and up GEMMs run as one tcgen05 GEMM with a SwiGLU epilogue. */
+int beacon_swiglu_adjoint_fwd(void* out, const void* x, const void* gate_proj, const void* up_proj,
+                              const void* down_proj, int64_t tokens, int64_t d_model, int64_t d_ff, int dtype,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
+/* swiglu_bwd (mlp.rs:31-52); adjoint lib.rs:100-107 recomputes gate and up. */
+int beacon_swiglu_adjoint_bwd(void* dx, void* dgate_proj, void* dup_proj, void* ddown_proj, const void* dy,
+                              const void* x, const void* gate_proj, const void* up_proj, const void* down_proj,
+                              int64_t tokens, int64_t d_model, int64_t d_ff, int dtype, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
+size_t beacon_swiglu_workspace_size(int64_t tokens, int64_t d_model, int64_t d_ff, int dtype, int backward);
+
+/* ---- elementwise: crates/beacon-cuda/src/elementwise.rs -------------------- */
+
+/* residual_add (elementwise.rs:47-55): out = a + b */
+int beacon_residual_add_fwd(void* out, const void* a, const void* b, int64_t n, int dtype, void* stream);
+/* residual_add_backward (elementwise.rs:57-65): d_a = d_b = d_out */
+int beacon_residual_add_bwd(void* d_a, void* d_b, const void* d_out, int64_t n, int dtype, void* stream);
+/* cast (elementwise.rs:120-128) with the reference's rounding rules (dtype.rs:58-66, 163-195). */
+int beacon_cast(void* dst, const void* src, int64_t n, int kind, void* stream);
+
+/* ---- arena launcher: the KernelLauncher::launch boundary ------------------
+ * crates/beacon-cuda/src/runtime.rs:31-47 (Launcher::launch) and
+ * crates/beacon-cuda/src/launcher.rs:21-63 (KernelArg = byte offset into one arena).
+ * A Rust `Launcher` implements KernelLauncher::launch by forwarding here; the
+ * typed traits' shapes, which they drop before launch, travel in `scalars`
+ * (see INTEGRATION.md for the order per kernel).  */
+typedef struct beacon_arena beacon_arena;
+
+typedef struct beacon_kernel_arg {
+    uint64_t offset;     /* byte offset into the arena */
+    uint64_t len_bytes;  /* extent, checked against the arena and the shapes */
+    int32_t access;      /* 0 Read, 1 Write, 2 ReadWrite (launcher.rs:14-19) */
+} beacon_kernel_arg;
+
+/* Creates an arena of `bytes` device memory on `device` (256-byte aligned
+ * regions are the caller's business, crates/beacon-core/src/arena.rs:7). */
+beacon_arena* beacon_arena_create(int device, uint64_t bytes);
+void beacon_arena_destroy(beacon_arena* arena);
+void* beacon_arena_base(beacon_arena* arena);
+uint64_t beacon_arena_size(beacon_arena* arena);
+
+/* Dispatch by kernel ID string (the adjoint-table launcher names plus the
+ * elementwise IDs).  `scalars` carries the dropped shapes, then dtype. */
+int beacon_launch(beacon_arena* arena, const char* kernel, const beacon_kernel_arg* args, size_t nargs,
+                  const int64_t* scalars, size_t nscalars, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BEACON_CUDA_H */

@@ -1,0 +1,261 @@
+"""CPU oracle for the beacon hot path -- TEST INFRASTRUCTURE ONLY.
+
+ctypes front end over ``libbeacon_oracle.so`` (built from ``beacon_oracle.c`` by
+``oracle/Makefile``).  Only ``tests/``, ``__graft_entry__.smoke()`` and the
+``cpu_baseline`` / ``--impl reference`` legs of ``bench.py`` may import this
+package: it is the checker, never the thing measured or shipped.
+
+Parity status: the dtype codecs restate crates/beacon-core/src/dtype.rs and are
+pinned by that file's known-answer tests; the op results (attention, GEMM,
+RMSNorm, SwiGLU) are parity unpinned by the reference, which has no numeric
+implementation (crates/beacon-ops/src/lib.rs:1), and are cross-checked against
+torch float64 instead.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "libbeacon_oracle.so")
+_lib = None
+
+_f = ctypes.POINTER(ctypes.c_float)
+_i64 = ctypes.c_int64
+
+
+def build() -> str:
+    """Compile the oracle library in place (gcc + OpenMP)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = ctypes.CDLL(_LIB_PATH)
+        L.bo_splitmix64.restype = ctypes.c_uint64
+        L.bo_splitmix64.argtypes = [ctypes.c_uint64, ctypes.c_uint64]
+        L.bo_fill_uniform.argtypes = [_f, ctypes.c_size_t, ctypes.c_float, ctypes.c_float,
+                                      ctypes.c_uint64, ctypes.c_uint64]
+        L.bo_fill_normal.argtypes = [_f, ctypes.c_size_t, ctypes.c_float, ctypes.c_float,
+                                     ctypes.c_uint64, ctypes.c_uint64]
+        L.bo_bf16_from_f32.restype = ctypes.c_uint16
+        L.bo_bf16_from_f32.argtypes = [ctypes.c_float]
+        L.bo_bf16_to_f32.restype = ctypes.c_float
+        L.bo_bf16_to_f32.argtypes = [ctypes.c_uint16]
+        L.bo_fp8e4m3_from_f32.restype = ctypes.c_uint8
+        L.bo_fp8e4m3_from_f32.argtypes = [ctypes.c_float]
+        L.bo_fp8e4m3_to_f32.restype = ctypes.c_float
+        L.bo_fp8e4m3_to_f32.argtypes = [ctypes.c_uint8]
+        L.bo_f32_to_bf16.argtypes = [ctypes.c_void_p, _f, ctypes.c_size_t]
+        L.bo_bf16_to_f32_n.argtypes = [_f, ctypes.c_void_p, ctypes.c_size_t]
+        L.bo_round_bf16_inplace.argtypes = [_f, ctypes.c_size_t]
+        L.bo_f32_to_fp8e4m3.argtypes = [ctypes.c_void_p, _f, ctypes.c_size_t]
+        L.bo_fp8e4m3_to_f32_n.argtypes = [_f, ctypes.c_void_p, ctypes.c_size_t]
+        L.bo_matmul_fwd.argtypes = [_f, _f, _f, _i64, _i64, _i64]
+        L.bo_matmul_bwd.argtypes = [_f, _f, _f, _f, _f, _i64, _i64, _i64]
+        L.bo_linear_fwd.argtypes = [_f, _f, _f, _f, _i64, _i64, _i64]
+        L.bo_linear_bwd.argtypes = [_f, _f, _f, _f, _f, _f, _i64, _i64, _i64]
+        L.bo_attention_fwd.argtypes = [_f, _f, _f, _f, _f, _i64, _i64, _i64, _i64, _i64,
+                                       ctypes.c_int, ctypes.c_float]
+        L.bo_attention_fwd_heads.argtypes = [_f, _f, _f, _f, _f, _i64, _i64, _i64, _i64, _i64,
+                                             ctypes.c_int, ctypes.c_float,
+                                             ctypes.POINTER(ctypes.c_int64), _i64]
+        L.bo_attention_bwd.argtypes = [_f, _f, _f, _f, _f, _f, _f, _f, _i64, _i64, _i64, _i64,
+                                       _i64, ctypes.c_int, ctypes.c_float]
+        L.bo_rmsnorm_fwd.argtypes = [_f, _f, _f, _f, _i64, _i64, ctypes.c_float]
+        L.bo_rmsnorm_bwd.argtypes = [_f, _f, _f, _f, _f, _f, _i64, _i64]
+        L.bo_swiglu_fwd.argtypes = [_f, _f, _f, _f, _f, _i64, _i64, _i64]
+        L.bo_swiglu_bwd.argtypes = [_f, _f, _f, _f, _f, _f, _f, _f, _f, _i64, _i64, _i64]
+        L.bo_residual_add_fwd.argtypes = [_f, _f, _f, _i64]
+        L.bo_residual_add_bwd.argtypes = [_f, _f, _f, _i64]
+        L.bo_num_threads.restype = ctypes.c_int
+        L.bo_set_num_threads.argtypes = [ctypes.c_int]
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray | None):
+    if a is None:
+        return None
+    assert a.dtype == np.float32 and a.flags["C_CONTIGUOUS"], (a.dtype, a.flags)
+    return a.ctypes.data_as(_f)
+
+
+def _empty(*shape) -> np.ndarray:
+    return np.empty(shape, dtype=np.float32)
+
+
+# ---- inputs -----------------------------------------------------------------
+
+def normal(shape, seed: int, mean: float = 0.0, std: float = 1.0, offset: int = 0) -> np.ndarray:
+    out = _empty(*shape)
+    lib().bo_fill_normal(_p(out), out.size, mean, std, seed, offset)
+    return out
+
+
+def uniform(shape, seed: int, lo: float = -1.0, hi: float = 1.0, offset: int = 0) -> np.ndarray:
+    out = _empty(*shape)
+    lib().bo_fill_uniform(_p(out), out.size, lo, hi, seed, offset)
+    return out
+
+
+# ---- codecs -----------------------------------------------------------------
+
+def to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.shape, dtype=np.uint16)
+    lib().bo_f32_to_bf16(out.ctypes.data, _p(x), x.size)
+    return out
+
+
+def from_bf16_bits(h: np.ndarray) -> np.ndarray:
+    h = np.ascontiguousarray(h, dtype=np.uint16)
+    out = _empty(*h.shape)
+    lib().bo_bf16_to_f32_n(_p(out), h.ctypes.data, h.size)
+    return out
+
+
+def round_bf16(x: np.ndarray) -> np.ndarray:
+    out = np.array(x, dtype=np.float32, copy=True, order="C")
+    lib().bo_round_bf16_inplace(_p(out), out.size)
+    return out
+
+
+def to_fp8_bits(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.shape, dtype=np.uint8)
+    lib().bo_f32_to_fp8e4m3(out.ctypes.data, _p(x), x.size)
+    return out
+
+
+def from_fp8_bits(b: np.ndarray) -> np.ndarray:
+    b = np.ascontiguousarray(b, dtype=np.uint8)
+    out = _empty(*b.shape)
+    lib().bo_fp8e4m3_to_f32_n(_p(out), b.ctypes.data, b.size)
+    return out
+
+
+# ---- ops ----------------------------------------------------------------------
+
+def matmul_fwd(lhs, rhs):
+    M, K = lhs.shape
+    N = rhs.shape[1]
+    out = _empty(M, N)
+    lib().bo_matmul_fwd(_p(out), _p(lhs), _p(rhs), M, K, N)
+    return out
+
+
+def matmul_bwd(dout, lhs, rhs):
+    M, K = lhs.shape
+    N = rhs.shape[1]
+    dl, dr = _empty(M, K), _empty(K, N)
+    lib().bo_matmul_bwd(_p(dl), _p(dr), _p(dout), _p(lhs), _p(rhs), M, K, N)
+    return dl, dr
+
+
+def linear_fwd(x, w, bias=None):
+    M, K = x.shape
+    N = w.shape[1]
+    out = _empty(M, N)
+    lib().bo_linear_fwd(_p(out), _p(x), _p(w), _p(bias), M, K, N)
+    return out
+
+
+def linear_bwd(dy, x, w):
+    M, K = x.shape
+    N = w.shape[1]
+    dx, dw, db = _empty(M, K), _empty(K, N), _empty(N)
+    lib().bo_linear_bwd(_p(dx), _p(dw), _p(db), _p(dy), _p(x), _p(w), M, K, N)
+    return dx, dw, db
+
+
+def attention_fwd(q, k, v, causal=True, scale=0.0):
+    B, Hq, S, D = q.shape
+    Hkv = k.shape[1]
+    out, lse = _empty(B, Hq, S, D), _empty(B, Hq, S)
+    lib().bo_attention_fwd(_p(out), _p(lse), _p(q), _p(k), _p(v), B, Hq, Hkv, S, D, int(causal), scale)
+    return out, lse
+
+
+def attention_fwd_heads(q, k, v, heads, causal=True, scale=0.0):
+    """Forward for the listed flat (b*Hq + h) query heads only; other rows stay NaN."""
+    B, Hq, S, D = q.shape
+    Hkv = k.shape[1]
+    out = np.full((B, Hq, S, D), np.nan, dtype=np.float32)
+    lse = np.full((B, Hq, S), np.nan, dtype=np.float32)
+    hs = np.ascontiguousarray(np.asarray(heads, dtype=np.int64))
+    lib().bo_attention_fwd_heads(_p(out), _p(lse), _p(q), _p(k), _p(v), B, Hq, Hkv, S, D,
+                                 int(causal), scale,
+                                 hs.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)), hs.size)
+    return out, lse
+
+
+def attention_bwd(dout, q, k, v, lse, causal=True, scale=0.0):
+    B, Hq, S, D = q.shape
+    Hkv = k.shape[1]
+    dq, dk, dv = _empty(B, Hq, S, D), _empty(B, Hkv, S, D), _empty(B, Hkv, S, D)
+    lib().bo_attention_bwd(_p(dq), _p(dk), _p(dv), _p(dout), _p(q), _p(k), _p(v), _p(lse),
+                           B, Hq, Hkv, S, D, int(causal), scale)
+    return dq, dk, dv
+
+
+def rmsnorm_fwd(x, g, eps=1e-5):
+    T, dim = x.shape
+    y, rms = _empty(T, dim), _empty(T)
+    lib().bo_rmsnorm_fwd(_p(y), _p(rms), _p(x), _p(g), T, dim, eps)
+    return y, rms
+
+
+def rmsnorm_bwd(dy, x, rms, g):
+    T, dim = x.shape
+    dx, dg = _empty(T, dim), _empty(dim)
+    lib().bo_rmsnorm_bwd(_p(dx), _p(dg), _p(dy), _p(x), _p(rms), _p(g), T, dim)
+    return dx, dg
+
+
+def swiglu_fwd(x, wg, wu, wd):
+    T, dm = x.shape
+    F = wg.shape[1]
+    out = _empty(T, dm)
+    lib().bo_swiglu_fwd(_p(out), _p(x), _p(wg), _p(wu), _p(wd), T, dm, F)
+    return out
+
+
+def swiglu_bwd(dy, x, wg, wu, wd):
+    T, dm = x.shape
+    F = wg.shape[1]
+    dx, dwg, dwu, dwd = _empty(T, dm), _empty(dm, F), _empty(dm, F), _empty(F, dm)
+    lib().bo_swiglu_bwd(_p(dx), _p(dwg), _p(dwu), _p(dwd), _p(dy), _p(x), _p(wg), _p(wu), _p(wd),
+                        T, dm, F)
+    return dx, dwg, dwu, dwd
+
+
+def residual_add_fwd(a, b):
+    out = _empty(*a.shape)
+    lib().bo_residual_add_fwd(_p(out), _p(a), _p(b), a.size)
+    return out
+
+
+def num_threads() -> int:
+    return int(lib().bo_num_threads())
+
+
+def set_num_threads(n: int) -> None:
+    lib().bo_set_num_threads(int(n))
+
+
+def rel_err(x: np.ndarray, ref: np.ndarray) -> float:
+    """Norm-wise relative error max|x - ref| / max|ref| (the tolerance measure of the tests)."""
+    x = np.asarray(x, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    denom = float(np.max(np.abs(ref))) if ref.size else 0.0
+    if denom == 0.0:
+        return float(np.max(np.abs(x - ref))) if ref.size else 0.0
+    return float(np.max(np.abs(x - ref)) / denom)

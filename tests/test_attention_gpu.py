@@ -1,0 +1,113 @@
+"""Causal attention parity (attention.rs:21-64) through the C ABI against the CPU oracle."""
+import numpy as np
+import pytest
+
+import oracle as O
+from helpers import BF16_TOL, F32_TOL, as_bf16, normal, rel_err, to_dev, to_np
+
+pytestmark = pytest.mark.gpu
+
+
+def _ops():
+    from beacon_b200 import ops
+    return ops
+
+
+def _qkv(B, Hq, Hkv, S, D, seed, bf16=True):
+    r = as_bf16 if bf16 else (lambda x: x)
+    nq, nk = B * Hq * S * D, B * Hkv * S * D
+    q = r(normal((B, Hq, S, D), seed))
+    k = r(normal((B, Hkv, S, D), seed, offset=nq))
+    v = r(normal((B, Hkv, S, D), seed, offset=nq + nk))
+    do = r(normal((B, Hq, S, D), seed, offset=nq + 2 * nk))
+    return q, k, v, do
+
+
+def test_config1_f32_forward():
+    """f32 causal SDPA B=1 H=4 S=128 D=64, seed 0, at 1e-5."""
+    import torch
+    ops = _ops()
+    q, k, v, _ = _qkv(1, 4, 4, 128, 64, 0, bf16=False)
+    out, lse = ops.attention_fwd(to_dev(q, torch.float32), to_dev(k, torch.float32), to_dev(v, torch.float32))
+    ro, rl = O.attention_fwd(q, k, v)
+    assert rel_err(to_np(out), ro) <= F32_TOL
+    assert rel_err(to_np(lse), rl) <= F32_TOL
+
+
+@pytest.mark.parametrize("B,H,S,D,causal", [
+    (1, 4, 128, 64, True),
+    (2, 4, 256, 128, True),
+    (1, 2, 384, 128, True),
+    (1, 2, 200, 128, True),   # S tail: keys >= S masked, rows >= S not stored
+    (1, 2, 256, 128, False),
+    (1, 1, 1, 64, True),
+    (1, 2, 130, 64, False),
+])
+def test_forward_bf16(B, H, S, D, causal):
+    import torch
+    ops = _ops()
+    q, k, v, _ = _qkv(B, H, H, S, D, 2)
+    out, lse = ops.attention_fwd(to_dev(q, torch.bfloat16), to_dev(k, torch.bfloat16), to_dev(v, torch.bfloat16),
+                                 causal=causal)
+    ro, rl = O.attention_fwd(q, k, v, causal=causal)
+    assert rel_err(to_np(out), ro) <= BF16_TOL
+    assert rel_err(to_np(lse), rl) <= 1e-3
+
+
+def test_forward_gqa_bf16():
+    import torch
+    ops = _ops()
+    q, k, v, _ = _qkv(1, 8, 2, 256, 128, 4)
+    out, lse = ops.attention_fwd(to_dev(q, torch.bfloat16), to_dev(k, torch.bfloat16), to_dev(v, torch.bfloat16))
+    ro, rl = O.attention_fwd(q, k, v)
+    assert rel_err(to_np(out), ro) <= BF16_TOL
+    assert rel_err(to_np(lse), rl) <= 1e-3
+
+
+def test_forward_config3_sampled_heads():
+    """B=8 H=32 S=4096 D=128 (the fwd+bwd benchmark shape): oracle on 2 sampled heads."""
+    import torch
+    ops = _ops()
+    B, H, S, D = 8, 32, 4096, 128
+    q, k, v, _ = _qkv(B, H, H, S, D, 2)
+    out, lse = ops.attention_fwd(to_dev(q, torch.bfloat16), to_dev(k, torch.bfloat16), to_dev(v, torch.bfloat16))
+    heads = [0, 8 * 32 - 1]
+    ro, rl = O.attention_fwd_heads(q, k, v, heads)
+    out_np, lse_np = to_np(out).reshape(B * H, S, D), to_np(lse).reshape(B * H, S)
+    for hh in heads:
+        assert rel_err(out_np[hh], ro.reshape(B * H, S, D)[hh]) <= BF16_TOL
+        assert rel_err(lse_np[hh], rl.reshape(B * H, S)[hh]) <= 1e-3
+    assert np.isfinite(out_np).all()
+
+
+@pytest.mark.parametrize("B,H,Hkv,S,D", [(1, 2, 2, 256, 64), (1, 2, 2, 256, 128), (1, 4, 2, 200, 128)])
+def test_backward_bf16(B, H, Hkv, S, D):
+    import torch
+    ops = _ops()
+    q, k, v, do = _qkv(B, H, Hkv, S, D, 5)
+    _, rl = O.attention_fwd(q, k, v)
+    dq, dk, dv = ops.attention_bwd(to_dev(do, torch.bfloat16), to_dev(q, torch.bfloat16), to_dev(k, torch.bfloat16),
+                                   to_dev(v, torch.bfloat16), to_dev(rl, torch.float32))
+    rq, rk, rv = O.attention_bwd(do, q, k, v, rl)
+    assert rel_err(to_np(dq), rq) <= BF16_TOL
+    assert rel_err(to_np(dk), rk) <= BF16_TOL
+    assert rel_err(to_np(dv), rv) <= BF16_TOL
+
+
+def test_backward_f32():
+    import torch
+    ops = _ops()
+    q, k, v, do = _qkv(1, 4, 4, 128, 64, 0, bf16=False)
+    _, rl = O.attention_fwd(q, k, v)
+    t = lambda a: to_dev(a, torch.float32)
+    dq, dk, dv = ops.attention_bwd(t(do), t(q), t(k), t(v), t(rl))
+    rq, rk, rv = O.attention_bwd(do, q, k, v, rl)
+    assert rel_err(to_np(dq), rq) <= F32_TOL
+    assert rel_err(to_np(dk), rk) <= F32_TOL
+    assert rel_err(to_np(dv), rv) <= F32_TOL
+
+
+def test_no_device_fault_recorded():
+    ops = _ops()
+    code, site, count = ops.device_status(0)
+    assert (code, count) == (0, 0)

@@ -1,0 +1,112 @@
+"""GEMM family parity (matmul.rs:18-78) through the C ABI against the CPU oracle."""
+import numpy as np
+import pytest
+
+import oracle as O
+from helpers import BF16_TOL, F32_TOL, as_bf16, rel_err, to_dev, to_np, uniform, normal
+
+pytestmark = pytest.mark.gpu
+
+
+def _ops():
+    from beacon_b200 import ops
+    return ops
+
+
+@pytest.mark.parametrize("m,k,n", [
+    (128, 64, 256),      # one tile
+    (256, 512, 512),     # several K tiles, 2 N tiles
+    (1024, 1024, 1024),
+    (200, 136, 328),     # M / N / K tails on the TMA path
+    (33, 47, 29),        # row strides not 16-byte multiples: exact SIMT path
+    (1, 8, 8),
+])
+def test_matmul_fwd_bf16(m, k, n):
+    import torch
+    ops = _ops()
+    a = as_bf16(uniform((m, k), 1))
+    b = as_bf16(uniform((k, n), 1, offset=m * k))
+    out = ops.matmul_fwd(to_dev(a, torch.bfloat16), to_dev(b, torch.bfloat16))
+    ref = O.matmul_fwd(a, b)
+    assert rel_err(to_np(out), ref) <= BF16_TOL
+
+
+@pytest.mark.parametrize("m,k,n", [(128, 64, 96), (37, 51, 29)])
+def test_matmul_fwd_f32(m, k, n):
+    import torch
+    ops = _ops()
+    a = uniform((m, k), 3)
+    b = uniform((k, n), 4)
+    out = ops.matmul_fwd(to_dev(a, torch.float32), to_dev(b, torch.float32))
+    assert rel_err(to_np(out), O.matmul_fwd(a, b)) <= F32_TOL
+
+
+def test_matmul_4096_sampled_rows():
+    """The 4096^3 workload: full GPU product, oracle on a sample of 64 rows."""
+    import torch
+    ops = _ops()
+    m = k = n = 4096
+    a = as_bf16(uniform((m, k), 1))
+    b = as_bf16(uniform((k, n), 1, offset=m * k))
+    out = to_np(ops.matmul_fwd(to_dev(a, torch.bfloat16), to_dev(b, torch.bfloat16)))
+    rows = np.random.default_rng(0).choice(m, 64, replace=False)
+    ref = O.matmul_fwd(np.ascontiguousarray(a[rows]), b)
+    assert rel_err(out[rows], ref) <= BF16_TOL
+    assert np.isfinite(out).all()
+
+
+@pytest.mark.parametrize("m,k,n", [(256, 192, 320), (128, 64, 64), (72, 40, 24)])
+def test_matmul_bwd_bf16(m, k, n):
+    import torch
+    ops = _ops()
+    a = as_bf16(uniform((m, k), 5))
+    b = as_bf16(uniform((k, n), 6))
+    dy = as_bf16(uniform((m, n), 7))
+    dl, dr = ops.matmul_bwd(to_dev(dy, torch.bfloat16), to_dev(a, torch.bfloat16), to_dev(b, torch.bfloat16))
+    rl, rr = O.matmul_bwd(dy, a, b)
+    assert rel_err(to_np(dl), rl) <= BF16_TOL
+    assert rel_err(to_np(dr), rr) <= BF16_TOL
+
+
+def test_matmul_bwd_f32():
+    import torch
+    ops = _ops()
+    a, b, dy = uniform((64, 48), 8), uniform((48, 80), 9), uniform((64, 80), 10)
+    dl, dr = ops.matmul_bwd(to_dev(dy, torch.float32), to_dev(a, torch.float32), to_dev(b, torch.float32))
+    rl, rr = O.matmul_bwd(dy, a, b)
+    assert rel_err(to_np(dl), rl) <= F32_TOL
+    assert rel_err(to_np(dr), rr) <= F32_TOL
+
+
+@pytest.mark.parametrize("dtype_name", ["bf16", "f32"])
+def test_linear_fwd_bwd(dtype_name):
+    import torch
+    ops = _ops()
+    dt = torch.bfloat16 if dtype_name == "bf16" else torch.float32
+    tol = BF16_TOL if dtype_name == "bf16" else F32_TOL
+    r = as_bf16 if dtype_name == "bf16" else (lambda x: x)
+    m, k, n = 256, 128, 192
+    x, w, bias, dy = r(normal((m, k), 11)), r(normal((k, n), 12, std=0.1)), r(normal((n,), 13)), r(normal((m, n), 14))
+    out = ops.linear_fwd(to_dev(x, dt), to_dev(w, dt), to_dev(bias, dt))
+    assert rel_err(to_np(out), O.linear_fwd(x, w, bias)) <= tol
+    dx, dw, db = ops.linear_bwd(to_dev(dy, dt), to_dev(x, dt), to_dev(w, dt))
+    rx, rw, rb = O.linear_bwd(dy, x, w)
+    assert rel_err(to_np(dx), rx) <= tol
+    assert rel_err(to_np(dw), rw) <= tol
+    assert rel_err(to_np(db), rb) <= tol
+
+
+def test_empty_reduction_gives_zeros():
+    import torch
+    ops = _ops()
+    a = torch.empty(64, 0, dtype=torch.bfloat16, device="cuda")
+    b = torch.empty(0, 64, dtype=torch.bfloat16, device="cuda")
+    out = ops.matmul_fwd(a, b)
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(out).item() == 0
+
+
+def test_no_device_fault_recorded():
+    ops = _ops()
+    code, site, count = ops.device_status(0)
+    assert (code, count) == (0, 0)

@@ -1,0 +1,89 @@
+"""RMSNorm (norm.rs:19-51), SwiGLU MLP (mlp.rs:12-52), residual add and casts
+(elementwise.rs) through the C ABI against the CPU oracle."""
+import numpy as np
+import pytest
+
+import oracle as O
+from helpers import BF16_TOL, F32_TOL, as_bf16, normal, rel_err, to_dev, to_np
+
+pytestmark = pytest.mark.gpu
+
+
+def _ops():
+    from beacon_b200 import ops
+    return ops
+
+
+@pytest.mark.parametrize("T,dim,dt", [(64, 4096, "bf16"), (8, 14336, "bf16"), (33, 1000, "f32"), (16, 256, "f32"),
+                                      (5, 100, "bf16")])
+def test_rmsnorm(T, dim, dt):
+    import torch
+    ops = _ops()
+    tdt = torch.bfloat16 if dt == "bf16" else torch.float32
+    tol = BF16_TOL if dt == "bf16" else F32_TOL
+    r = as_bf16 if dt == "bf16" else (lambda a: a)
+    x, g, dy = r(normal((T, dim), 3)), r(normal((dim,), 4)), r(normal((T, dim), 5))
+    y, rms = ops.rmsnorm_fwd(to_dev(x, tdt), to_dev(g, tdt))
+    ry, rr = O.rmsnorm_fwd(x, g)
+    assert rel_err(to_np(y), ry) <= tol
+    assert rel_err(to_np(rms), rr) <= 1e-5
+    dx, dg = ops.rmsnorm_bwd(to_dev(dy, tdt), to_dev(x, tdt), rms, to_dev(g, tdt))
+    rdx, rdg = O.rmsnorm_bwd(dy, x, rr, g)
+    assert rel_err(to_np(dx), rdx) <= tol
+    assert rel_err(to_np(dg), rdg) <= tol
+
+
+@pytest.mark.parametrize("T,dm,F,dt", [(128, 256, 512, "bf16"), (200, 128, 320, "bf16"), (64, 64, 96, "f32")])
+def test_swiglu(T, dm, F, dt):
+    import torch
+    ops = _ops()
+    tdt = torch.bfloat16 if dt == "bf16" else torch.float32
+    tol = BF16_TOL if dt == "bf16" else F32_TOL
+    r = as_bf16 if dt == "bf16" else (lambda a: a)
+    x = r(normal((T, dm), 3))
+    wg, wu = r(normal((dm, F), 31, std=0.05)), r(normal((dm, F), 32, std=0.05))
+    wd, dy = r(normal((F, dm), 33, std=0.05)), r(normal((T, dm), 34))
+    dev = lambda a: to_dev(a, tdt)
+    out = ops.swiglu_fwd(dev(x), dev(wg), dev(wu), dev(wd))
+    assert rel_err(to_np(out), O.swiglu_fwd(x, wg, wu, wd)) <= tol
+    grads = ops.swiglu_bwd(dev(dy), dev(x), dev(wg), dev(wu), dev(wd))
+    refs = O.swiglu_bwd(dy, x, wg, wu, wd)
+    for g, rf in zip(grads, refs):
+        assert rel_err(to_np(g), rf) <= tol
+
+
+def test_residual_add_bitexact():
+    import torch
+    ops = _ops()
+    a, b = normal((1000003,), 1), normal((1000003,), 2)
+    out = ops.residual_add(to_dev(a, torch.float32), to_dev(b, torch.float32))
+    assert np.array_equal(to_np(out), a + b)
+    da, db = ops.residual_add_bwd(to_dev(a, torch.float32))
+    assert np.array_equal(to_np(da), a) and np.array_equal(to_np(db), a)
+    ab, bb = as_bf16(a), as_bf16(b)
+    outb = ops.residual_add(to_dev(ab, torch.bfloat16), to_dev(bb, torch.bfloat16))
+    assert np.array_equal(to_np(outb), O.round_bf16(ab + bb))
+
+
+def test_casts_bitexact():
+    import torch
+    ops = _ops()
+    x = np.concatenate([normal((200000,), 9, std=50.0), normal((50000,), 10, std=0.01),
+                        np.array([0.0, -0.0, 448.0, 464.0, -1e9, 1e9, np.nan, np.inf, -np.inf, 2.0 ** -9,
+                                  2.0 ** -10, 3 * 2.0 ** -11, 1.0 + 2.0 ** -4, 255.99998], np.float32)]).astype(np.float32)
+    f8 = ops.cast(to_dev(x, torch.float32), ops.CAST_F32_TO_FP8E4M3)
+    assert np.array_equal(f8.cpu().numpy(), O.to_fp8_bits(x))
+    back = ops.cast(f8, ops.CAST_FP8E4M3_TO_F32).cpu().numpy()
+    ref_back = O.from_fp8_bits(O.to_fp8_bits(x))
+    assert np.array_equal(np.isnan(back), np.isnan(ref_back))
+    assert np.array_equal(back[~np.isnan(back)], ref_back[~np.isnan(ref_back)])
+    b16 = ops.cast(to_dev(x, torch.float32), ops.CAST_F32_TO_BF16)
+    assert np.array_equal(b16.view(torch.int16).cpu().numpy().view(np.uint16), O.to_bf16_bits(x))
+    f32 = ops.cast(b16, ops.CAST_BF16_TO_F32).cpu().numpy()
+    assert np.array_equal(f32.view(np.uint32), O.from_bf16_bits(O.to_bf16_bits(x)).view(np.uint32))
+
+
+def test_no_device_fault_recorded():
+    ops = _ops()
+    code, site, count = ops.device_status(0)
+    assert (code, count) == (0, 0)
