@@ -31,6 +31,7 @@ F32, F16, BF16, FP8E4M3 = 0, 1, 2, 3
 # Every symbol include/beacon_cuda.h declares.
 EXPORTS = (
     "beacon_version", "beacon_last_error", "beacon_device_status", "beacon_launch_count",
+    "beacon_profile_enable", "beacon_profile_read",
     "beacon_matmul_fwd", "beacon_matmul_bwd", "beacon_linear_fwd", "beacon_linear_bwd",
     "beacon_attention_adjoint_fwd", "beacon_attention_adjoint_bwd", "beacon_attention_bwd_workspace_size",
     "beacon_attention_gqa_fwd", "beacon_attention_gqa_bwd", "beacon_attention_bwd_with_out",
@@ -82,6 +83,9 @@ def lib():
     _sig(L, "beacon_last_error", _int, [ctypes.c_char_p, _sz])
     _sig(L, "beacon_device_status", _int, [_int, ctypes.POINTER(ctypes.c_uint)])
     _sig(L, "beacon_launch_count", ctypes.c_uint64, [])
+    _sig(L, "beacon_profile_enable", None, [_int])
+    _sig(L, "beacon_profile_read", _int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_double),
+                                          ctypes.POINTER(ctypes.c_uint64)])
     _sig(L, "beacon_matmul_fwd", _int, [_vp, _vp, _vp, _i64, _i64, _i64, _int, _vp])
     _sig(L, "beacon_matmul_bwd", _int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp])
     _sig(L, "beacon_linear_fwd", _int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp])

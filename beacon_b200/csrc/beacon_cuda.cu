@@ -9,7 +9,9 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -19,6 +21,7 @@
 
 #include "../../include/beacon_cuda.h"
 #include "attention.cuh"
+#include "attention_bwd.cuh"
 #include "elementwise.cuh"
 #include "gemm.cuh"
 #include "sm100.cuh"
@@ -52,6 +55,58 @@ int check_launch(const char* what) {
   if (e != cudaSuccess) return fail(BEACON_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
   return BEACON_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Per-kernel device timing: when enabled, the tensor-core kernels are bracketed by
+// CUDA events recorded on the stream they are launched on; beacon_profile_read()
+// synchronises on those events and returns the accumulated time per kernel name.
+// ---------------------------------------------------------------------------
+struct ProfRec {
+  const char* name;
+  cudaEvent_t e0, e1;
+};
+std::mutex g_prof_mu;
+bool g_prof_on = false;
+std::vector<ProfRec> g_prof_pending;
+std::vector<cudaEvent_t> g_prof_pool;
+struct ProfTotal {
+  std::string name;
+  double ms;
+  uint64_t count;
+};
+std::vector<ProfTotal> g_prof_totals;
+
+cudaEvent_t prof_event() {
+  if (!g_prof_pool.empty()) {
+    cudaEvent_t e = g_prof_pool.back();
+    g_prof_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+struct ProfScope {
+  const char* name = nullptr;
+  cudaStream_t st = nullptr;
+  cudaEvent_t e0 = nullptr;
+  ProfScope(const char* n, cudaStream_t s) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    if (!g_prof_on) return;
+    name = n;
+    st = s;
+    e0 = prof_event();
+    cudaEventRecord(e0, st);
+  }
+  ~ProfScope() {
+    if (!e0) return;
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    cudaEvent_t e1 = prof_event();
+    cudaEventRecord(e1, st);
+    g_prof_pending.push_back(ProfRec{name, e0, e1});
+  }
+};
 
 #define BEACON_TRY(expr)             \
   do {                               \
@@ -212,7 +267,10 @@ int launch_gemm_tc_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtenso
   }
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = tiles < sms ? tiles : sms;
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tb2, p);
+  {
+    ProfScope prof("k_gemm_bf16_tc", st);
+    kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tb2, p);
+  }
   return check_launch("k_gemm_bf16_tc");
 }
 
@@ -377,6 +435,43 @@ extern "C" int beacon_last_error(char* buf, size_t len) {
 }
 
 extern "C" uint64_t beacon_launch_count(void) { return g_launches.load(); }
+
+extern "C" void beacon_profile_enable(int on) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  g_prof_on = on != 0;
+}
+
+extern "C" int beacon_profile_read(const char* kernel, double* total_ms, uint64_t* count) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  for (const ProfRec& r : g_prof_pending) {
+    cudaEventSynchronize(r.e1);
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, r.e0, r.e1);
+    bool found = false;
+    for (ProfTotal& t : g_prof_totals)
+      if (t.name == r.name) {
+        t.ms += ms;
+        t.count += 1;
+        found = true;
+      }
+    if (!found) g_prof_totals.push_back(ProfTotal{r.name, (double)ms, 1});
+    g_prof_pool.push_back(r.e0);
+    g_prof_pool.push_back(r.e1);
+  }
+  g_prof_pending.clear();
+  if (total_ms) *total_ms = 0.0;
+  if (count) *count = 0;
+  if (kernel == nullptr) {  // reset
+    g_prof_totals.clear();
+    return BEACON_OK;
+  }
+  for (const ProfTotal& t : g_prof_totals)
+    if (t.name == kernel) {
+      if (total_ms) *total_ms = t.ms;
+      if (count) *count = t.count;
+    }
+  return BEACON_OK;
+}
 
 extern "C" int beacon_device_status(int device, unsigned int out[3]) {
   int prev = 0;

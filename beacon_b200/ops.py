@@ -233,3 +233,20 @@ def device_status(device: int = 0):
 
 def launch_count() -> int:
     return int(_lib.lib().beacon_launch_count())
+
+
+def profile_enable(on: bool = True) -> None:
+    """Bracket the tensor-core kernels with CUDA events on their launch stream."""
+    _lib.lib().beacon_profile_enable(int(on))
+
+
+def profile_read(kernel: str):
+    """(total milliseconds, launches) recorded for `kernel` since the last reset."""
+    ms = ctypes.c_double()
+    cnt = ctypes.c_uint64()
+    check(_lib.lib().beacon_profile_read(kernel.encode(), ctypes.byref(ms), ctypes.byref(cnt)))
+    return ms.value, int(cnt.value)
+
+
+def profile_reset() -> None:
+    check(_lib.lib().beacon_profile_read(None, None, None))

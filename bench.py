@@ -1,0 +1,398 @@
+#!/usr/bin/env python
+"""bench.py -- beacon hot-path benchmark on B200.
+
+Headline workload: bf16 causal attention forward + backward, B=8, H=32, S=4096,
+D=128, Q/K/V/dO i.i.d. N(0,1) (synthetic, seeded), scale 1/sqrt(128), fp32
+softmax statistics; the B*H = 256 heads are sharded across ranks (strong
+scaling, no collective on the data path).  One step = attention_adjoint_fwd +
+attention_adjoint_bwd through the C ABI, the drop-in path of the reference's
+adjoint entry (the backward is not given O and recomputes it).  TFLOP/s use the
+FlashAttention convention: fwd 2*B*H*S^2*D (causal), bwd 2.5x fwd; recompute
+work is not counted.
+
+Also reported on the same JSON line:
+  "gemm":      4096^3 bf16 GEMM, columns of B sharded across ranks, L2 flushed
+               between timed iterations;
+  "with_out":  the same fwd+bwd when the backward is given O (no recompute);
+  "roofline":  the dominant kernel (k_attn_bwd_tc) timed live with CUDA events on
+               its launch stream against the measured dense bf16 peak;
+  "cpu_baseline": the CPU oracle on a bounded sample of heads (rank 0, N=1);
+  "e2e":       the step with pinned-host inputs copied in and results copied out.
+
+`--impl reference` times the reference's CPU path for this op (the oracle: the
+reference itself has no numeric implementation) on rank 0 with all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+B, H, S, D = 8, 32, 4096, 128
+FWD_FLOPS = 2.0 * B * H * S * S * D          # causal forward
+BWD_FLOPS = 2.5 * FWD_FLOPS
+STEP_FLOPS = FWD_FLOPS + BWD_FLOPS
+GEMM_N = 4096
+METRIC = "causal attn fwd+bwd TFLOP/s & % bf16 peak at 1/2/4/8 B200; GEMM TFLOP/s"
+CONFIG = {"workload": "bf16 causal attention fwd+bwd B=8 H=32 S=4096 D=128, heads sharded across ranks",
+          "batch": B, "heads": H, "seq_len": S, "head_dim": D, "causal": True,
+          "parallelism": "heads sharded, no collective on the hot path",
+          "l2": "inputs larger than L2 (1 GiB per GPU at N=1; 128 MiB of inputs + outputs per GPU at N=8)"}
+# k_attn_bwd_tc DRAM traffic per launch (bytes) from the ncu capture summarised in
+# profiles/attn_bwd_tc.md (B*H=32 heads captured, scaled to 256 heads by head count).
+ATTN_BWD_TRAFFIC_PER_HEAD = None
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["beacon", "reference"], default="beacon")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gemm", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), float(p["bf16_tflops_sustained"]), "measured"
+    except Exception:
+        return 1590.0, 1400.0, "fallback"
+
+
+# --------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampler running during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_id: str):
+        self.device_id = device_id
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        import tempfile
+        fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
+        os.close(fd)
+        try:
+            self.out = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", self.device_id], stdout=self.out, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.out.close()
+        sm, smax, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    smax.append(float(parts[2]))
+                    power.append(float(parts[3]))
+                except ValueError:
+                    continue
+                for nm, val in zip(names, parts[5:9]):
+                    if val.lower() == "active":
+                        reasons.add(nm)
+        os.unlink(self.path)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        # samples under load: the upper half by power draw
+        pw_med = statistics.median(power)
+        loaded = [c for c, p in zip(sm, power) if p >= pw_med] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- distributed
+
+def dist_setup(n_gpus):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    import torch
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x, world):
+    import torch
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# --------------------------------------------------------------------------- CPU baseline
+
+def cpu_attention_sample(n_heads_max=None):
+    """Time the oracle's attention fwd+bwd on a bounded sample of heads (all host threads)."""
+    import oracle as O
+    nthreads = O.num_threads()
+    nh = min(nthreads if n_heads_max is None else n_heads_max, B * H)
+    q = O.normal((1, nh, S, D), 2)
+    k = O.normal((1, nh, S, D), 2, offset=q.size)
+    v = O.normal((1, nh, S, D), 2, offset=2 * q.size)
+    do = O.normal((1, nh, S, D), 2, offset=3 * q.size)
+    t0 = time.perf_counter()
+    _, lse = O.attention_fwd(q, k, v)
+    O.attention_bwd(do, q, k, v, lse)
+    dt = time.perf_counter() - t0
+    flops = STEP_FLOPS * nh / (B * H)
+    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": nthreads, "kind": "port",
+            "sample": f"{nh} of {B * H} heads (S={S}, D={D}) fwd+bwd, float64-accumulating C oracle, "
+                      f"{dt:.2f} s"}, dt
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    steps_t = []
+    info = None
+    for i in range(args.warmup + args.steps):
+        info, dt = cpu_attention_sample()
+        if i >= args.warmup:
+            steps_t.append(dt)
+    ms = 1e3 * statistics.mean(steps_t)
+    line = {"metric": METRIC, "value": info["value"], "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32 (f64 accumulation)", "data": "synthetic", "config": CONFIG,
+            "impl": "reference", "cpu_baseline": info,
+            "e2e": {"value": info["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- GPU arm
+
+def run_beacon(args, rank, world, local):
+    import torch
+    from beacon_b200 import ops
+
+    if (B * H) % world != 0:
+        raise SystemExit(f"{B * H} heads do not shard over {world} ranks")
+    nh = B * H // world
+    dev = torch.device("cuda", local)
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        uuid = str(local)
+    burst, sustained, peak_kind = peaks()
+
+    # inputs: pinned host buffers (used by e2e), copied once for the device-resident loop
+    g = torch.Generator().manual_seed(2 + 1000 * rank)
+    host = [torch.randn(1, nh, S, D, generator=g, dtype=torch.float32).to(torch.bfloat16).pin_memory()
+            for _ in range(4)]
+    q, k, v, do = [h.to(dev) for h in host]
+    out = torch.empty_like(q)
+    lse = torch.empty(1, nh, S, dtype=torch.float32, device=dev)
+    L = ops._lib.lib()
+    stream = torch.cuda.current_stream(dev)
+    sp = ops._stream()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def step():
+        ops.check(L.beacon_attention_adjoint_fwd(ops._p(out), ops._p(q), ops._p(k), ops._p(v), ops._p(lse), 1, nh,
+                                                 S, D, 1, ops._lib.BF16, sp))
+        ops.check(L.beacon_attention_adjoint_bwd(ops._p(dq), ops._p(dk), ops._p(dv), ops._p(do), ops._p(q),
+                                                 ops._p(k), ops._p(v), ops._p(lse), 1, nh, S, D, 1, ops._lib.BF16,
+                                                 None, 0, sp))
+
+    def step_with_out():
+        ops.check(L.beacon_attention_adjoint_fwd(ops._p(out), ops._p(q), ops._p(k), ops._p(v), ops._p(lse), 1, nh,
+                                                 S, D, 1, ops._lib.BF16, sp))
+        ops.check(L.beacon_attention_bwd_with_out(ops._p(dq), ops._p(dk), ops._p(dv), ops._p(do), ops._p(q),
+                                                  ops._p(k), ops._p(v), ops._p(out), ops._p(lse), 1, nh, nh, S, D, 1,
+                                                  ops._lib.BF16, None, 0, sp))
+
+    def timed(fn, steps, warmup):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        return e0.elapsed_time(e1) / steps
+
+    # ---- headline: drop-in fwd + bwd, device-resident
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(uuid)
+    clocks.start()
+    ops.profile_reset()
+    ops.profile_enable(True)
+    n0 = ops.launch_count()
+    ms_local = timed(step, args.steps, 0)
+    n_launch = ops.launch_count() - n0
+    ops.profile_enable(False)
+    clk = clocks.stop()
+    bwd_ms, bwd_n = ops.profile_read("k_attn_bwd_tc")
+    fwd_ms, fwd_n = ops.profile_read("k_attn_fwd_tc")
+    ms = max_over_ranks(ms_local, world)
+    value = STEP_FLOPS / (ms * 1e-3) / 1e12
+
+    # roofline of the dominant kernel: k_attn_bwd_tc, algorithmic bwd FLOPs per launch
+    bwd_avg_ms = bwd_ms / max(bwd_n, 1)
+    bwd_flops_local = BWD_FLOPS * nh / (B * H)
+    achieved = bwd_flops_local / (bwd_avg_ms * 1e-3) / 1e12
+    traffic = None if ATTN_BWD_TRAFFIC_PER_HEAD is None else ATTN_BWD_TRAFFIC_PER_HEAD * nh
+    roofline = {"kernel": "k_attn_bwd_tc", "bound": "tensor", "achieved": achieved, "peak": sustained,
+                "unit": "TFLOP/s", "frac": achieved / sustained, "traffic": traffic,
+                "peak_kind": f"{peak_kind} bf16_tflops_sustained (kernel timed inside a multi-second loop)",
+                "avg_launch_ms": bwd_avg_ms, "launches": bwd_n,
+                "fwd_kernel": {"kernel": "k_attn_fwd_tc", "avg_launch_ms": fwd_ms / max(fwd_n, 1),
+                               "launches_per_step": fwd_n / max(args.steps, 1)}}
+
+    # ---- with_out variant
+    ms_wo = max_over_ranks(timed(step_with_out, args.steps, 2), world)
+    with_out = {"value": STEP_FLOPS / (ms_wo * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms_wo,
+                "note": "backward given the forward output (beacon_attention_bwd_with_out), no recompute"}
+
+    # ---- e2e: pinned host -> device, fwd+bwd, device -> host of out, dq, dk, dv
+    e2e = None
+    if not args.no_e2e:
+        host_out = [torch.empty(1, nh, S, D, dtype=torch.bfloat16).pin_memory() for _ in range(4)]
+        h2d = sum(h.numel() * h.element_size() for h in host)
+        d2h = sum(h.numel() * h.element_size() for h in host_out)
+
+        def e2e_step():
+            for dst, src in zip((q, k, v, do), host):
+                dst.copy_(src, non_blocking=True)
+            step()
+            for dst, src in zip(host_out, (out, dq, dk, dv)):
+                dst.copy_(src, non_blocking=True)
+
+        ms_e2e = max_over_ranks(timed(e2e_step, max(2, args.steps // 2), 1), world)
+        e2e = {"value": STEP_FLOPS / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms_e2e,
+               "h2d_bytes_per_step": int(sum_over_ranks(h2d, world)),
+               "d2h_bytes_per_step": int(sum_over_ranks(d2h, world)),
+               "api": "beacon_attention_adjoint_fwd + beacon_attention_adjoint_bwd"}
+
+    del q, k, v, do, out, dq, dk, dv, host
+    torch.cuda.empty_cache()
+
+    # ---- GEMM 4096^3, columns of B sharded
+    gemm = None
+    if not args.no_gemm:
+        ncols = GEMM_N // world
+        gg = torch.Generator(device=dev).manual_seed(1 + rank)
+        a = (torch.rand(GEMM_N, GEMM_N, generator=gg, device=dev) * 2 - 1).to(torch.bfloat16)
+        bm = (torch.rand(GEMM_N, ncols, generator=gg, device=dev) * 2 - 1).to(torch.bfloat16)
+        c = torch.empty(GEMM_N, ncols, dtype=torch.bfloat16, device=dev)
+        flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+        for _ in range(3):
+            ops.matmul_fwd(a, bm, out=c)
+        torch.cuda.synchronize()
+        barrier(world)
+        times = []
+        for _ in range(max(args.steps, 5)):
+            flush.fill_(1)  # evict A, B, C from the 126 MB L2
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            ops.matmul_fwd(a, bm, out=c)
+            e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+        barrier(world)
+        gms = max_over_ranks(statistics.median(times), world)
+        gt = 2.0 * GEMM_N ** 3 / (gms * 1e-3) / 1e12
+        gemm = {"value": gt, "unit": "TFLOP/s", "ms": gms, "frac_of_burst_peak": gt / burst / world,
+                "config": f"bf16 {GEMM_N}^3, B columns sharded {world}-way, L2 flushed between iterations",
+                "per_gpu_tflops": gt / world}
+        del a, bm, c, flush
+
+    if rank != 0:
+        return
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu, _ = cpu_attention_sample()
+    line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic: i.i.d. N(0,1) Q/K/V/dO, seeded",
+            "config": CONFIG, "frac_of_peak": value / (sustained * world),
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "with_out": with_out, "gemm": gemm,
+            "clocks": clk, "gpu_launches": int(n_launch), "impl": "beacon"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        run_reference(args, rank, world)
+        return
+    rank, world, local = dist_setup(args.gpus)
+    try:
+        run_beacon(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -80,6 +80,15 @@ int beacon_device_status(int device, unsigned int out[3]);
 /* Number of kernels launched by this library since load (all devices, all threads). */
 uint64_t beacon_launch_count(void);
 
+/* Device timing of the tensor-core kernels (k_gemm_bf16_tc, k_attn_fwd_tc,
+ * k_attn_bwd_tc): while enabled, each launch is bracketed by CUDA events on its
+ * own stream.  beacon_profile_read(name, ...) waits for those events and returns the
+ * accumulated milliseconds and launch count for `name`; name == NULL resets.
+ * No reference counterpart (the reference bench is a stub,
+ * crates/beacon-bench/src/main.rs:1-3). */
+void beacon_profile_enable(int on);
+int beacon_profile_read(const char* kernel, double* total_ms, uint64_t* count);
+
 /* ---- matmul / linear: crates/beacon-cuda/src/matmul.rs ---------------------- */
 
 /* matmul_fwd (matmul.rs:18-29): out[m,n] = lhs[m,k] . rhs[k,n] */

@@ -111,3 +111,50 @@ def test_no_device_fault_recorded():
     ops = _ops()
     code, site, count = ops.device_status(0)
     assert (code, count) == (0, 0)
+
+
+def test_backward_with_out_matches_drop_in():
+    """beacon_attention_bwd_with_out (O given) and the drop-in backward (O recomputed) agree."""
+    import torch
+    ops = _ops()
+    q, k, v, do = _qkv(1, 4, 4, 384, 128, 6)
+    t = lambda a: to_dev(a, torch.bfloat16)
+    out, lse = ops.attention_fwd(t(q), t(k), t(v))
+    g1 = ops.attention_bwd(t(do), t(q), t(k), t(v), lse)
+    g2 = ops.attention_bwd(t(do), t(q), t(k), t(v), lse, out=out)
+    for a, b in zip(g1, g2):
+        assert torch.equal(a, b)
+    _, rl = O.attention_fwd(q, k, v)
+    refs = O.attention_bwd(do, q, k, v, rl)
+    for a, r in zip(g2, refs):
+        assert rel_err(to_np(a), r) <= BF16_TOL
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_backward_long_sampled_head(causal):
+    """S=2048 backward (16 query tiles per key tile) against the oracle on one head."""
+    import torch
+    ops = _ops()
+    q, k, v, do = _qkv(1, 2, 2, 2048, 128, 7)
+    t = lambda a: to_dev(a, torch.bfloat16)
+    _, lse = ops.attention_fwd(t(q), t(k), t(v), causal=causal)
+    dq, dk, dv = ops.attention_bwd(t(do), t(q), t(k), t(v), lse, causal=causal)
+    sl = slice(1, 2)
+    qs, ks, vs, dos = (np.ascontiguousarray(a[:, sl]) for a in (q, k, v, do))
+    _, rl = O.attention_fwd(qs, ks, vs, causal=causal)
+    rq, rk, rv = O.attention_bwd(dos, qs, ks, vs, rl, causal=causal)
+    assert rel_err(to_np(dq)[:, sl], rq) <= BF16_TOL
+    assert rel_err(to_np(dk)[:, sl], rk) <= BF16_TOL
+    assert rel_err(to_np(dv)[:, sl], rv) <= BF16_TOL
+
+
+def test_backward_gqa_group4_bf16():
+    import torch
+    ops = _ops()
+    q, k, v, do = _qkv(2, 8, 2, 256, 64, 8)
+    t = lambda a: to_dev(a, torch.bfloat16)
+    _, rl = O.attention_fwd(q, k, v)
+    g = ops.attention_bwd(t(do), t(q), t(k), t(v), to_dev(rl, torch.float32))
+    refs = O.attention_bwd(do, q, k, v, rl)
+    for a, r in zip(g, refs):
+        assert rel_err(to_np(a), r) <= BF16_TOL
