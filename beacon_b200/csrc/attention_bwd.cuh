@@ -394,22 +394,21 @@ __global__ void __launch_bounds__(320, 1)
       if (!__all_sync(0xffffffffu, mbar_wait(dq_full, n & 1, abort_flag, kSiteBwdDqFull))) break;
       tc_fence_after();
       float* dst = p.dq_acc + ((long long)bh * p.S + qi) * D;
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t a[32];
-        tmem_ld32(tmem + lane_base + Cfg::DQ_COL + c * 32, a);
-        tmem_wait_ld();
-        if (qi < p.S) {
+      // whole dQ row into registers, release TMEM to the next dP^T / dQ MMAs, then reduce
+      uint32_t a[D];
 #pragma unroll
-          for (int e = 0; e < 32; e += 4)
-            atomicAdd(reinterpret_cast<float4*>(dst + c * 32 + e),
-                      make_float4(__uint_as_float(a[e]) * p.scale, __uint_as_float(a[e + 1]) * p.scale,
-                                  __uint_as_float(a[e + 2]) * p.scale, __uint_as_float(a[e + 3]) * p.scale));
-        }
-      }
+      for (int c = 0; c < D / 32; ++c) tmem_ld32(tmem + lane_base + Cfg::DQ_COL + c * 32,
+                                                 *reinterpret_cast<uint32_t(*)[32]>(&a[c * 32]));
+      tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_empty);
+      if (qi < p.S) {
+#pragma unroll
+        for (int e = 0; e < D; e += 4)
+          red_add_v4(dst + e, __uint_as_float(a[e]) * p.scale, __uint_as_float(a[e + 1]) * p.scale,
+                     __uint_as_float(a[e + 2]) * p.scale, __uint_as_float(a[e + 3]) * p.scale);
+      }
     }
   }
 

@@ -1,0 +1,78 @@
+"""The C-ABI library without a GPU: it loads, exports every symbol the header
+declares, and its host-side checks (dtype, shapes, arena extents, kernel-ID
+dispatch) answer with the right LaunchError variant before touching a device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from beacon_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "beacon_cuda.h")
+
+
+def header_symbols():
+    text = open(HEADER).read()
+    # function declarations: "<type> [*]beacon_name(" at the start of a line
+    return sorted(set(re.findall(r"^[a-z_0-9]+\*?\s+\*?(beacon_[a-z0-9_]+)\s*\(", text, re.M)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    L = _lib.lib()
+    declared = header_symbols()
+    assert len(declared) >= 25
+    missing = [s for s in declared if not hasattr(L, s)]
+    assert not missing, missing
+    assert sorted(_lib.EXPORTS) == declared
+
+
+def test_version_and_workspace_sizes():
+    L = _lib.lib()
+    assert L.beacon_version() == 100
+    ws = L.beacon_attention_bwd_workspace_size(8, 32, 4096, 128, _lib.BF16)
+    rows = 8 * 32 * 4096
+    assert ws >= rows * 4 * 2 + rows * 128 * (4 + 2)
+    assert L.beacon_attention_bwd_workspace_size(0, 32, 4096, 128, _lib.BF16) == 0
+    assert L.beacon_swiglu_workspace_size(8192, 4096, 14336, _lib.BF16, 0) >= 8192 * 14336 * 2
+
+
+def test_host_side_errors_map_to_launch_error_variants():
+    L = _lib.lib()
+    rc = L.beacon_matmul_fwd(None, None, None, 8, 8, 8, _lib.FP8E4M3, None)
+    assert rc == _lib.ERR_UNIMPLEMENTED
+    assert "dtype" in _lib.last_error()
+    assert L.beacon_cast(None, None, 16, 9, None) == _lib.ERR_INVALID_LAUNCH_CONFIG
+    assert L.beacon_residual_add_fwd(None, None, None, -1, _lib.BF16, None) == _lib.ERR_INVALID_LAUNCH_CONFIG
+    assert L.beacon_launch(None, b"matmul_fwd", None, 0, None, 0, None) == _lib.ERR_INVALID_LAUNCH_CONFIG
+
+
+class _FakeArena(ctypes.Structure):
+    # layout of struct beacon_arena (beacon_b200/csrc/abi_arena.inc)
+    _fields_ = [("device", ctypes.c_int), ("base", ctypes.c_void_p), ("bytes", ctypes.c_uint64)]
+
+
+def _launch(kernel, args, scalars):
+    L = _lib.lib()
+    buf = ctypes.create_string_buffer(4096)
+    arena = _FakeArena(0, ctypes.cast(buf, ctypes.c_void_p), 4096)
+    arr = (_lib.KernelArgC * len(args))(*[_lib.KernelArgC(o, n, 0) for o, n in args])
+    sc = (ctypes.c_int64 * max(len(scalars), 1))(*scalars)
+    return L.beacon_launch(ctypes.byref(arena), kernel, arr, len(args), sc, len(scalars), None)
+
+
+def test_arena_dispatch_host_checks():
+    # IDs outside the hot path answer Unimplemented with their name, like runtime.rs:41
+    assert _launch(b"layernorm_adjoint_fwd", [(0, 16)] * 6, [4, 4]) == _lib.ERR_UNIMPLEMENTED
+    assert "layernorm_adjoint_fwd" in _lib.last_error()
+    assert _launch(b"no_such_kernel", [(0, 16)], []) == _lib.ERR_FUNCTION_NOT_FOUND
+    # an argument reaching past the arena
+    assert _launch(b"matmul_fwd", [(4000, 512), (0, 128), (0, 128)], [8, 4, 8, _lib.BF16]) == \
+        _lib.ERR_INVALID_LAUNCH_CONFIG
+    # extents too small for the stated shapes
+    assert _launch(b"matmul_fwd", [(0, 64), (0, 64), (0, 64)], [8, 8, 8, _lib.BF16]) == _lib.ERR_SHAPE_MISMATCH
+    assert "expected argument 0 of matmul_fwd" in _lib.last_error()
+    # attention scalars must describe the tensors
+    assert _launch(b"attention_adjoint_fwd", [(0, 8)] * 5, [1, 1, 4, 0, 1, _lib.BF16]) == \
+        _lib.ERR_INVALID_LAUNCH_CONFIG
