@@ -132,6 +132,17 @@ __global__ void k_attn_dq_convert(__nv_bfloat16* __restrict__ dq, const float* _
 
 // ---------------------------------------------------------------------------
 // 2. main backward kernel
+//
+// Each 128-query tile is processed as two halves of 64 queries so that the tensor
+// core works on one half while the softmax warps turn the other into P^T / dS^T:
+//   MMA issue order per tile:  S^T_0 dP^T_0  S^T_1 dP^T_1 | dV_0 dK_0 dQ_0 | dV_1 dK_1 dQ_1
+//   softmax warps:                          (half 0)      (half 1)
+// TMEM columns: S^T / P^T [0,128) (half h at 64h; P^T_h packed bf16 in its first 32
+// columns), dP^T / dQ [128,256) (half h at 128+64h), dV [256,256+D), dK [256+D,256+2D).
+// D=128: dQ^T_h = K^T dS^T_h (M = 128 head-dim lanes, N = 64 queries) so the dQ
+//        epilogue thread of lane d adds dQ[q][d] for q = 0..63 with coalesced
+//        128-byte fp32 reductions.
+// D=64:  dQ = dS K once per tile after both halves (M = 128 queries, N = 64).
 // ---------------------------------------------------------------------------
 template <int D>
 __global__ void __launch_bounds__(320, 1)
@@ -139,25 +150,26 @@ __global__ void __launch_bounds__(320, 1)
                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                   const AttnBwdParams p) {
   using Cfg = AttnBwdCfg<D>;
+  constexpr bool DQT = (D == 128);  // dQ^T per half (else dQ per tile)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem;
   uint8_t* sV = sK + Cfg::TILE_BYTES;
-  uint8_t* sQ = sV + Cfg::TILE_BYTES;    // [2]
+  uint8_t* sQ = sV + Cfg::TILE_BYTES;       // [2]
   uint8_t* sdO = sQ + 2 * Cfg::TILE_BYTES;  // [2]
   uint8_t* sdS = sdO + 2 * Cfg::TILE_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sdS + Cfg::DS_BYTES);
   uint64_t* kv_full = bars + 0;
-  uint64_t* qd_full = bars + 1;   // [2]
-  uint64_t* qd_empty = bars + 3;  // [2]
-  uint64_t* st_full = bars + 5;
-  uint64_t* ds_full = bars + 6;
-  uint64_t* dq_full = bars + 7;
-  uint64_t* dq_empty = bars + 8;
-  uint64_t* mma_done = bars + 9;
-  uint64_t* dkv_full = bars + 10;
-  uint64_t* drain = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* qd_full = bars + 1;    // [2] Q/dO stage
+  uint64_t* qd_empty = bars + 3;   // [2]
+  uint64_t* s_full = bars + 5;     // [2] half
+  uint64_t* ds_full = bars + 7;    // [2] half
+  uint64_t* dq_full = bars + 9;    // [2] half (D=64: [0] only)
+  uint64_t* dq_empty = bars + 11;  // [2]
+  uint64_t* half_done = bars + 13; // [2] every MMA reading P^T_h / dS^T_h has completed
+  uint64_t* dkv_full = bars + 15;
+  uint64_t* drain = bars + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const uint32_t warp = warp_id(), lane = lane_id();
@@ -177,12 +189,12 @@ __global__ void __launch_bounds__(320, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&qd_full[i], 1);
       mbar_init(&qd_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&ds_full[i], 4);
+      mbar_init(&dq_full[i], 1);
+      mbar_init(&dq_empty[i], 4);
+      mbar_init(&half_done[i], 1);
     }
-    mbar_init(st_full, 1);
-    mbar_init(ds_full, 4);
-    mbar_init(dq_full, 1);
-    mbar_init(dq_empty, 4);
-    mbar_init(mma_done, 1);
     mbar_init(dkv_full, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -234,55 +246,74 @@ __global__ void __launch_bounds__(320, 1)
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc_s = make_idesc_f16(128, 128, false, false);  // S^T, dP^T
+      constexpr uint32_t idesc_s = make_idesc_f16(128, 64, false, false);   // S^T_h, dP^T_h
       constexpr uint32_t idesc_kv = make_idesc_f16(128, D, false, true);    // dV (A in TMEM), dK
-      constexpr uint32_t idesc_q = make_idesc_f16(128, D, true, true);      // dQ
+      constexpr uint32_t idesc_qt = make_idesc_f16(128, 64, true, true);    // dQ^T_h (D = 128)
+      constexpr uint32_t idesc_q = make_idesc_f16(128, D, true, true);      // dQ (D = 64)
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV), ds_addr = smem_u32(sdS);
       bool ok = mbar_wait(kv_full, 0, abort_flag, kSiteBwdKV);
       for (int n = 0; n < n_iter && ok; ++n) {
         const int st = n & 1;
         const uint32_t ph = (n >> 1) & 1;
+        const uint32_t prev = (uint32_t)(n - 1) & 1u;
         if (!mbar_wait(&qd_full[st], ph, abort_flag, kSiteBwdQDFull)) { ok = false; break; }
-        if (n > 0) {
-          // previous dV/dK/dQ MMAs done (TMEM [0,64) P^T and the dS tile are free) and
-          // the dQ epilogue has read TMEM [128, 128+D)
-          if (!mbar_wait(mma_done, (n - 1) & 1, abort_flag, kSiteBwdMmaDone)) { ok = false; break; }
-          if (!mbar_wait(dq_empty, (n - 1) & 1, abort_flag, kSiteBwdDqEmpty)) { ok = false; break; }
-        }
-        tc_fence_after();
         const uint32_t q_addr = smem_u32(sQ + st * Cfg::TILE_BYTES);
         const uint32_t do_addr = smem_u32(sdO + st * Cfg::TILE_BYTES);
+        for (int h = 0; h < 2 && ok; ++h) {
+          if (n > 0) {
+            // P^T_h / dS^T_h of the previous tile consumed, and its dQ columns read out
+            if (!mbar_wait(&half_done[h], prev, abort_flag, kSiteBwdMmaDone)) { ok = false; break; }
+            if ((DQT || h == 0) && !mbar_wait(&dq_empty[DQT ? h : 0], prev, abort_flag, kSiteBwdDqEmpty)) {
+              ok = false;
+              break;
+            }
+          }
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma_f16_ss(tmem + Cfg::ST_COL, make_sdesc_sw128(k_addr + off, 16, 1024),
-                      make_sdesc_sw128(q_addr + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+            umma_f16_ss(tmem + Cfg::ST_COL + 64 * h, make_sdesc_sw128(k_addr + off, 16, 1024),
+                        make_sdesc_sw128(q_addr + off + h * 8192, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+          }
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+            umma_f16_ss(tmem + Cfg::DPT_COL + 64 * h, make_sdesc_sw128(v_addr + off, 16, 1024),
+                        make_sdesc_sw128(do_addr + off + h * 8192, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[h]);
         }
+        if (!ok) break;
+        for (int h = 0; h < 2; ++h) {
+          if (!mbar_wait(&ds_full[h], (uint32_t)n & 1u, abort_flag, kSiteBwdDsFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t acc0 = (n > 0 || h > 0) ? 1u : 0u;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma_f16_ss(tmem + Cfg::DPT_COL, make_sdesc_sw128(v_addr + off, 16, 1024),
-                      make_sdesc_sw128(do_addr + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk)  // dV += P^T_h dO_h   (K = 64 queries)
+            umma_f16_ts(tmem + Cfg::DV_COL, tmem + Cfg::ST_COL + 64 * h + kk * 8,
+                        make_sdesc_sw128(do_addr + h * 8192 + kk * 2048, 16384, 1024), idesc_kv, (acc0 | kk) ? 1u : 0u);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)  // dK += dS^T_h Q_h
+            umma_f16_ss(tmem + Cfg::DK_COL, make_sdesc_sw128(ds_addr + h * 16384 + kk * 32, 16, 1024),
+                        make_sdesc_sw128(q_addr + h * 8192 + kk * 2048, 16384, 1024), idesc_kv, (acc0 | kk) ? 1u : 0u);
+          if constexpr (DQT) {
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)  // dQ^T_h = K^T dS^T_h   (K = 128 keys)
+              umma_f16_ss(tmem + Cfg::DQ_COL + 64 * h, make_sdesc_sw128(k_addr + kk * 2048, 16384, 1024),
+                          make_sdesc_sw128(ds_addr + h * 16384 + kk * 2048, 16384, 1024), idesc_qt,
+                          kk > 0 ? 1u : 0u);
+            umma_commit(&dq_full[h]);
+          } else if (h == 1) {
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)  // dQ = dS K   (M = 128 queries, K = 128 keys)
+              umma_f16_ss(tmem + Cfg::DQ_COL, make_sdesc_sw128(ds_addr + kk * 2048, 16384, 1024),
+                          make_sdesc_sw128(k_addr + kk * 2048, 16384, 1024), idesc_q, kk > 0 ? 1u : 0u);
+            umma_commit(&dq_full[0]);
+          }
+          umma_commit(&half_done[h]);
         }
-        umma_commit(st_full);
-        if (!mbar_wait(ds_full, n & 1, abort_flag, kSiteBwdDsFull)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t acc_kv = (n > 0) ? 1u : 0u;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)  // dV += P^T dO   (K = 128 queries)
-          umma_f16_ts(tmem + Cfg::DV_COL, tmem + Cfg::ST_COL + kk * 8,
-                      make_sdesc_sw128(do_addr + kk * 2048, 16384, 1024), idesc_kv, (acc_kv | kk) ? 1u : 0u);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)  // dK += dS^T Q
-          umma_f16_ss(tmem + Cfg::DK_COL, make_sdesc_sw128(ds_addr + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                      make_sdesc_sw128(q_addr + kk * 2048, 16384, 1024), idesc_kv, (acc_kv | kk) ? 1u : 0u);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)  // dQ = dS K      (K = 128 keys)
-          umma_f16_ss(tmem + Cfg::DQ_COL, make_sdesc_sw128(ds_addr + kk * 2048, 16384, 1024),
-                      make_sdesc_sw128(k_addr + kk * 2048, 16384, 1024), idesc_q, kk > 0 ? 1u : 0u);
+        if (!ok) break;
         umma_commit(&qd_empty[st]);
-        umma_commit(dq_full);
-        umma_commit(mma_done);
       }
       if (ok) umma_commit(dkv_full);
       umma_commit(drain);
@@ -295,63 +326,73 @@ __global__ void __launch_bounds__(320, 1)
     const int r = (int)(quarter * 32 + lane);  // key row within the tile == TMEM lane
     const int kj = j0 + r;
     const uint32_t lane_base = (quarter * 32u) << 16;
+    const bool key_ok = kj < p.S;
     bool ok = true;
-    for (int n = 0; n < n_iter; ++n) {
+    for (int n = 0; n < n_iter && ok; ++n) {
       const int g = n / iters_per_head, it = it0 + n % iters_per_head;
       const int bh = b * p.Hq + hk * group + g;
       const int q0 = it * 128;
-      if (!__all_sync(0xffffffffu, mbar_wait(st_full, n & 1, abort_flag, kSiteBwdStFull))) { ok = false; break; }
-      tc_fence_after();
       const float* lse2p = p.lse2 + (long long)bh * p.S_pad + q0;
       const float* dtp = p.dt + (long long)bh * p.S_pad + q0;
-      // keys beyond S, and (causal) queries before this key, get P = dS = 0
-      const bool key_ok = kj < p.S;
-      const int qmin = p.causal ? kj - q0 : -1;  // column index must be >= qmin
+      if (n + 1 < n_iter && lane < 8) {  // next tile's row statistics into L1 (1 KB)
+        const int g1 = (n + 1) / iters_per_head, it1 = it0 + (n + 1) % iters_per_head;
+        const long long row1 = (long long)(b * p.Hq + hk * group + g1) * p.S_pad + it1 * 128;
+        prefetch_l1(p.lse2 + row1 + (lane & 3) * 32);
+        prefetch_l1(p.dt + row1 + (lane & 3) * 32);
+      }
+      const int qmin = p.causal ? kj - q0 : -1;  // live columns: col >= qmin (and key < S)
+      for (int h = 0; h < 2; ++h) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[h], (uint32_t)n & 1u, abort_flag, kSiteBwdStFull))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t s[32], dp[32];
-        tmem_ld32(tmem + lane_base + Cfg::ST_COL + c * 32, s);
-        tmem_ld32(tmem + lane_base + Cfg::DPT_COL + c * 32, dp);
-        tmem_wait_ld();
-        float pv[32], dsv[32];
+        for (int c = 0; c < 4; ++c) {  // 16 queries per chunk
+          const int col0 = 64 * h + 16 * c;
+          uint32_t s[16], dp[16];
+          tmem_ld16(tmem + lane_base + Cfg::ST_COL + col0, s);
+          tmem_ld16(tmem + lane_base + Cfg::DPT_COL + col0, dp);
+          float lv[16], dv[16];
 #pragma unroll
-        for (int e4 = 0; e4 < 8; ++e4) {
-          const float4 l4 = __ldg(reinterpret_cast<const float4*>(lse2p + c * 32 + e4 * 4));
-          const float4 d4 = __ldg(reinterpret_cast<const float4*>(dtp + c * 32 + e4 * 4));
-          const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
-          const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
+          for (int e4 = 0; e4 < 4; ++e4) {
+            const float4 l4 = __ldg(reinterpret_cast<const float4*>(lse2p + col0 + e4 * 4));
+            const float4 d4 = __ldg(reinterpret_cast<const float4*>(dtp + col0 + e4 * 4));
+            lv[4 * e4 + 0] = l4.x; lv[4 * e4 + 1] = l4.y; lv[4 * e4 + 2] = l4.z; lv[4 * e4 + 3] = l4.w;
+            dv[4 * e4 + 0] = d4.x; dv[4 * e4 + 1] = d4.y; dv[4 * e4 + 2] = d4.z; dv[4 * e4 + 3] = d4.w;
+          }
+          tmem_wait_ld();
+          uint32_t pk[8];
+          float dsv[16];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int e = e4 * 4 + u;
-            const int col = c * 32 + e;
-            const bool live = key_ok && col >= qmin;
-            const float pe = live ? ex2_approx(__uint_as_float(s[e]) * p.scale_log2 - lv[u]) : 0.0f;
-            pv[e] = pe;
-            dsv[e] = pe * (__uint_as_float(dp[e]) - dv[u]);
+          for (int e = 0; e < 16; e += 2) {
+            const bool live0 = key_ok && (col0 + e) >= qmin;
+            const bool live1 = key_ok && (col0 + e + 1) >= qmin;
+            const float p0 = live0 ? ex2_approx(__uint_as_float(s[e]) * p.scale_log2 - lv[e]) : 0.0f;
+            const float p1 = live1 ? ex2_approx(__uint_as_float(s[e + 1]) * p.scale_log2 - lv[e + 1]) : 0.0f;
+            pk[e >> 1] = pack_bf16x2(p0, p1);
+            dsv[e] = p0 * (__uint_as_float(dp[e]) - dv[e]);
+            dsv[e + 1] = p1 * (__uint_as_float(dp[e + 1]) - dv[e + 1]);
+          }
+          // P^T chunk -> TMEM columns [64h + 8c, +8), over S^T columns already read
+          tmem_st8(tmem + lane_base + Cfg::ST_COL + 64 * h + 8 * c, pk);
+          uint8_t* blk = sdS + h * 16384;
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            uint4 w;
+            w.x = pack_bf16x2(dsv[8 * t + 0], dsv[8 * t + 1]);
+            w.y = pack_bf16x2(dsv[8 * t + 2], dsv[8 * t + 3]);
+            w.z = pack_bf16x2(dsv[8 * t + 4], dsv[8 * t + 5]);
+            w.w = pack_bf16x2(dsv[8 * t + 6], dsv[8 * t + 7]);
+            *reinterpret_cast<uint4*>(blk + sw128_offset((uint32_t)r, (uint32_t)(2 * c + t))) = w;
           }
         }
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) pk[e] = pack_bf16x2(pv[2 * e], pv[2 * e + 1]);
-        // P^T chunk c (32 queries) -> TMEM columns [16c, 16c+16): over S^T columns already read
-        tmem_st16(tmem + lane_base + Cfg::ST_COL + c * 16, pk);
-        // dS^T chunk -> shared memory, K-major rows (key) of 64-query swizzled blocks
-        uint8_t* blk = sdS + (c >> 1) * 16384;
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          uint4 w;
-          w.x = pack_bf16x2(dsv[8 * t + 0], dsv[8 * t + 1]);
-          w.y = pack_bf16x2(dsv[8 * t + 2], dsv[8 * t + 3]);
-          w.z = pack_bf16x2(dsv[8 * t + 4], dsv[8 * t + 5]);
-          w.w = pack_bf16x2(dsv[8 * t + 6], dsv[8 * t + 7]);
-          *reinterpret_cast<uint4*>(blk + sw128_offset((uint32_t)r, (uint32_t)((c & 1) * 4 + t))) = w;
-        }
+        tmem_wait_st();
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ds_full[h]);
       }
-      tmem_wait_st();
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(ds_full);
     }
     // final dK, dV rows
     if (ok && __all_sync(0xffffffffu, mbar_wait(dkv_full, 0, abort_flag, kSiteBwdDkvFull))) {
@@ -385,29 +426,52 @@ __global__ void __launch_bounds__(320, 1)
   } else {
     // ---------------------------------------------------------------- dQ epilogue (warps 6..9)
     const uint32_t quarter = warp & 3u;
-    const int r = (int)(quarter * 32 + lane);  // query row within the tile == TMEM lane
     const uint32_t lane_base = (quarter * 32u) << 16;
-    for (int n = 0; n < n_iter; ++n) {
+    bool ok = true;
+    for (int n = 0; n < n_iter && ok; ++n) {
       const int g = n / iters_per_head, it = it0 + n % iters_per_head;
       const int bh = b * p.Hq + hk * group + g;
-      const int qi = it * 128 + r;
-      if (!__all_sync(0xffffffffu, mbar_wait(dq_full, n & 1, abort_flag, kSiteBwdDqFull))) break;
-      tc_fence_after();
-      float* dst = p.dq_acc + ((long long)bh * p.S + qi) * D;
-      // whole dQ row into registers, release TMEM to the next dP^T / dQ MMAs, then reduce
-      uint32_t a[D];
+      if constexpr (DQT) {
+        const int d = (int)(quarter * 32 + lane);  // TMEM lane == head-dim index
+        for (int h = 0; h < 2; ++h) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&dq_full[h], (uint32_t)n & 1u, abort_flag, kSiteBwdDqFull))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint32_t a[64];
+          tmem_ld32(tmem + lane_base + Cfg::DQ_COL + 64 * h, *reinterpret_cast<uint32_t(*)[32]>(&a[0]));
+          tmem_ld32(tmem + lane_base + Cfg::DQ_COL + 64 * h + 32, *reinterpret_cast<uint32_t(*)[32]>(&a[32]));
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&dq_empty[h]);
+          const int qb = it * 128 + 64 * h;
+          float* dst = p.dq_acc + ((long long)bh * p.S + qb) * D + d;
+          const int nq = min(64, p.S - qb);
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) tmem_ld32(tmem + lane_base + Cfg::DQ_COL + c * 32,
-                                                 *reinterpret_cast<uint32_t(*)[32]>(&a[c * 32]));
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dq_empty);
-      if (qi < p.S) {
+          for (int j = 0; j < 64; ++j)  // fully unrolled: a[] stays in registers
+            if (j < nq) red_add_f32(dst + (long long)j * D, __uint_as_float(a[j]) * p.scale);
+        }
+      } else {
+        const int qi = it * 128 + (int)(quarter * 32 + lane);  // TMEM lane == query row
+        if (!__all_sync(0xffffffffu, mbar_wait(&dq_full[0], (uint32_t)n & 1u, abort_flag, kSiteBwdDqFull))) break;
+        tc_fence_after();
+        uint32_t a[D];
 #pragma unroll
-        for (int e = 0; e < D; e += 4)
-          red_add_v4(dst + e, __uint_as_float(a[e]) * p.scale, __uint_as_float(a[e + 1]) * p.scale,
-                     __uint_as_float(a[e + 2]) * p.scale, __uint_as_float(a[e + 3]) * p.scale);
+        for (int c = 0; c < D / 32; ++c)
+          tmem_ld32(tmem + lane_base + Cfg::DQ_COL + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&a[c * 32]));
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&dq_empty[0]);
+        if (qi < p.S) {
+          float* dst = p.dq_acc + ((long long)bh * p.S + qi) * D;
+#pragma unroll
+          for (int e = 0; e < D; e += 4)
+            red_add_v4(dst + e, __uint_as_float(a[e]) * p.scale, __uint_as_float(a[e + 1]) * p.scale,
+                       __uint_as_float(a[e + 2]) * p.scale, __uint_as_float(a[e + 3]) * p.scale);
+        }
       }
     }
   }
