@@ -44,7 +44,8 @@ template <int D>
 struct AttnBwdCfg {
   static constexpr uint32_t TILE_BYTES = 128 * D * 2;  // K, V, Q, dO tiles (128 rows x D)
   static constexpr uint32_t DS_BYTES = 128 * 128 * 2;
-  static constexpr size_t SMEM_BYTES = 1024 + 6 * (size_t)TILE_BYTES + DS_BYTES + 512;
+  static constexpr uint32_t STATS_BYTES = 2 * 128 * 4;  // lse2 and Dt of the current query tile
+  static constexpr size_t SMEM_BYTES = 1024 + 6 * (size_t)TILE_BYTES + DS_BYTES + STATS_BYTES + 256;
   static constexpr int THREADS = 320;  // producer, MMA, 4 softmax warps, 4 dQ warps
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t ST_COL = 0, DPT_COL = 128, DQ_COL = 128, DV_COL = 256, DK_COL = 256 + D;
@@ -61,6 +62,7 @@ enum : unsigned int {
   kSiteBwdDqFull = 0x308,
   kSiteBwdDkvFull = 0x309,
   kSiteBwdDrain = 0x30a,
+  kSiteBwdStats = 0x30b,
 };
 
 // ---------------------------------------------------------------------------
@@ -158,7 +160,8 @@ __global__ void __launch_bounds__(320, 1)
   uint8_t* sQ = sV + Cfg::TILE_BYTES;       // [2]
   uint8_t* sdO = sQ + 2 * Cfg::TILE_BYTES;  // [2]
   uint8_t* sdS = sdO + 2 * Cfg::TILE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sdS + Cfg::DS_BYTES);
+  float* sStats = reinterpret_cast<float*>(sdS + Cfg::DS_BYTES);  // [0,128) lse2, [128,256) Dt
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sdS + Cfg::DS_BYTES + Cfg::STATS_BYTES);
   uint64_t* kv_full = bars + 0;
   uint64_t* qd_full = bars + 1;    // [2] Q/dO stage
   uint64_t* qd_empty = bars + 3;   // [2]
@@ -169,7 +172,9 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* half_done = bars + 13; // [2] every MMA reading P^T_h / dS^T_h has completed
   uint64_t* dkv_full = bars + 15;
   uint64_t* drain = bars + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  uint64_t* stats_full = bars + 17;  // the 4 softmax warps stored this tile's lse2 / Dt
+  uint64_t* stats_free = bars + 18;  // ... and finished reading them
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const uint32_t warp = warp_id(), lane = lane_id();
@@ -197,6 +202,8 @@ __global__ void __launch_bounds__(320, 1)
     }
     mbar_init(dkv_full, 1);
     mbar_init(drain, 1);
+    mbar_init(stats_full, 4);
+    mbar_init(stats_free, 4);
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -327,71 +334,90 @@ __global__ void __launch_bounds__(320, 1)
     const int kj = j0 + r;
     const uint32_t lane_base = (quarter * 32u) << 16;
     const bool key_ok = kj < p.S;
+    const bool keys_full = j0 + 128 <= p.S;
     bool ok = true;
     for (int n = 0; n < n_iter && ok; ++n) {
       const int g = n / iters_per_head, it = it0 + n % iters_per_head;
       const int bh = b * p.Hq + hk * group + g;
       const int q0 = it * 128;
-      const float* lse2p = p.lse2 + (long long)bh * p.S_pad + q0;
-      const float* dtp = p.dt + (long long)bh * p.S_pad + q0;
-      if (n + 1 < n_iter && lane < 8) {  // next tile's row statistics into L1 (1 KB)
-        const int g1 = (n + 1) / iters_per_head, it1 = it0 + (n + 1) % iters_per_head;
-        const long long row1 = (long long)(b * p.Hq + hk * group + g1) * p.S_pad + it1 * 128;
-        prefetch_l1(p.lse2 + row1 + (lane & 3) * 32);
-        prefetch_l1(p.dt + row1 + (lane & 3) * 32);
+      // Stage this query tile's lse2 / Dt (1 KB) while the tensor core computes S^T and
+      // dP^T: every softmax thread has finished the previous tile's reads (first barrier).
+      const long long srow = (long long)bh * p.S_pad + q0 + r;
+      const float l_r = __ldg(p.lse2 + srow), d_r = __ldg(p.dt + srow);
+      if (n > 0 && !__all_sync(0xffffffffu, mbar_wait(stats_free, (uint32_t)(n - 1) & 1u, abort_flag, kSiteBwdStats))) {
+        ok = false;
+        break;
       }
-      const int qmin = p.causal ? kj - q0 : -1;  // live columns: col >= qmin (and key < S)
+      sStats[r] = l_r;
+      sStats[128 + r] = d_r;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(stats_full);
+      if (!__all_sync(0xffffffffu, mbar_wait(stats_full, (uint32_t)n & 1u, abort_flag, kSiteBwdStats))) {
+        ok = false;
+        break;
+      }
+      // off-diagonal tiles need no mask: every key < S and every query >= every key
+      const bool masked = !keys_full || (p.causal && it == jt);
+      const int qmin = p.causal ? kj - q0 : -1;
       for (int h = 0; h < 2; ++h) {
         if (!__all_sync(0xffffffffu, mbar_wait(&s_full[h], (uint32_t)n & 1u, abort_flag, kSiteBwdStFull))) {
           ok = false;
           break;
         }
         tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {  // 16 queries per chunk
-          const int col0 = 64 * h + 16 * c;
-          uint32_t s[16], dp[16];
-          tmem_ld16(tmem + lane_base + Cfg::ST_COL + col0, s);
-          tmem_ld16(tmem + lane_base + Cfg::DPT_COL + col0, dp);
-          float lv[16], dv[16];
+        uint32_t s[2][32], dp[2][32];
+        tmem_ld32(tmem + lane_base + Cfg::ST_COL + 64 * h, s[0]);
+        tmem_ld32(tmem + lane_base + Cfg::DPT_COL + 64 * h, dp[0]);
+        tmem_wait_ld();
 #pragma unroll
-          for (int e4 = 0; e4 < 4; ++e4) {
-            const float4 l4 = __ldg(reinterpret_cast<const float4*>(lse2p + col0 + e4 * 4));
-            const float4 d4 = __ldg(reinterpret_cast<const float4*>(dtp + col0 + e4 * 4));
-            lv[4 * e4 + 0] = l4.x; lv[4 * e4 + 1] = l4.y; lv[4 * e4 + 2] = l4.z; lv[4 * e4 + 3] = l4.w;
-            dv[4 * e4 + 0] = d4.x; dv[4 * e4 + 1] = d4.y; dv[4 * e4 + 2] = d4.z; dv[4 * e4 + 3] = d4.w;
+        for (int c = 0; c < 2; ++c) {  // 32 queries per chunk; chunk 1's TMEM load overlaps chunk 0
+          if (c == 0) {
+            tmem_ld32(tmem + lane_base + Cfg::ST_COL + 64 * h + 32, s[1]);
+            tmem_ld32(tmem + lane_base + Cfg::DPT_COL + 64 * h + 32, dp[1]);
           }
-          tmem_wait_ld();
-          uint32_t pk[8];
-          float dsv[16];
+          const int col0 = 64 * h + 32 * c;
+          uint32_t pk[16];
+          float dsv[32];
 #pragma unroll
-          for (int e = 0; e < 16; e += 2) {
-            const bool live0 = key_ok && (col0 + e) >= qmin;
-            const bool live1 = key_ok && (col0 + e + 1) >= qmin;
-            const float p0 = live0 ? ex2_approx(__uint_as_float(s[e]) * p.scale_log2 - lv[e]) : 0.0f;
-            const float p1 = live1 ? ex2_approx(__uint_as_float(s[e + 1]) * p.scale_log2 - lv[e + 1]) : 0.0f;
-            pk[e >> 1] = pack_bf16x2(p0, p1);
-            dsv[e] = p0 * (__uint_as_float(dp[e]) - dv[e]);
-            dsv[e + 1] = p1 * (__uint_as_float(dp[e + 1]) - dv[e + 1]);
+          for (int e4 = 0; e4 < 8; ++e4) {
+            const float4 l4 = *reinterpret_cast<const float4*>(&sStats[col0 + 4 * e4]);
+            const float4 d4 = *reinterpret_cast<const float4*>(&sStats[128 + col0 + 4 * e4]);
+            const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+            const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
+            float pe[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int e = 4 * e4 + u;
+              float pv = ex2_approx(fmaf(__uint_as_float(s[c][e]), p.scale_log2, -lv[u]));
+              if (masked && !(key_ok && col0 + e >= qmin)) pv = 0.0f;
+              pe[u] = pv;
+              dsv[e] = pv * (__uint_as_float(dp[c][e]) - dv[u]);
+            }
+            pk[2 * e4] = pack_bf16x2(pe[0], pe[1]);
+            pk[2 * e4 + 1] = pack_bf16x2(pe[2], pe[3]);
           }
-          // P^T chunk -> TMEM columns [64h + 8c, +8), over S^T columns already read
-          tmem_st8(tmem + lane_base + Cfg::ST_COL + 64 * h + 8 * c, pk);
+          // P^T chunk -> TMEM columns [64h + 16c, +16): over S^T columns already read
+          tmem_st16(tmem + lane_base + Cfg::ST_COL + 64 * h + 16 * c, pk);
           uint8_t* blk = sdS + h * 16384;
 #pragma unroll
-          for (int t = 0; t < 2; ++t) {
+          for (int t = 0; t < 4; ++t) {
             uint4 w;
             w.x = pack_bf16x2(dsv[8 * t + 0], dsv[8 * t + 1]);
             w.y = pack_bf16x2(dsv[8 * t + 2], dsv[8 * t + 3]);
             w.z = pack_bf16x2(dsv[8 * t + 4], dsv[8 * t + 5]);
             w.w = pack_bf16x2(dsv[8 * t + 6], dsv[8 * t + 7]);
-            *reinterpret_cast<uint4*>(blk + sw128_offset((uint32_t)r, (uint32_t)(2 * c + t))) = w;
+            *reinterpret_cast<uint4*>(blk + sw128_offset((uint32_t)r, (uint32_t)(4 * c + t))) = w;
           }
+          if (c == 0) tmem_wait_ld();
         }
         tmem_wait_st();
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&ds_full[h]);
+        if (lane == 0) {
+          mbar_arrive(&ds_full[h]);
+          if (h == 1) mbar_arrive(stats_free);
+        }
       }
     }
     // final dK, dV rows
