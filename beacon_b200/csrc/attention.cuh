@@ -1,22 +1,23 @@
-// attention.cuh -- causal scaled-dot-product attention on tcgen05 tensor cores.
+// attention.cuh -- causal scaled-dot-product attention forward on tcgen05 tensor cores.
 //
-// Forward (kernel ID `attention_adjoint_fwd`, crates/beacon-cuda/src/attention.rs:21-40):
-// one CTA per (query tile of 128 rows, batch*head); online softmax in the log2
-// domain with fp32 statistics; LSE written in natural-log units.
+// Kernel ID `attention_adjoint_fwd` (crates/beacon-cuda/src/attention.rs:21-40).
+// One CTA per (pair of 128-row query tiles, batch*head).  The two tiles (A, B)
+// share every K/V tile and ping-pong on the tensor core: while one softmax
+// warpgroup turns S_A into P_A, the tensor core computes S_B, and so on:
 //
-//   warp 0     TMA producer: Q once, then K_j and V_j (128 keys x D) into 2-deep rings.
-//   warp 1     TMEM allocator + tcgen05.mma issuer:
-//                S[j&1] = Q K_j^T        (M=128, N=128, K=D;   A,B K-major in smem)
-//                O     += P[j&1] V_j     (M=128, N=D,   K=128; P K-major, V MN-major)
-//              S_{j+1} is issued before O += P_j V_j so the tensor core works on
-//              the next scores while the softmax warps turn S_j into P_j.
-//   warps 2-5  softmax: one query row per thread (TMEM lane = row), P_j written
-//              to shared memory as bf16 in the 128B-swizzled K-major layout the
-//              MMA reads.  O is rescaled in TMEM only when a row maximum grows by
-//              more than 2^8 (the final O / l is exact either way because P and l
-//              use the same stale maximum); then the epilogue normalises O.
+//   MMA issue order per key tile j:   S_A(j) S_B(j) | O_A += P_A(j) V_j | O_B += P_B(j) V_j
 //
-// TMEM: S0 cols [0,128), S1 [128,256), O [256, 256+D).
+//   warp 0      TMA producer: Q_A, Q_B once, then K_j and V_j into 2-deep rings.
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer.
+//   warps 2-5   softmax of tile A, warps 6-9 softmax of tile B: one query row per
+//               thread (TMEM lane = row), online softmax in the log2 domain with fp32
+//               statistics.  P (bf16) is written back into the first 64 TMEM columns
+//               of its own S region and read from there as the A operand of the PV
+//               MMA, so P never touches shared memory.  O is rescaled in TMEM only
+//               when a row maximum grows by more than 2^8 (P and l share the stale
+//               maximum, so O / l is exact either way).
+//
+// TMEM: S_A [0,128), S_B [128,256), O_A [256,256+D), O_B [256+D,256+2D).
 #pragma once
 
 #include "sm100.cuh"
@@ -30,6 +31,7 @@ struct AttnParams {
   __nv_bfloat16* out;  // [B, Hq, S, D]
   float* lse;          // [B, Hq, S]
   int n_qtiles;
+  int n_pairs;         // ceil(n_qtiles / 2)
 };
 
 template <int D>
@@ -37,11 +39,11 @@ struct AttnFwdCfg {
   static constexpr int BM = 128, BN = 128;
   static constexpr uint32_t Q_BYTES = BM * D * 2;
   static constexpr uint32_t KV_BYTES = BN * D * 2;
-  static constexpr uint32_t P_BYTES = BM * BN * 2;
-  static constexpr size_t SMEM_BYTES = 1024 + Q_BYTES + 4 * (size_t)KV_BYTES + 2 * (size_t)P_BYTES + 512;
-  static constexpr int THREADS = 192;
+  static constexpr size_t SMEM_BYTES = 1024 + 2 * (size_t)Q_BYTES + 4 * (size_t)KV_BYTES + 256;
+  static constexpr int THREADS = 320;
   static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr uint32_t O_COL = 256;
+  static constexpr uint32_t S_COL_STRIDE = 128;  // S_A at column 0, S_B at column 128
+  static constexpr uint32_t O_COL0 = 256;
 };
 
 enum : unsigned int {
@@ -51,9 +53,8 @@ enum : unsigned int {
   kSiteAttnVFull = 0x204,
   kSiteAttnVEmpty = 0x205,
   kSiteAttnSFull = 0x206,
-  kSiteAttnSFree = 0x207,
+  kSiteAttnPvDone = 0x207,
   kSiteAttnPFull = 0x208,
-  kSiteAttnPEmpty = 0x209,
   kSiteAttnOFull = 0x20a,
   kSiteAttnDrain = 0x20b,
 };
@@ -64,6 +65,20 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// 2^x on the FMA pipe, to take part of the softmax's exponentials off the MUFU
+// unit: Cody-Waite range reduction x = i + f (i = floor x, f in [0,1)), a cubic in
+// f fitted to 2^f by iteratively reweighted least squares (max relative error
+// 7.5e-5, far below the bf16 rounding P receives), and 2^i added to the exponent
+// field.  Arguments below -126 return ~2^-126 instead of 0, so callers use it only
+// where no element is masked to -inf.
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -126.0f);
+  const float fi = floorf(x);
+  const float f = x - fi;
+  const float p = fmaf(fmaf(fmaf(7.8024031e-2f, f, 2.2606707e-1f), f, 6.9583399e-1f), f, 9.9992513e-1f);
+  return __int_as_float(__float_as_int(p) + (static_cast<int>(fi) << 23));
+}
+
 // Loads one 128-row x D tile (rows `row0..row0+127` of head `z`) as D/64 swizzled
 // column blocks of 128 rows x 128 bytes.
 template <int D>
@@ -72,40 +87,75 @@ __device__ __forceinline__ void tma_load_rows(uint8_t* dst, const CUtensorMap* m
   for (int b = 0; b < D / 64; ++b) tma_load_3d(dst + b * 128 * 128, m, bar, b * 64, row0, z);
 }
 
+// P = 2^(x * scale_log2 - m) for one 128-wide S row, packed to bf16 pairs into the
+// 64 TMEM columns at `taddr`; returns the row sum of P (fp32, before rounding).
+template <bool POLY>
+__device__ __forceinline__ float softmax_p_to_tmem(const float* x, float scale_log2, float neg_m, uint32_t taddr) {
+  float ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    uint32_t pk[32];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      const float p0 = ex2_approx(fmaf(x[64 * c + 2 * e], scale_log2, neg_m));
+      const float a1 = fmaf(x[64 * c + 2 * e + 1], scale_log2, neg_m);
+      float p1;
+      if constexpr (POLY) {
+        if (e & 1)
+          p1 = exp2_fma(a1);
+        else
+          p1 = ex2_approx(a1);
+      } else {
+        p1 = ex2_approx(a1);
+      }
+      ls[e & 3] += p0 + p1;
+      pk[e] = pack_bf16x2(p0, p1);
+    }
+    tmem_st32(taddr + 32 * c, pk);
+  }
+  return (ls[0] + ls[1]) + (ls[2] + ls[3]);
+}
+
 template <int D>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     k_attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
   using Cfg = AttnFwdCfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + Cfg::Q_BYTES;             // [2]
-  uint8_t* sV = sK + 2 * Cfg::KV_BYTES;        // [2]
-  uint8_t* sP = sV + 2 * Cfg::KV_BYTES;        // [2]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * Cfg::P_BYTES);
+  uint8_t* sQ = smem;                      // [2] tiles A, B
+  uint8_t* sK = sQ + 2 * Cfg::Q_BYTES;     // [2] stages
+  uint8_t* sV = sK + 2 * Cfg::KV_BYTES;    // [2] stages
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + 2 * Cfg::KV_BYTES);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;   // [2]
-  uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [2]
-  uint64_t* s_free = bars + 11;  // [2]
-  uint64_t* p_full = bars + 13;  // [2]
-  uint64_t* p_empty = bars + 15; // [2]
-  uint64_t* o_full = bars + 17;
-  uint64_t* drain = bars + 18;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
+  uint64_t* k_full = bars + 1;    // [2]
+  uint64_t* k_empty = bars + 3;   // [2]
+  uint64_t* v_full = bars + 5;    // [2]
+  uint64_t* v_empty = bars + 7;   // [2]
+  uint64_t* s_full = bars + 9;    // [2] per tile
+  uint64_t* p_full = bars + 11;   // [2] per tile
+  uint64_t* pv_done = bars + 13;  // [2] per tile
+  uint64_t* o_full = bars + 15;   // [2] per tile
+  uint64_t* drain = bars + 17;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const uint32_t warp = warp_id(), lane = lane_id();
   const int n_bh = p.B * p.Hq;
-  const int qt = p.n_qtiles - 1 - (int)(blockIdx.x / n_bh);  // heaviest causal tiles first
+  const int pair = p.n_pairs - 1 - (int)(blockIdx.x / n_bh);  // heaviest causal pairs first
   const int bh = (int)(blockIdx.x % n_bh);
   const int b = bh / p.Hq, h = bh % p.Hq;
   const int kvz = b * p.Hkv + h / (p.Hq / p.Hkv);
-  const int q0 = qt * Cfg::BM;
-  const int n_kv = p.causal ? min(qt + 1, (p.S + Cfg::BN - 1) / Cfg::BN) : (p.S + Cfg::BN - 1) / Cfg::BN;
+  const int n_ktiles = (p.S + Cfg::BN - 1) / Cfg::BN;
+  // per tile: first query row, number of key tiles it attends to (0: tile beyond S)
+  int q0[2], nkv[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int qt = 2 * pair + t;
+    q0[t] = qt * Cfg::BM;
+    nkv[t] = (q0[t] >= p.S) ? 0 : (p.causal ? min(qt + 1, n_ktiles) : n_ktiles);
+  }
+  const int n_j = max(nkv[0], nkv[1]);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -115,11 +165,10 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 4);
       mbar_init(&p_full[i], 4);
-      mbar_init(&p_empty[i], 1);
+      mbar_init(&pv_done[i], 1);
+      mbar_init(&o_full[i], 1);
     }
-    mbar_init(o_full, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbarrier_init();
@@ -139,11 +188,12 @@ __global__ void __launch_bounds__(192, 1)
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_arrive_expect_tx(q_full, Cfg::Q_BYTES);
-      tma_load_rows<D>(sQ, &tmQ, q_full, q0, bh);
+      mbar_arrive_expect_tx(q_full, 2 * Cfg::Q_BYTES);
+      tma_load_rows<D>(sQ, &tmQ, q_full, q0[0], bh);
+      tma_load_rows<D>(sQ + Cfg::Q_BYTES, &tmQ, q_full, q0[1], bh);  // rows >= S read as zeros
       uint32_t kissued = 0, vissued = 0, kpar = 0, vpar = 0;
       bool ok = true;
-      for (int j = 0; j < n_kv && ok; ++j) {
+      for (int j = 0; j < n_j && ok; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
         if (!mbar_wait(&k_empty[st], ph ^ 1u, abort_flag, kSiteAttnKEmpty)) { ok = false; break; }
@@ -173,101 +223,100 @@ __global__ void __launch_bounds__(192, 1)
       constexpr uint32_t idesc_o = make_idesc_f16(128, D, false, true);
       const uint32_t q_addr = smem_u32(sQ);
       bool ok = mbar_wait(q_full, 0, abort_flag, kSiteAttnQ);
-      auto issue_pv = [&](int t) -> bool {
-        const int st = t & 1;
-        const uint32_t ph = (t >> 1) & 1;
-        if (!mbar_wait(&p_full[st], ph, abort_flag, kSiteAttnPFull)) return false;
-        if (!mbar_wait(&v_full[st], ph, abort_flag, kSiteAttnVFull)) return false;
-        tc_fence_after();
-        const uint32_t p_addr = smem_u32(sP + st * Cfg::P_BYTES);
-        const uint32_t v_addr = smem_u32(sV + st * Cfg::KV_BYTES);
-#pragma unroll
-        for (int kk = 0; kk < 128 / 16; ++kk) {
-          const uint64_t ad = make_sdesc_sw128(p_addr + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = make_sdesc_sw128(v_addr + kk * 2048, 128 * 128, 1024);
-          umma_f16_ss(tmem + Cfg::O_COL, ad, bd, idesc_o, (t > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(&p_empty[st]);
-        umma_commit(&v_empty[st]);
-        return true;
-      };
-      for (int j = 0; j < n_kv && ok; ++j) {
+      for (int j = 0; j < n_j && ok; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
         if (!mbar_wait(&k_full[st], ph, abort_flag, kSiteAttnKFull)) { ok = false; break; }
-        if (!mbar_wait(&s_free[st], ph ^ 1u, abort_flag, kSiteAttnSFree)) { ok = false; break; }
-        tc_fence_after();
         const uint32_t k_addr = smem_u32(sK + st * Cfg::KV_BYTES);
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (j >= nkv[t]) continue;
+          // S_t(j) overwrites P_t(j-1): its PV must have completed
+          if (j > 0 && !mbar_wait(&pv_done[t], (uint32_t)(j - 1) & 1u, abort_flag, kSiteAttnPvDone)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          const uint64_t ad = make_sdesc_sw128(q_addr + off, 16, 1024);
-          const uint64_t bd = make_sdesc_sw128(k_addr + off, 16, 1024);
-          umma_f16_ss(tmem + st * 128, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+            umma_f16_ss(tmem + (Cfg::S_COL_STRIDE * t), make_sdesc_sw128(q_addr + t * Cfg::Q_BYTES + off, 16, 1024),
+                        make_sdesc_sw128(k_addr + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[t]);
         }
-        umma_commit(&s_full[st]);
+        if (!ok) break;
         umma_commit(&k_empty[st]);
-        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+        if (!mbar_wait(&v_full[st], ph, abort_flag, kSiteAttnVFull)) { ok = false; break; }
+        const uint32_t v_addr = smem_u32(sV + st * Cfg::KV_BYTES);
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (j >= nkv[t]) continue;
+          if (!mbar_wait(&p_full[t], (uint32_t)j & 1u, abort_flag, kSiteAttnPFull)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 128 / 16; ++kk)  // O_t += P_t V_j, P_t from TMEM (K = 128 keys)
+            umma_f16_ts(tmem + Cfg::O_COL0 + t * D, tmem + (Cfg::S_COL_STRIDE * t) + kk * 8,
+                        make_sdesc_sw128(v_addr + kk * 2048, 128 * 128, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&pv_done[t]);
+          if (j == nkv[t] - 1) umma_commit(&o_full[t]);
+        }
+        if (!ok) break;
+        umma_commit(&v_empty[st]);
       }
-      if (ok && n_kv > 0) ok = issue_pv(n_kv - 1);
-      if (ok) umma_commit(o_full);
       umma_commit(drain);
       volatile int no_abort = 0;
       mbar_wait(drain, 0, &no_abort, kSiteAttnDrain);
     }
   } else {
-    // ---------------------------------------------------------------- softmax (warps 2..5)
+    // ---------------------------------------------------------------- softmax (warps 2-5: A, 6-9: B)
+    const int t = (warp < 6) ? 0 : 1;
     const uint32_t quarter = warp & 3u;
     const int r = (int)(quarter * 32 + lane);  // row within the Q tile == TMEM lane
-    const int qi = q0 + r;                     // query index
+    const int qi = q0[t] + r;                  // query index
     const uint32_t lane_base = (quarter * 32u) << 16;
+    const uint32_t s_col = (Cfg::S_COL_STRIDE * t), o_col = Cfg::O_COL0 + t * D;
     float m_used = -INFINITY, l = 0.0f;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      const int st = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
+    for (int j = 0; j < nkv[t]; ++j) {
       // warp-uniform outcome: the tcgen05.ld / st that follow are warp-collective
-      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[st], ph, abort_flag, kSiteAttnSFull))) { ok = false; break; }
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], (uint32_t)j & 1u, abort_flag, kSiteAttnSFull))) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
-      float x[128];
-      {
-        uint32_t u[32];
+      uint32_t xu[128];  // the S row, loaded straight into the registers it is used from
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld32(tmem + lane_base + st * 128 + c * 32, u);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(u[e]);
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[st]);
-      // scale + mask, row max
+      for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_base + s_col + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&xu[32 * c]));
+      tmem_wait_ld();
+      float* x = reinterpret_cast<float*>(xu);
       const int k0 = j * 128;
-      int limit = p.S - k0;                         // keys at or beyond S are masked
+      int limit = p.S - k0;                           // keys at or beyond S are masked
       if (p.causal) limit = min(limit, qi - k0 + 1);  // keys after the query are masked
-      float mx = -INFINITY;
+      // warp-uniform: the P store below (tcgen05.st) is warp-collective, so the
+      // polynomial/MUFU variant is chosen per warp, never per row
+      const bool unmasked = __all_sync(0xffffffffu, limit >= 128);
+      if (!unmasked) {
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        x[c] = (c < limit) ? x[c] * p.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, x[c]);
+        for (int c = 0; c < 128; ++c) x[c] = (c < limit) ? x[c] : -INFINITY;
       }
-      // P buffer st must be free (PV_{j-2} done)
-      if (!__all_sync(0xffffffffu, mbar_wait(&p_empty[st], ph ^ 1u, abort_flag, kSiteAttnPEmpty))) { ok = false; break; }
+      float mx;
+      {  // tree reduction: 8 independent chains
+        float m8[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) m8[u] = x[u];
+#pragma unroll
+        for (int c = 8; c < 128; c += 8)
+#pragma unroll
+          for (int u = 0; u < 8; ++u) m8[u] = fmaxf(m8[u], x[c + u]);
+        mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+      }
+      mx *= p.scale_log2;
       const float m_new = fmaxf(m_used, mx);
       if (j == 0) {
         m_used = m_new;
       } else {
         const bool need = m_new > m_used + 8.0f;
         if (__any_sync(0xffffffffu, need)) {
-          // O must hold PV_{j-1} before it is rescaled
-          const int pt = (j - 1) & 1;
-          if (!__all_sync(0xffffffffu, mbar_wait(&p_empty[pt], ((j - 1) >> 1) & 1, abort_flag, kSiteAttnPEmpty))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
+          // O_t holds PV(j-1) (S_t(j) was issued after it completed); no PV is in flight
           const float alpha = need ? ex2_approx(m_used - m_new) : 1.0f;
           if (need) {
             l *= alpha;
@@ -276,48 +325,36 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll 1
           for (int c = 0; c < D / 32; ++c) {
             uint32_t u[32];
-            tmem_ld32(tmem + lane_base + Cfg::O_COL + c * 32, u);
+            tmem_ld32(tmem + lane_base + o_col + c * 32, u);
             tmem_wait_ld();
 #pragma unroll
             for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * alpha);
-            tmem_st32(tmem + lane_base + Cfg::O_COL + c * 32, u);
+            tmem_st32(tmem + lane_base + o_col + c * 32, u);
           }
-          tmem_wait_st();
         }
       }
-      // P = exp2(x - m_used) -> bf16, 128B-swizzled K-major rows in sP[st]
-      uint8_t* prow = sP + st * Cfg::P_BYTES;
-      float lsum = 0.0f;
-#pragma unroll
-      for (int c = 0; c < 16; ++c) {  // 16 chunks of 8 keys
-        float pv[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          pv[e] = ex2_approx(x[c * 8 + e] - m_used);
-          lsum += pv[e];
-        }
-        uint4 w;
-        w.x = pack_bf16x2(pv[0], pv[1]);
-        w.y = pack_bf16x2(pv[2], pv[3]);
-        w.z = pack_bf16x2(pv[4], pv[5]);
-        w.w = pack_bf16x2(pv[6], pv[7]);
-        *reinterpret_cast<uint4*>(prow + (c >> 3) * 16384 + sw128_offset((uint32_t)r, (uint32_t)(c & 7))) = w;
-      }
+      // P = exp2(x * scale_log2 - m_used) -> bf16 pairs into TMEM columns [s_col, s_col + 64)
+      const float neg_m = -m_used;
+      float lsum;
+      if (unmasked)  // one exponential in four on the FMA pipe
+        lsum = softmax_p_to_tmem<true>(x, p.scale_log2, neg_m, tmem + lane_base + s_col);
+      else
+        lsum = softmax_p_to_tmem<false>(x, p.scale_log2, neg_m, tmem + lane_base + s_col);
       l += lsum;
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[st]);
+      if (lane == 0) mbar_arrive(&p_full[t]);
     }
     // epilogue: O / l -> bf16, LSE
-    if (ok && __all_sync(0xffffffffu, mbar_wait(o_full, 0, abort_flag, kSiteAttnOFull))) {
+    if (ok && nkv[t] > 0 && __all_sync(0xffffffffu, mbar_wait(&o_full[t], 0, abort_flag, kSiteAttnOFull))) {
       tc_fence_after();
       const float inv = 1.0f / l;
       __nv_bfloat16* orow = p.out + ((long long)bh * p.S + qi) * D;
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         uint32_t u[32];
-        tmem_ld32(tmem + lane_base + Cfg::O_COL + c * 32, u);
+        tmem_ld32(tmem + lane_base + o_col + c * 32, u);
         tmem_wait_ld();
         if (qi < p.S) {
 #pragma unroll
