@@ -696,6 +696,94 @@ extern "C" int beacon_rmsnorm_adjoint_bwd(void* dx, void* dweight, const void* d
   return BEACON_OK;
 }
 
+// ===========================================================================
+// RMSNorm backward without any allocation.
+//
+// For callers that cannot allocate device memory on their own: a launcher that
+// hands out only pointers into one preallocated arena (the reference's model,
+// crates/beacon-core/src/arena.rs), a latency-critical path where a first-call
+// cudaMalloc and its device synchronisation are not acceptable, or a host under
+// an allocator that forbids allocations it does not see.  beacon_rmsnorm_adjoint_bwd
+// takes a workspace from the caller or grows its own with cudaMalloc; this variant
+// keeps the dweight partial sums in a fixed array compiled into the library.
+//
+// The array is a file-scope __device__ buffer of kNoAllocScratchFloats floats
+// (4 MiB).  Every GPU that loads this library holds it until the process exits.
+// Its address is looked up once per device, on the first call made with that
+// device current (cudaGetSymbolAddress); make that first call before any stream
+// capture.  All calls share the one array and it keeps the last call's contents:
+// each CTA zeroes its own partial row before accumulating, so nothing carries
+// over, but two calls that overlap on the GPU (different streams, or different
+// host threads on one device) race on it and must be serialised by the caller.
+// ===========================================================================
+namespace {
+
+constexpr size_t kNoAllocScratchFloats = size_t(1) << 20;  // 4 MiB
+static __device__ __align__(256) float g_rmsnorm_bwd_scratch[kNoAllocScratchFloats];
+
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[64] = {};
+
+int noalloc_scratch(int dev, float** out) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_rmsnorm_bwd_scratch);  // device `dev` is current
+    if (e != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      return fail(BEACON_ERR_CUDA, "rmsnorm_bwd_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+                  cudaGetErrorString(e));
+    }
+    g_noalloc_ptr[dev] = reinterpret_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return BEACON_OK;
+}
+
+}  // namespace
+
+extern "C" int beacon_rmsnorm_adjoint_bwd_noalloc(void* dx, void* dweight, const void* dy, const void* x,
+                                                  const float* rms, const void* weight, int64_t tokens, int64_t dim,
+                                                  int dtype, void* stream) {
+  if (tokens < 0 || dim <= 0 || dim > INT32_MAX)
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "rmsnorm_bwd_noalloc: bad shape");
+  if ((size_t)dim > kNoAllocScratchFloats)
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG,
+                "rmsnorm_bwd_noalloc: dim %lld exceeds the fixed scratch of %zu floats (4 MiB); "
+                "use beacon_rmsnorm_adjoint_bwd with a workspace",
+                (long long)dim, kNoAllocScratchFloats);
+  if (dtype != BEACON_BF16 && dtype != BEACON_F32)
+    return fail(BEACON_ERR_UNIMPLEMENTED, "rmsnorm_bwd_noalloc: dtype %d", dtype);
+  int dev;
+  DeviceInfo* di;
+  BEACON_TRY(current_device(&dev, &di));
+  cudaStream_t st = as_stream(stream);
+  if (tokens == 0) {  // empty batch: dweight = 0 (a memset, no allocation)
+    if (dweight) return zero_fill(dweight, (size_t)dim * (dtype == BEACON_F32 ? 4 : 2), st);
+    return BEACON_OK;
+  }
+  if (!(aligned16(dx) && aligned16(x) && aligned16(dy) && aligned16(weight)))
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "rmsnorm_bwd_noalloc: pointers must be 16-byte aligned");
+  // partial rows: as many CTAs as the fixed scratch holds rows of `dim` floats
+  const int64_t cap_rows = (int64_t)(kNoAllocScratchFloats / (size_t)dim);
+  const int grid = (int)std::min<int64_t>(std::min<int64_t>(tokens, (int64_t)di->sms * 4), cap_rows);
+  float* part = nullptr;
+  if (dweight) BEACON_TRY(noalloc_scratch(dev, &part));
+  if (dtype == BEACON_BF16) {
+    k_rmsnorm_bwd<bf16><<<grid, 256, 0, st>>>((bf16*)dx, part, (const bf16*)dy, (const bf16*)x, rms,
+                                              (const bf16*)weight, tokens, (int)dim);
+    BEACON_TRY(check_launch("rmsnorm_bwd_noalloc"));
+    if (dweight) k_colsum<bf16><<<(unsigned)((dim + 255) / 256), 256, 0, st>>>((bf16*)dweight, part, grid, (int)dim);
+  } else {
+    k_rmsnorm_bwd<float><<<grid, 256, 0, st>>>((float*)dx, part, (const float*)dy, (const float*)x, rms,
+                                               (const float*)weight, tokens, (int)dim);
+    BEACON_TRY(check_launch("rmsnorm_bwd_noalloc"));
+    if (dweight) k_colsum<float><<<(unsigned)((dim + 255) / 256), 256, 0, st>>>((float*)dweight, part, grid, (int)dim);
+  }
+  if (dweight) BEACON_TRY(check_launch("rmsnorm_bwd_noalloc colsum"));
+  return BEACON_OK;
+}
+
 #include "abi_attention.inc"
 #include "abi_swiglu.inc"
 #include "abi_arena.inc"

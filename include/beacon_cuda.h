@@ -165,6 +165,19 @@ int beacon_rmsnorm_adjoint_bwd(void* dx, void* dweight, const void* dy, const vo
                                const void* weight, int64_t tokens, int64_t dim, int dtype, void* workspace,
                                size_t workspace_bytes, void* stream);
 
+/* RMSNorm backward that allocates nothing.  No counterpart in the reference: it is
+ * for callers that cannot allocate device memory themselves (a launcher that only
+ * hands out pointers into one preallocated arena, a path that cannot afford the
+ * first-call cudaMalloc and device synchronisation of the library's own workspace).
+ * Same results as beacon_rmsnorm_adjoint_bwd; the dweight partial sums live in a
+ * fixed 4 MiB (1,048,576-float) array compiled into the library, which every GPU
+ * that loads the library holds until exit.  dim above 1,048,576 is rejected with
+ * BEACON_ERR_INVALID_LAUNCH_CONFIG.  The array's address is looked up on the first
+ * call made on each device (make that call before any stream capture).  All calls
+ * share the array: calls that overlap on the GPU race and must be serialised. */
+int beacon_rmsnorm_adjoint_bwd_noalloc(void* dx, void* dweight, const void* dy, const void* x, const float* rms,
+                                       const void* weight, int64_t tokens, int64_t dim, int dtype, void* stream);
+
 /* ---- SwiGLU MLP: crates/beacon-cuda/src/mlp.rs:12-52 ----------------------- */
 
 /* swiglu_fwd (mlp.rs:12-29): out[t, dm] = (silu(x Wg) * (x Wu)) Wd;
