@@ -223,29 +223,35 @@ __global__ void __launch_bounds__(320, 1)
       constexpr uint32_t idesc_o = make_idesc_f16(128, D, false, true);
       const uint32_t q_addr = smem_u32(sQ);
       bool ok = mbar_wait(q_full, 0, abort_flag, kSiteAttnQ);
+      // S_t(j) = Q_t K_j^T into tile t's S columns
+      auto issue_s = [&](int t, int j) {
+        const uint32_t k_addr = smem_u32(sK + (j & 1) * Cfg::KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_f16_ss(tmem + (Cfg::S_COL_STRIDE * t), make_sdesc_sw128(q_addr + t * Cfg::Q_BYTES + off, 16, 1024),
+                      make_sdesc_sw128(k_addr + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[t]);
+      };
+      // Issue order: S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) | ...  tcgen05.mma
+      // executes in issue order, so S_t(j+1) may follow PV_t(j), which reads P_t(j) from
+      // the same TMEM columns, without waiting for it; each softmax warpgroup then has the
+      // other tile's PV and S (1024 tensor-core cycles) to hide behind.
+      if (ok && n_j > 0) {
+        if (!mbar_wait(&k_full[0], 0, abort_flag, kSiteAttnKFull)) {
+          ok = false;
+        } else {
+          tc_fence_after();
+          for (int t = 0; t < 2; ++t)
+            if (nkv[t] > 0) issue_s(t, 0);
+          umma_commit(&k_empty[0]);
+        }
+      }
       for (int j = 0; j < n_j && ok; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&k_full[st], ph, abort_flag, kSiteAttnKFull)) { ok = false; break; }
-        const uint32_t k_addr = smem_u32(sK + st * Cfg::KV_BYTES);
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (j >= nkv[t]) continue;
-          // S_t(j) overwrites P_t(j-1): its PV must have completed
-          if (j > 0 && !mbar_wait(&pv_done[t], (uint32_t)(j - 1) & 1u, abort_flag, kSiteAttnPvDone)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-            umma_f16_ss(tmem + (Cfg::S_COL_STRIDE * t), make_sdesc_sw128(q_addr + t * Cfg::Q_BYTES + off, 16, 1024),
-                        make_sdesc_sw128(k_addr + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
-          }
-          umma_commit(&s_full[t]);
-        }
-        if (!ok) break;
-        umma_commit(&k_empty[st]);
+        bool k_next = false;  // K_{j+1} has landed
         if (!mbar_wait(&v_full[st], ph, abort_flag, kSiteAttnVFull)) { ok = false; break; }
         const uint32_t v_addr = smem_u32(sV + st * Cfg::KV_BYTES);
         for (int t = 0; t < 2 && ok; ++t) {
@@ -256,11 +262,22 @@ __global__ void __launch_bounds__(320, 1)
           for (int kk = 0; kk < 128 / 16; ++kk)  // O_t += P_t V_j, P_t from TMEM (K = 128 keys)
             umma_f16_ts(tmem + Cfg::O_COL0 + t * D, tmem + (Cfg::S_COL_STRIDE * t) + kk * 8,
                         make_sdesc_sw128(v_addr + kk * 2048, 128 * 128, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&pv_done[t]);
           if (j == nkv[t] - 1) umma_commit(&o_full[t]);
+          if (j + 1 < nkv[t]) {
+            if (!k_next) {
+              if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, kSiteAttnKFull)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              k_next = true;
+            }
+            issue_s(t, j + 1);
+          }
         }
         if (!ok) break;
         umma_commit(&v_empty[st]);
+        if (k_next) umma_commit(&k_empty[(j + 1) & 1]);
       }
       umma_commit(drain);
       volatile int no_abort = 0;

@@ -267,14 +267,8 @@ __global__ void __launch_bounds__(320, 1)
         const uint32_t q_addr = smem_u32(sQ + st * Cfg::TILE_BYTES);
         const uint32_t do_addr = smem_u32(sdO + st * Cfg::TILE_BYTES);
         for (int h = 0; h < 2 && ok; ++h) {
-          if (n > 0) {
-            // P^T_h / dS^T_h of the previous tile consumed, and its dQ columns read out
-            if (!mbar_wait(&half_done[h], prev, abort_flag, kSiteBwdMmaDone)) { ok = false; break; }
-            if ((DQT || h == 0) && !mbar_wait(&dq_empty[DQT ? h : 0], prev, abort_flag, kSiteBwdDqEmpty)) {
-              ok = false;
-              break;
-            }
-          }
+          // S^T_h overwrites P^T_h of the previous tile, which the previous dV_h MMA reads:
+          // tcgen05.mma executes in issue order, so that needs no wait.
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
@@ -282,6 +276,14 @@ __global__ void __launch_bounds__(320, 1)
             umma_f16_ss(tmem + Cfg::ST_COL + 64 * h, make_sdesc_sw128(k_addr + off, 16, 1024),
                         make_sdesc_sw128(q_addr + off + h * 8192, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
           }
+          // dP^T_h shares its columns with dQ, which the dQ warps read with tcgen05.ld:
+          // those reads must have drained first.
+          if (n > 0 && (DQT || h == 0) &&
+              !mbar_wait(&dq_empty[DQT ? h : 0], prev, abort_flag, kSiteBwdDqEmpty)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
@@ -317,7 +319,6 @@ __global__ void __launch_bounds__(320, 1)
                           make_sdesc_sw128(k_addr + kk * 2048, 16384, 1024), idesc_q, kk > 0 ? 1u : 0u);
             umma_commit(&dq_full[0]);
           }
-          umma_commit(&half_done[h]);
         }
         if (!ok) break;
         umma_commit(&qd_empty[st]);
