@@ -48,14 +48,14 @@ CONFIG = {"workload": "bf16 causal attention fwd+bwd B=8 H=32 S=4096 D=128, head
           "parallelism": "heads sharded, no collective on the hot path",
           "l2": "inputs larger than L2 (1 GiB per GPU at N=1; 128 MiB of inputs + outputs per GPU at N=8)"}
 # k_attn_bwd_tc DRAM traffic per launch (bytes) from the ncu capture summarised in
-# profiles/attn_bwd_tc.md (B*H=32 heads captured, scaled to 256 heads by head count).
-ATTN_BWD_TRAFFIC_PER_HEAD = None
+# profiles/k_attn_bwd_tc_h32s4096.md (B*H=32 heads captured, scaled by the head count).
+ATTN_BWD_TRAFFIC_PER_HEAD = 670.1e6 / 32  # 446.9 MB read + 223.2 MB written at 32 heads
 
 
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["beacon", "reference"], default="beacon")
     ap.add_argument("--no-e2e", action="store_true")
@@ -95,7 +95,7 @@ class ClockSampler:
         try:
             self.out = open(self.path, "w")
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
                  "-i", self.device_id], stdout=self.out, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -276,12 +276,15 @@ def run_beacon(args, rank, world, local):
         barrier(world)
         return e0.elapsed_time(e1) / steps
 
-    # ---- headline: drop-in fwd + bwd, device-resident
+    # ---- headline: drop-in fwd + bwd, device-resident.  The clock sampler starts
+    # before the warm-up so that its first samples (nvidia-smi needs ~0.1 s to start)
+    # already fall under load, and runs until the timed steps end.
+    clocks = ClockSampler(uuid)
+    clocks.start()
+    time.sleep(0.3)
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    clocks = ClockSampler(uuid)
-    clocks.start()
     ops.profile_reset()
     ops.profile_enable(True)
     n0 = ops.launch_count()
