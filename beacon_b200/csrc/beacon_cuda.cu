@@ -14,6 +14,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -283,6 +284,57 @@ int launch_gemm_tc_bn(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtenso
   return launch_gemm_tc_t<BN, true, false>(ta, tb, tb2, p, sms, st);
 }
 
+template <bool A_MN, bool B_MN>
+int launch_gemm_tc2_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb2, const GemmParams& p,
+                      int sms, cudaStream_t st) {
+  using Cfg = GemmCfg2;
+  auto kern = k_gemm_bf16_tc2<A_MN, B_MN>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return fail(BEACON_ERR_CUDA, "gemm2 smem attribute: %s", cudaGetErrorString(e));
+    attr_set[dev] = true;
+  }
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int pairs = std::min(tiles, sms / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * pairs));
+  cfg.blockDim = dim3(Cfg::THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  {
+    ProfScope prof("k_gemm_bf16_tc", st);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tb2, p);
+    if (e != cudaSuccess) return fail(BEACON_ERR_CUDA, "k_gemm_bf16_tc2 launch: %s", cudaGetErrorString(e));
+  }
+  return check_launch("k_gemm_bf16_tc2");
+}
+
+// Kernel choice override for tests: BEACON_GEMM_PATH = "1sm" | "2sm" (default: by shape).
+int gemm_path_override() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("BEACON_GEMM_PATH");
+    v = (e && !strcmp(e, "1sm")) ? 1 : (e && !strcmp(e, "2sm")) ? 2 : 0;
+  }
+  return v;
+}
+
+// SM-wave efficiency of `tiles` work units over `slots` parallel slots.
+double wave_eff(int64_t tiles, int64_t slots) {
+  const int64_t waves = (tiles + slots - 1) / slots;
+  return (double)tiles / (double)(waves * slots);
+}
+
 // Pick the N tile: the widest tile keeps shared-memory traffic per FLOP lowest,
 // narrower tiles win back idle SMs when the tile count is a poor multiple of the SM count.
 int choose_bn(int64_t M, int64_t Nout, bool swiglu, int sms) {
@@ -324,6 +376,44 @@ int gemm_bf16(const Operand& A, const Operand& B, const Operand* B2, GemmParams 
     k_gemm_simt<bf16><<<grid, 256, 0, st>>>(reinterpret_cast<const bf16*>(A.ptr), sam, sak,
                                             reinterpret_cast<const bf16*>(B.ptr), sbk, sbn, p);
     return check_launch("k_gemm_simt<bf16>");
+  }
+  // 2-SM 256x256 pair tiles halve each SM's operand stream; they win whenever their
+  // wave efficiency is close to the best 1-SM tile's.
+  bool pair = false;
+  {
+    const int ov = gemm_path_override();
+    const int64_t cols2 = swiglu ? 128 : 256;
+    const int64_t tiles2 = ((p.M + 255) / 256) * ((p.N + cols2 - 1) / cols2);
+    const double score2 = wave_eff(tiles2, di->sms / 2) * 1.15;
+    const int bn1 = choose_bn(p.M, p.N, swiglu, di->sms);
+    const int64_t c1 = swiglu ? bn1 / 2 : bn1;
+    const double cost1 = bn1 == 256 ? 1.0 : bn1 == 128 ? 0.93 : 0.80;
+    const double score1 = wave_eff(((p.M + 127) / 128) * ((p.N + c1 - 1) / c1), di->sms) * cost1;
+    pair = ov == 2 || (ov == 0 && !force_bn && score2 > score1);
+  }
+  if (pair) {
+    p.tiles_m = (p.M + 255) / 256;
+    p.tiles_n = swiglu ? (p.N + 127) / 128 : (p.N + 255) / 256;
+    CUtensorMap ta, tb, tb2;
+    if (!A.mn_major)
+      BEACON_TRY(make_map_2d(&ta, A.ptr, (uint64_t)p.K, (uint64_t)p.M, (uint64_t)A.ld, 64, 128));
+    else
+      BEACON_TRY(make_map_2d(&ta, A.ptr, (uint64_t)p.M, (uint64_t)p.K, (uint64_t)A.ld, 64, 64));
+    auto map_b2 = [&](CUtensorMap* m, const Operand& op) -> int {
+      if (op.mn_major) return make_map_2d(m, op.ptr, (uint64_t)p.N, (uint64_t)p.K, (uint64_t)op.ld, 64, 64);
+      return make_map_2d(m, op.ptr, (uint64_t)p.K, (uint64_t)p.N, (uint64_t)op.ld, 64, 128);
+    };
+    BEACON_TRY(map_b2(&tb, B));
+    if (swiglu) {
+      if (B2->mn_major != B.mn_major) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "swiglu operands differ in major");
+      BEACON_TRY(map_b2(&tb2, *B2));
+    } else {
+      tb2 = tb;
+    }
+    if (!A.mn_major && B.mn_major) return launch_gemm_tc2_t<false, true>(ta, tb, tb2, p, di->sms, st);
+    if (!A.mn_major && !B.mn_major) return launch_gemm_tc2_t<false, false>(ta, tb, tb2, p, di->sms, st);
+    if (A.mn_major && B.mn_major) return launch_gemm_tc2_t<true, true>(ta, tb, tb2, p, di->sms, st);
+    return launch_gemm_tc2_t<true, false>(ta, tb, tb2, p, di->sms, st);
   }
   const int bn = force_bn ? force_bn : choose_bn(p.M, p.N, swiglu, di->sms);
   const int cols = swiglu ? bn / 2 : bn;

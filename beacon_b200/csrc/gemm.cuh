@@ -329,6 +329,227 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // ---------------------------------------------------------------------------
+// 2-SM variant: a cluster of two CTAs computes a 256x256 tile with
+// tcgen05.mma.cta_group::2 (M = 256 over the pair).  Each CTA TMA-loads its own 128 rows
+// of A and its own 128-column half of B (for SwiGLU: CTA 0 the gate columns, CTA 1 the
+// up columns), so every SM streams half the B operand a 1-SM 128x256 tile would, and
+// the pair's loads complete on the leader CTA's barrier.  Only the leader issues MMAs;
+// each CTA's TMEM receives its 128 accumulator rows and its own epilogue warps drain
+// them.  No load uses multicast.
+// ---------------------------------------------------------------------------
+struct GemmCfg2 {
+  static constexpr int BM = 128, BN = 256, BK = 64, STAGES = 6;
+  static constexpr uint32_t A_BYTES = BM * BK * 2;           // this CTA's 128 rows of A
+  static constexpr uint32_t B_BYTES = (BN / 2) * BK * 2;     // this CTA's half of B
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  static constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+  static constexpr int THREADS = 192;
+};
+
+template <bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(192, 1)
+    k_gemm_bf16_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmB2, const GemmParams p) {
+  using Cfg = GemmCfg2;
+  constexpr int BK = Cfg::BK, STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * Cfg::B_BYTES);  // used in the leader
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;  // [2]
+  uint64_t* tempty = tfull + 2;      // [2] used in the leader: 4 epilogue warps x 2 CTAs
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t warp = warp_id(), lane = lane_id();
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster = (int)(blockIdx.x >> 1), n_clusters = (int)(gridDim.x >> 1);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 8);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (p.epi == kEpiSwiglu) tma_prefetch_desc(&tmB2);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrive or commit
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_tiles = p.tiles_m * p.tiles_n;  // tiles of 256 x 256 (SwiGLU: 256 x 128 outputs)
+  const int ktiles = (p.K + BK - 1) / BK;
+  const bool swiglu = (p.epi == kEpiSwiglu);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0, issued_parity = 0;
+      bool ok = true;
+      for (int tile = cluster; tile < num_tiles && ok; tile += n_clusters) {
+        const int tm = tile / p.tiles_n, tn = tile % p.tiles_n;
+        const int m0 = tm * 256 + 128 * (int)rank;
+        const CUtensorMap* mb = (swiglu && rank == 1) ? &tmB2 : &tmB;
+        const int n0 = swiglu ? tn * 128 : tn * 256 + 128 * (int)rank;
+        for (int kt = 0; kt < ktiles; ++kt) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteGemmEmpty)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
+          const uint32_t lb = cluster_map(&full[stage], 0);  // the leader's barrier
+          uint8_t* a = sA + stage * Cfg::A_BYTES;
+          uint8_t* b = sB + stage * Cfg::B_BYTES;
+          const int k0 = kt * BK;
+          if constexpr (!A_MN) {
+            tma_load_2d_pair(a, &tmA, lb, k0, m0);
+          } else {
+            tma_load_2d_pair(a, &tmA, lb, m0, k0);
+            tma_load_2d_pair(a + 64 * BK * 2, &tmA, lb, m0 + 64, k0);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d_pair(b, mb, lb, k0, n0);
+          } else {
+            tma_load_2d_pair(b, mb, lb, n0, k0);
+            tma_load_2d_pair(b + 64 * BK * 2, mb, lb, n0 + 64, k0);
+          }
+          issued |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok && leader) {
+        // the leader's barriers count both CTAs' copies: let every one in flight land
+        volatile int no_abort = 0;
+        for (int s = 0; s < STAGES; ++s)
+          if (issued & (1u << s)) mbar_wait(&full[s], (issued_parity >> s) & 1u, &no_abort, kSiteGemmDrain);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = make_idesc_f16(256, Cfg::BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = cluster; tile < num_tiles && ok; tile += n_clusters) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, kSiteGemmTmemEmpty)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(acc * Cfg::BN);
+        for (int kt = 0; kt < ktiles; ++kt) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, kSiteGemmFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * Cfg::A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * Cfg::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = A_MN ? make_sdesc_sw128(a_addr + kk * 2048, 64 * BK * 2, 1024)
+                                     : make_sdesc_sw128(a_addr + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? make_sdesc_sw128(b_addr + kk * 2048, 64 * BK * 2, 1024)
+                                     : make_sdesc_sw128(b_addr + kk * 32, 16, 1024);
+            umma_f16_ss_pair(d, ad, bd, idesc, (kt | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(&empty[stage]);  // both CTAs' stages are free once these MMAs read them
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      umma_commit_leader(drain);
+      volatile int no_abort = 0;
+      mbar_wait(drain, 0, &no_abort, kSiteGemmDrain);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
+    const uint32_t q = warp & 3u;
+    const uint32_t tempty_leader[2] = {cluster_map(&tempty[0], 0), cluster_map(&tempty[1], 0)};
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = cluster; tile < num_tiles; tile += n_clusters) {
+      const int tm = tile / p.tiles_n, tn = tile % p.tiles_n;
+      const bool got = mbar_wait(&tfull[acc], acc_phase, abort_flag, kSiteGemmTmemFull);
+      if (!__all_sync(0xffffffffu, got)) break;  // warp-uniform: tcgen05.ld below is warp-collective
+      tc_fence_after();
+      const int row = tm * 256 + 128 * (int)rank + (int)(q * 32 + lane);
+      const uint32_t tbase = tmem_base + ((q * 32u) << 16) + (uint32_t)(acc * Cfg::BN);
+      if (!swiglu) {
+#pragma unroll 1
+        for (int c = 0; c < Cfg::BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c * 32, r);
+          tmem_wait_ld();
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          const int col0 = tn * Cfg::BN + c * 32;
+          if (col0 < p.N) gemm_store_chunk(p, row, col0, v);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < Cfg::BN / 64; ++c) {
+          uint32_t g[32], u[32];
+          tmem_ld32(tbase + c * 32, g);
+          tmem_ld32(tbase + Cfg::BN / 2 + c * 32, u);
+          tmem_wait_ld();
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = silu_f(__uint_as_float(g[j])) * __uint_as_float(u[j]);
+          const int col0 = tn * (Cfg::BN / 2) + c * 32;
+          if (col0 < p.N) gemm_store_chunk(p, row, col0, v);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still arrive on its barriers
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Exact-FP32 SIMT GEMM (FFMA only, no TF32) for f32 operands and for bf16 shapes
 // the TMA path cannot describe (row strides not a multiple of 16 bytes).
 // A(m,k) = A[m*sam + k*sak], B(k,n) = B[k*sbk + n*sbn]; 64x64 tile, 4x4 per thread.
