@@ -33,6 +33,7 @@ EXPORTS = (
     "beacon_version", "beacon_last_error", "beacon_device_status", "beacon_launch_count",
     "beacon_profile_enable", "beacon_profile_read",
     "beacon_matmul_fwd", "beacon_matmul_bwd", "beacon_linear_fwd", "beacon_linear_bwd",
+    "beacon_matmul_fp8w_fwd", "beacon_linear_fp8w_fwd",
     "beacon_attention_adjoint_fwd", "beacon_attention_adjoint_bwd", "beacon_attention_bwd_workspace_size",
     "beacon_attention_gqa_fwd", "beacon_attention_gqa_bwd", "beacon_attention_bwd_with_out",
     "beacon_rmsnorm_adjoint_fwd", "beacon_rmsnorm_adjoint_bwd", "beacon_rmsnorm_adjoint_bwd_noalloc",
@@ -90,6 +91,8 @@ def lib():
     _sig(L, "beacon_matmul_bwd", _int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp])
     _sig(L, "beacon_linear_fwd", _int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp])
     _sig(L, "beacon_linear_bwd", _int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp])
+    _sig(L, "beacon_matmul_fp8w_fwd", _int, [_vp, _vp, _vp, ctypes.c_float, _i64, _i64, _i64, _vp])
+    _sig(L, "beacon_linear_fp8w_fwd", _int, [_vp, _vp, _vp, ctypes.c_float, _vp, _i64, _i64, _i64, _vp])
     _sig(L, "beacon_attention_adjoint_fwd", _int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int, _vp])
     _sig(L, "beacon_attention_adjoint_bwd", _int,
          [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int, _vp, _sz, _vp])

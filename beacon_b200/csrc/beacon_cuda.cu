@@ -464,6 +464,7 @@ GemmParams gemm_params(int64_t M, int64_t N, int64_t K, void* out, int64_t ldo, 
   p.out_f32 = out_f32 ? 1 : 0;
   p.epi = kEpiStore;
   p.aux_f32 = out_f32 ? 1 : 0;
+  p.out_scale = 1.0f;
   return p;
 }
 
@@ -587,8 +588,53 @@ extern "C" int beacon_device_status(int device, unsigned int out[3]) {
 // ===========================================================================
 // matmul / linear
 // ===========================================================================
+namespace {
+
+// fp8 e4m3 weights [k, n] (crates/beacon-core/src/dtype.rs:134-195) dequantised to bf16 in
+// the library workspace, then the bf16 tensor-core GEMM with `scale` folded into its
+// epilogue: out = (lhs . decode(rhs)) * scale (+ bias).
+int gemm_fp8w(void* out, const void* lhs, const void* rhs_fp8, float scale, const void* bias, int64_t m, int64_t k,
+              int64_t n, cudaStream_t st) {
+  BEACON_TRY(check_dims("fp8-weight GEMM", m, k, n));
+  int dev;
+  DeviceInfo* di;
+  BEACON_TRY(current_device(&dev, &di));
+  if (m == 0 || n == 0) return BEACON_OK;
+  if (!out || (k && (!lhs || !rhs_fp8))) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "fp8-weight GEMM: null pointer");
+  void* ws = nullptr;
+  const size_t wbytes = align256((size_t)k * n * 2);
+  BEACON_TRY(get_workspace(dev, wbytes, nullptr, 0, &ws));
+  if (k > 0) {
+    if (!aligned16(rhs_fp8))
+      return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "fp8-weight GEMM: weights must be 16-byte aligned");
+    k_fp8_to_bf16<<<grid_for(k * n / 16 + 1, 256, di->sms), 256, 0, st>>>(
+        reinterpret_cast<uint16_t*>(ws), reinterpret_cast<const uint8_t*>(rhs_fp8), k * n);
+    BEACON_TRY(check_launch("k_fp8_to_bf16"));
+  }
+  GemmParams p = gemm_params(m, n, k, out, n, false);
+  p.out_scale = scale;
+  if (bias) {
+    p.epi = kEpiBias;
+    p.bias = bias;
+  }
+  return gemm_any(BEACON_BF16, Operand{lhs, false, k}, Operand{ws, true, n}, p, st);
+}
+
+}  // namespace
+
+extern "C" int beacon_matmul_fp8w_fwd(void* out, const void* lhs, const void* rhs_fp8, float rhs_scale, int64_t m,
+                                      int64_t k, int64_t n, void* stream) {
+  return gemm_fp8w(out, lhs, rhs_fp8, rhs_scale, nullptr, m, k, n, as_stream(stream));
+}
+
+extern "C" int beacon_linear_fp8w_fwd(void* out, const void* x, const void* weight_fp8, float weight_scale,
+                                      const void* bias, int64_t m, int64_t k, int64_t n, void* stream) {
+  return gemm_fp8w(out, x, weight_fp8, weight_scale, bias, m, k, n, as_stream(stream));
+}
+
 extern "C" int beacon_matmul_fwd(void* out, const void* lhs, const void* rhs, int64_t m, int64_t k, int64_t n,
                                  int dtype, void* stream) {
+  if (dtype == BEACON_FP8E4M3) return gemm_fp8w(out, lhs, rhs, 1.0f, nullptr, m, k, n, as_stream(stream));
   BEACON_TRY(check_dtype_gemm(dtype));
   BEACON_TRY(check_dims("matmul_fwd", m, k, n));
   if (m && n && (!out || (k && (!lhs || !rhs))))
@@ -616,6 +662,7 @@ extern "C" int beacon_matmul_bwd(void* dlhs, void* drhs, const void* dout, const
 
 extern "C" int beacon_linear_fwd(void* out, const void* x, const void* weight, const void* bias, int64_t m,
                                  int64_t k, int64_t n, int dtype, void* stream) {
+  if (dtype == BEACON_FP8E4M3) return gemm_fp8w(out, x, weight, 1.0f, bias, m, k, n, as_stream(stream));
   BEACON_TRY(check_dtype_gemm(dtype));
   BEACON_TRY(check_dims("linear_fwd", m, k, n));
   GemmParams p = gemm_params(m, n, k, out, n, dtype == BEACON_F32);

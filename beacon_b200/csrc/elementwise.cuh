@@ -142,6 +142,24 @@ __global__ void k_cast(void* __restrict__ dst, const void* __restrict__ src, lon
   }
 }
 
+// fp8 e4m3 -> bf16, 16 elements per thread-step (every e4m3 value is exact in bf16).
+__global__ void k_fp8_to_bf16(uint16_t* __restrict__ dst, const uint8_t* __restrict__ src, long long n) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const long long nvec = n / 16;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+    const uint4 in = reinterpret_cast<const uint4*>(src)[i];
+    const uint8_t* b = reinterpret_cast<const uint8_t*>(&in);
+    uint4 o[2];
+    uint16_t* h = reinterpret_cast<uint16_t*>(o);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) h[j] = (uint16_t)(__float_as_uint(fp8e4m3_to_f32(b[j])) >> 16);
+    reinterpret_cast<uint4*>(dst)[2 * i] = o[0];
+    reinterpret_cast<uint4*>(dst)[2 * i + 1] = o[1];
+  }
+  for (long long i = nvec * 16 + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    dst[i] = (uint16_t)(__float_as_uint(fp8e4m3_to_f32(src[i])) >> 16);
+}
+
 // ---------------------------------------------------------------------------
 // RMSNorm
 // ---------------------------------------------------------------------------

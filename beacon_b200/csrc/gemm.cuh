@@ -39,6 +39,7 @@ struct GemmParams {
   const float* row_scale; // [M]
   const void* residual;   // [M, ldr]
   long long ldr;
+  float out_scale;        // every accumulator is multiplied by it first (dequantisation scale; 1 = none)
 };
 
 __device__ __forceinline__ float gemm_aux(const void* base, long long idx, int is_f32) {
@@ -64,6 +65,10 @@ __device__ __forceinline__ float silu_f(float z) { return z / (1.0f + __expf(-z)
 // Apply the epilogue to 32 consecutive columns [col0, col0+32) of one row and store.
 __device__ __forceinline__ void gemm_store_chunk(const GemmParams& p, int row, int col0, float (&v)[32]) {
   if (row >= p.M) return;
+  if (p.out_scale != 1.0f) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] *= p.out_scale;
+  }
   if (p.epi == kEpiRowScale) {
     const float s = p.row_scale[row];
 #pragma unroll
@@ -599,7 +604,7 @@ __global__ void __launch_bounds__(256)
     for (int j = 0; j < 4; ++j) {
       const int n = n0 + tx * 4 + j;
       if (n >= p.N) continue;
-      float v = acc[i][j];
+      float v = acc[i][j] * p.out_scale;
       if (p.epi == kEpiRowScale) v *= p.row_scale[m];
       if ((p.epi == kEpiBias || p.epi == kEpiRowScale) && p.bias) v += gemm_aux(p.bias, n, p.aux_f32);
       if (p.epi == kEpiResidual) v += gemm_aux(p.residual, m * p.ldr + n, p.aux_f32);

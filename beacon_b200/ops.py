@@ -93,6 +93,26 @@ def linear_bwd(dout, x, weight, need_dbias=True):
     return dx, dw, db
 
 
+def matmul_fp8w_fwd(lhs, rhs_fp8, scale=1.0, bias=None, out=None):
+    """out = (lhs . decode_e4m3(rhs_fp8)) * scale (+ bias); lhs/bias/out bf16, rhs uint8 [k, n]."""
+    m, k = lhs.shape
+    k2, n = rhs_fp8.shape
+    if k != k2 or rhs_fp8.dtype != torch.uint8 or lhs.dtype != torch.bfloat16:
+        raise InvalidLaunchConfig("matmul_fp8w_fwd: lhs bf16 [m,k], rhs uint8 (fp8 e4m3) [k,n]")
+    _dtype(lhs, bias)
+    if not rhs_fp8.is_cuda or not rhs_fp8.is_contiguous():
+        raise InvalidLaunchConfig("matmul_fp8w_fwd: rhs must be a contiguous CUDA tensor")
+    if out is None:
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=lhs.device)
+    if bias is None:
+        rc = _lib.lib().beacon_matmul_fp8w_fwd(_p(out), _p(lhs), _p(rhs_fp8), float(scale), m, k, n, _stream())
+    else:
+        rc = _lib.lib().beacon_linear_fp8w_fwd(_p(out), _p(lhs), _p(rhs_fp8), float(scale), _p(bias), m, k, n,
+                                               _stream())
+    check(rc)
+    return out
+
+
 # ---------------------------------------------------------------- attention
 
 def attention_fwd(q, k, v, causal=True, out=None, lse=None):

@@ -104,6 +104,19 @@ int beacon_matmul_bwd(void* dlhs, void* drhs, const void* dout, const void* lhs,
 int beacon_linear_fwd(void* out, const void* x, const void* weight, const void* bias, int64_t m, int64_t k,
                       int64_t n, int dtype, void* stream);
 
+/* fp8 e4m3 weights (DType::Fp8E4M3, crates/beacon-core/src/dtype.rs:6; codec dtype.rs:134-195;
+ * the reference's "cublasLt fp8" / "fp32 master -> fp8 weights" plan, crates/beacon-cuda/Cargo.toml:7,
+ * crates/beacon-train/Cargo.toml:7).  `dtype = BEACON_FP8E4M3` in beacon_matmul_fwd /
+ * beacon_linear_fwd means: lhs / x, bias and out are bf16, rhs / weight is fp8 e4m3 [k, n]
+ * with scale 1.  The _fp8w_ entry points take the per-tensor dequantisation scale:
+ * out = (lhs . decode(rhs)) * scale (+ bias).  The weights are decoded to bf16 (exactly) in
+ * the library workspace and multiplied on the bf16 tensor cores, the scale folded into
+ * the GEMM epilogue. */
+int beacon_matmul_fp8w_fwd(void* out, const void* lhs, const void* rhs_fp8, float rhs_scale, int64_t m, int64_t k,
+                           int64_t n, void* stream);
+int beacon_linear_fp8w_fwd(void* out, const void* x, const void* weight_fp8, float weight_scale, const void* bias,
+                           int64_t m, int64_t k, int64_t n, void* stream);
+
 /* linear_bwd (matmul.rs:60-78): dx = dout . weight^T ; dweight = x^T . dout ; dbias = sum_rows dout.
  * Any gradient pointer may be NULL to skip it. */
 int beacon_linear_bwd(void* dx, void* dweight, void* dbias, const void* dout, const void* x, const void* weight,

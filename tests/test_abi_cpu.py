@@ -40,7 +40,7 @@ def test_version_and_workspace_sizes():
 
 def test_host_side_errors_map_to_launch_error_variants():
     L = _lib.lib()
-    rc = L.beacon_matmul_fwd(None, None, None, 8, 8, 8, _lib.FP8E4M3, None)
+    rc = L.beacon_matmul_fwd(None, None, None, 8, 8, 8, _lib.F16, None)
     assert rc == _lib.ERR_UNIMPLEMENTED
     assert "dtype" in _lib.last_error()
     assert L.beacon_cast(None, None, 16, 9, None) == _lib.ERR_INVALID_LAUNCH_CONFIG

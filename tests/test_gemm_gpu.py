@@ -110,3 +110,42 @@ def test_no_device_fault_recorded():
     ops = _ops()
     code, site, count = ops.device_status(0)
     assert (code, count) == (0, 0)
+
+
+@pytest.mark.parametrize("m,k,n,scale,with_bias", [(256, 512, 384, 1.0, False), (4096, 4096, 4096, 0.03125, True),
+                                                   (100, 64, 48, 2.5, True)])
+def test_fp8_weight_gemm(m, k, n, scale, with_bias):
+    """fp8 e4m3 weights (reference codec) dequantised in the GEMM path; bf16 activations."""
+    import torch
+    ops = _ops()
+    a = as_bf16(normal((m, k), 21))
+    w = normal((k, n), 22, std=20.0)
+    w8 = O.to_fp8_bits(w)
+    wdec = O.from_fp8_bits(w8)
+    bias = as_bf16(normal((n,), 23)) if with_bias else None
+    out = ops.matmul_fp8w_fwd(to_dev(a, torch.bfloat16), torch.from_numpy(w8).cuda(), scale,
+                              None if bias is None else to_dev(bias, torch.bfloat16))
+    if m > 1024:
+        rows = np.random.default_rng(1).choice(m, 64, replace=False)
+        ref = O.linear_fwd(np.ascontiguousarray(a[rows]), (wdec * scale).astype(np.float32), bias)
+        got = to_np(out)[rows]
+    else:
+        ref = O.linear_fwd(a, (wdec * scale).astype(np.float32), bias)
+        got = to_np(out)
+    assert rel_err(got, ref) <= BF16_TOL
+
+
+def test_fp8_dtype_through_matmul_fwd_entry():
+    """dtype = Fp8E4M3 on the reference's matmul_fwd signature: rhs fp8, scale 1."""
+    import ctypes
+    import torch
+    from beacon_b200 import _lib
+    a = as_bf16(normal((128, 256), 24))
+    w8 = O.to_fp8_bits(normal((256, 128), 25, std=4.0))
+    A, W = to_dev(a, torch.bfloat16), torch.from_numpy(w8).cuda()
+    out = torch.empty(128, 128, dtype=torch.bfloat16, device="cuda")
+    p = lambda t: ctypes.c_void_p(t.data_ptr())
+    rc = _lib.lib().beacon_matmul_fwd(p(out), p(A), p(W), 128, 256, 128, _lib.FP8E4M3,
+                                      ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0, _lib.last_error()
+    assert rel_err(to_np(out), O.matmul_fwd(a, O.from_fp8_bits(w8))) <= BF16_TOL
