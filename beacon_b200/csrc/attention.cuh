@@ -32,6 +32,7 @@ struct AttnParams {
   float* lse;          // [B, Hq, S]
   int n_qtiles;
   int n_pairs;         // ceil(n_qtiles / 2)
+  int out_tokens;      // 1: out is token-major [B, S, Hq, D] (the input of an output projection)
 };
 
 template <int D>
@@ -367,7 +368,8 @@ __global__ void __launch_bounds__(320, 1)
     if (ok && nkv[t] > 0 && __all_sync(0xffffffffu, mbar_wait(&o_full[t], 0, abort_flag, kSiteAttnOFull))) {
       tc_fence_after();
       const float inv = 1.0f / l;
-      __nv_bfloat16* orow = p.out + ((long long)bh * p.S + qi) * D;
+      __nv_bfloat16* orow = p.out + (p.out_tokens ? (((long long)b * p.S + qi) * p.Hq + h) * D
+                                                  : ((long long)bh * p.S + qi) * D);
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         uint32_t u[32];

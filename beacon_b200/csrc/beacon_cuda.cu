@@ -368,7 +368,8 @@ int gemm_bf16(const Operand& A, const Operand& B, const Operand* B2, GemmParams 
   const bool tma_ok = aligned16(A.ptr) && aligned16(B.ptr) && (A.ld % 8 == 0) && (B.ld % 8 == 0) &&
                       (!swiglu || (aligned16(B2->ptr) && B2->ld % 8 == 0)) && p.K > 0;
   if (!tma_ok) {
-    if (swiglu) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "swiglu GEMM needs 16-byte aligned rows");
+    if (swiglu || p.sc_hd > 0)
+      return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "fused GEMM epilogue needs 16-byte aligned rows");
     // exact SIMT path for shapes TMA cannot describe
     const long long sam = A.mn_major ? 1 : A.ld, sak = A.mn_major ? A.ld : 1;
     const long long sbk = B.mn_major ? B.ld : 1, sbn = B.mn_major ? 1 : B.ld;
@@ -923,4 +924,5 @@ extern "C" int beacon_rmsnorm_adjoint_bwd_noalloc(void* dx, void* dweight, const
 
 #include "abi_attention.inc"
 #include "abi_swiglu.inc"
+#include "abi_block.inc"
 #include "abi_arena.inc"

@@ -40,6 +40,12 @@ struct GemmParams {
   const void* residual;   // [M, ldr]
   long long ldr;
   float out_scale;        // every accumulator is multiplied by it first (dequantisation scale; 1 = none)
+  // Head scatter (hd > 0): output column c of row r = b*seq + s is stored head-major,
+  // [B, heads, seq, hd], into `out` for c < hq*hd, then `out_k`, then `out_v` (kv heads
+  // each).  hd is a multiple of 32, so every 32-column chunk lands contiguously.
+  int sc_seq, sc_hd, sc_hq, sc_hkv;
+  void* out_k;
+  void* out_v;
 };
 
 __device__ __forceinline__ float gemm_aux(const void* base, long long idx, int is_f32) {
@@ -79,16 +85,50 @@ __device__ __forceinline__ void gemm_store_chunk(const GemmParams& p, int row, i
     for (int j = 0; j < 32; ++j)
       if (col0 + j < p.N) v[j] += gemm_aux(p.bias, col0 + j, p.aux_f32);
   }
+  bool full = (col0 + 32 <= p.N);
   if (p.epi == kEpiResidual) {
     const long long rbase = (long long)row * p.ldr;
+    if (!p.aux_f32 && full && (p.ldr & 7) == 0 && (col0 & 7) == 0 &&
+        (reinterpret_cast<uintptr_t>(p.residual) & 15) == 0) {
+      const uint4* r4 = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.residual) + rbase + col0);
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (col0 + j < p.N) v[j] += gemm_aux(p.residual, rbase + col0 + j, p.aux_f32);
+      for (int j = 0; j < 4; ++j) {
+        const uint4 w = __ldg(r4 + j);
+        const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          v[8 * j + 2 * e] += __uint_as_float(u[e] << 16);
+          v[8 * j + 2 * e + 1] += __uint_as_float(u[e] & 0xffff0000u);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < p.N) v[j] += gemm_aux(p.residual, rbase + col0 + j, p.aux_f32);
+    }
   }
-  const bool full = (col0 + 32 <= p.N);
+  void* base = p.out;
+  long long off = (long long)row * p.ldo + col0;
+  long long ld = p.ldo;
+  if (p.sc_hd > 0) {
+    int head = col0 / p.sc_hd, nh = p.sc_hq;
+    if (head >= p.sc_hq) {
+      head -= p.sc_hq;
+      nh = p.sc_hkv;
+      base = p.out_k;
+      if (head >= p.sc_hkv) {
+        head -= p.sc_hkv;
+        base = p.out_v;
+      }
+    }
+    const int bb = row / p.sc_seq, s = row - bb * p.sc_seq;
+    off = (((long long)bb * nh + head) * p.sc_seq + s) * p.sc_hd + (col0 % p.sc_hd);
+    ld = 0;  // chunks never straddle a head: the vector path's alignment holds
+    full = true;
+  }
   if (p.out_f32) {
-    float* o = reinterpret_cast<float*>(p.out) + (long long)row * p.ldo + col0;
-    if (full && ((p.ldo & 3) == 0)) {
+    float* o = reinterpret_cast<float*>(base) + off;
+    if (full && ((ld & 3) == 0)) {
 #pragma unroll
       for (int j = 0; j < 32; j += 4)
         *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
@@ -97,8 +137,8 @@ __device__ __forceinline__ void gemm_store_chunk(const GemmParams& p, int row, i
         if (col0 + j < p.N) o[j] = v[j];
     }
   } else {
-    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + (long long)row * p.ldo + col0;
-    if (full && ((p.ldo & 7) == 0)) {
+    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(base) + off;
+    if (full && ((ld & 7) == 0)) {
 #pragma unroll
       for (int j = 0; j < 32; j += 8) {
         uint4 w;

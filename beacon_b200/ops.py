@@ -209,6 +209,34 @@ def swiglu_bwd(dy, x, gate_proj, up_proj, down_proj):
     return dx, dg, du, dd
 
 
+# ---------------------------------------------------------------- pre-norm block
+
+def llama_block_workspace_bytes(batch, seq, d_model, heads, kv_heads, head_dim, d_ff) -> int:
+    return int(_lib.lib().beacon_llama_block_workspace_size(batch, seq, d_model, heads, kv_heads, head_dim, d_ff,
+                                                            _lib.BF16))
+
+
+def llama_block_fwd(x, attn_norm, w_qkv, w_o, ffn_norm, w_gate, w_up, w_down, batch, seq, heads, kv_heads=None,
+                    eps=1e-5, out=None, workspace=None):
+    """One pre-norm block: h = x + attn(rmsnorm(x)) Wo; out = h + swiglu(rmsnorm(h)).
+
+    x: [batch*seq, d_model] bf16; w_qkv: [d_model, (heads + 2*kv_heads)*head_dim]
+    (query, key, value heads in that order); w_o: [heads*head_dim, d_model].
+    """
+    kv_heads = heads if kv_heads is None else kv_heads
+    T, dm = x.shape
+    hd = w_o.shape[0] // heads
+    F = w_gate.shape[1]
+    dt = _dtype(x, attn_norm, w_qkv, w_o, ffn_norm, w_gate, w_up, w_down)
+    if out is None:
+        out = torch.empty_like(x)
+    ws, wsb = (None, 0) if workspace is None else (_p(workspace), workspace.numel() * workspace.element_size())
+    check(_lib.lib().beacon_llama_block_fwd(_p(out), _p(x), _p(attn_norm), _p(w_qkv), _p(w_o), _p(ffn_norm),
+                                            _p(w_gate), _p(w_up), _p(w_down), batch, seq, dm, heads, kv_heads, hd, F,
+                                            eps, dt, ws, wsb, _stream()))
+    return out
+
+
 # ---------------------------------------------------------------- elementwise
 
 def residual_add(a, b):

@@ -17,7 +17,11 @@ Also reported on the same JSON line:
   "roofline":  the dominant kernel (k_attn_bwd_tc) timed live with CUDA events on
                its launch stream against the measured dense bf16 peak;
   "cpu_baseline": the CPU oracle on a bounded sample of heads (rank 0, N=1);
-  "e2e":       the step with pinned-host inputs copied in and results copied out.
+  "e2e":       the step with pinned-host inputs copied in and results copied out;
+  "block":     one pre-norm Llama block forward (batch 4 x seq 2048, d_model 4096,
+               32 x 128 heads, SwiGLU hidden 14336), one replica per rank;
+  "gqa":       long-context grouped-query causal forward (64 query heads, 8 KV heads,
+               S=32768, D=128), KV groups sharded across ranks.
 
 `--impl reference` times the reference's CPU path for this op (the oracle: the
 reference itself has no numeric implementation) on rank 0 with all host threads.
@@ -51,6 +55,18 @@ CONFIG = {"workload": "bf16 causal attention fwd+bwd B=8 H=32 S=4096 D=128, head
 # profiles/k_attn_bwd_tc_h32s4096.md (B*H=32 heads captured, scaled by the head count).
 ATTN_BWD_TRAFFIC_PER_HEAD = 670.1e6 / 32  # 446.9 MB read + 223.2 MB written at 32 heads
 
+# pre-norm Llama block forward
+BLK_B, BLK_S, BLK_DM, BLK_H, BLK_D, BLK_F = 4, 2048, 4096, 32, 128, 14336
+BLK_T = BLK_B * BLK_S
+BLK_FLOPS = (2.0 * BLK_T * BLK_DM * 3 * BLK_H * BLK_D        # QKV projection
+             + 2.0 * BLK_T * BLK_H * BLK_D * BLK_DM          # output projection
+             + 2.0 * BLK_T * BLK_DM * 2 * BLK_F              # gate + up
+             + 2.0 * BLK_T * BLK_F * BLK_DM                  # down
+             + 2.0 * BLK_B * BLK_H * BLK_S * BLK_S * BLK_D)  # causal attention (QK^T and PV, half)
+# long-context grouped-query forward
+GQA_HQ, GQA_HKV, GQA_S, GQA_D = 64, 8, 32768, 128
+GQA_FLOPS = 2.0 * GQA_HQ * GQA_S * GQA_S * GQA_D
+
 
 def parse_args():
     ap = argparse.ArgumentParser()
@@ -61,6 +77,8 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemm", action="store_true")
+    ap.add_argument("--no-block", action="store_true")
+    ap.add_argument("--no-gqa", action="store_true")
     return ap.parse_args()
 
 
@@ -367,6 +385,9 @@ def run_beacon(args, rank, world, local):
                 "per_gpu_tflops": gt / world}
         del a, bm, c, flush
 
+    block = None if args.no_block else bench_block(args, rank, world, dev, stream)
+    gqa = None if args.no_gqa else bench_gqa(args, rank, world, dev, stream)
+
     if rank != 0:
         return
     cpu = None
@@ -377,8 +398,89 @@ def run_beacon(args, rank, world, local):
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic: i.i.d. N(0,1) Q/K/V/dO, seeded",
             "config": CONFIG, "frac_of_peak": value / (sustained * world),
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "with_out": with_out, "gemm": gemm,
+            "block": block, "gqa": gqa,
             "clocks": clk, "gpu_launches": int(n_launch), "impl": "beacon"}
     print(json.dumps(line), flush=True)
+
+
+def _time_calls(fn, stream, iters, warmup):
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(iters):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def bench_block(args, rank, world, dev, stream):
+    """One pre-norm Llama block forward per rank (replicas), weights N(0, 0.02), x N(0, 1)."""
+    import torch
+    from beacon_b200 import ops
+    g = torch.Generator(device=dev).manual_seed(3 + 1000 * rank)
+
+    def w(*shape, std=0.02):
+        return (torch.randn(*shape, generator=g, device=dev) * std).to(torch.bfloat16)
+
+    x = torch.randn(BLK_T, BLK_DM, generator=g, device=dev).to(torch.bfloat16)
+    n1 = torch.ones(BLK_DM, device=dev, dtype=torch.bfloat16)
+    n2 = torch.ones(BLK_DM, device=dev, dtype=torch.bfloat16)
+    wqkv, wo = w(BLK_DM, 3 * BLK_H * BLK_D), w(BLK_H * BLK_D, BLK_DM)
+    wg, wu, wd = w(BLK_DM, BLK_F), w(BLK_DM, BLK_F), w(BLK_F, BLK_DM)
+    out = torch.empty_like(x)
+    ws = torch.empty(ops.llama_block_workspace_bytes(BLK_B, BLK_S, BLK_DM, BLK_H, BLK_H, BLK_D, BLK_F),
+                     dtype=torch.uint8, device=dev)
+
+    def fn():
+        ops.llama_block_fwd(x, n1, wqkv, wo, n2, wg, wu, wd, BLK_B, BLK_S, BLK_H, BLK_H, out=out, workspace=ws)
+
+    barrier(world)
+    ms = max_over_ranks(_time_calls(fn, stream, max(5, args.steps // 3), 2), world)
+    torch.cuda.synchronize()
+    ok = bool(torch.isfinite(out.float()).all().item())
+    del x, wqkv, wo, wg, wu, wd, out, ws
+    torch.cuda.empty_cache()
+    return {"value": BLK_FLOPS * world / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": ms,
+            "per_gpu_tflops": BLK_FLOPS / (ms * 1e-3) / 1e12, "flops_per_block": BLK_FLOPS, "finite": ok,
+            "config": f"pre-norm Llama block forward, batch {BLK_B} x seq {BLK_S}, d_model {BLK_DM}, "
+                      f"{BLK_H} x {BLK_D} heads, SwiGLU {BLK_F}, bf16; one replica per rank",
+            "api": "beacon_llama_block_fwd (7 launches)"}
+
+
+def bench_gqa(args, rank, world, dev, stream):
+    """Causal GQA forward, S=32768; the 8 KV groups (8 query heads each) sharded across ranks."""
+    import torch
+    from beacon_b200 import ops
+    if GQA_HKV % world != 0:
+        return None
+    hkv = GQA_HKV // world
+    hq = hkv * (GQA_HQ // GQA_HKV)
+    g = torch.Generator(device=dev).manual_seed(4 + 1000 * rank)
+    q = torch.randn(1, hq, GQA_S, GQA_D, generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn(1, hkv, GQA_S, GQA_D, generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn(1, hkv, GQA_S, GQA_D, generator=g, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    lse = torch.empty(1, hq, GQA_S, dtype=torch.float32, device=dev)
+    L = ops._lib.lib()
+    sp = ops._stream()
+
+    def fn():
+        ops.check(L.beacon_attention_gqa_fwd(ops._p(out), ops._p(q), ops._p(k), ops._p(v), ops._p(lse), 1, hq, hkv,
+                                             GQA_S, GQA_D, 1, ops._lib.BF16, sp))
+
+    barrier(world)
+    ms = max_over_ranks(_time_calls(fn, stream, 3, 1), world)
+    del q, k, v, out, lse
+    torch.cuda.empty_cache()
+    return {"value": GQA_FLOPS / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": ms,
+            "per_gpu_tflops": GQA_FLOPS / world / (ms * 1e-3) / 1e12,
+            "config": f"causal GQA forward B=1, {GQA_HQ} query / {GQA_HKV} KV heads, S={GQA_S}, D={GQA_D}, bf16; "
+                      f"{hq} query heads ({hkv} KV groups) per rank",
+            "api": "beacon_attention_gqa_fwd"}
 
 
 def main():

@@ -208,6 +208,30 @@ int beacon_swiglu_adjoint_bwd(void* dx, void* dgate_proj, void* dup_proj, void* 
 
 size_t beacon_swiglu_workspace_size(int64_t tokens, int64_t d_model, int64_t d_ff, int dtype, int backward);
 
+/* ---- pre-norm Llama-style block forward (no reference counterpart) ---------
+ * The composition beacon-nn would make of rmsnorm_fwd (norm.rs:19-31), linear_fwd
+ * (matmul.rs:46-58), attention_fwd (attention.rs:21-40), residual_add
+ * (elementwise.rs:47-55) and swiglu_fwd (mlp.rs:12-29), in seven launches:
+ *   h   = x + attention(rmsnorm(x, attn_norm) . w_qkv) . w_o        (causal)
+ *   out = h + (silu(xn . w_gate) * (xn . w_up)) . w_down,  xn = rmsnorm(h, ffn_norm)
+ * The QKV GEMM stores q, k, v head-major straight from its epilogue, attention writes
+ * its output token-major, and both residual adds are GEMM epilogues.
+ * x, out: [batch*seq, d_model]; attn_norm, ffn_norm: [d_model];
+ * w_qkv: [d_model, (heads + 2*kv_heads)*head_dim] (query heads, then key heads, then
+ * value heads); w_o: [heads*head_dim, d_model]; w_gate, w_up: [d_model, d_ff];
+ * w_down: [d_ff, d_model].  bf16 only; head_dim 64 or 128; d_model and d_ff multiples
+ * of 8; pointers 16-byte aligned.  Scratch (beacon_llama_block_workspace_size bytes,
+ * or the library's workspace when `workspace` is NULL) holds, at the offsets the
+ * layout in abi_block.inc gives, the normalised rows, both rms vectors, q, k, v, the
+ * attention output, h and the SwiGLU activations. */
+int beacon_llama_block_fwd(void* out, const void* x, const void* attn_norm, const void* w_qkv, const void* w_o,
+                           const void* ffn_norm, const void* w_gate, const void* w_up, const void* w_down,
+                           int64_t batch, int64_t seq, int64_t d_model, int64_t heads, int64_t kv_heads,
+                           int64_t head_dim, int64_t d_ff, float eps, int dtype, void* workspace,
+                           size_t workspace_bytes, void* stream);
+size_t beacon_llama_block_workspace_size(int64_t batch, int64_t seq, int64_t d_model, int64_t heads,
+                                         int64_t kv_heads, int64_t head_dim, int64_t d_ff, int dtype);
+
 /* ---- elementwise: crates/beacon-cuda/src/elementwise.rs -------------------- */
 
 /* residual_add (elementwise.rs:47-55): out = a + b */

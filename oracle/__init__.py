@@ -243,6 +243,35 @@ def residual_add_fwd(a, b):
     return out
 
 
+def llama_block_fwd(x, attn_norm, w_qkv, w_o, ffn_norm, w_gate, w_up, w_down, batch, seq, heads, kv_heads,
+                    eps=1e-5, round_between=True):
+    """Pre-norm Llama block composed from the operator restatements above, in the order a
+    caller of the reference's ops would make: rmsnorm_fwd (crates/beacon-cuda/src/norm.rs:19-31),
+    linear_fwd (crates/beacon-cuda/src/matmul.rs:46-58), attention_fwd
+    (crates/beacon-cuda/src/attention.rs:21-40) on [B, H, S, D] tensors, residual_add
+    (crates/beacon-cuda/src/elementwise.rs:47-55) and swiglu_fwd (crates/beacon-cuda/src/mlp.rs:12-29).
+    With ``round_between`` every operator output is rounded to bf16, as bf16 operators
+    would store it."""
+    rnd = round_bf16 if round_between else (lambda a: a)
+    T, dm = x.shape
+    hd = w_o.shape[0] // heads
+    xn, _ = rmsnorm_fwd(x, attn_norm, eps)
+    qkv = rnd(matmul_fwd(rnd(xn), w_qkv))
+
+    def heads_major(cols, nh):
+        return np.ascontiguousarray(cols.reshape(batch, seq, nh, hd).transpose(0, 2, 1, 3))
+
+    q = heads_major(qkv[:, :heads * hd], heads)
+    k = heads_major(qkv[:, heads * hd:(heads + kv_heads) * hd], kv_heads)
+    v = heads_major(qkv[:, (heads + kv_heads) * hd:], kv_heads)
+    ao, _ = attention_fwd(q, k, v, causal=True)
+    ao = rnd(np.ascontiguousarray(ao.transpose(0, 2, 1, 3)).reshape(T, heads * hd))
+    h = rnd(residual_add_fwd(rnd(matmul_fwd(ao, w_o)), x)) if round_between else matmul_fwd(ao, w_o) + x
+    hn, _ = rmsnorm_fwd(h, ffn_norm, eps)
+    f = swiglu_fwd(rnd(hn), w_gate, w_up, w_down)
+    return residual_add_fwd(rnd(f), h)
+
+
 def num_threads() -> int:
     return int(lib().bo_num_threads())
 
