@@ -5,11 +5,13 @@
 // share every K/V tile and ping-pong on the tensor core: while one softmax
 // warpgroup turns S_A into P_A, the tensor core computes S_B, and so on:
 //
-//   MMA issue order per key tile j:   S_A(j) S_B(j) | O_A += P_A(j) V_j | O_B += P_B(j) V_j
+//   MMA issue order:   S_A(0) S_B(0) | O_A += P_A(j) V_j, S_A(j+1), O_B += P_B(j) V_j, S_B(j+1) | ...
 //
 //   warp 0      TMA producer: Q_A, Q_B once, then K_j and V_j into 2-deep rings.
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer.
-//   warps 2-5   softmax of tile A, warps 6-9 softmax of tile B: one query row per
+//   warps 2-3   idle; warps 0-3 hand most of their registers to the softmax warpgroups
+//               (setmaxnreg), so a thread holds its whole S row without spilling.
+//   warps 4-7   softmax of tile A, warps 8-11 softmax of tile B: one query row per
 //               thread (TMEM lane = row), online softmax in the log2 domain with fp32
 //               statistics.  P (bf16) is written back into the first 64 TMEM columns
 //               of its own S region and read from there as the A operand of the PV
@@ -41,7 +43,7 @@ struct AttnFwdCfg {
   static constexpr uint32_t Q_BYTES = BM * D * 2;
   static constexpr uint32_t KV_BYTES = BN * D * 2;
   static constexpr size_t SMEM_BYTES = 1024 + 2 * (size_t)Q_BYTES + 4 * (size_t)KV_BYTES + 256;
-  static constexpr int THREADS = 320;
+  static constexpr int THREADS = 384;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t S_COL_STRIDE = 128;  // S_A at column 0, S_B at column 128
   static constexpr uint32_t O_COL0 = 256;
@@ -118,7 +120,7 @@ __device__ __forceinline__ float softmax_p_to_tmem(const float* x, float scale_l
 }
 
 template <int D>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(384, 1)
     k_attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
   using Cfg = AttnFwdCfg<D>;
@@ -182,111 +184,117 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
-  if (warp == 0) {
-    // ---------------------------------------------------------------- producer
-    if (lane == 0) {
-      tma_prefetch_desc(&tmQ);
-      tma_prefetch_desc(&tmK);
-      tma_prefetch_desc(&tmV);
-      mbar_arrive_expect_tx(q_full, 2 * Cfg::Q_BYTES);
-      tma_load_rows<D>(sQ, &tmQ, q_full, q0[0], bh);
-      tma_load_rows<D>(sQ + Cfg::Q_BYTES, &tmQ, q_full, q0[1], bh);  // rows >= S read as zeros
-      uint32_t kissued = 0, vissued = 0, kpar = 0, vpar = 0;
-      bool ok = true;
-      for (int j = 0; j < n_j && ok; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&k_empty[st], ph ^ 1u, abort_flag, kSiteAttnKEmpty)) { ok = false; break; }
-        mbar_arrive_expect_tx(&k_full[st], Cfg::KV_BYTES);
-        tma_load_rows<D>(sK + st * Cfg::KV_BYTES, &tmK, &k_full[st], j * Cfg::BN, kvz);
-        kissued |= 1u << st;
-        kpar = (kpar & ~(1u << st)) | (ph << st);
-        if (!mbar_wait(&v_empty[st], ph ^ 1u, abort_flag, kSiteAttnVEmpty)) { ok = false; break; }
-        mbar_arrive_expect_tx(&v_full[st], Cfg::KV_BYTES);
-        tma_load_rows<D>(sV + st * Cfg::KV_BYTES, &tmV, &v_full[st], j * Cfg::BN, kvz);
-        vissued |= 1u << st;
-        vpar = (vpar & ~(1u << st)) | (ph << st);
-      }
-      if (!ok) {
-        volatile int no_abort = 0;
-        mbar_wait(q_full, 0, &no_abort, kSiteAttnDrain);
-        for (int s = 0; s < 2; ++s) {
-          if (kissued & (1u << s)) mbar_wait(&k_full[s], (kpar >> s) & 1u, &no_abort, kSiteAttnDrain);
-          if (vissued & (1u << s)) mbar_wait(&v_full[s], (vpar >> s) & 1u, &no_abort, kSiteAttnDrain);
+  // Registers: the producer / MMA warpgroup gives up most of its share to the two
+  // softmax warpgroups, which hold a whole 128-column S row per thread.
+  // 128 x 56 + 256 x 224 = 384 x 168, the allocation the CTA is launched with.
+  if (warp < 4) {
+    warpgroup_reg_dealloc<56>();
+    if (warp == 0) {
+      // ---------------------------------------------------------------- producer
+      if (lane == 0) {
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
+        mbar_arrive_expect_tx(q_full, 2 * Cfg::Q_BYTES);
+        tma_load_rows<D>(sQ, &tmQ, q_full, q0[0], bh);
+        tma_load_rows<D>(sQ + Cfg::Q_BYTES, &tmQ, q_full, q0[1], bh);  // rows >= S read as zeros
+        uint32_t kissued = 0, vissued = 0, kpar = 0, vpar = 0;
+        bool ok = true;
+        for (int j = 0; j < n_j && ok; ++j) {
+          const int st = j & 1;
+          const uint32_t ph = (j >> 1) & 1;
+          if (!mbar_wait(&k_empty[st], ph ^ 1u, abort_flag, kSiteAttnKEmpty)) { ok = false; break; }
+          mbar_arrive_expect_tx(&k_full[st], Cfg::KV_BYTES);
+          tma_load_rows<D>(sK + st * Cfg::KV_BYTES, &tmK, &k_full[st], j * Cfg::BN, kvz);
+          kissued |= 1u << st;
+          kpar = (kpar & ~(1u << st)) | (ph << st);
+          if (!mbar_wait(&v_empty[st], ph ^ 1u, abort_flag, kSiteAttnVEmpty)) { ok = false; break; }
+          mbar_arrive_expect_tx(&v_full[st], Cfg::KV_BYTES);
+          tma_load_rows<D>(sV + st * Cfg::KV_BYTES, &tmV, &v_full[st], j * Cfg::BN, kvz);
+          vissued |= 1u << st;
+          vpar = (vpar & ~(1u << st)) | (ph << st);
         }
-      }
-    }
-  } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc_s = make_idesc_f16(128, 128, false, false);
-      constexpr uint32_t idesc_o = make_idesc_f16(128, D, false, true);
-      const uint32_t q_addr = smem_u32(sQ);
-      bool ok = mbar_wait(q_full, 0, abort_flag, kSiteAttnQ);
-      // S_t(j) = Q_t K_j^T into tile t's S columns
-      auto issue_s = [&](int t, int j) {
-        const uint32_t k_addr = smem_u32(sK + (j & 1) * Cfg::KV_BYTES);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma_f16_ss(tmem + (Cfg::S_COL_STRIDE * t), make_sdesc_sw128(q_addr + t * Cfg::Q_BYTES + off, 16, 1024),
-                      make_sdesc_sw128(k_addr + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(&s_full[t]);
-      };
-      // Issue order: S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) | ...  tcgen05.mma
-      // executes in issue order, so S_t(j+1) may follow PV_t(j), which reads P_t(j) from
-      // the same TMEM columns, without waiting for it; each softmax warpgroup then has the
-      // other tile's PV and S (1024 tensor-core cycles) to hide behind.
-      if (ok && n_j > 0) {
-        if (!mbar_wait(&k_full[0], 0, abort_flag, kSiteAttnKFull)) {
-          ok = false;
-        } else {
-          tc_fence_after();
-          for (int t = 0; t < 2; ++t)
-            if (nkv[t] > 0) issue_s(t, 0);
-          umma_commit(&k_empty[0]);
-        }
-      }
-      for (int j = 0; j < n_j && ok; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        bool k_next = false;  // K_{j+1} has landed
-        if (!mbar_wait(&v_full[st], ph, abort_flag, kSiteAttnVFull)) { ok = false; break; }
-        const uint32_t v_addr = smem_u32(sV + st * Cfg::KV_BYTES);
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (j >= nkv[t]) continue;
-          if (!mbar_wait(&p_full[t], (uint32_t)j & 1u, abort_flag, kSiteAttnPFull)) { ok = false; break; }
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < 128 / 16; ++kk)  // O_t += P_t V_j, P_t from TMEM (K = 128 keys)
-            umma_f16_ts(tmem + Cfg::O_COL0 + t * D, tmem + (Cfg::S_COL_STRIDE * t) + kk * 8,
-                        make_sdesc_sw128(v_addr + kk * 2048, 128 * 128, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
-          if (j == nkv[t] - 1) umma_commit(&o_full[t]);
-          if (j + 1 < nkv[t]) {
-            if (!k_next) {
-              if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, kSiteAttnKFull)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              k_next = true;
-            }
-            issue_s(t, j + 1);
+        if (!ok) {
+          volatile int no_abort = 0;
+          mbar_wait(q_full, 0, &no_abort, kSiteAttnDrain);
+          for (int s = 0; s < 2; ++s) {
+            if (kissued & (1u << s)) mbar_wait(&k_full[s], (kpar >> s) & 1u, &no_abort, kSiteAttnDrain);
+            if (vissued & (1u << s)) mbar_wait(&v_full[s], (vpar >> s) & 1u, &no_abort, kSiteAttnDrain);
           }
         }
-        if (!ok) break;
-        umma_commit(&v_empty[st]);
-        if (k_next) umma_commit(&k_empty[(j + 1) & 1]);
       }
-      umma_commit(drain);
-      volatile int no_abort = 0;
-      mbar_wait(drain, 0, &no_abort, kSiteAttnDrain);
+    } else if (warp == 1) {
+      // ---------------------------------------------------------------- MMA issuer
+      if (lane == 0) {
+        constexpr uint32_t idesc_s = make_idesc_f16(128, 128, false, false);
+        constexpr uint32_t idesc_o = make_idesc_f16(128, D, false, true);
+        const uint32_t q_addr = smem_u32(sQ);
+        bool ok = mbar_wait(q_full, 0, abort_flag, kSiteAttnQ);
+        // S_t(j) = Q_t K_j^T into tile t's S columns
+        auto issue_s = [&](int t, int j) {
+          const uint32_t k_addr = smem_u32(sK + (j & 1) * Cfg::KV_BYTES);
+  #pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+            umma_f16_ss(tmem + (Cfg::S_COL_STRIDE * t), make_sdesc_sw128(q_addr + t * Cfg::Q_BYTES + off, 16, 1024),
+                        make_sdesc_sw128(k_addr + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[t]);
+        };
+        // Issue order: S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) | ...  tcgen05.mma
+        // executes in issue order, so S_t(j+1) may follow PV_t(j), which reads P_t(j) from
+        // the same TMEM columns, without waiting for it; each softmax warpgroup then has the
+        // other tile's PV and S (1024 tensor-core cycles) to hide behind.
+        if (ok && n_j > 0) {
+          if (!mbar_wait(&k_full[0], 0, abort_flag, kSiteAttnKFull)) {
+            ok = false;
+          } else {
+            tc_fence_after();
+            for (int t = 0; t < 2; ++t)
+              if (nkv[t] > 0) issue_s(t, 0);
+            umma_commit(&k_empty[0]);
+          }
+        }
+        for (int j = 0; j < n_j && ok; ++j) {
+          const int st = j & 1;
+          const uint32_t ph = (j >> 1) & 1;
+          bool k_next = false;  // K_{j+1} has landed
+          if (!mbar_wait(&v_full[st], ph, abort_flag, kSiteAttnVFull)) { ok = false; break; }
+          const uint32_t v_addr = smem_u32(sV + st * Cfg::KV_BYTES);
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (j >= nkv[t]) continue;
+            if (!mbar_wait(&p_full[t], (uint32_t)j & 1u, abort_flag, kSiteAttnPFull)) { ok = false; break; }
+            tc_fence_after();
+  #pragma unroll
+            for (int kk = 0; kk < 128 / 16; ++kk)  // O_t += P_t V_j, P_t from TMEM (K = 128 keys)
+              umma_f16_ts(tmem + Cfg::O_COL0 + t * D, tmem + (Cfg::S_COL_STRIDE * t) + kk * 8,
+                          make_sdesc_sw128(v_addr + kk * 2048, 128 * 128, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+            if (j == nkv[t] - 1) umma_commit(&o_full[t]);
+            if (j + 1 < nkv[t]) {
+              if (!k_next) {
+                if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, kSiteAttnKFull)) {
+                  ok = false;
+                  break;
+                }
+                tc_fence_after();
+                k_next = true;
+              }
+              issue_s(t, j + 1);
+            }
+          }
+          if (!ok) break;
+          umma_commit(&v_empty[st]);
+          if (k_next) umma_commit(&k_empty[(j + 1) & 1]);
+        }
+        umma_commit(drain);
+        volatile int no_abort = 0;
+        mbar_wait(drain, 0, &no_abort, kSiteAttnDrain);
+      }
     }
   } else {
-    // ---------------------------------------------------------------- softmax (warps 2-5: A, 6-9: B)
-    const int t = (warp < 6) ? 0 : 1;
+    warpgroup_reg_alloc<224>();
+    // ---------------------------------------------------------------- softmax (warps 4-7: A, 8-11: B)
+    const int t = (warp < 8) ? 0 : 1;
     const uint32_t quarter = warp & 3u;
     const int r = (int)(quarter * 32 + lane);  // row within the Q tile == TMEM lane
     const int qi = q0[t] + r;                  // query index

@@ -269,6 +269,8 @@ __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bul
 __device__ __forceinline__ void bulk_wait_group_read0() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
+// Waits until every committed bulk group has completed (its global writes done).
+__device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // Fire-and-forget fp32 reduction into global memory.
 __device__ __forceinline__ void red_add_f32(float* addr, float a) {
