@@ -48,9 +48,9 @@ def main(argv=None):
         if a.case == "attn_fwd":
             fn, flops, kname = (lambda: ops.attention_fwd(q, k, v, out=out, lse=lse)), fwd, "k_attn_fwd_tc"
         elif a.case == "attn_bwd":
-            fn, flops, kname = (lambda: ops.attention_bwd(do, q, k, v, lse, out=out)), 2.5 * fwd, "k_attn_bwd_tc"
+            fn, flops, kname = (lambda: ops.attention_bwd(do, q, k, v, lse, out=out)), 2.5 * fwd, "k_attn_bwd_dkdv"
         else:
-            fn, flops, kname = (lambda: ops.attention_bwd(do, q, k, v, lse)), 2.5 * fwd, "k_attn_bwd_tc"
+            fn, flops, kname = (lambda: ops.attention_bwd(do, q, k, v, lse)), 2.5 * fwd, "k_attn_bwd_dkdv"
     else:
         A = (torch.rand(a.m, a.k, device=dev) * 2 - 1).bfloat16()
         Bm = (torch.rand(a.k, a.n, device=dev) * 2 - 1).bfloat16()

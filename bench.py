@@ -14,7 +14,7 @@ Also reported on the same JSON line:
   "gemm":      4096^3 bf16 GEMM, columns of B sharded across ranks, L2 flushed
                between timed iterations;
   "with_out":  the same fwd+bwd when the backward is given O (no recompute);
-  "roofline":  the dominant kernel (k_attn_bwd_tc) timed live with CUDA events on
+  "roofline":  the dominant kernel (k_attn_bwd_dkdv) timed live with CUDA events on
                its launch stream against the measured dense bf16 peak;
   "cpu_baseline": the CPU oracle on a bounded sample of heads (rank 0, N=1);
   "e2e":       the step with pinned-host inputs copied in and results copied out;
@@ -51,9 +51,14 @@ CONFIG = {"workload": "bf16 causal attention fwd+bwd B=8 H=32 S=4096 D=128, head
           "batch": B, "heads": H, "seq_len": S, "head_dim": D, "causal": True,
           "parallelism": "heads sharded, no collective on the hot path",
           "l2": "inputs larger than L2 (1 GiB per GPU at N=1; 128 MiB of inputs + outputs per GPU at N=8)"}
-# k_attn_bwd_tc DRAM traffic per launch (bytes) from the ncu capture summarised in
-# profiles/k_attn_bwd_tc_h32s4096.md (B*H=32 heads captured, scaled by the head count).
-ATTN_BWD_TRAFFIC_PER_HEAD = 670.1e6 / 32  # 446.9 MB read + 223.2 MB written at 32 heads
+# FLOPs the backward kernels execute per head, in products of 2*S^2*D/2 (causal) each:
+# k_attn_bwd_dkdv computes S^T, dP^T, dV and dK (4 products, 2x the forward),
+# k_attn_bwd_dq computes S, dP and dQ (3 products, 1.5x the forward).
+DKDV_FLOPS = 2.0 * FWD_FLOPS
+DQ_FLOPS = 1.5 * FWD_FLOPS
+# k_attn_bwd_dkdv DRAM traffic per launch (bytes per head) from an ncu capture, or None
+# until one is summarised under profiles/.
+DKDV_TRAFFIC_PER_HEAD = None
 
 # pre-norm Llama block forward
 BLK_B, BLK_S, BLK_DM, BLK_H, BLK_D, BLK_F = 4, 2048, 4096, 32, 128, 14336
@@ -310,20 +315,24 @@ def run_beacon(args, rank, world, local):
     n_launch = ops.launch_count() - n0
     ops.profile_enable(False)
     clk = clocks.stop()
-    bwd_ms, bwd_n = ops.profile_read("k_attn_bwd_tc")
+    bwd_ms, bwd_n = ops.profile_read("k_attn_bwd_dkdv")
+    dq_ms, dq_n = ops.profile_read("k_attn_bwd_dq")
     fwd_ms, fwd_n = ops.profile_read("k_attn_fwd_tc")
     ms = max_over_ranks(ms_local, world)
     value = STEP_FLOPS / (ms * 1e-3) / 1e12
 
-    # roofline of the dominant kernel: k_attn_bwd_tc, algorithmic bwd FLOPs per launch
+    # roofline of the dominant kernel: k_attn_bwd_dkdv, the FLOPs it executes per launch
     bwd_avg_ms = bwd_ms / max(bwd_n, 1)
-    bwd_flops_local = BWD_FLOPS * nh / (B * H)
+    bwd_flops_local = DKDV_FLOPS * nh / (B * H)
     achieved = bwd_flops_local / (bwd_avg_ms * 1e-3) / 1e12
-    traffic = None if ATTN_BWD_TRAFFIC_PER_HEAD is None else ATTN_BWD_TRAFFIC_PER_HEAD * nh
-    roofline = {"kernel": "k_attn_bwd_tc", "bound": "tensor", "achieved": achieved, "peak": sustained,
+    traffic = None if DKDV_TRAFFIC_PER_HEAD is None else DKDV_TRAFFIC_PER_HEAD * nh
+    dq_avg_ms = dq_ms / max(dq_n, 1)
+    roofline = {"kernel": "k_attn_bwd_dkdv", "bound": "tensor", "achieved": achieved, "peak": sustained,
                 "unit": "TFLOP/s", "frac": achieved / sustained, "traffic": traffic,
                 "peak_kind": f"{peak_kind} bf16_tflops_sustained (kernel timed inside a multi-second loop)",
                 "avg_launch_ms": bwd_avg_ms, "launches": bwd_n,
+                "dq_kernel": {"kernel": "k_attn_bwd_dq", "avg_launch_ms": dq_avg_ms,
+                              "tflops_executed": DQ_FLOPS * nh / (B * H) / (dq_avg_ms * 1e-3) / 1e12},
                 "fwd_kernel": {"kernel": "k_attn_fwd_tc", "avg_launch_ms": fwd_ms / max(fwd_n, 1),
                                "launches_per_step": fwd_n / max(args.steps, 1)}}
 
