@@ -90,6 +90,13 @@ __device__ __forceinline__ void tma_load_rows(uint8_t* dst, const CUtensorMap* m
   for (int b = 0; b < D / 64; ++b) tma_load_3d(dst + b * 128 * 128, m, bar, b * 64, row0, z);
 }
 
+// Prefetches the same 128-row tile into L2.
+template <int D>
+__device__ __forceinline__ void tma_prefetch_rows(const CUtensorMap* m, int row0, int z) {
+#pragma unroll
+  for (int b = 0; b < D / 64; ++b) tma_prefetch_l2_3d(m, b * 64, row0, z);
+}
+
 // P = 2^(x * scale_log2 - m) for one 128-wide S row, packed to bf16 pairs into the
 // 64 TMEM columns at `taddr`; returns the row sum of P (fp32, before rounding).
 template <bool POLY>

@@ -149,7 +149,7 @@ __device__ __forceinline__ void pack32(const float (&v)[32], uint32_t (&pk)[16])
 //     dS^T = P^T (dP^T - Dt[q])                     bf16 -> TMEM [64g + 32 + 16c, +16)
 //   and the tensor core accumulates, with A read from TMEM,
 //     dV += P^T dO   and   dK += dS^T Q   over that chunk's 32 + 32 queries.
-//   dP^T(n+1) is issued as soon as every warp holds dP^T(n) in registers (after chunk 0),
+//   dP^T(n+1) is issued behind chunk 0's dV/dK (every warp holds dP^T(n) in registers by then),
 //   S^T(n+1) right behind the last dV/dK of tile n (tcgen05.mma runs in issue order).
 // TMEM: S^T/P^T/dS^T [0,128) | dP^T [128,256) | dV [256,256+D) | dK [256+D,256+2D).
 // ---------------------------------------------------------------------------
@@ -241,6 +241,12 @@ __global__ void __launch_bounds__(384, 1)
         const long long srow = (long long)bh * p.S_pad + it * 128;
         bulk_load(sStats + st * 256, p.lse2 + srow, 512, &qd_full[st]);
         bulk_load(sStats + st * 256 + 128, p.dt + srow, 512, &qd_full[st]);
+        if (n + 1 < n_iter) {  // the tile after: into L2 now, so its load finds it there
+          const int g1 = (n + 1) / iters_per_head, it1 = it0 + (n + 1) % iters_per_head;
+          const int bh1 = b * p.Hq + hk * group + g1;
+          tma_prefetch_rows<D>(&tmdO, it1 * 128, bh1);
+          tma_prefetch_rows<D>(&tmQ, it1 * 128, bh1);
+        }
         issued |= 1u << st;
         par = (par & ~(1u << st)) | (ph << st);
       }
@@ -275,14 +281,6 @@ __global__ void __launch_bounds__(384, 1)
             break;
           }
           tc_fence_after();
-          if (c == 0 && more) {  // every warp holds dP^T(n) in registers by now
-            if (!mbar_wait(&qd_full[st1], ((n + 1) >> 1) & 1, abort_flag, kSiteBwdQDFull)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            issue_score_tile<D>(tmem + T_DP, v_addr, smem_u32(sdO + st1 * TILE));
-          }
 #pragma unroll
           for (int i = 0; i < 4; ++i) {  // this chunk's K-steps: 16 queries each
             const int kk = (i >> 1) * 4 + 2 * c + (i & 1);
@@ -292,6 +290,16 @@ __global__ void __launch_bounds__(384, 1)
                         acc);
             umma_f16_ts(tmem + T_DK, tmem + T_S + 32 + col, make_sdesc_sw128(q_addr + kk * 2048, 16384, 1024),
                         idesc_kv, acc);
+          }
+          // every warp holds dP^T(n) in registers once chunk 0 is in: dP^T(n+1) may follow
+          // (behind this chunk's dV/dK, so a late Q/dO tile does not idle the tensor core)
+          if (c == 0 && more) {
+            if (!mbar_wait(&qd_full[st1], ((n + 1) >> 1) & 1, abort_flag, kSiteBwdQDFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_score_tile<D>(tmem + T_DP, v_addr, smem_u32(sdO + st1 * TILE));
           }
         }
         if (!ok) break;

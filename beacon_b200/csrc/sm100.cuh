@@ -131,6 +131,15 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* m, uin
       : "memory");
 }
 
+// Brings a tile of a 3-D tensor into L2 ahead of its tma_load_3d (no shared memory, no
+// completion to wait for).
+__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* m, int x, int y, int z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+
 // Untiled bulk copy global -> shared (both 16-byte aligned, bytes a multiple of 16),
 // completing on `bar` with complete_tx.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
