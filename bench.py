@@ -56,9 +56,9 @@ CONFIG = {"workload": "bf16 causal attention fwd+bwd B=8 H=32 S=4096 D=128, head
 # k_attn_bwd_dq computes S, dP and dQ (3 products, 1.5x the forward).
 DKDV_FLOPS = 2.0 * FWD_FLOPS
 DQ_FLOPS = 1.5 * FWD_FLOPS
-# k_attn_bwd_dkdv DRAM traffic per launch (bytes per head) from an ncu capture, or None
-# until one is summarised under profiles/.
-DKDV_TRAFFIC_PER_HEAD = None
+# k_attn_bwd_dkdv DRAM traffic per launch from the ncu capture summarised in
+# profiles/k_attn_bwd_dkdv_h32s4096.md (B*H=32 heads captured, scaled by the head count).
+DKDV_TRAFFIC_PER_HEAD = (186.0e6 + 37.4e6) / 32
 
 # pre-norm Llama block forward
 BLK_B, BLK_S, BLK_DM, BLK_H, BLK_D, BLK_F = 4, 2048, 4096, 32, 128, 14336
