@@ -68,20 +68,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-// 2^x on the FMA pipe, to take part of the softmax's exponentials off the MUFU
-// unit: Cody-Waite range reduction x = i + f (i = floor x, f in [0,1)), a cubic in
-// f fitted to 2^f by iteratively reweighted least squares (max relative error
-// 7.5e-5, far below the bf16 rounding P receives), and 2^i added to the exponent
-// field.  Arguments below -126 return ~2^-126 instead of 0, so callers use it only
-// where no element is masked to -inf.
-__device__ __forceinline__ float exp2_fma(float x) {
-  x = fmaxf(x, -126.0f);
-  const float fi = floorf(x);
-  const float f = x - fi;
-  const float p = fmaf(fmaf(fmaf(7.8024031e-2f, f, 2.2606707e-1f), f, 6.9583399e-1f), f, 9.9992513e-1f);
-  return __int_as_float(__float_as_int(p) + (static_cast<int>(fi) << 23));
-}
-
 // Loads one 128-row x D tile (rows `row0..row0+127` of head `z`) as D/64 swizzled
 // column blocks of 128 rows x 128 bytes.
 template <int D>
@@ -98,8 +84,9 @@ __device__ __forceinline__ void tma_prefetch_rows(const CUtensorMap* m, int row0
 }
 
 // P = 2^(x * scale_log2 - m) for one 128-wide S row, packed to bf16 pairs into the
-// 64 TMEM columns at `taddr`; returns the row sum of P (fp32, before rounding).
-template <bool POLY>
+// 64 TMEM columns at `taddr`; returns the row sum of P (fp32, before rounding).  The
+// argument and the running sums use packed f32x2 instructions: the softmax is bound by
+// instruction issue, not by the exponential unit.
 __device__ __forceinline__ float softmax_p_to_tmem(const float* x, float scale_log2, float neg_m, uint32_t taddr) {
   float ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
@@ -107,18 +94,11 @@ __device__ __forceinline__ float softmax_p_to_tmem(const float* x, float scale_l
     uint32_t pk[32];
 #pragma unroll
     for (int e = 0; e < 32; ++e) {
-      const float p0 = ex2_approx(fmaf(x[64 * c + 2 * e], scale_log2, neg_m));
-      const float a1 = fmaf(x[64 * c + 2 * e + 1], scale_log2, neg_m);
-      float p1;
-      if constexpr (POLY) {
-        if (e & 1)
-          p1 = exp2_fma(a1);
-        else
-          p1 = ex2_approx(a1);
-      } else {
-        p1 = ex2_approx(a1);
-      }
-      ls[e & 3] += p0 + p1;
+      float a0, a1;
+      fma2(a0, a1, x[64 * c + 2 * e], x[64 * c + 2 * e + 1], scale_log2, scale_log2, neg_m, neg_m);
+      const float p0 = ex2_approx(a0), p1 = ex2_approx(a1);
+      const int q = 2 * (e & 1);
+      add2(ls[q], ls[q + 1], ls[q], ls[q + 1], p0, p1);
       pk[e] = pack_bf16x2(p0, p1);
     }
     tmem_st32(taddr + 32 * c, pk);
@@ -324,23 +304,21 @@ __global__ void __launch_bounds__(384, 1)
       const int k0 = j * 128;
       int limit = p.S - k0;                           // keys at or beyond S are masked
       if (p.causal) limit = min(limit, qi - k0 + 1);  // keys after the query are masked
-      // warp-uniform: the P store below (tcgen05.st) is warp-collective, so the
-      // polynomial/MUFU variant is chosen per warp, never per row
       const bool unmasked = __all_sync(0xffffffffu, limit >= 128);
       if (!unmasked) {
 #pragma unroll
         for (int c = 0; c < 128; ++c) x[c] = (c < limit) ? x[c] : -INFINITY;
       }
       float mx;
-      {  // tree reduction: 8 independent chains
+      {  // tree reduction: 8 independent chains of three-input maxima
         float m8[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) m8[u] = x[u];
+        for (int u = 0; u < 8; ++u) m8[u] = fmaxf(x[u], x[8 + u]);
 #pragma unroll
-        for (int c = 8; c < 128; c += 8)
+        for (int c = 16; c < 128; c += 16)
 #pragma unroll
-          for (int u = 0; u < 8; ++u) m8[u] = fmaxf(m8[u], x[c + u]);
-        mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+          for (int u = 0; u < 8; ++u) m8[u] = fmax3(m8[u], x[c + u], x[c + 8 + u]);
+        mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
       }
       mx *= p.scale_log2;
       const float m_new = fmaxf(m_used, mx);
@@ -367,13 +345,7 @@ __global__ void __launch_bounds__(384, 1)
         }
       }
       // P = exp2(x * scale_log2 - m_used) -> bf16 pairs into TMEM columns [s_col, s_col + 64)
-      const float neg_m = -m_used;
-      float lsum;
-      if (unmasked)  // one exponential in four on the FMA pipe
-        lsum = softmax_p_to_tmem<true>(x, p.scale_log2, neg_m, tmem + lane_base + s_col);
-      else
-        lsum = softmax_p_to_tmem<false>(x, p.scale_log2, neg_m, tmem + lane_base + s_col);
-      l += lsum;
+      l += softmax_p_to_tmem(x, p.scale_log2, -m_used, tmem + lane_base + s_col);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();

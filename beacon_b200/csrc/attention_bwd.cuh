@@ -3,8 +3,9 @@
 // Kernel ID `attention_adjoint_bwd` (crates/beacon-cuda/src/attention.rs:42-64); the
 // adjoint entry (crates/beacon-adjoint-table/src/lib.rs:86-99) saves q, k, v, lse and
 // recomputes the scores.  Three launches:
-//   1. k_attn_bwd_prep  per query row: Dt = rowsum(dO * O), lse2 = lse * log2(e), padded
-//                       to whole 128-row tiles (+inf / 0), so no tile needs a row check.
+//   1. k_attn_bwd_prep  per query row: Dt = rowsum(dO * O), nlse2 = -lse * log2(e),
+//                       padded to whole 128-row tiles (-inf / 0), so no tile needs a row
+//                       check; P = exp2(S * scale*log2e + nlse2) is one packed FMA and MUFU.
 //                       (O is the forward output, recomputed by the forward kernel when
 //                       the caller lacks it.)
 //   2. k_attn_bwd_dkdv  one CTA per (128-key tile, KV head): dK and dV accumulate in TMEM
@@ -34,7 +35,7 @@ struct AttnBwdParams {
   float scale;       // softmax scale (natural units)
   float scale_log2;  // scale * log2(e)
   int causal;
-  const float* lse2;  // [B*Hq, S_pad]  lse * log2(e); +inf on padded rows
+  const float* lse2;  // [B*Hq, S_pad]  -lse * log2(e); -inf on padded rows
   const float* dt;    // [B*Hq, S_pad]  rowsum(dO * O); 0 on padded rows
   __nv_bfloat16* dq;  // [B*Hq, S, D]
   __nv_bfloat16* dk;  // [B*Hkv, S, D]
@@ -116,7 +117,7 @@ __global__ void __launch_bounds__(256) k_attn_bwd_prep(const __nv_bfloat16* __re
     for (int off = LPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
     if (row < total && l == 0) {
       dt[row] = valid ? acc : 0.0f;
-      lse2[row] = valid ? lse[bh * S + q] * 1.4426950408889634f : INFINITY;
+      lse2[row] = valid ? lse[bh * S + q] * -1.4426950408889634f : -INFINITY;
     }
   }
 }
@@ -359,12 +360,20 @@ __global__ void __launch_bounds__(384, 1)
           const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
           const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
+          for (int u = 0; u < 4; u += 2) {  // pairs: packed f32x2 arithmetic
             const int e = 4 * e4 + u;
-            float pv = ex2_approx(fmaf(__uint_as_float(s[c][e]), p.scale_log2, -lv[u]));
-            if (masked && !(key_ok && col0 + e >= qmin)) pv = 0.0f;
-            pe[e] = pv;
-            dsv[e] = pv * (__uint_as_float(dp[c][e]) - dv[u]);
+            float a0, a1, t0, t1;
+            fma2(a0, a1, __uint_as_float(s[c][e]), __uint_as_float(s[c][e + 1]), p.scale_log2, p.scale_log2, lv[u],
+                 lv[u + 1]);
+            float p0 = ex2_approx(a0), p1 = ex2_approx(a1);
+            if (masked) {
+              if (!(key_ok && col0 + e >= qmin)) p0 = 0.0f;
+              if (!(key_ok && col0 + e + 1 >= qmin)) p1 = 0.0f;
+            }
+            pe[e] = p0;
+            pe[e + 1] = p1;
+            fma2(t0, t1, dv[u], dv[u + 1], -1.0f, -1.0f, __uint_as_float(dp[c][e]), __uint_as_float(dp[c][e + 1]));
+            mul2(dsv[e], dsv[e + 1], p0, p1, t0, t1);
           }
         }
         uint32_t pk[16], dk[16];
@@ -598,8 +607,8 @@ __global__ void __launch_bounds__(384, 1)
     const int r = (int)(quarter * 32 + lane);  // TMEM lane = query row
     const int qi = q0 + r;
     const uint32_t lane_base = (quarter * 32u) << 16;
-    const long long srow = (long long)bh * p.S_pad + qi;  // padded rows: lse2 = +inf, Dt = 0
-    const float l2 = __ldg(p.lse2 + srow), dtr = __ldg(p.dt + srow);
+    const long long srow = (long long)bh * p.S_pad + qi;  // padded rows: -lse2 = -inf, Dt = 0
+    const float nl2 = __ldg(p.lse2 + srow), dtr = __ldg(p.dt + srow);
     bool ok = true;
     for (int j = 0; j < n_kt && ok; ++j) {
       const uint32_t sb = T_S + 128 * (j & 1) + 64 * g;
@@ -625,10 +634,16 @@ __global__ void __launch_bounds__(384, 1)
       for (int c = 0; c < 2; ++c) {
         float dsv[32];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          float pv = ex2_approx(fmaf(__uint_as_float(s[c][e]), p.scale_log2, -l2));
-          if (masked && 32 * c + e >= klim) pv = 0.0f;
-          dsv[e] = pv * (__uint_as_float(dp[c][e]) - dtr);
+        for (int e = 0; e < 32; e += 2) {  // pairs: packed f32x2 arithmetic
+          float a0, a1, t0, t1;
+          fma2(a0, a1, __uint_as_float(s[c][e]), __uint_as_float(s[c][e + 1]), p.scale_log2, p.scale_log2, nl2, nl2);
+          float p0 = ex2_approx(a0), p1 = ex2_approx(a1);
+          if (masked) {
+            if (32 * c + e >= klim) p0 = 0.0f;
+            if (32 * c + e + 1 >= klim) p1 = 0.0f;
+          }
+          fma2(t0, t1, dtr, dtr, -1.0f, -1.0f, __uint_as_float(dp[c][e]), __uint_as_float(dp[c][e + 1]));
+          mul2(dsv[e], dsv[e + 1], p0, p1, t0, t1);
         }
         uint32_t pk[16];
         pack32(dsv, pk);

@@ -384,6 +384,34 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Packed fp32 pairs (Blackwell f32x2 instructions: one issue slot for two IEEE-rounded
+// operations, each lane identical to its scalar fmaf / + / *).
+__device__ __forceinline__ void fma2(float& r0, float& r1, float a0, float a1, float b0, float b1, float c0,
+                                     float c1) {
+  asm("{\n .reg .b64 a, b, c, d;\n mov.b64 a, {%2, %3};\n mov.b64 b, {%4, %5};\n mov.b64 c, {%6, %7};\n"
+      " fma.rn.f32x2 d, a, b, c;\n mov.b64 {%0, %1}, d;\n}"
+      : "=f"(r0), "=f"(r1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void add2(float& r0, float& r1, float a0, float a1, float b0, float b1) {
+  asm("{\n .reg .b64 a, b, d;\n mov.b64 a, {%2, %3};\n mov.b64 b, {%4, %5};\n"
+      " add.rn.f32x2 d, a, b;\n mov.b64 {%0, %1}, d;\n}"
+      : "=f"(r0), "=f"(r1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ void mul2(float& r0, float& r1, float a0, float a1, float b0, float b1) {
+  asm("{\n .reg .b64 a, b, d;\n mov.b64 a, {%2, %3};\n mov.b64 b, {%4, %5};\n"
+      " mul.rn.f32x2 d, a, b;\n mov.b64 {%0, %1}, d;\n}"
+      : "=f"(r0), "=f"(r1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+// max of three (one instruction on sm_100)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
