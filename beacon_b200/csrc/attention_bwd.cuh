@@ -124,13 +124,14 @@ __global__ void __launch_bounds__(256) k_attn_bwd_prep(const __nv_bfloat16* __re
 
 // A score tile: D/16 K-steps of M=128 x N=128 with both operands K-major (A and B are
 // 128 rows x D, each stored as D/64 swizzled 64-column blocks of 16 KB).
+// Called by the whole issuing warp; the elected `leader` lane executes the MMAs.
 template <int D>
-__device__ __forceinline__ void issue_score_tile(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr) {
+__device__ __forceinline__ void issue_score_tile(bool leader, uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr) {
   constexpr uint32_t idesc = make_idesc_f16(128, 128, false, false);
 #pragma unroll
   for (int kk = 0; kk < D / 16; ++kk) {
     const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-    umma_f16_ss(d_tmem, make_sdesc_sw128(a_addr + off, 16, 1024), make_sdesc_sw128(b_addr + off, 16, 1024), idesc,
+    if (leader) umma_f16_ss(d_tmem, make_sdesc_sw128(a_addr + off, 16, 1024), make_sdesc_sw128(b_addr + off, 16, 1024), idesc,
                 kk > 0 ? 1u : 0u);
   }
 }
@@ -142,16 +143,19 @@ __device__ __forceinline__ void pack32(const float (&v)[32], uint32_t (&pk)[16])
 }
 
 // ---------------------------------------------------------------------------
-// 2. dK / dV.  Per query tile n of the CTA's 128 keys:
-//   S^T(n)  = K Q^T  -> TMEM [0,128)        dP^T(n) = V dO^T -> TMEM [128,256)
-//   softmax warp (g, quarter): key rows 32*quarter.., query columns 64g..64g+63 in two
-//   chunks of 32; per chunk c it writes, over S^T columns it has already read,
-//     P^T  = exp2(S^T * scale*log2e - lse2[q])      bf16 -> TMEM [64g + 16c, +16)
-//     dS^T = P^T (dP^T - Dt[q])                     bf16 -> TMEM [64g + 32 + 16c, +16)
-//   and the tensor core accumulates, with A read from TMEM,
-//     dV += P^T dO   and   dK += dS^T Q   over that chunk's 32 + 32 queries.
-//   dP^T(n+1) is issued behind chunk 0's dV/dK (every warp holds dP^T(n) in registers by then),
-//   S^T(n+1) right behind the last dV/dK of tile n (tcgen05.mma runs in issue order).
+// 2. dK / dV.  Each query tile n of the CTA's 128 keys is handled as two halves h of
+//   64 queries, each with its own score MMAs (M=128 keys x N=64 queries):
+//     S^T_h(n)  = K Q_h^T  -> TMEM [64h, 64h+64)      dP^T_h(n) = V dO_h^T -> TMEM [128+64h, +64)
+//   softmax warp (g, quarter): key rows 32*quarter.., queries 32g..32g+31 of the half; it
+//   writes, over the 32 S^T columns it has read,
+//     P^T  = exp2(S^T * scale*log2e - lse2[q])   bf16 -> TMEM [64h + 32g, +16)
+//     dS^T = P^T (dP^T - Dt[q])                  bf16 -> TMEM [64h + 32g + 16, +16)
+//   and the tensor core accumulates dV += P^T dO_h and dK += dS^T Q_h (A from TMEM).
+//   MMA issue order:  ... dV/dK_0(n), S/dP_0(n+1), dV/dK_1(n), S/dP_1(n+1), dV/dK_0(n+1) ...
+//   so while the warps work on one half the tensor core has the other half's dV/dK and
+//   the next tile's scores queued: the pipe never drains between tiles.  (An N=64 MMA
+//   costs as much as an N=128 one, so the scores cost twice the N=128 form: 48 MMAs per
+//   tile instead of 32, all of them overlapped.)
 // TMEM: S^T/P^T/dS^T [0,128) | dP^T [128,256) | dV [256,256+D) | dK [256+D,256+2D).
 // ---------------------------------------------------------------------------
 template <int D>
@@ -172,11 +176,11 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* kv_full = bars + 0;
   uint64_t* qd_full = bars + 1;   // [2] Q, dO and statistics of a query tile
   uint64_t* qd_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // S^T(n) and dP^T(n) computed
-  uint64_t* ds_chunk = bars + 6;  // [2] chunk c of P^T / dS^T stored by all 8 warps
-  uint64_t* dkv_full = bars + 8;
-  uint64_t* drain = bars + 9;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  uint64_t* s_full = bars + 5;    // [2] S^T_h(n) and dP^T_h(n) computed
+  uint64_t* ds_full = bars + 7;   // [2] P^T_h / dS^T_h stored by all 8 warps
+  uint64_t* dkv_full = bars + 9;
+  uint64_t* drain = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   constexpr uint32_t T_S = 0, T_DP = 128, T_DV = 256, T_DK = 256 + D;
 
@@ -197,9 +201,9 @@ __global__ void __launch_bounds__(384, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&qd_full[i], 1);
       mbar_init(&qd_empty[i], 1);
-      mbar_init(&ds_chunk[i], 8);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&ds_full[i], 8);
     }
-    mbar_init(s_full, 1);
     mbar_init(dkv_full, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -257,69 +261,82 @@ __global__ void __launch_bounds__(384, 1)
         for (int s = 0; s < 2; ++s)
           if (issued & (1u << s)) mbar_wait(&qd_full[s], (par >> s) & 1u, &no_abort, kSiteBwdDrain);
       }
-    } else if (warp == 1 && lane == 0) {
-      // ---------------------------------------------------------------- MMA issuer
-      constexpr uint32_t idesc_kv = make_idesc_f16(128, D, false, true);  // dV, dK: A in TMEM, B MN-major
+    } else if (warp == 1) {
+      // ---------------------------------------------------------------- MMA issuer (whole warp, one elected lane issues)
+      const bool leader = elect_one();
+      constexpr uint32_t idesc_s = make_idesc_f16(128, 64, false, false);  // S^T_h, dP^T_h
+      constexpr uint32_t idesc_kv = make_idesc_f16(128, D, false, true);   // dV, dK: A in TMEM, B MN-major
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
-      bool ok = mbar_wait(kv_full, 0, abort_flag, kSiteBwdKV);
+      // S^T_h and dP^T_h of the tile in stage st, then announce them
+      auto issue_half = [&](int h, int st) {
+        const uint32_t q_addr = smem_u32(sQ + st * TILE) + h * 8192, do_addr = smem_u32(sdO + st * TILE) + h * 8192;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          if (leader) umma_f16_ss(tmem + T_S + 64 * h, make_sdesc_sw128(k_addr + off, 16, 1024),
+                      make_sdesc_sw128(q_addr + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          if (leader) umma_f16_ss(tmem + T_DP + 64 * h, make_sdesc_sw128(v_addr + off, 16, 1024),
+                      make_sdesc_sw128(do_addr + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+        }
+        if (leader) umma_commit(&s_full[h]);
+      };
+      bool ok = warp_wait(kv_full, 0, abort_flag, kSiteBwdKV);
       if (ok && n_iter > 0) {
-        if (!mbar_wait(&qd_full[0], 0, abort_flag, kSiteBwdQDFull)) {
+        if (!warp_wait(&qd_full[0], 0, abort_flag, kSiteBwdQDFull)) {
           ok = false;
         } else {
           tc_fence_after();
-          issue_score_tile<D>(tmem + T_S, k_addr, smem_u32(sQ));
-          issue_score_tile<D>(tmem + T_DP, v_addr, smem_u32(sdO));
-          umma_commit(s_full);
+          issue_half(0, 0);
+          issue_half(1, 0);
         }
       }
       for (int n = 0; n < n_iter && ok; ++n) {
         const int st = n & 1, st1 = (n + 1) & 1;
         const bool more = n + 1 < n_iter;
         const uint32_t q_addr = smem_u32(sQ + st * TILE), do_addr = smem_u32(sdO + st * TILE);
-        for (int c = 0; c < 2 && ok; ++c) {
-          if (!mbar_wait(&ds_chunk[c], (uint32_t)n & 1u, abort_flag, kSiteBwdDsFull)) {
+        for (int h = 0; h < 2 && ok; ++h) {
+          if (!warp_wait(&ds_full[h], (uint32_t)n & 1u, abort_flag, kSiteBwdDsFull)) {
             ok = false;
             break;
           }
           tc_fence_after();
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {  // this chunk's K-steps: 16 queries each
-            const int kk = (i >> 1) * 4 + 2 * c + (i & 1);
-            const uint32_t acc = (n > 0 || c > 0 || i > 0) ? 1u : 0u;
-            const uint32_t col = (uint32_t)((kk >> 2) * 64 + (kk & 3) * 8);
-            umma_f16_ts(tmem + T_DV, tmem + T_S + col, make_sdesc_sw128(do_addr + kk * 2048, 16384, 1024), idesc_kv,
+          for (int k4 = 0; k4 < 4; ++k4) {  // 16 queries per K-step: warp group k4 >> 1, block k4 & 1
+            const int kk = 4 * h + k4;       // query rows 16kk.. of the tile
+            const uint32_t acc = (n > 0 || h > 0 || k4 > 0) ? 1u : 0u;
+            const uint32_t col = (uint32_t)(64 * h + 32 * (k4 >> 1) + 8 * (k4 & 1));
+            if (leader) umma_f16_ts(tmem + T_DV, tmem + T_S + col, make_sdesc_sw128(do_addr + kk * 2048, 16384, 1024), idesc_kv,
                         acc);
-            umma_f16_ts(tmem + T_DK, tmem + T_S + 32 + col, make_sdesc_sw128(q_addr + kk * 2048, 16384, 1024),
+            if (leader) umma_f16_ts(tmem + T_DK, tmem + T_S + col + 16, make_sdesc_sw128(q_addr + kk * 2048, 16384, 1024),
                         idesc_kv, acc);
           }
-          // every warp holds dP^T(n) in registers once chunk 0 is in: dP^T(n+1) may follow
-          // (behind this chunk's dV/dK, so a late Q/dO tile does not idle the tensor core)
-          if (c == 0 && more) {
-            if (!mbar_wait(&qd_full[st1], ((n + 1) >> 1) & 1, abort_flag, kSiteBwdQDFull)) {
-              ok = false;
-              break;
+          if (h == 1 && leader) umma_commit(&qd_empty[st]);  // Q(n), dO(n) free once these have read them
+          if (more) {  // the next tile's half h goes where this tile's half h just left
+            if (h == 0) {
+              if (!warp_wait(&qd_full[st1], ((n + 1) >> 1) & 1, abort_flag, kSiteBwdQDFull)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
             }
-            tc_fence_after();
-            issue_score_tile<D>(tmem + T_DP, v_addr, smem_u32(sdO + st1 * TILE));
+            issue_half(h, st1);
           }
         }
-        if (!ok) break;
-        umma_commit(&qd_empty[st]);  // Q(n), dO(n) free once the MMAs above have read them
-        if (more) {
-          issue_score_tile<D>(tmem + T_S, k_addr, smem_u32(sQ + st1 * TILE));  // behind dV/dK(n)
-          umma_commit(s_full);
-        }
       }
-      if (ok) umma_commit(dkv_full);
-      umma_commit(drain);
+      if (ok && leader) umma_commit(dkv_full);
+      if (leader) umma_commit(drain);
       volatile int no_abort = 0;
-      mbar_wait(drain, 0, &no_abort, kSiteBwdDrain);
+      warp_wait(drain, 0, &no_abort, kSiteBwdDrain);
     }
   } else {
     warpgroup_reg_alloc<192>();
     // ---------------------------------------------------------------- softmax (warps 4..11)
     const uint32_t quarter = warp & 3u;
-    const int g = (int)(warp - 4) >> 2;        // query-column half (softmax) / dV or dK (epilogue)
+    const int g = (int)(warp - 4) >> 2;        // 32-query group within a half / dV or dK (epilogue)
     const int r = (int)(quarter * 32 + lane);  // TMEM lane = key row
     const int kj = j0 + r;
     const uint32_t lane_base = (quarter * 32u) << 16;
@@ -333,25 +350,22 @@ __global__ void __launch_bounds__(384, 1)
       // off-diagonal tiles need no mask: every key < S and every query >= every key
       const bool masked = !keys_full || (p.causal && it == jt);
       const int qmin = p.causal ? kj - q0 : -1;
-      // s_full: the scores; qd_full: makes the TMA-written statistics visible to this thread
-      if (!__all_sync(0xffffffffu, mbar_wait(s_full, (uint32_t)n & 1u, abort_flag, kSiteBwdStFull) &&
-                                       mbar_wait(&qd_full[st], (n >> 1) & 1, abort_flag, kSiteBwdQDFull))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
       const float* lse2 = sStats + st * 256;
       const float* dtq = lse2 + 128;
-      uint32_t s[2][32], dp[2][32];
-      const uint32_t cs = T_S + 64 * g, cdp = T_DP + 64 * g;
-      tmem_ld32(tmem + lane_base + cs, s[0]);
-      tmem_ld32(tmem + lane_base + cdp, dp[0]);
-      tmem_wait_ld();
-      tmem_ld32(tmem + lane_base + cs + 32, s[1]);  // chunk 1 lands while chunk 0 is computed
-      tmem_ld32(tmem + lane_base + cdp + 32, dp[1]);
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {  // 32 queries per chunk
-        const int col0 = 64 * g + 32 * c;
+      for (int h = 0; h < 2 && ok; ++h) {
+        // s_full: the scores; qd_full: makes the TMA-written statistics visible to this thread
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[h], (uint32_t)n & 1u, abort_flag, kSiteBwdStFull) &&
+                                         mbar_wait(&qd_full[st], (n >> 1) & 1, abort_flag, kSiteBwdQDFull))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t cs = T_S + 64 * h + 32 * g;  // this warp's 32 S^T columns
+        uint32_t sv[32], dpv[32];
+        tmem_ld32(tmem + lane_base + cs, sv);
+        tmem_ld32(tmem + lane_base + T_DP + 64 * h + 32 * g, dpv);
+        tmem_wait_ld();
+        const int col0 = 64 * h + 32 * g;  // query index within the tile
         float pe[32], dsv[32];
 #pragma unroll
         for (int e4 = 0; e4 < 8; ++e4) {
@@ -363,7 +377,7 @@ __global__ void __launch_bounds__(384, 1)
           for (int u = 0; u < 4; u += 2) {  // pairs: packed f32x2 arithmetic
             const int e = 4 * e4 + u;
             float a0, a1, t0, t1;
-            fma2(a0, a1, __uint_as_float(s[c][e]), __uint_as_float(s[c][e + 1]), p.scale_log2, p.scale_log2, lv[u],
+            fma2(a0, a1, __uint_as_float(sv[e]), __uint_as_float(sv[e + 1]), p.scale_log2, p.scale_log2, lv[u],
                  lv[u + 1]);
             float p0 = ex2_approx(a0), p1 = ex2_approx(a1);
             if (masked) {
@@ -372,21 +386,19 @@ __global__ void __launch_bounds__(384, 1)
             }
             pe[e] = p0;
             pe[e + 1] = p1;
-            fma2(t0, t1, dv[u], dv[u + 1], -1.0f, -1.0f, __uint_as_float(dp[c][e]), __uint_as_float(dp[c][e + 1]));
+            fma2(t0, t1, dv[u], dv[u + 1], -1.0f, -1.0f, __uint_as_float(dpv[e]), __uint_as_float(dpv[e + 1]));
             mul2(dsv[e], dsv[e + 1], p0, p1, t0, t1);
           }
         }
         uint32_t pk[16], dk[16];
         pack32(pe, pk);
         pack32(dsv, dk);
-        // chunk 1's S^T (columns 32..63) must be in registers before dS^T of chunk 0 goes there
-        if (c == 0) tmem_wait_ld();
-        tmem_st16(tmem + lane_base + cs + 16 * c, pk);
-        tmem_st16(tmem + lane_base + cs + 32 + 16 * c, dk);
+        tmem_st16(tmem + lane_base + cs, pk);
+        tmem_st16(tmem + lane_base + cs + 16, dk);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&ds_chunk[c]);
+        if (lane == 0) mbar_arrive(&ds_full[h]);
       }
     }
     // final dV (g = 0) / dK (g = 1) rows
@@ -541,30 +553,31 @@ __global__ void __launch_bounds__(384, 1)
         for (int s = 0; s < 2; ++s)
           if (viss & (1u << s)) mbar_wait(&v_full[s], (vpar >> s) & 1u, &no_abort, kSiteQDrain);
       }
-    } else if (warp == 1 && lane == 0) {
-      // ---------------------------------------------------------------- MMA issuer
+    } else if (warp == 1) {
+      // ---------------------------------------------------------------- MMA issuer (whole warp, one elected lane issues)
+      const bool leader = elect_one();
       constexpr uint32_t idesc_q = make_idesc_f16(128, D, false, true);  // dQ: A = dS in TMEM, B = K MN-major
       const uint32_t q_addr = smem_u32(sQ), do_addr = smem_u32(sdO);
-      bool ok = mbar_wait(qd_full, 0, abort_flag, kSiteQQd);
+      bool ok = warp_wait(qd_full, 0, abort_flag, kSiteQQd);
       auto issue_s = [&](int j) -> bool {  // S(j) into buffer j&1
-        if (!mbar_wait(&k_full[j % KST], (uint32_t)(j / KST) & 1u, abort_flag, kSiteQKFull)) return false;
+        if (!warp_wait(&k_full[j % KST], (uint32_t)(j / KST) & 1u, abort_flag, kSiteQKFull)) return false;
         tc_fence_after();
-        issue_score_tile<D>(tmem + T_S + 128 * (j & 1), q_addr, smem_u32(sK + (j % KST) * TILE));
+        issue_score_tile<D>(leader, tmem + T_S + 128 * (j & 1), q_addr, smem_u32(sK + (j % KST) * TILE));
         return true;
       };
       auto issue_dp = [&](int j) -> bool {  // dP(j); then S(j) and dP(j) are announced together
-        if (!mbar_wait(&v_full[j & 1], (uint32_t)(j >> 1) & 1u, abort_flag, kSiteQVFull)) return false;
+        if (!warp_wait(&v_full[j & 1], (uint32_t)(j >> 1) & 1u, abort_flag, kSiteQVFull)) return false;
         tc_fence_after();
-        issue_score_tile<D>(tmem + T_DP, do_addr, smem_u32(sV + (j & 1) * TILE));
-        umma_commit(&v_empty[j & 1]);
-        umma_commit(&s_full[j & 1]);
+        issue_score_tile<D>(leader, tmem + T_DP, do_addr, smem_u32(sV + (j & 1) * TILE));
+        if (leader) umma_commit(&v_empty[j & 1]);
+        if (leader) umma_commit(&s_full[j & 1]);
         return true;
       };
       if (ok && n_kt > 0) ok = issue_s(0) && issue_dp(0) && (n_kt < 2 || issue_s(1));
       for (int j = 0; j < n_kt && ok; ++j) {
         const uint32_t sb = T_S + 128 * (j & 1);
         const uint32_t k_addr = smem_u32(sK + (j % KST) * TILE);
-        if (!mbar_wait(dp_free, (uint32_t)j & 1u, abort_flag, kSiteQDpFree)) {
+        if (!warp_wait(dp_free, (uint32_t)j & 1u, abort_flag, kSiteQDpFree)) {
           ok = false;
           break;
         }
@@ -574,7 +587,7 @@ __global__ void __launch_bounds__(384, 1)
           break;
         }
         for (int c = 0; c < 2 && ok; ++c) {
-          if (!mbar_wait(&ds_chunk[c], (uint32_t)j & 1u, abort_flag, kSiteQDsFull)) {
+          if (!warp_wait(&ds_chunk[c], (uint32_t)j & 1u, abort_flag, kSiteQDsFull)) {
             ok = false;
             break;
           }
@@ -583,21 +596,21 @@ __global__ void __launch_bounds__(384, 1)
           for (int i = 0; i < 4; ++i) {  // this chunk's K-steps: 16 keys each
             const int kk = (i >> 1) * 4 + 2 * c + (i & 1);
             const uint32_t acc = (j > 0 || c > 0 || i > 0) ? 1u : 0u;
-            umma_f16_ts(tmem + T_DQ, tmem + sb + (uint32_t)((kk >> 2) * 64 + (kk & 3) * 8),
+            if (leader) umma_f16_ts(tmem + T_DQ, tmem + sb + (uint32_t)((kk >> 2) * 64 + (kk & 3) * 8),
                         make_sdesc_sw128(k_addr + kk * 2048, 16384, 1024), idesc_q, acc);
           }
         }
         if (!ok) break;
-        umma_commit(&k_empty[j % KST]);  // K(j) read by S(j) and dQ(j)
+        if (leader) umma_commit(&k_empty[j % KST]);  // K(j) read by S(j) and dQ(j)
         if (j + 2 < n_kt && !issue_s(j + 2)) {  // behind dQ(j), which read dS(j) from that buffer
           ok = false;
           break;
         }
       }
-      if (ok) umma_commit(dq_full);
-      umma_commit(drain);
+      if (ok && leader) umma_commit(dq_full);
+      if (leader) umma_commit(drain);
       volatile int no_abort = 0;
-      mbar_wait(drain, 0, &no_abort, kSiteQDrain);
+      warp_wait(drain, 0, &no_abort, kSiteQDrain);
     }
   } else {
     warpgroup_reg_alloc<192>();
