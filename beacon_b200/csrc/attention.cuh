@@ -173,9 +173,9 @@ __global__ void __launch_bounds__(384, 1)
   const uint32_t tmem = *tmem_slot;
   // Registers: the producer / MMA warpgroup gives up most of its share to the two
   // softmax warpgroups, which hold a whole 128-column S row per thread.
-  // 128 x 56 + 256 x 224 = 384 x 168, the allocation the CTA is launched with.
+  // 128 x 72 + 256 x 216 = 384 x 168, the allocation the CTA is launched with.
   if (warp < 4) {
-    warpgroup_reg_dealloc<56>();
+    warpgroup_reg_dealloc<72>();
     if (warp == 0) {
       // ---------------------------------------------------------------- producer
       if (lane == 0) {
@@ -211,55 +211,56 @@ __global__ void __launch_bounds__(384, 1)
         }
       }
     } else if (warp == 1) {
-      // ---------------------------------------------------------------- MMA issuer
-      if (lane == 0) {
+      // ---------------------------------------------------------------- MMA issuer (whole warp, one elected lane issues)
+      {
+        const bool leader = elect_one();
         constexpr uint32_t idesc_s = make_idesc_f16(128, 128, false, false);
         constexpr uint32_t idesc_o = make_idesc_f16(128, D, false, true);
         const uint32_t q_addr = smem_u32(sQ);
-        bool ok = mbar_wait(q_full, 0, abort_flag, kSiteAttnQ);
+        bool ok = warp_wait(q_full, 0, abort_flag, kSiteAttnQ);
         // S_t(j) = Q_t K_j^T into tile t's S columns
         auto issue_s = [&](int t, int j) {
           const uint32_t k_addr = smem_u32(sK + (j & 1) * Cfg::KV_BYTES);
   #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-            umma_f16_ss(tmem + (Cfg::S_COL_STRIDE * t), make_sdesc_sw128(q_addr + t * Cfg::Q_BYTES + off, 16, 1024),
+            if (leader) umma_f16_ss(tmem + (Cfg::S_COL_STRIDE * t), make_sdesc_sw128(q_addr + t * Cfg::Q_BYTES + off, 16, 1024),
                         make_sdesc_sw128(k_addr + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
           }
-          umma_commit(&s_full[t]);
+          if (leader) umma_commit(&s_full[t]);
         };
         // Issue order: S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) | ...  tcgen05.mma
         // executes in issue order, so S_t(j+1) may follow PV_t(j), which reads P_t(j) from
         // the same TMEM columns, without waiting for it; each softmax warpgroup then has the
         // other tile's PV and S (1024 tensor-core cycles) to hide behind.
         if (ok && n_j > 0) {
-          if (!mbar_wait(&k_full[0], 0, abort_flag, kSiteAttnKFull)) {
+          if (!warp_wait(&k_full[0], 0, abort_flag, kSiteAttnKFull)) {
             ok = false;
           } else {
             tc_fence_after();
             for (int t = 0; t < 2; ++t)
               if (nkv[t] > 0) issue_s(t, 0);
-            umma_commit(&k_empty[0]);
+            if (leader) umma_commit(&k_empty[0]);
           }
         }
         for (int j = 0; j < n_j && ok; ++j) {
           const int st = j & 1;
           const uint32_t ph = (j >> 1) & 1;
           bool k_next = false;  // K_{j+1} has landed
-          if (!mbar_wait(&v_full[st], ph, abort_flag, kSiteAttnVFull)) { ok = false; break; }
+          if (!warp_wait(&v_full[st], ph, abort_flag, kSiteAttnVFull)) { ok = false; break; }
           const uint32_t v_addr = smem_u32(sV + st * Cfg::KV_BYTES);
           for (int t = 0; t < 2 && ok; ++t) {
             if (j >= nkv[t]) continue;
-            if (!mbar_wait(&p_full[t], (uint32_t)j & 1u, abort_flag, kSiteAttnPFull)) { ok = false; break; }
+            if (!warp_wait(&p_full[t], (uint32_t)j & 1u, abort_flag, kSiteAttnPFull)) { ok = false; break; }
             tc_fence_after();
   #pragma unroll
             for (int kk = 0; kk < 128 / 16; ++kk)  // O_t += P_t V_j, P_t from TMEM (K = 128 keys)
-              umma_f16_ts(tmem + Cfg::O_COL0 + t * D, tmem + (Cfg::S_COL_STRIDE * t) + kk * 8,
+              if (leader) umma_f16_ts(tmem + Cfg::O_COL0 + t * D, tmem + (Cfg::S_COL_STRIDE * t) + kk * 8,
                           make_sdesc_sw128(v_addr + kk * 2048, 128 * 128, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
-            if (j == nkv[t] - 1) umma_commit(&o_full[t]);
+            if (j == nkv[t] - 1 && leader) umma_commit(&o_full[t]);
             if (j + 1 < nkv[t]) {
               if (!k_next) {
-                if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, kSiteAttnKFull)) {
+                if (!warp_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, kSiteAttnKFull)) {
                   ok = false;
                   break;
                 }
@@ -270,16 +271,16 @@ __global__ void __launch_bounds__(384, 1)
             }
           }
           if (!ok) break;
-          umma_commit(&v_empty[st]);
-          if (k_next) umma_commit(&k_empty[(j + 1) & 1]);
+          if (leader) umma_commit(&v_empty[st]);
+          if (k_next && leader) umma_commit(&k_empty[(j + 1) & 1]);
         }
-        umma_commit(drain);
+        if (leader) umma_commit(drain);
         volatile int no_abort = 0;
-        mbar_wait(drain, 0, &no_abort, kSiteAttnDrain);
+        warp_wait(drain, 0, &no_abort, kSiteAttnDrain);
       }
     }
   } else {
-    warpgroup_reg_alloc<224>();
+    warpgroup_reg_alloc<216>();
     // ---------------------------------------------------------------- softmax (warps 4-7: A, 8-11: B)
     const int t = (warp < 8) ? 0 : 1;
     const uint32_t quarter = warp & 3u;

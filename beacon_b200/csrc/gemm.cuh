@@ -8,7 +8,8 @@
 // Persistent, warp-specialised CTA of 6 warps, one CTA per SM:
 //   warp 0      TMA producer: STAGES-deep ring of (A 128x64, B BNx64) bf16 tiles,
 //               128-byte swizzle, one mbarrier "full" and "empty" per stage.
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16).
+//   warp 1      TMEM allocator + tcgen05.mma issuer (M=128, N=BN, K=16): the whole warp runs
+//               the loop, one elected lane issues.
 //   warps 2-5   epilogue: tcgen05.ld of the fp32 accumulator (one TMEM lane per
 //               thread), fused bias / row-scale / residual / SwiGLU, bf16 or f32 store.
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
@@ -276,7 +277,10 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the loop and waits; one elected lane issues. A lane-confined issuer
+    // loses issue slots to the epilogue warp sharing its SM sub-partition.
+    {
+      const bool issuer = elect_one();
       constexpr uint32_t idesc = make_idesc_f16(BM, BN, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
@@ -284,11 +288,11 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, kSiteGemmTmemEmpty)) break;
+        if (!warp_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, kSiteGemmTmemEmpty)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(acc * BN);
         for (int kt = 0; kt < ktiles; ++kt) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, kSiteGemmFull)) {
+          if (!warp_wait(&full[stage], phase, abort_flag, kSiteGemmFull)) {
             ok = false;
             break;
           }
@@ -301,23 +305,23 @@ __global__ void __launch_bounds__(192, 1)
                                      : make_sdesc_sw128(a_addr + kk * 32, 16, 1024);
             const uint64_t bd = B_MN ? make_sdesc_sw128(b_addr + kk * 2048, 64 * BK * 2, 1024)
                                      : make_sdesc_sw128(b_addr + kk * 32, 16, 1024);
-            umma_f16_ss(d, ad, bd, idesc, (kt | kk) != 0 ? 1u : 0u);
+            if (issuer) umma_f16_ss(d, ad, bd, idesc, (kt | kk) != 0 ? 1u : 0u);
           }
-          umma_commit(&empty[stage]);  // frees the smem stage once these MMAs have read it
+          if (issuer) umma_commit(&empty[stage]);  // frees the smem stage once these MMAs have read it
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&tfull[acc]);  // accumulator ready for the epilogue
+        if (issuer) umma_commit(&tfull[acc]);  // accumulator ready for the epilogue
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
       }
       // Drain: every MMA this thread issued has finished before TMEM is freed.
-      umma_commit(drain);
+      if (issuer) umma_commit(drain);
       volatile int no_abort = 0;
-      mbar_wait(drain, 0, &no_abort, kSiteGemmDrain);
+      warp_wait(drain, 0, &no_abort, kSiteGemmDrain);
     }
   } else {
     // ------------------------------------------------------------ epilogue (warps 2..5)
@@ -495,8 +499,10 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer (leader only)
-    if (leader && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer (leader CTA only)
+    // The whole warp runs the loop and waits; one elected lane issues.
+    if (leader) {
+      const bool issuer = elect_one();
       constexpr uint32_t idesc = make_idesc_f16(256, Cfg::BN, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
@@ -504,11 +510,11 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int tile = cluster; tile < num_tiles && ok; tile += n_clusters) {
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, kSiteGemmTmemEmpty)) break;
+        if (!warp_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, kSiteGemmTmemEmpty)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(acc * Cfg::BN);
         for (int kt = 0; kt < ktiles; ++kt) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, kSiteGemmFull)) {
+          if (!warp_wait(&full[stage], phase, abort_flag, kSiteGemmFull)) {
             ok = false;
             break;
           }
@@ -521,22 +527,22 @@ __global__ void __launch_bounds__(192, 1)
                                      : make_sdesc_sw128(a_addr + kk * 32, 16, 1024);
             const uint64_t bd = B_MN ? make_sdesc_sw128(b_addr + kk * 2048, 64 * BK * 2, 1024)
                                      : make_sdesc_sw128(b_addr + kk * 32, 16, 1024);
-            umma_f16_ss_pair(d, ad, bd, idesc, (kt | kk) != 0 ? 1u : 0u);
+            if (issuer) umma_f16_ss_pair(d, ad, bd, idesc, (kt | kk) != 0 ? 1u : 0u);
           }
-          umma_commit_pair(&empty[stage]);  // both CTAs' stages are free once these MMAs read them
+          if (issuer) umma_commit_pair(&empty[stage]);  // both CTAs' stages are free once these MMAs read them
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit_pair(&tfull[acc]);
+        if (issuer) umma_commit_pair(&tfull[acc]);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
       }
-      umma_commit_leader(drain);
+      if (issuer) umma_commit_leader(drain);
       volatile int no_abort = 0;
-      mbar_wait(drain, 0, &no_abort, kSiteGemmDrain);
+      warp_wait(drain, 0, &no_abort, kSiteGemmDrain);
     }
   } else {
     // ------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
