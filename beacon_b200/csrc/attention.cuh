@@ -83,10 +83,36 @@ __device__ __forceinline__ void tma_prefetch_rows(const CUtensorMap* m, int row0
   for (int b = 0; b < D / 64; ++b) tma_prefetch_l2_3d(m, b * 64, row0, z);
 }
 
+// 2^a for a pair of arguments without the MUFU unit: a = n + f with n = rint(a) (1.5 x 2^23
+// added and subtracted in fp32 round-to-nearest, n then sits in the low mantissa bits),
+// a cubic in f in [-0.5, 0.5] fitted to 2^f by iteratively reweighted least squares on the
+// relative error (max relative error 7.5e-5, far below the bf16 rounding P receives), and n
+// shifted into the exponent field.  Arguments are clamped at -126, which returns less than
+// 2^-125 instead of 0, so callers use it only where no element is masked to -inf.
+__device__ __forceinline__ void exp2_poly2(float& r0, float& r1, float a0, float a1) {
+  constexpr float kMagic = 12582912.0f;
+  a0 = fmaxf(a0, -126.0f);
+  a1 = fmaxf(a1, -126.0f);
+  float t0, t1, n0, n1, f0, f1, p0, p1;
+  add2(t0, t1, a0, a1, kMagic, kMagic);
+  add2(n0, n1, t0, t1, -kMagic, -kMagic);
+  fma2(f0, f1, n0, n1, -1.0f, -1.0f, a0, a1);
+  fma2(p0, p1, 5.5171408e-2f, 5.5171408e-2f, f0, f1, 2.4261075e-1f, 2.4261075e-1f);
+  fma2(p0, p1, p0, p1, f0, f1, 6.9326097e-1f, 6.9326097e-1f);
+  fma2(p0, p1, p0, p1, f0, f1, 9.9992812e-1f, 9.9992812e-1f);
+  r0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  r1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+}
+
+// Pairs of S columns whose exponentials run on the FMA pipe on unmasked tiles, one bit per
+// pair index mod 8: the exponential unit (16 results per clock per SM) and the FMA pipe
+// then finish the row in about the same time.
+constexpr uint32_t kPolyPairs = 0x11u;
+
 // P = 2^(x * scale_log2 - m) for one 128-wide S row, packed to bf16 pairs into the
 // 64 TMEM columns at `taddr`; returns the row sum of P (fp32, before rounding).  The
-// argument and the running sums use packed f32x2 instructions: the softmax is bound by
-// instruction issue, not by the exponential unit.
+// argument and the running sums use packed f32x2 instructions.
+template <bool POLY>
 __device__ __forceinline__ float softmax_p_to_tmem(const float* x, float scale_log2, float neg_m, uint32_t taddr) {
   float ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
@@ -94,9 +120,14 @@ __device__ __forceinline__ float softmax_p_to_tmem(const float* x, float scale_l
     uint32_t pk[32];
 #pragma unroll
     for (int e = 0; e < 32; ++e) {
-      float a0, a1;
+      float a0, a1, p0, p1;
       fma2(a0, a1, x[64 * c + 2 * e], x[64 * c + 2 * e + 1], scale_log2, scale_log2, neg_m, neg_m);
-      const float p0 = ex2_approx(a0), p1 = ex2_approx(a1);
+      if (POLY && ((kPolyPairs >> (e & 7)) & 1u)) {
+        exp2_poly2(p0, p1, a0, a1);
+      } else {
+        p0 = ex2_approx(a0);
+        p1 = ex2_approx(a1);
+      }
       const int q = 2 * (e & 1);
       add2(ls[q], ls[q + 1], ls[q], ls[q + 1], p0, p1);
       pk[e] = pack_bf16x2(p0, p1);
@@ -346,7 +377,10 @@ __global__ void __launch_bounds__(384, 1)
         }
       }
       // P = exp2(x * scale_log2 - m_used) -> bf16 pairs into TMEM columns [s_col, s_col + 64)
-      l += softmax_p_to_tmem(x, p.scale_log2, -m_used, tmem + lane_base + s_col);
+      if (unmasked)
+        l += softmax_p_to_tmem<true>(x, p.scale_log2, -m_used, tmem + lane_base + s_col);
+      else
+        l += softmax_p_to_tmem<false>(x, p.scale_log2, -m_used, tmem + lane_base + s_col);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();

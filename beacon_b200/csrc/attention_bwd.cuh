@@ -17,10 +17,10 @@
 // of fp32 reductions per tile through L2, which is both slower than the repeated S and
 // dP products and a serialising step inside the pass.
 //
-// Both main kernels run 12 warps: warp 0 loads with TMA, warp 1 issues tcgen05.mma from
-// one thread, warps 2-3 idle, and warps 4-11 (two warpgroups, 2 warps per SM
-// sub-partition) do the elementwise work; warps 0-3 hand most of their registers to
-// warps 4-11 (setmaxnreg: 128 x 120 + 256 x 192 = 384 x 168, the launch allocation;
+// Both main kernels run 12 warps: warp 0 loads with TMA, warp 1 issues tcgen05.mma (the
+// whole warp runs the issue loop, one elected lane issues), warps 2-3 idle, and warps
+// 4-11 (two warpgroups, 2 warps per SM sub-partition) do the elementwise work; warps 0-3
+// hand most of their registers to warps 4-11 (setmaxnreg: 128 x 120 + 256 x 192 = 384 x 168, the launch allocation;
 // the MMA issuer keeps 120 registers so that no descriptor is spilled).
 // Every MMA is M=128 x N=128 (N=64 MMAs take as long as N=128 ones on this tensor core).
 #pragma once
@@ -143,20 +143,26 @@ __device__ __forceinline__ void pack32(const float (&v)[32], uint32_t (&pk)[16])
 }
 
 // ---------------------------------------------------------------------------
-// 2. dK / dV.  Each query tile n of the CTA's 128 keys is handled as two halves h of
-//   64 queries, each with its own score MMAs (M=128 keys x N=64 queries):
-//     S^T_h(n)  = K Q_h^T  -> TMEM [64h, 64h+64)      dP^T_h(n) = V dO_h^T -> TMEM [128+64h, +64)
-//   softmax warp (g, quarter): key rows 32*quarter.., queries 32g..32g+31 of the half; it
-//   writes, over the 32 S^T columns it has read,
-//     P^T  = exp2(S^T * scale*log2e - lse2[q])   bf16 -> TMEM [64h + 32g, +16)
-//     dS^T = P^T (dP^T - Dt[q])                  bf16 -> TMEM [64h + 32g + 16, +16)
-//   and the tensor core accumulates dV += P^T dO_h and dK += dS^T Q_h (A from TMEM).
-//   MMA issue order:  ... dV/dK_0(n), S/dP_0(n+1), dV/dK_1(n), S/dP_1(n+1), dV/dK_0(n+1) ...
-//   so while the warps work on one half the tensor core has the other half's dV/dK and
-//   the next tile's scores queued: the pipe never drains between tiles.  (An N=64 MMA
-//   costs as much as an N=128 one, so the scores cost twice the N=128 form: 48 MMAs per
-//   tile instead of 32, all of them overlapped.)
-// TMEM: S^T/P^T/dS^T [0,128) | dP^T [128,256) | dV [256,256+D) | dK [256+D,256+2D).
+// 2. dK / dV.  Per query tile n of the CTA's 128 keys (M=128 keys x N=128 queries):
+//     S^T(n)  = K Q(n)^T  -> TMEM region R_S(n)      dP^T(n) = V dO(n)^T -> region R_P(n)
+//   The two 128-column regions X = [0,128) and Y = [128,256) swap roles every tile
+//   (R_S(n) = X for even n, Y for odd n; R_P(n) is the other one), so the next tile's
+//   S^T goes into the region whose dP^T the warps have just read, and its dP^T into the
+//   region whose P^T / dS^T the dV / dK MMAs have just read.  MMA issue order per tile:
+//     S^T(n+1) -> R_P(n)      as soon as every warp holds dP^T(n)
+//     dV(n) += P^T(n) dO(n)   (P^T(n) is stored before dP^T(n) is read)
+//     dK(n) += dS^T(n) Q(n)   as soon as dS^T(n) is stored
+//     dP^T(n+1) -> R_S(n)     after dV(n) and dK(n) in issue order (MMAs run in order)
+//   (S^T(n+1) is issued ahead of dV(n), whose inputs are ready first: the next P phase
+//   waits for S^T(n+1), nothing waits for dV(n)), so the warps' P phase overlaps
+//   dK(n-1) / dP^T(n) and their dS phase overlaps S^T(n+1) / dV(n): the tensor pipe
+//   stays busy with 32 MMAs of N=128 per tile.
+//   Softmax warp (g, quarter): key rows 32*quarter.., queries 64g..64g+63; over the 64
+//   S^T columns it has read it writes
+//     P^T  = exp2(S^T * scale*log2e - lse2[q])   bf16 -> R_S(n) + [64g, 64g+32)
+//     dS^T = P^T (dP^T - Dt[q])                  bf16 -> R_S(n) + [64g+32, 64g+64)
+//   and dV / dK read them as the A operand from TMEM.
+// TMEM: X [0,128) | Y [128,256) | dV [256,256+D) | dK [256+D,256+2D).
 // ---------------------------------------------------------------------------
 template <int D>
 __global__ void __launch_bounds__(384, 1)
@@ -176,13 +182,16 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* kv_full = bars + 0;
   uint64_t* qd_full = bars + 1;   // [2] Q, dO and statistics of a query tile
   uint64_t* qd_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2] S^T_h(n) and dP^T_h(n) computed
-  uint64_t* ds_full = bars + 7;   // [2] P^T_h / dS^T_h stored by all 8 warps
-  uint64_t* dkv_full = bars + 9;
-  uint64_t* drain = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  uint64_t* s_full = bars + 5;    // S^T(n) computed
+  uint64_t* dp_full = bars + 6;   // dP^T(n) computed
+  uint64_t* p_ready = bars + 7;   // P^T(n) stored by all 8 warps
+  uint64_t* rp_free = bars + 8;   // dP^T(n) read by all 8 warps: R_P(n) may take S^T(n+1)
+  uint64_t* ds_ready = bars + 9;  // dS^T(n) stored by all 8 warps
+  uint64_t* dkv_full = bars + 10;
+  uint64_t* drain = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  constexpr uint32_t T_S = 0, T_DP = 128, T_DV = 256, T_DK = 256 + D;
+  constexpr uint32_t T_DV = 256, T_DK = 256 + D;
 
   const uint32_t warp = warp_id(), lane = lane_id();
   const int n_kvh = p.B * p.Hkv;
@@ -201,9 +210,12 @@ __global__ void __launch_bounds__(384, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&qd_full[i], 1);
       mbar_init(&qd_empty[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&ds_full[i], 8);
     }
+    mbar_init(s_full, 1);
+    mbar_init(dp_full, 1);
+    mbar_init(p_ready, 8);
+    mbar_init(rp_free, 8);
+    mbar_init(ds_ready, 8);
     mbar_init(dkv_full, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -264,25 +276,17 @@ __global__ void __launch_bounds__(384, 1)
     } else if (warp == 1) {
       // ---------------------------------------------------------------- MMA issuer (whole warp, one elected lane issues)
       const bool leader = elect_one();
-      constexpr uint32_t idesc_s = make_idesc_f16(128, 64, false, false);  // S^T_h, dP^T_h
-      constexpr uint32_t idesc_kv = make_idesc_f16(128, D, false, true);   // dV, dK: A in TMEM, B MN-major
+      constexpr uint32_t idesc_kv = make_idesc_f16(128, D, false, true);  // dV, dK: A in TMEM, B MN-major
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
-      // S^T_h and dP^T_h of the tile in stage st, then announce them
-      auto issue_half = [&](int h, int st) {
-        const uint32_t q_addr = smem_u32(sQ + st * TILE) + h * 8192, do_addr = smem_u32(sdO + st * TILE) + h * 8192;
+      // dV += P^T dO or dK += dS^T Q: A at TMEM columns `a_col` + [64g, 64g+32) for g = 0, 1
+      auto issue_kv = [&](uint32_t d_col, uint32_t a_col, uint32_t b_addr, bool first) {
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          if (leader) umma_f16_ss(tmem + T_S + 64 * h, make_sdesc_sw128(k_addr + off, 16, 1024),
-                      make_sdesc_sw128(q_addr + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 8; ++kk) {  // 16 queries per K-step
+          const uint32_t col = a_col + (uint32_t)(64 * (kk >> 2) + 8 * (kk & 3));
+          if (leader)
+            umma_f16_ts(tmem + d_col, tmem + col, make_sdesc_sw128(b_addr + kk * 2048, 16384, 1024), idesc_kv,
+                        (!first || kk > 0) ? 1u : 0u);
         }
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          if (leader) umma_f16_ss(tmem + T_DP + 64 * h, make_sdesc_sw128(v_addr + off, 16, 1024),
-                      make_sdesc_sw128(do_addr + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
-        }
-        if (leader) umma_commit(&s_full[h]);
       };
       bool ok = warp_wait(kv_full, 0, abort_flag, kSiteBwdKV);
       if (ok && n_iter > 0) {
@@ -290,44 +294,39 @@ __global__ void __launch_bounds__(384, 1)
           ok = false;
         } else {
           tc_fence_after();
-          issue_half(0, 0);
-          issue_half(1, 0);
+          issue_score_tile<D>(leader, tmem + 0, k_addr, smem_u32(sQ));
+          if (leader) umma_commit(s_full);
+          issue_score_tile<D>(leader, tmem + 128, v_addr, smem_u32(sdO));
+          if (leader) umma_commit(dp_full);
         }
       }
       for (int n = 0; n < n_iter && ok; ++n) {
         const int st = n & 1, st1 = (n + 1) & 1;
+        const uint32_t par = (uint32_t)n & 1u;
         const bool more = n + 1 < n_iter;
+        const uint32_t rs = (n & 1) ? 128u : 0u, rp = 128u - rs;  // R_S(n), R_P(n)
         const uint32_t q_addr = smem_u32(sQ + st * TILE), do_addr = smem_u32(sdO + st * TILE);
-        for (int h = 0; h < 2 && ok; ++h) {
-          if (!warp_wait(&ds_full[h], (uint32_t)n & 1u, abort_flag, kSiteBwdDsFull)) {
-            ok = false;
-            break;
-          }
+        // S^T(n+1) ahead of dV(n): the warps' next P phase waits for it, nothing waits for dV(n)
+        if (!warp_wait(p_ready, par, abort_flag, kSiteBwdDsFull) || !warp_wait(rp_free, par, abort_flag, kSiteBwdDsFull))
+          break;
+        if (more) {
+          if (!warp_wait(&qd_full[st1], ((n + 1) >> 1) & 1, abort_flag, kSiteBwdQDFull)) break;
           tc_fence_after();
-#pragma unroll
-          for (int k4 = 0; k4 < 4; ++k4) {  // 16 queries per K-step: warp group k4 >> 1, block k4 & 1
-            const int kk = 4 * h + k4;       // query rows 16kk.. of the tile
-            const uint32_t acc = (n > 0 || h > 0 || k4 > 0) ? 1u : 0u;
-            const uint32_t col = (uint32_t)(64 * h + 32 * (k4 >> 1) + 8 * (k4 & 1));
-            if (leader) umma_f16_ts(tmem + T_DV, tmem + T_S + col, make_sdesc_sw128(do_addr + kk * 2048, 16384, 1024), idesc_kv,
-                        acc);
-            if (leader) umma_f16_ts(tmem + T_DK, tmem + T_S + col + 16, make_sdesc_sw128(q_addr + kk * 2048, 16384, 1024),
-                        idesc_kv, acc);
-          }
-          if (h == 1 && leader) umma_commit(&qd_empty[st]);  // Q(n), dO(n) free once these have read them
-          if (more) {  // the next tile's half h goes where this tile's half h just left
-            if (h == 0) {
-              if (!warp_wait(&qd_full[st1], ((n + 1) >> 1) & 1, abort_flag, kSiteBwdQDFull)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-            }
-            issue_half(h, st1);
-          }
+          issue_score_tile<D>(leader, tmem + rp, k_addr, smem_u32(sQ + st1 * TILE));
+          if (leader) umma_commit(s_full);
         }
+        tc_fence_after();
+        issue_kv(T_DV, rs, do_addr, n == 0);
+        if (!warp_wait(ds_ready, par, abort_flag, kSiteBwdDsFull)) break;
+        tc_fence_after();
+        issue_kv(T_DK, rs + 32, q_addr, n == 0);
+        if (leader) umma_commit(&qd_empty[st]);  // Q(n), dO(n) free once these have read them
+        if (more) {
+          issue_score_tile<D>(leader, tmem + rs, v_addr, smem_u32(sdO + st1 * TILE));
+          if (leader) umma_commit(dp_full);
+        }
+        if (!more && leader) umma_commit(dkv_full);
       }
-      if (ok && leader) umma_commit(dkv_full);
       if (leader) umma_commit(drain);
       volatile int no_abort = 0;
       warp_wait(drain, 0, &no_abort, kSiteBwdDrain);
@@ -336,7 +335,7 @@ __global__ void __launch_bounds__(384, 1)
     warpgroup_reg_alloc<192>();
     // ---------------------------------------------------------------- softmax (warps 4..11)
     const uint32_t quarter = warp & 3u;
-    const int g = (int)(warp - 4) >> 2;        // 32-query group within a half / dV or dK (epilogue)
+    const int g = (int)(warp - 4) >> 2;        // 64-query group / dV or dK (epilogue)
     const int r = (int)(quarter * 32 + lane);  // TMEM lane = key row
     const int kj = j0 + r;
     const uint32_t lane_base = (quarter * 32u) << 16;
@@ -347,59 +346,86 @@ __global__ void __launch_bounds__(384, 1)
       const int it = it0 + n % iters_per_head;
       const int q0 = it * 128;
       const int st = n & 1;
+      const uint32_t par = (uint32_t)n & 1u;
+      const uint32_t rs = (n & 1) ? 128u : 0u, rp = 128u - rs;
       // off-diagonal tiles need no mask: every key < S and every query >= every key
       const bool masked = !keys_full || (p.causal && it == jt);
       const int qmin = p.causal ? kj - q0 : -1;
-      const float* lse2 = sStats + st * 256;
+      const float* lse2 = sStats + st * 256 + 64 * g;
       const float* dtq = lse2 + 128;
-      for (int h = 0; h < 2 && ok; ++h) {
-        // s_full: the scores; qd_full: makes the TMA-written statistics visible to this thread
-        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[h], (uint32_t)n & 1u, abort_flag, kSiteBwdStFull) &&
-                                         mbar_wait(&qd_full[st], (n >> 1) & 1, abort_flag, kSiteBwdQDFull))) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t cs = T_S + 64 * h + 32 * g;  // this warp's 32 S^T columns
-        uint32_t sv[32], dpv[32];
-        tmem_ld32(tmem + lane_base + cs, sv);
-        tmem_ld32(tmem + lane_base + T_DP + 64 * h + 32 * g, dpv);
+      // s_full: the scores; qd_full: makes the TMA-written statistics visible to this thread
+      if (!__all_sync(0xffffffffu, mbar_wait(s_full, par, abort_flag, kSiteBwdStFull) &&
+                                       mbar_wait(&qd_full[st], (n >> 1) & 1, abort_flag, kSiteBwdQDFull))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t cs = rs + 64 * g;  // this warp's 64 S^T columns
+      float pe[64];
+      {
+        uint32_t sv[64];
+        tmem_ld32(tmem + lane_base + cs, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_ld32(tmem + lane_base + cs + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
         tmem_wait_ld();
-        const int col0 = 64 * h + 32 * g;  // query index within the tile
-        float pe[32], dsv[32];
 #pragma unroll
-        for (int e4 = 0; e4 < 8; ++e4) {
-          const float4 l4 = *reinterpret_cast<const float4*>(&lse2[col0 + 4 * e4]);
-          const float4 d4 = *reinterpret_cast<const float4*>(&dtq[col0 + 4 * e4]);
+        for (int e4 = 0; e4 < 16; ++e4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(&lse2[4 * e4]);
           const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
-          const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
 #pragma unroll
           for (int u = 0; u < 4; u += 2) {  // pairs: packed f32x2 arithmetic
             const int e = 4 * e4 + u;
-            float a0, a1, t0, t1;
+            float a0, a1;
             fma2(a0, a1, __uint_as_float(sv[e]), __uint_as_float(sv[e + 1]), p.scale_log2, p.scale_log2, lv[u],
                  lv[u + 1]);
             float p0 = ex2_approx(a0), p1 = ex2_approx(a1);
             if (masked) {
-              if (!(key_ok && col0 + e >= qmin)) p0 = 0.0f;
-              if (!(key_ok && col0 + e + 1 >= qmin)) p1 = 0.0f;
+              if (!(key_ok && 64 * g + e >= qmin)) p0 = 0.0f;
+              if (!(key_ok && 64 * g + e + 1 >= qmin)) p1 = 0.0f;
             }
             pe[e] = p0;
             pe[e + 1] = p1;
-            fma2(t0, t1, dv[u], dv[u + 1], -1.0f, -1.0f, __uint_as_float(dpv[e]), __uint_as_float(dpv[e + 1]));
-            mul2(dsv[e], dsv[e + 1], p0, p1, t0, t1);
           }
         }
-        uint32_t pk[16], dk[16];
-        pack32(pe, pk);
-        pack32(dsv, dk);
-        tmem_st16(tmem + lane_base + cs, pk);
-        tmem_st16(tmem + lane_base + cs + 16, dk);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&ds_full[h]);
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) pk[i] = pack_bf16x2(pe[2 * i], pe[2 * i + 1]);
+        tmem_st32(tmem + lane_base + cs, pk);  // P^T over the S^T columns just read
       }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_ready);
+      if (!__all_sync(0xffffffffu, mbar_wait(dp_full, par, abort_flag, kSiteBwdStFull))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t dpv[64];
+      tmem_ld32(tmem + lane_base + rp + 64 * g, *reinterpret_cast<uint32_t(*)[32]>(&dpv[0]));
+      tmem_ld32(tmem + lane_base + rp + 64 * g + 32, *reinterpret_cast<uint32_t(*)[32]>(&dpv[32]));
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(rp_free);  // R_P(n) may take S^T(n+1)
+      uint32_t dk[32];
+#pragma unroll
+      for (int e4 = 0; e4 < 16; ++e4) {
+        const float4 d4 = *reinterpret_cast<const float4*>(&dtq[4 * e4]);
+        const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+        for (int u = 0; u < 4; u += 2) {
+          const int e = 4 * e4 + u;
+          float t0, t1, d0, d1;
+          fma2(t0, t1, dv[u], dv[u + 1], -1.0f, -1.0f, __uint_as_float(dpv[e]), __uint_as_float(dpv[e + 1]));
+          mul2(d0, d1, pe[e], pe[e + 1], t0, t1);
+          dk[e >> 1] = pack_bf16x2(d0, d1);
+        }
+      }
+      tmem_st32(tmem + lane_base + cs + 32, dk);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ds_ready);
     }
     // final dV (g = 0) / dK (g = 1) rows
     if (ok && __all_sync(0xffffffffu, mbar_wait(dkv_full, 0, abort_flag, kSiteBwdDkvFull))) {
