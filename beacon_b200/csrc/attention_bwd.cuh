@@ -150,13 +150,12 @@ __device__ __forceinline__ void pack32(const float (&v)[32], uint32_t (&pk)[16])
 //   S^T goes into the region whose dP^T the warps have just read, and its dP^T into the
 //   region whose P^T / dS^T the dV / dK MMAs have just read.  MMA issue order per tile:
 //     S^T(n+1) -> R_P(n)      as soon as every warp holds dP^T(n)
-//     dV(n) += P^T(n) dO(n)   (P^T(n) is stored before dP^T(n) is read)
 //     dK(n) += dS^T(n) Q(n)   as soon as dS^T(n) is stored
-//     dP^T(n+1) -> R_S(n)     after dV(n) and dK(n) in issue order (MMAs run in order)
-//   (S^T(n+1) is issued ahead of dV(n), whose inputs are ready first: the next P phase
-//   waits for S^T(n+1), nothing waits for dV(n)), so the warps' P phase overlaps
-//   dK(n-1) / dP^T(n) and their dS phase overlaps S^T(n+1) / dV(n): the tensor pipe
-//   stays busy with 32 MMAs of N=128 per tile.
+//     dV(n) += P^T(n) dO(n)
+//     dP^T(n+1) -> R_S(n)     after dK(n) and dV(n) in issue order (MMAs run in order)
+//   so the warps' dS phase (short) overlaps S^T(n+1) and their P phase (long: the
+//   exponentials) overlaps dK(n-1), dV(n-1) and dP^T(n): 32 MMAs of N=128 per tile, the
+//   tensor pipe idle only while the warps hand dP^T over.
 //   Softmax warp (g, quarter): key rows 32*quarter.., queries 64g..64g+63; over the 64
 //   S^T columns it has read it writes
 //     P^T  = exp2(S^T * scale*log2e - lse2[q])   bf16 -> R_S(n) + [64g, 64g+32)
@@ -180,16 +179,18 @@ __global__ void __launch_bounds__(384, 1)
   float* sStats = reinterpret_cast<float*>(sdO + 2 * TILE);  // [2][256]: lse2 [0,128), Dt [128,256)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sStats + 2 * 256);
   uint64_t* kv_full = bars + 0;
-  uint64_t* qd_full = bars + 1;   // [2] Q, dO and statistics of a query tile
-  uint64_t* qd_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // S^T(n) computed
-  uint64_t* dp_full = bars + 6;   // dP^T(n) computed
-  uint64_t* p_ready = bars + 7;   // P^T(n) stored by all 8 warps
-  uint64_t* rp_free = bars + 8;   // dP^T(n) read by all 8 warps: R_P(n) may take S^T(n+1)
-  uint64_t* ds_ready = bars + 9;  // dS^T(n) stored by all 8 warps
-  uint64_t* dkv_full = bars + 10;
-  uint64_t* drain = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* q_full = bars + 1;     // [2] Q and lse2 of a query tile
+  uint64_t* q_empty = bars + 3;    // [2] Q read by S^T and dK
+  uint64_t* do_full = bars + 5;    // [2] dO and Dt of a query tile
+  uint64_t* do_empty = bars + 7;   // [2] dO read by dP^T and dV
+  uint64_t* s_full = bars + 9;     // S^T(n) computed
+  uint64_t* dp_full = bars + 10;   // dP^T(n) computed
+  uint64_t* p_ready = bars + 11;   // P^T(n) stored by all 8 warps
+  uint64_t* rp_free = bars + 12;   // dP^T(n) read by all 8 warps: R_P(n) may take S^T(n+1)
+  uint64_t* ds_ready = bars + 13;  // dS^T(n) stored by all 8 warps
+  uint64_t* dkv_full = bars + 14;
+  uint64_t* drain = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   constexpr uint32_t T_DV = 256, T_DK = 256 + D;
 
@@ -208,8 +209,10 @@ __global__ void __launch_bounds__(384, 1)
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&qd_full[i], 1);
-      mbar_init(&qd_empty[i], 1);
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&do_full[i], 1);
+      mbar_init(&do_empty[i], 1);
     }
     mbar_init(s_full, 1);
     mbar_init(dp_full, 1);
@@ -241,37 +244,48 @@ __global__ void __launch_bounds__(384, 1)
       mbar_arrive_expect_tx(kv_full, 2 * TILE);
       tma_load_rows<D>(sK, &tmK, kv_full, j0, kvz);
       tma_load_rows<D>(sV, &tmV, kv_full, j0, kvz);
-      uint32_t issued = 0, par = 0;
+      // Q (with lse2) and dO (with Dt) have rings of their own: Q(n) is released by dK(n),
+      // a third of a tile before dV(n) releases dO(n), and Q(n+2) is needed first.
+      uint32_t qiss = 0, qpar = 0, diss = 0, dpar = 0;
       bool ok = true;
       for (int n = 0; n < n_iter && ok; ++n) {
         const int g = n / iters_per_head, it = it0 + n % iters_per_head;
         const int bh = b * p.Hq + hk * group + g;
         const int st = n & 1;
         const uint32_t ph = (n >> 1) & 1;
-        if (!mbar_wait(&qd_empty[st], ph ^ 1u, abort_flag, kSiteBwdQDEmpty)) {
+        const long long srow = (long long)bh * p.S_pad + it * 128;
+        if (!mbar_wait(&q_empty[st], ph ^ 1u, abort_flag, kSiteBwdQDEmpty)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&qd_full[st], 2 * TILE + Cfg::STATS_BYTES);
-        tma_load_rows<D>(sQ + st * TILE, &tmQ, &qd_full[st], it * 128, bh);
-        tma_load_rows<D>(sdO + st * TILE, &tmdO, &qd_full[st], it * 128, bh);
-        const long long srow = (long long)bh * p.S_pad + it * 128;
-        bulk_load(sStats + st * 256, p.lse2 + srow, 512, &qd_full[st]);
-        bulk_load(sStats + st * 256 + 128, p.dt + srow, 512, &qd_full[st]);
+        mbar_arrive_expect_tx(&q_full[st], TILE + Cfg::STATS_BYTES / 2);
+        tma_load_rows<D>(sQ + st * TILE, &tmQ, &q_full[st], it * 128, bh);
+        bulk_load(sStats + st * 256, p.lse2 + srow, 512, &q_full[st]);
+        qiss |= 1u << st;
+        qpar = (qpar & ~(1u << st)) | (ph << st);
+        if (!mbar_wait(&do_empty[st], ph ^ 1u, abort_flag, kSiteBwdQDEmpty)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&do_full[st], TILE + Cfg::STATS_BYTES / 2);
+        tma_load_rows<D>(sdO + st * TILE, &tmdO, &do_full[st], it * 128, bh);
+        bulk_load(sStats + st * 256 + 128, p.dt + srow, 512, &do_full[st]);
+        diss |= 1u << st;
+        dpar = (dpar & ~(1u << st)) | (ph << st);
         if (n + 1 < n_iter) {  // the tile after: into L2 now, so its load finds it there
           const int g1 = (n + 1) / iters_per_head, it1 = it0 + (n + 1) % iters_per_head;
           const int bh1 = b * p.Hq + hk * group + g1;
-          tma_prefetch_rows<D>(&tmdO, it1 * 128, bh1);
           tma_prefetch_rows<D>(&tmQ, it1 * 128, bh1);
+          tma_prefetch_rows<D>(&tmdO, it1 * 128, bh1);
         }
-        issued |= 1u << st;
-        par = (par & ~(1u << st)) | (ph << st);
       }
       if (!ok) {
         volatile int no_abort = 0;
         mbar_wait(kv_full, 0, &no_abort, kSiteBwdDrain);
-        for (int s = 0; s < 2; ++s)
-          if (issued & (1u << s)) mbar_wait(&qd_full[s], (par >> s) & 1u, &no_abort, kSiteBwdDrain);
+        for (int s = 0; s < 2; ++s) {
+          if (qiss & (1u << s)) mbar_wait(&q_full[s], (qpar >> s) & 1u, &no_abort, kSiteBwdDrain);
+          if (diss & (1u << s)) mbar_wait(&do_full[s], (dpar >> s) & 1u, &no_abort, kSiteBwdDrain);
+        }
       }
     } else if (warp == 1) {
       // ---------------------------------------------------------------- MMA issuer (whole warp, one elected lane issues)
@@ -290,7 +304,7 @@ __global__ void __launch_bounds__(384, 1)
       };
       bool ok = warp_wait(kv_full, 0, abort_flag, kSiteBwdKV);
       if (ok && n_iter > 0) {
-        if (!warp_wait(&qd_full[0], 0, abort_flag, kSiteBwdQDFull)) {
+        if (!warp_wait(&q_full[0], 0, abort_flag, kSiteBwdQDFull) || !warp_wait(&do_full[0], 0, abort_flag, kSiteBwdQDFull)) {
           ok = false;
         } else {
           tc_fence_after();
@@ -306,22 +320,26 @@ __global__ void __launch_bounds__(384, 1)
         const bool more = n + 1 < n_iter;
         const uint32_t rs = (n & 1) ? 128u : 0u, rp = 128u - rs;  // R_S(n), R_P(n)
         const uint32_t q_addr = smem_u32(sQ + st * TILE), do_addr = smem_u32(sdO + st * TILE);
-        // S^T(n+1) ahead of dV(n): the warps' next P phase waits for it, nothing waits for dV(n)
+        // S^T(n+1) as soon as R_P(n) is free: the warps' next P phase waits for it.  dV(n)
+        // waits with dK(n) for dS^T(n): the three products of that group (24 MMAs) then run
+        // during the next P phase, the longest stretch of the warps' work.
         if (!warp_wait(p_ready, par, abort_flag, kSiteBwdDsFull) || !warp_wait(rp_free, par, abort_flag, kSiteBwdDsFull))
           break;
         if (more) {
-          if (!warp_wait(&qd_full[st1], ((n + 1) >> 1) & 1, abort_flag, kSiteBwdQDFull)) break;
+          if (!warp_wait(&q_full[st1], ((n + 1) >> 1) & 1, abort_flag, kSiteBwdQDFull)) break;
           tc_fence_after();
           issue_score_tile<D>(leader, tmem + rp, k_addr, smem_u32(sQ + st1 * TILE));
           if (leader) umma_commit(s_full);
         }
-        tc_fence_after();
-        issue_kv(T_DV, rs, do_addr, n == 0);
         if (!warp_wait(ds_ready, par, abort_flag, kSiteBwdDsFull)) break;
         tc_fence_after();
         issue_kv(T_DK, rs + 32, q_addr, n == 0);
-        if (leader) umma_commit(&qd_empty[st]);  // Q(n), dO(n) free once these have read them
-        if (more) {
+        if (leader) umma_commit(&q_empty[st]);  // Q(n) read by S^T(n) and dK(n)
+        issue_kv(T_DV, rs, do_addr, n == 0);
+        if (leader) umma_commit(&do_empty[st]);  // dO(n) read by dP^T(n) and dV(n)
+        if (more) {  // into R_S(n), behind dK(n) and dV(n), which read P^T / dS^T(n) from it
+          if (!warp_wait(&do_full[st1], ((n + 1) >> 1) & 1, abort_flag, kSiteBwdQDFull)) break;
+          tc_fence_after();
           issue_score_tile<D>(leader, tmem + rs, v_addr, smem_u32(sdO + st1 * TILE));
           if (leader) umma_commit(dp_full);
         }
@@ -353,9 +371,9 @@ __global__ void __launch_bounds__(384, 1)
       const int qmin = p.causal ? kj - q0 : -1;
       const float* lse2 = sStats + st * 256 + 64 * g;
       const float* dtq = lse2 + 128;
-      // s_full: the scores; qd_full: makes the TMA-written statistics visible to this thread
+      // s_full: the scores; q_full: makes the TMA-written lse2 visible to this thread
       if (!__all_sync(0xffffffffu, mbar_wait(s_full, par, abort_flag, kSiteBwdStFull) &&
-                                       mbar_wait(&qd_full[st], (n >> 1) & 1, abort_flag, kSiteBwdQDFull))) {
+                                       mbar_wait(&q_full[st], (n >> 1) & 1, abort_flag, kSiteBwdQDFull))) {
         ok = false;
         break;
       }
@@ -395,7 +413,9 @@ __global__ void __launch_bounds__(384, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_ready);
-      if (!__all_sync(0xffffffffu, mbar_wait(dp_full, par, abort_flag, kSiteBwdStFull))) {
+      // dp_full: dP^T(n); do_full: makes the TMA-written Dt visible to this thread
+      if (!__all_sync(0xffffffffu, mbar_wait(dp_full, par, abort_flag, kSiteBwdStFull) &&
+                                       mbar_wait(&do_full[st], (n >> 1) & 1, abort_flag, kSiteBwdQDFull))) {
         ok = false;
         break;
       }

@@ -79,15 +79,16 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
-// Waits (suspended, not spinning) until the phase with the given parity completes or
-// about 0.1 ms passes.  A suspended warp takes no issue slots from the warps that share
-// its SM sub-partition -- the single-thread MMA issuer among them.
+// Waits (suspended, not spinning) until the phase with the given parity completes or a
+// system-dependent time passes.  A suspended warp takes no issue slots from the warps
+// that share its SM sub-partition.  (An explicit 0.1 ms suspend-time hint measured about
+// 1% slower on the attention kernels; a non-blocking test_wait spin 2% slower.)
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred P;\n mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2, %3;\n selp.b32 %0, 1, 0, P;\n}\n"
+      "{\n .reg .pred P;\n mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n selp.b32 %0, 1, 0, P;\n}\n"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(100000u)
+      : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
 }
