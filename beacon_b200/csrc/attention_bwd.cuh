@@ -136,10 +136,50 @@ __device__ __forceinline__ void issue_score_tile(bool leader, uint32_t d_tmem, u
   }
 }
 
-// Packs 32 fp32 values into 16 bf16 pairs.
-__device__ __forceinline__ void pack32(const float (&v)[32], uint32_t (&pk)[16]) {
+// P^T for one warp's 64 query columns of a dK/dV tile: exp2(S^T * scale*log2e + lse2[q]),
+// lse2 read from shared memory at `lse2_addr`.  MASKED zeroes the columns below
+// `first_ok` (keys at or beyond S, or after the query); unmasked tiles take the variant
+// without the selects.
+template <bool MASKED>
+__device__ __forceinline__ void bwd_p_cols(const uint32_t (&sv)[64], uint32_t lse2_addr, float scale_log2, int first_ok,
+                                           float (&pe)[64]) {
 #pragma unroll
-  for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+  for (int e4 = 0; e4 < 16; ++e4) {
+    const float4 l4 = lds_f4(lse2_addr + 16 * e4);
+    float a0, a1, a2, a3;
+    fma2(a0, a1, __uint_as_float(sv[4 * e4]), __uint_as_float(sv[4 * e4 + 1]), scale_log2, scale_log2, l4.x, l4.y);
+    fma2(a2, a3, __uint_as_float(sv[4 * e4 + 2]), __uint_as_float(sv[4 * e4 + 3]), scale_log2, scale_log2, l4.z, l4.w);
+    pe[4 * e4] = ex2_approx(a0);
+    pe[4 * e4 + 1] = ex2_approx(a1);
+    pe[4 * e4 + 2] = ex2_approx(a2);
+    pe[4 * e4 + 3] = ex2_approx(a3);
+    if (MASKED) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (4 * e4 + u < first_ok) pe[4 * e4 + u] = 0.0f;
+    }
+  }
+}
+
+// dS = P (dP - Dt) for one 32-key chunk of a dQ row, packed to bf16 pairs, with
+// P = exp2(S * scale*log2e + nl2).  MASKED zeroes P from key `klim` on (keys at or beyond
+// S, or after the query); unmasked tiles take the variant without the selects.
+template <bool MASKED>
+__device__ __forceinline__ void dq_ds_chunk(const uint32_t (&sc)[32], const uint32_t (&dpc)[32], float scale_log2,
+                                            float nl2, float dtr, int klim, uint32_t (&pk)[16]) {
+#pragma unroll
+  for (int e = 0; e < 32; e += 2) {  // pairs: packed f32x2 arithmetic
+    float a0, a1, t0, t1, d0, d1;
+    fma2(a0, a1, __uint_as_float(sc[e]), __uint_as_float(sc[e + 1]), scale_log2, scale_log2, nl2, nl2);
+    float p0 = ex2_approx(a0), p1 = ex2_approx(a1);
+    if (MASKED) {
+      if (e >= klim) p0 = 0.0f;
+      if (e + 1 >= klim) p1 = 0.0f;
+    }
+    fma2(t0, t1, dtr, dtr, -1.0f, -1.0f, __uint_as_float(dpc[e]), __uint_as_float(dpc[e + 1]));
+    mul2(d0, d1, p0, p1, t0, t1);
+    pk[e >> 1] = pack_bf16x2(d0, d1);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -369,8 +409,9 @@ __global__ void __launch_bounds__(384, 1)
       // off-diagonal tiles need no mask: every key < S and every query >= every key
       const bool masked = !keys_full || (p.causal && it == jt);
       const int qmin = p.causal ? kj - q0 : -1;
-      const float* lse2 = sStats + st * 256 + 64 * g;
-      const float* dtq = lse2 + 128;
+      const uint32_t lse2_addr = smem_u32(sStats + st * 256 + 64 * g), dt_addr = lse2_addr + 512;
+      // first of this warp's 64 query columns that the key sees (64: none)
+      const int first_ok = key_ok ? max(qmin - 64 * g, 0) : 64;
       // s_full: the scores; q_full: makes the TMA-written lse2 visible to this thread
       if (!__all_sync(0xffffffffu, mbar_wait(s_full, par, abort_flag, kSiteBwdStFull) &&
                                        mbar_wait(&q_full[st], (n >> 1) & 1, abort_flag, kSiteBwdQDFull))) {
@@ -385,25 +426,10 @@ __global__ void __launch_bounds__(384, 1)
         tmem_ld32(tmem + lane_base + cs, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
         tmem_ld32(tmem + lane_base + cs + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
         tmem_wait_ld();
-#pragma unroll
-        for (int e4 = 0; e4 < 16; ++e4) {
-          const float4 l4 = *reinterpret_cast<const float4*>(&lse2[4 * e4]);
-          const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
-#pragma unroll
-          for (int u = 0; u < 4; u += 2) {  // pairs: packed f32x2 arithmetic
-            const int e = 4 * e4 + u;
-            float a0, a1;
-            fma2(a0, a1, __uint_as_float(sv[e]), __uint_as_float(sv[e + 1]), p.scale_log2, p.scale_log2, lv[u],
-                 lv[u + 1]);
-            float p0 = ex2_approx(a0), p1 = ex2_approx(a1);
-            if (masked) {
-              if (!(key_ok && 64 * g + e >= qmin)) p0 = 0.0f;
-              if (!(key_ok && 64 * g + e + 1 >= qmin)) p1 = 0.0f;
-            }
-            pe[e] = p0;
-            pe[e + 1] = p1;
-          }
-        }
+        if (masked)
+          bwd_p_cols<true>(sv, lse2_addr, p.scale_log2, first_ok, pe);
+        else
+          bwd_p_cols<false>(sv, lse2_addr, p.scale_log2, first_ok, pe);
         uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) pk[i] = pack_bf16x2(pe[2 * i], pe[2 * i + 1]);
@@ -430,7 +456,7 @@ __global__ void __launch_bounds__(384, 1)
       uint32_t dk[32];
 #pragma unroll
       for (int e4 = 0; e4 < 16; ++e4) {
-        const float4 d4 = *reinterpret_cast<const float4*>(&dtq[4 * e4]);
+        const float4 d4 = lds_f4(dt_addr + 16 * e4);
         const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
 #pragma unroll
         for (int u = 0; u < 4; u += 2) {
@@ -691,21 +717,11 @@ __global__ void __launch_bounds__(384, 1)
       if (lane == 0) mbar_arrive(dp_free);  // dP(j+1) may overwrite dP(j)
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        float dsv[32];
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {  // pairs: packed f32x2 arithmetic
-          float a0, a1, t0, t1;
-          fma2(a0, a1, __uint_as_float(s[c][e]), __uint_as_float(s[c][e + 1]), p.scale_log2, p.scale_log2, nl2, nl2);
-          float p0 = ex2_approx(a0), p1 = ex2_approx(a1);
-          if (masked) {
-            if (32 * c + e >= klim) p0 = 0.0f;
-            if (32 * c + e + 1 >= klim) p1 = 0.0f;
-          }
-          fma2(t0, t1, dtr, dtr, -1.0f, -1.0f, __uint_as_float(dp[c][e]), __uint_as_float(dp[c][e + 1]));
-          mul2(dsv[e], dsv[e + 1], p0, p1, t0, t1);
-        }
         uint32_t pk[16];
-        pack32(dsv, pk);
+        if (masked)
+          dq_ds_chunk<true>(s[c], dp[c], p.scale_log2, nl2, dtr, klim - 32 * c, pk);
+        else
+          dq_ds_chunk<false>(s[c], dp[c], p.scale_log2, nl2, dtr, klim - 32 * c, pk);
         tmem_st16(tmem + lane_base + sb + 16 * c, pk);  // over S columns this thread has read
         tmem_wait_st();
         tc_fence_before();

@@ -425,6 +425,14 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return r;
 }
 
+// 16-byte shared-memory load by shared-window address (a generic pointer into shared
+// memory compiles to a generic load, which is slower).
+__device__ __forceinline__ float4 lds_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
