@@ -163,8 +163,11 @@ __global__ void __launch_bounds__(384, 1)
 
   const uint32_t warp = warp_id(), lane = lane_id();
   const int n_bh = p.B * p.Hq;
-  const int pair = p.n_pairs - 1 - (int)(blockIdx.x / n_bh);  // heaviest causal pairs first
-  const int bh = (int)(blockIdx.x % n_bh);
+  // Head-major order: the CTAs that run at the same time share few heads, so each K/V tile
+  // comes from HBM about once and from L2 for the other query tiles of its head; within a
+  // head the heaviest causal pairs go first.
+  const int pair = p.n_pairs - 1 - (int)(blockIdx.x % p.n_pairs);
+  const int bh = (int)(blockIdx.x / p.n_pairs);
   const int b = bh / p.Hq, h = bh % p.Hq;
   const int kvz = b * p.Hkv + h / (p.Hq / p.Hkv);
   const int n_ktiles = (p.S + Cfg::BN - 1) / Cfg::BN;

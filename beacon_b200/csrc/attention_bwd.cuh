@@ -236,8 +236,12 @@ __global__ void __launch_bounds__(384, 1)
 
   const uint32_t warp = warp_id(), lane = lane_id();
   const int n_kvh = p.B * p.Hkv;
-  const int jt = (int)(blockIdx.x / n_kvh);  // key tile: 0 first (the most causal work)
-  const int kvz = (int)(blockIdx.x % n_kvh);
+  // Head-major order: the CTAs that run at the same time share few heads, so each Q/dO tile
+  // comes from HBM about once and from L2 for the other key tiles of its head; within a
+  // head key tile 0 (the most causal work) goes first.
+  const int n_kt = (p.S + 127) / 128;
+  const int jt = (int)(blockIdx.x % n_kt);
+  const int kvz = (int)(blockIdx.x / n_kt);
   const int b = kvz / p.Hkv, hk = kvz % p.Hkv;
   const int group = p.Hq / p.Hkv;
   const int j0 = jt * 128;
@@ -508,16 +512,50 @@ __global__ void __launch_bounds__(384, 1)
 }
 
 // ---------------------------------------------------------------------------
-// 3. dQ.  Per key tile j of the CTA's 128 queries (thread = query row, so lse2 and Dt
-//    are per-thread registers):
-//   S(j)  = Q K_j^T -> TMEM [128 (j&1), +128)  (double-buffered: S(j+1) is computed while
-//                                               the warps work on tile j)
-//   dP(j) = dO V_j^T -> TMEM [256,384)          (issued once every warp holds dP(j-1))
+// 3. dQ.  Persistent: one CTA per SM walks work items (128-query tile, query head),
+//    heaviest causal tiles first, item w = blockIdx.x + k * gridDim.x.  Per key tile of
+//    an item (thread = query row, so lse2 and Dt are per-thread registers):
+//   S(t)  = Q K_j^T -> TMEM [128 (t&1), +128)  (double-buffered: S(t+1) is computed while
+//                                               the warps work on tile t)
+//   dP(t) = dO V_j^T -> TMEM [256,384)          (issued once every warp holds dP(t-1))
 //   softmax warp (g, quarter): query rows 32*quarter.., key columns 64g..64g+63 in two
 //   chunks; dS = P (dP - Dt), P = exp2(S * scale*log2e - lse2), bf16 -> TMEM over the S
 //   columns already read, then  dQ += dS K_j  with A read from TMEM.
+//   t counts key tiles over all of the CTA's items, so the rings, the S buffers and the
+//   barrier phases run on across items: the next item's S and dP are computed while the
+//   warps finish the current one and store its dQ, and its Q (dO) loads as soon as the
+//   current item's last S (dP) has read Q (dO).  The first dQ MMA of an item waits until
+//   the warps have read the previous item's dQ out of TMEM.
 // TMEM: S [0,256) | dP [256,384) | dQ [384,384+D).
 // ---------------------------------------------------------------------------
+struct DqItem {
+  bool valid;
+  int w, ci, j, n_kt, it, bh, kvz;
+};
+
+// Work item `w` (the ci-th of this CTA), positioned at its key tile 0.
+__device__ __forceinline__ DqItem dq_item(const AttnBwdParams& p, int w, int ci) {
+  DqItem x;
+  const int n_bh = p.B * p.Hq, n_qt = (p.S + 127) / 128;
+  x.valid = w < n_qt * n_bh;
+  x.w = w;
+  x.ci = ci;
+  x.j = 0;
+  // head-major (the items in flight share few heads, so K/V tiles are re-read from L2, not
+  // HBM); within a head the last query tile (most causal work) first
+  x.it = n_qt - 1 - w % n_qt;
+  x.bh = w / n_qt;
+  x.kvz = (x.bh / p.Hq) * p.Hkv + (x.bh % p.Hq) / (p.Hq / p.Hkv);
+  x.n_kt = p.causal ? x.it + 1 : n_qt;
+  return x;
+}
+
+// The key tile after `x`: the next tile of the item, or tile 0 of the CTA's next item.
+__device__ __forceinline__ DqItem dq_next(const AttnBwdParams& p, DqItem x) {
+  if (++x.j < x.n_kt) return x;
+  return dq_item(p, x.w + (int)gridDim.x, x.ci + 1);
+}
+
 template <int D>
 __global__ void __launch_bounds__(384, 1)
     k_attn_bwd_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -525,7 +563,7 @@ __global__ void __launch_bounds__(384, 1)
                   const AttnBwdParams p) {
   using Cfg = AttnBwdCfg<D>;
   constexpr uint32_t TILE = Cfg::TILE_BYTES;
-  constexpr int KST = 3;  // K ring depth: S(j+2) is issued while K(j), K(j+1) are in use
+  constexpr int KST = 3;  // K ring depth: S(t+2) is issued while K(t), K(t+1) are in use
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
@@ -533,32 +571,34 @@ __global__ void __launch_bounds__(384, 1)
   uint8_t* sK = sdO + TILE;       // [3]
   uint8_t* sV = sK + KST * TILE;  // [2]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + 2 * TILE);
-  uint64_t* qd_full = bars + 0;
+  uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;    // [3]
   uint64_t* k_empty = bars + 4;   // [3]
   uint64_t* v_full = bars + 7;    // [2]
   uint64_t* v_empty = bars + 9;   // [2]
-  uint64_t* s_full = bars + 11;   // [2] S(j) and dP(j) computed, by S buffer
-  uint64_t* dp_free = bars + 13;  // dP(j) read by all 8 warps
-  uint64_t* ds_chunk = bars + 14; // [2]
-  uint64_t* dq_full = bars + 16;
-  uint64_t* drain = bars + 17;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  uint64_t* s_full = bars + 11;   // [2] S(t) and dP(t) computed, by S buffer
+  uint64_t* dp_free = bars + 13;  // dP(t) read by all 8 warps
+  // [chunk][tile parity]: dS chunk c of tile t stored by all 8 warps.  By tile parity
+  // because the warps may store tile t+1's chunks (S(t+1) and dP(t+1) are issued before
+  // the MMA warp waits for tile t's) before the MMA warp has seen tile t's.
+  uint64_t* ds_chunk = bars + 14;  // [2][2]
+  uint64_t* dq_full = bars + 18;   // an item's dQ complete
+  uint64_t* drain = bars + 19;
+  uint64_t* q_empty = bars + 20;   // Q read by the item's last S
+  uint64_t* do_full = bars + 21;
+  uint64_t* do_empty = bars + 22;  // dO read by the item's last dP
+  uint64_t* dq_free = bars + 23;   // an item's dQ read out of TMEM by all 8 warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   constexpr uint32_t T_S = 0, T_DP = 256, T_DQ = 384;
 
   const uint32_t warp = warp_id(), lane = lane_id();
-  const int n_bh = p.B * p.Hq;
-  const int n_qt = (p.S + 127) / 128;
-  const int it = n_qt - 1 - (int)(blockIdx.x / n_bh);  // query tile: the last (most causal work) first
-  const int bh = (int)(blockIdx.x % n_bh);
-  const int b = bh / p.Hq, h = bh % p.Hq;
-  const int kvz = b * p.Hkv + h / (p.Hq / p.Hkv);
-  const int q0 = it * 128;
-  const int n_kt = p.causal ? it + 1 : n_qt;
 
   if (threadIdx.x == 0) {
-    mbar_init(qd_full, 1);
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    mbar_init(do_full, 1);
+    mbar_init(do_empty, 1);
     for (int i = 0; i < KST; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
@@ -568,9 +608,11 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&ds_chunk[i], 8);
+      mbar_init(&ds_chunk[2 + i], 8);
     }
     mbar_init(dp_free, 8);
     mbar_init(dq_full, 1);
+    mbar_init(dq_free, 8);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbarrier_init();
@@ -588,38 +630,60 @@ __global__ void __launch_bounds__(384, 1)
     warpgroup_reg_dealloc<120>();
     if (warp == 0 && lane == 0) {
       // ---------------------------------------------------------------- producer
+      // per item: Q, then K/V of its key tiles with dO after the first K/V pair (the first
+      // S needs Q and K, the first dP dO and V)
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       tma_prefetch_desc(&tmdO);
-      mbar_arrive_expect_tx(qd_full, 2 * TILE);
-      tma_load_rows<D>(sQ, &tmQ, qd_full, q0, bh);
-      tma_load_rows<D>(sdO, &tmdO, qd_full, q0, bh);
-      uint32_t kiss = 0, viss = 0, kpar = 0, vpar = 0;
+      uint32_t kiss = 0, viss = 0, kpar = 0, vpar = 0, qiss = 0, qpar = 0, diss = 0, dpar = 0;
       bool ok = true;
-      for (int j = 0; j < n_kt && ok; ++j) {
-        const int ks = j % KST, vs = j & 1;
-        const uint32_t kph = (uint32_t)(j / KST) & 1u, vph = (uint32_t)(j >> 1) & 1u;
-        if (!mbar_wait(&k_empty[ks], kph ^ 1u, abort_flag, kSiteQKEmpty)) {
+      uint32_t t = 0;
+      for (DqItem x = dq_item(p, (int)blockIdx.x, 0); x.valid && ok; x = dq_item(p, x.w + (int)gridDim.x, x.ci + 1)) {
+        const uint32_t iph = (uint32_t)x.ci & 1u;
+        if (!mbar_wait(q_empty, iph ^ 1u, abort_flag, kSiteQKEmpty)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&k_full[ks], TILE);
-        tma_load_rows<D>(sK + ks * TILE, &tmK, &k_full[ks], j * 128, kvz);
-        kiss |= 1u << ks;
-        kpar = (kpar & ~(1u << ks)) | (kph << ks);
-        if (!mbar_wait(&v_empty[vs], vph ^ 1u, abort_flag, kSiteQVEmpty)) {
-          ok = false;
-          break;
+        mbar_arrive_expect_tx(q_full, TILE);
+        tma_load_rows<D>(sQ, &tmQ, q_full, x.it * 128, x.bh);
+        qiss = 1;
+        qpar = iph;
+        for (int j = 0; j < x.n_kt; ++j, ++t) {
+          const int ks = (int)(t % KST), vs = (int)(t & 1);
+          const uint32_t kph = (t / KST) & 1u, vph = (t >> 1) & 1u;
+          if (!mbar_wait(&k_empty[ks], kph ^ 1u, abort_flag, kSiteQKEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&k_full[ks], TILE);
+          tma_load_rows<D>(sK + ks * TILE, &tmK, &k_full[ks], j * 128, x.kvz);
+          kiss |= 1u << ks;
+          kpar = (kpar & ~(1u << ks)) | (kph << ks);
+          if (!mbar_wait(&v_empty[vs], vph ^ 1u, abort_flag, kSiteQVEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&v_full[vs], TILE);
+          tma_load_rows<D>(sV + vs * TILE, &tmV, &v_full[vs], j * 128, x.kvz);
+          viss |= 1u << vs;
+          vpar = (vpar & ~(1u << vs)) | (vph << vs);
+          if (j == 0) {
+            if (!mbar_wait(do_empty, iph ^ 1u, abort_flag, kSiteQVEmpty)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(do_full, TILE);
+            tma_load_rows<D>(sdO, &tmdO, do_full, x.it * 128, x.bh);
+            diss = 1;
+            dpar = iph;
+          }
         }
-        mbar_arrive_expect_tx(&v_full[vs], TILE);
-        tma_load_rows<D>(sV + vs * TILE, &tmV, &v_full[vs], j * 128, kvz);
-        viss |= 1u << vs;
-        vpar = (vpar & ~(1u << vs)) | (vph << vs);
       }
       if (!ok) {
         volatile int no_abort = 0;
-        mbar_wait(qd_full, 0, &no_abort, kSiteQDrain);
+        if (qiss) mbar_wait(q_full, qpar, &no_abort, kSiteQDrain);
+        if (diss) mbar_wait(do_full, dpar, &no_abort, kSiteQDrain);
         for (int s = 0; s < KST; ++s)
           if (kiss & (1u << s)) mbar_wait(&k_full[s], (kpar >> s) & 1u, &no_abort, kSiteQDrain);
         for (int s = 0; s < 2; ++s)
@@ -630,36 +694,56 @@ __global__ void __launch_bounds__(384, 1)
       const bool leader = elect_one();
       constexpr uint32_t idesc_q = make_idesc_f16(128, D, false, true);  // dQ: A = dS in TMEM, B = K MN-major
       const uint32_t q_addr = smem_u32(sQ), do_addr = smem_u32(sdO);
-      bool ok = warp_wait(qd_full, 0, abort_flag, kSiteQQd);
-      auto issue_s = [&](int j) -> bool {  // S(j) into buffer j&1
-        if (!warp_wait(&k_full[j % KST], (uint32_t)(j / KST) & 1u, abort_flag, kSiteQKFull)) return false;
+      auto issue_s = [&](const DqItem& x, uint32_t t) -> bool {  // S(t) into buffer t&1
+        if (x.j == 0 && !warp_wait(q_full, (uint32_t)x.ci & 1u, abort_flag, kSiteQQd)) return false;
+        if (!warp_wait(&k_full[t % KST], (t / KST) & 1u, abort_flag, kSiteQKFull)) return false;
         tc_fence_after();
-        issue_score_tile<D>(leader, tmem + T_S + 128 * (j & 1), q_addr, smem_u32(sK + (j % KST) * TILE));
+        issue_score_tile<D>(leader, tmem + T_S + 128 * (t & 1), q_addr, smem_u32(sK + (t % KST) * TILE));
+        if (x.j == x.n_kt - 1 && leader) umma_commit(q_empty);  // the item's last S has read Q
         return true;
       };
-      auto issue_dp = [&](int j) -> bool {  // dP(j); then S(j) and dP(j) are announced together
-        if (!warp_wait(&v_full[j & 1], (uint32_t)(j >> 1) & 1u, abort_flag, kSiteQVFull)) return false;
+      auto issue_dp = [&](const DqItem& x, uint32_t t) -> bool {  // dP(t); then S(t) and dP(t) are announced
+        if (x.j == 0 && !warp_wait(do_full, (uint32_t)x.ci & 1u, abort_flag, kSiteQQd)) return false;
+        if (!warp_wait(&v_full[t & 1], (t >> 1) & 1u, abort_flag, kSiteQVFull)) return false;
         tc_fence_after();
-        issue_score_tile<D>(leader, tmem + T_DP, do_addr, smem_u32(sV + (j & 1) * TILE));
-        if (leader) umma_commit(&v_empty[j & 1]);
-        if (leader) umma_commit(&s_full[j & 1]);
+        issue_score_tile<D>(leader, tmem + T_DP, do_addr, smem_u32(sV + (t & 1) * TILE));
+        if (leader) umma_commit(&v_empty[t & 1]);
+        if (leader) umma_commit(&s_full[t & 1]);
+        if (x.j == x.n_kt - 1 && leader) umma_commit(do_empty);  // the item's last dP has read dO
         return true;
       };
-      if (ok && n_kt > 0) ok = issue_s(0) && issue_dp(0) && (n_kt < 2 || issue_s(1));
-      for (int j = 0; j < n_kt && ok; ++j) {
-        const uint32_t sb = T_S + 128 * (j & 1);
-        const uint32_t k_addr = smem_u32(sK + (j % KST) * TILE);
-        if (!warp_wait(dp_free, (uint32_t)j & 1u, abort_flag, kSiteQDpFree)) {
+      DqItem xq = dq_item(p, (int)blockIdx.x, 0);  // tile t: dQ
+      DqItem xp = xq, xs = xq;                     // tiles t+1: dP, t+2: S
+      bool ok = true;
+      if (xs.valid) {
+        ok = issue_s(xs, 0) && issue_dp(xp, 0);
+        xs = dq_next(p, xs);
+        xp = dq_next(p, xp);
+        if (ok && xs.valid) ok = issue_s(xs, 1);
+        xs = dq_next(p, xs);
+      }
+      for (uint32_t t = 0; xq.valid && ok; ++t, xq = dq_next(p, xq)) {
+        const uint32_t sb = T_S + 128 * (t & 1);
+        const uint32_t k_addr = smem_u32(sK + (t % KST) * TILE);
+        if (!warp_wait(dp_free, t & 1u, abort_flag, kSiteQDpFree)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (j + 1 < n_kt && !issue_dp(j + 1)) {
+        if (xp.valid) {
+          if (!issue_dp(xp, t + 1)) {
+            ok = false;
+            break;
+          }
+          xp = dq_next(p, xp);
+        }
+        // the item's first dQ MMA overwrites the accumulator: the previous item's dQ must be out
+        if (xq.j == 0 && xq.ci > 0 && !warp_wait(dq_free, (uint32_t)(xq.ci - 1) & 1u, abort_flag, kSiteQDqFull)) {
           ok = false;
           break;
         }
         for (int c = 0; c < 2 && ok; ++c) {
-          if (!warp_wait(&ds_chunk[c], (uint32_t)j & 1u, abort_flag, kSiteQDsFull)) {
+          if (!warp_wait(&ds_chunk[2 * c + (t & 1)], (t >> 1) & 1u, abort_flag, kSiteQDsFull)) {
             ok = false;
             break;
           }
@@ -667,19 +751,22 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
           for (int i = 0; i < 4; ++i) {  // this chunk's K-steps: 16 keys each
             const int kk = (i >> 1) * 4 + 2 * c + (i & 1);
-            const uint32_t acc = (j > 0 || c > 0 || i > 0) ? 1u : 0u;
+            const uint32_t acc = (xq.j > 0 || c > 0 || i > 0) ? 1u : 0u;
             if (leader) umma_f16_ts(tmem + T_DQ, tmem + sb + (uint32_t)((kk >> 2) * 64 + (kk & 3) * 8),
                         make_sdesc_sw128(k_addr + kk * 2048, 16384, 1024), idesc_q, acc);
           }
         }
         if (!ok) break;
-        if (leader) umma_commit(&k_empty[j % KST]);  // K(j) read by S(j) and dQ(j)
-        if (j + 2 < n_kt && !issue_s(j + 2)) {  // behind dQ(j), which read dS(j) from that buffer
-          ok = false;
-          break;
+        if (leader) umma_commit(&k_empty[t % KST]);  // K(t) read by S(t) and dQ(t)
+        if (xq.j == xq.n_kt - 1 && leader) umma_commit(dq_full);
+        if (xs.valid) {  // behind dQ(t), which read dS(t) from that buffer
+          if (!issue_s(xs, t + 2)) {
+            ok = false;
+            break;
+          }
+          xs = dq_next(p, xs);
         }
       }
-      if (ok && leader) umma_commit(dq_full);
       if (leader) umma_commit(drain);
       volatile int no_abort = 0;
       warp_wait(drain, 0, &no_abort, kSiteQDrain);
@@ -690,65 +777,74 @@ __global__ void __launch_bounds__(384, 1)
     const uint32_t quarter = warp & 3u;
     const int g = (int)(warp - 4) >> 2;        // key-column half (softmax) / head-dim half (epilogue)
     const int r = (int)(quarter * 32 + lane);  // TMEM lane = query row
-    const int qi = q0 + r;
     const uint32_t lane_base = (quarter * 32u) << 16;
-    const long long srow = (long long)bh * p.S_pad + qi;  // padded rows: -lse2 = -inf, Dt = 0
-    const float nl2 = __ldg(p.lse2 + srow), dtr = __ldg(p.dt + srow);
     bool ok = true;
-    for (int j = 0; j < n_kt && ok; ++j) {
-      const uint32_t sb = T_S + 128 * (j & 1) + 64 * g;
-      const int k0 = j * 128 + 64 * g;
-      // keys at or beyond S, and (causal) keys after the query, are masked
-      const bool masked = (k0 + 64 > p.S) || (p.causal && j == it);
-      const int klim = p.causal ? min(p.S - k0, qi - k0 + 1) : p.S - k0;
-      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (uint32_t)(j >> 1) & 1u, abort_flag, kSiteQSFull))) {
+    uint32_t t = 0;
+    for (DqItem x = dq_item(p, (int)blockIdx.x, 0); x.valid && ok; x = dq_item(p, x.w + (int)gridDim.x, x.ci + 1)) {
+      const int qi = x.it * 128 + r;
+      const long long srow = (long long)x.bh * p.S_pad + qi;  // padded rows: -lse2 = -inf, Dt = 0
+      const float nl2 = __ldg(p.lse2 + srow), dtr = __ldg(p.dt + srow);
+      for (int j = 0; j < x.n_kt; ++j, ++t) {
+        const uint32_t sb = T_S + 128 * (t & 1) + 64 * g;
+        const int k0 = j * 128 + 64 * g;
+        // keys at or beyond S, and (causal) keys after the query, are masked
+        const bool masked = (k0 + 64 > p.S) || (p.causal && j == x.it);
+        const int klim = p.causal ? min(p.S - k0, qi - k0 + 1) : p.S - k0;
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t & 1], (t >> 1) & 1u, abort_flag, kSiteQSFull))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t s[2][32], dp[2][32];
+        tmem_ld32(tmem + lane_base + sb, s[0]);
+        tmem_ld32(tmem + lane_base + T_DP + 64 * g, dp[0]);
+        tmem_ld32(tmem + lane_base + sb + 32, s[1]);
+        tmem_ld32(tmem + lane_base + T_DP + 64 * g + 32, dp[1]);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dp_free);  // dP(t+1) may overwrite dP(t)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t pk[16];
+          if (masked)
+            dq_ds_chunk<true>(s[c], dp[c], p.scale_log2, nl2, dtr, klim - 32 * c, pk);
+          else
+            dq_ds_chunk<false>(s[c], dp[c], p.scale_log2, nl2, dtr, klim - 32 * c, pk);
+          tmem_st16(tmem + lane_base + sb + 16 * c, pk);  // over S columns this thread has read
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ds_chunk[2 * c + (t & 1)]);
+        }
+      }
+      if (!ok) break;
+      // dQ rows: this warp stores head-dim columns [g D/2, (g+1) D/2)
+      if (!__all_sync(0xffffffffu, mbar_wait(dq_full, (uint32_t)x.ci & 1u, abort_flag, kSiteQDqFull))) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t s[2][32], dp[2][32];
-      tmem_ld32(tmem + lane_base + sb, s[0]);
-      tmem_ld32(tmem + lane_base + T_DP + 64 * g, dp[0]);
-      tmem_ld32(tmem + lane_base + sb + 32, s[1]);
-      tmem_ld32(tmem + lane_base + T_DP + 64 * g + 32, dp[1]);
+      uint32_t a[D / 64][32];
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) tmem_ld32(tmem + lane_base + T_DQ + g * (D / 2) + c * 32, a[c]);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(dp_free);  // dP(j+1) may overwrite dP(j)
+      if (lane == 0) mbar_arrive(dq_free);  // the next item's dQ may start
+      if (qi < p.S) {
+        __nv_bfloat16* row = p.dq + ((long long)x.bh * p.S + qi) * D + g * (D / 2);
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t pk[16];
-        if (masked)
-          dq_ds_chunk<true>(s[c], dp[c], p.scale_log2, nl2, dtr, klim - 32 * c, pk);
-        else
-          dq_ds_chunk<false>(s[c], dp[c], p.scale_log2, nl2, dtr, klim - 32 * c, pk);
-        tmem_st16(tmem + lane_base + sb + 16 * c, pk);  // over S columns this thread has read
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&ds_chunk[c]);
-      }
-    }
-    // dQ rows: this warp stores head-dim columns [g D/2, (g+1) D/2)
-    if (ok && __all_sync(0xffffffffu, mbar_wait(dq_full, 0, abort_flag, kSiteQDqFull))) {
-      tc_fence_after();
-      __nv_bfloat16* row = p.dq + ((long long)bh * p.S + qi) * D + g * (D / 2);
-#pragma unroll 1
-      for (int c = 0; c < D / 64; ++c) {
-        uint32_t a[32];
-        tmem_ld32(tmem + lane_base + T_DQ + g * (D / 2) + c * 32, a);
-        tmem_wait_ld();
-        if (qi < p.S) {
+        for (int c = 0; c < D / 64; ++c)
 #pragma unroll
           for (int e = 0; e < 32; e += 8) {
             uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(a[e + 0]) * p.scale, __uint_as_float(a[e + 1]) * p.scale);
-            w.y = pack_bf16x2(__uint_as_float(a[e + 2]) * p.scale, __uint_as_float(a[e + 3]) * p.scale);
-            w.z = pack_bf16x2(__uint_as_float(a[e + 4]) * p.scale, __uint_as_float(a[e + 5]) * p.scale);
-            w.w = pack_bf16x2(__uint_as_float(a[e + 6]) * p.scale, __uint_as_float(a[e + 7]) * p.scale);
+            w.x = pack_bf16x2(__uint_as_float(a[c][e + 0]) * p.scale, __uint_as_float(a[c][e + 1]) * p.scale);
+            w.y = pack_bf16x2(__uint_as_float(a[c][e + 2]) * p.scale, __uint_as_float(a[c][e + 3]) * p.scale);
+            w.z = pack_bf16x2(__uint_as_float(a[c][e + 4]) * p.scale, __uint_as_float(a[c][e + 5]) * p.scale);
+            w.w = pack_bf16x2(__uint_as_float(a[c][e + 6]) * p.scale, __uint_as_float(a[c][e + 7]) * p.scale);
             *reinterpret_cast<uint4*>(row + c * 32 + e) = w;
           }
-        }
       }
     }
   }

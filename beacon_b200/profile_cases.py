@@ -73,6 +73,11 @@ def main(argv=None):
     kms = ms / max(n, 1)
     print(f"{a.case}: {kname} {kms:.4f} ms/launch {flops / (kms * 1e-3) / 1e12:.1f} TFLOP/s; "
           f"call {e0.elapsed_time(e1) / a.iters:.4f} ms", flush=True)
+    if a.case.startswith("attn_bwd"):  # the dQ kernel of the same calls: 3 of the backward's 5 products
+        qms, qn = ops.profile_read("k_attn_bwd_dq")
+        qms /= max(qn, 1)
+        print(f"{a.case}: k_attn_bwd_dq {qms:.4f} ms/launch {0.6 * flops / (qms * 1e-3) / 1e12:.1f} TFLOP/s executed",
+              flush=True)
     ops.device_status(0)
     return 0
 
