@@ -7,8 +7,12 @@
 //
 //   MMA issue order:   S_A(0) S_B(0) | O_A += P_A(j) V_j, S_A(j+1), O_B += P_B(j) V_j, S_B(j+1) | ...
 //
+// with each PV product issued in two 64-key halves, each as soon as the softmax warps have
+// stored that half of P, so the tensor core starts on P while the warps finish it.
+//
 //   warp 0      TMA producer: Q_A, Q_B once, then K_j and V_j into 2-deep rings.
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer.
+//   warp 1      TMEM allocator + tcgen05.mma issuer (the whole warp runs the issue loop,
+//               one elected lane issues).
 //   warps 2-3   idle; warps 0-3 hand most of their registers to the softmax warpgroups
 //               (setmaxnreg), so a thread holds its whole S row without spilling.
 //   warps 4-7   softmax of tile A, warps 8-11 softmax of tile B: one query row per
@@ -112,8 +116,11 @@ constexpr uint32_t kPolyPairs = 0x11u;
 // P = 2^(x * scale_log2 - m) for one 128-wide S row, packed to bf16 pairs into the
 // 64 TMEM columns at `taddr`; returns the row sum of P (fp32, before rounding).  The
 // argument and the running sums use packed f32x2 instructions.
+// After each 64-key half is stored, the warp arrives on p_half[half]: the PV MMA of that
+// half starts while the warp works on the other.
 template <bool POLY>
-__device__ __forceinline__ float softmax_p_to_tmem(const float* x, float scale_log2, float neg_m, uint32_t taddr) {
+__device__ __forceinline__ float softmax_p_to_tmem(const float* x, float scale_log2, float neg_m, uint32_t taddr,
+                                                   uint64_t* p_half) {
   float ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
@@ -133,6 +140,10 @@ __device__ __forceinline__ float softmax_p_to_tmem(const float* x, float scale_l
       pk[e] = pack_bf16x2(p0, p1);
     }
     tmem_st32(taddr + 32 * c, pk);
+    tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane_id() == 0) mbar_arrive(&p_half[c]);
   }
   return (ls[0] + ls[1]) + (ls[2] + ls[3]);
 }
@@ -154,8 +165,7 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* v_full = bars + 5;    // [2]
   uint64_t* v_empty = bars + 7;   // [2]
   uint64_t* s_full = bars + 9;    // [2] per tile
-  uint64_t* p_full = bars + 11;   // [2] per tile
-  uint64_t* pv_done = bars + 13;  // [2] per tile
+  uint64_t* p_full = bars + 11;   // [2][2] per tile and 64-key half: P stored by its 4 warps
   uint64_t* o_full = bars + 15;   // [2] per tile
   uint64_t* drain = bars + 17;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
@@ -189,8 +199,8 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4);
-      mbar_init(&pv_done[i], 1);
+      mbar_init(&p_full[2 * i], 4);
+      mbar_init(&p_full[2 * i + 1], 4);
       mbar_init(&o_full[i], 1);
     }
     mbar_init(drain, 1);
@@ -285,12 +295,18 @@ __global__ void __launch_bounds__(384, 1)
           const uint32_t v_addr = smem_u32(sV + st * Cfg::KV_BYTES);
           for (int t = 0; t < 2 && ok; ++t) {
             if (j >= nkv[t]) continue;
-            if (!warp_wait(&p_full[t], (uint32_t)j & 1u, abort_flag, kSiteAttnPFull)) { ok = false; break; }
-            tc_fence_after();
+            // O_t += P_t V_j, P_t from TMEM (K = 128 keys), each 64-key half as soon as it is stored
+            for (int hf = 0; hf < 2 && ok; ++hf) {
+              if (!warp_wait(&p_full[2 * t + hf], (uint32_t)j & 1u, abort_flag, kSiteAttnPFull)) { ok = false; break; }
+              tc_fence_after();
   #pragma unroll
-            for (int kk = 0; kk < 128 / 16; ++kk)  // O_t += P_t V_j, P_t from TMEM (K = 128 keys)
-              if (leader) umma_f16_ts(tmem + Cfg::O_COL0 + t * D, tmem + (Cfg::S_COL_STRIDE * t) + kk * 8,
-                          make_sdesc_sw128(v_addr + kk * 2048, 128 * 128, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+              for (int k4 = 0; k4 < 4; ++k4) {
+                const int kk = 4 * hf + k4;
+                if (leader) umma_f16_ts(tmem + Cfg::O_COL0 + t * D, tmem + (Cfg::S_COL_STRIDE * t) + kk * 8,
+                            make_sdesc_sw128(v_addr + kk * 2048, 128 * 128, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+              }
+            }
+            if (!ok) break;
             if (j == nkv[t] - 1 && leader) umma_commit(&o_full[t]);
             if (j + 1 < nkv[t]) {
               if (!k_next) {
@@ -381,13 +397,9 @@ __global__ void __launch_bounds__(384, 1)
       }
       // P = exp2(x * scale_log2 - m_used) -> bf16 pairs into TMEM columns [s_col, s_col + 64)
       if (unmasked)
-        l += softmax_p_to_tmem<true>(x, p.scale_log2, -m_used, tmem + lane_base + s_col);
+        l += softmax_p_to_tmem<true>(x, p.scale_log2, -m_used, tmem + lane_base + s_col, &p_full[2 * t]);
       else
-        l += softmax_p_to_tmem<false>(x, p.scale_log2, -m_used, tmem + lane_base + s_col);
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[t]);
+        l += softmax_p_to_tmem<false>(x, p.scale_log2, -m_used, tmem + lane_base + s_col, &p_full[2 * t]);
     }
     // epilogue: O / l -> bf16, LSE
     if (ok && nkv[t] > 0 && __all_sync(0xffffffffu, mbar_wait(&o_full[t], 0, abort_flag, kSiteAttnOFull))) {
