@@ -10,8 +10,9 @@
 //                       the caller lacks it.)
 //   2. k_attn_bwd_dkdv  one CTA per (128-key tile, KV head): dK and dV accumulate in TMEM
 //                       over the query tiles (and grouped query heads) that see the keys.
-//   3. k_attn_bwd_dq    one CTA per (128-query tile, query head): dQ accumulates in TMEM
-//                       over the key tiles the queries see, and is stored once in bf16.
+//   3. k_attn_bwd_dq    persistent, one CTA per SM over (128-query tile, query head)
+//                       items: dQ accumulates in TMEM over the key tiles the queries
+//                       see, and is stored once in bf16.
 // Each score tile is therefore computed twice.  The alternative -- one pass that adds
 // every key tile's dQ contribution into an fp32 array in global memory -- moves 64 KB
 // of fp32 reductions per tile through L2, which is both slower than the repeated S and
@@ -20,8 +21,9 @@
 // Both main kernels run 12 warps: warp 0 loads with TMA, warp 1 issues tcgen05.mma (the
 // whole warp runs the issue loop, one elected lane issues), warps 2-3 idle, and warps
 // 4-11 (two warpgroups, 2 warps per SM sub-partition) do the elementwise work; warps 0-3
-// hand most of their registers to warps 4-11 (setmaxnreg: 128 x 120 + 256 x 192 = 384 x 168, the launch allocation;
-// the MMA issuer keeps 120 registers so that no descriptor is spilled).
+// hand most of their registers to warps 4-11 (setmaxnreg: 128 x 120 + 256 x 192 = 384 x
+// 168, the launch allocation; the MMA issuer keeps 120 registers so that no descriptor
+// is spilled).
 // Every MMA is M=128 x N=128 (N=64 MMAs take as long as N=128 ones on this tensor core).
 #pragma once
 
@@ -189,13 +191,12 @@ __device__ __forceinline__ void dq_ds_chunk(const uint32_t (&sc)[32], const uint
 //   (R_S(n) = X for even n, Y for odd n; R_P(n) is the other one), so the next tile's
 //   S^T goes into the region whose dP^T the warps have just read, and its dP^T into the
 //   region whose P^T / dS^T the dV / dK MMAs have just read.  MMA issue order per tile:
+//     dV(n) += P^T(n) dO(n)   as soon as P^T(n) is stored
 //     S^T(n+1) -> R_P(n)      as soon as every warp holds dP^T(n)
 //     dK(n) += dS^T(n) Q(n)   as soon as dS^T(n) is stored
-//     dV(n) += P^T(n) dO(n)
-//     dP^T(n+1) -> R_S(n)     after dK(n) and dV(n) in issue order (MMAs run in order)
-//   so the warps' dS phase (short) overlaps S^T(n+1) and their P phase (long: the
-//   exponentials) overlaps dK(n-1), dV(n-1) and dP^T(n): 32 MMAs of N=128 per tile, the
-//   tensor pipe idle only while the warps hand dP^T over.
+//     dP^T(n+1) -> R_S(n)     after dV(n) and dK(n) in issue order (MMAs run in order)
+//   so the warps' dS phase (short) overlaps dV(n) and S^T(n+1), and their P phase (long:
+//   the exponentials) overlaps dK(n-1) and dP^T(n): 32 MMAs of N=128 per tile.
 //   Softmax warp (g, quarter): key rows 32*quarter.., queries 64g..64g+63; over the 64
 //   S^T columns it has read it writes
 //     P^T  = exp2(S^T * scale*log2e - lse2[q])   bf16 -> R_S(n) + [64g, 64g+32)
@@ -364,11 +365,14 @@ __global__ void __launch_bounds__(384, 1)
         const bool more = n + 1 < n_iter;
         const uint32_t rs = (n & 1) ? 128u : 0u, rp = 128u - rs;  // R_S(n), R_P(n)
         const uint32_t q_addr = smem_u32(sQ + st * TILE), do_addr = smem_u32(sdO + st * TILE);
-        // S^T(n+1) as soon as R_P(n) is free: the warps' next P phase waits for it.  dV(n)
-        // waits with dK(n) for dS^T(n): the three products of that group (24 MMAs) then run
-        // during the next P phase, the longest stretch of the warps' work.
-        if (!warp_wait(p_ready, par, abort_flag, kSiteBwdDsFull) || !warp_wait(rp_free, par, abort_flag, kSiteBwdDsFull))
-          break;
+        // dV(n) as soon as P^T(n) is stored (the warps then wait for dP^T(n) and read it);
+        // S^T(n+1) as soon as R_P(n) is free (the warps' next P phase waits for it); dK(n)
+        // and dP^T(n+1) once dS^T(n) is stored, so dP^T(n+1) is done early in the next P phase.
+        if (!warp_wait(p_ready, par, abort_flag, kSiteBwdDsFull)) break;
+        tc_fence_after();
+        issue_kv(T_DV, rs, do_addr, n == 0);
+        if (leader) umma_commit(&do_empty[st]);  // dO(n) read by dP^T(n) and dV(n)
+        if (!warp_wait(rp_free, par, abort_flag, kSiteBwdDsFull)) break;
         if (more) {
           if (!warp_wait(&q_full[st1], ((n + 1) >> 1) & 1, abort_flag, kSiteBwdQDFull)) break;
           tc_fence_after();
@@ -379,9 +383,7 @@ __global__ void __launch_bounds__(384, 1)
         tc_fence_after();
         issue_kv(T_DK, rs + 32, q_addr, n == 0);
         if (leader) umma_commit(&q_empty[st]);  // Q(n) read by S^T(n) and dK(n)
-        issue_kv(T_DV, rs, do_addr, n == 0);
-        if (leader) umma_commit(&do_empty[st]);  // dO(n) read by dP^T(n) and dV(n)
-        if (more) {  // into R_S(n), behind dK(n) and dV(n), which read P^T / dS^T(n) from it
+        if (more) {  // into R_S(n), behind dV(n) and dK(n), which read P^T / dS^T(n) from it
           if (!warp_wait(&do_full[st1], ((n + 1) >> 1) & 1, abort_flag, kSiteBwdQDFull)) break;
           tc_fence_after();
           issue_score_tile<D>(leader, tmem + rs, v_addr, smem_u32(sdO + st1 * TILE));
