@@ -48,8 +48,14 @@ template <int D>
 struct AttnBwdCfg {
   static constexpr uint32_t TILE_BYTES = 128 * D * 2;   // one 128-row tile of Q, K, V or dO
   static constexpr uint32_t STATS_BYTES = 2 * 128 * 4;  // lse2 and Dt of one query tile
-  // dK/dV kernel: K, V, then two stages of (Q, dO) and two of the statistics.
-  static constexpr size_t DKDV_SMEM = 1024 + 6 * (size_t)TILE_BYTES + 2 * STATS_BYTES + 256;
+  // dK/dV kernel: K, V, three stages of Q (with lse2), two of dO (with Dt), barriers.  The
+  // 128-byte swizzled tiles need a 1024-byte aligned base; the window is allotted only 256
+  // bytes of alignment slack (the whole 227 KB is in use), and the kernel reports
+  // kFaultSmemAlign and does nothing if the window's placement needs more.
+  static constexpr int DKDV_QST = 3;
+  static constexpr uint32_t DKDV_BODY = (2 + DKDV_QST + 2) * TILE_BYTES + (DKDV_QST + 2) * 512 + 256;
+  static constexpr uint32_t DKDV_SLACK = 256;
+  static constexpr size_t DKDV_SMEM = (size_t)DKDV_BODY + DKDV_SLACK;
   // dQ kernel: Q, dO, three K stages, two V stages.
   static constexpr size_t DQ_SMEM = 1024 + 7 * (size_t)TILE_BYTES + 256;
   static constexpr int THREADS = 384;
@@ -213,25 +219,31 @@ __global__ void __launch_bounds__(384, 1)
   constexpr uint32_t TILE = Cfg::TILE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  if ((uint32_t)(smem - smem_raw) > Cfg::DKDV_SLACK) {  // uniform over the CTA: nothing has started
+    if (threadIdx.x == 0) record_fault(kFaultSmemAlign, kSiteBwdKV);
+    return;
+  }
   uint8_t* sK = smem;
   uint8_t* sV = sK + TILE;
-  uint8_t* sQ = sV + TILE;       // [2]
-  uint8_t* sdO = sQ + 2 * TILE;  // [2]
-  float* sStats = reinterpret_cast<float*>(sdO + 2 * TILE);  // [2][256]: lse2 [0,128), Dt [128,256)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sStats + 2 * 256);
+  constexpr int QST = Cfg::DKDV_QST;
+  uint8_t* sQ = sV + TILE;         // [QST]
+  uint8_t* sdO = sQ + QST * TILE;  // [2]
+  float* sLse = reinterpret_cast<float*>(sdO + 2 * TILE);  // [QST][128] lse2, with Q
+  float* sDt = sLse + QST * 128;                            // [2][128] Dt, with dO
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDt + 2 * 128);
   uint64_t* kv_full = bars + 0;
-  uint64_t* q_full = bars + 1;     // [2] Q and lse2 of a query tile
-  uint64_t* q_empty = bars + 3;    // [2] Q read by S^T and dK
-  uint64_t* do_full = bars + 5;    // [2] dO and Dt of a query tile
-  uint64_t* do_empty = bars + 7;   // [2] dO read by dP^T and dV
-  uint64_t* s_full = bars + 9;     // S^T(n) computed
-  uint64_t* dp_full = bars + 10;   // dP^T(n) computed
-  uint64_t* p_ready = bars + 11;   // P^T(n) stored by all 8 warps
-  uint64_t* rp_free = bars + 12;   // dP^T(n) read by all 8 warps: R_P(n) may take S^T(n+1)
-  uint64_t* ds_ready = bars + 13;  // dS^T(n) stored by all 8 warps
-  uint64_t* dkv_full = bars + 14;
-  uint64_t* drain = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* q_full = bars + 1;     // [3] Q and lse2 of a query tile
+  uint64_t* q_empty = bars + 4;    // [3] Q read by S^T and dK
+  uint64_t* do_full = bars + 7;    // [2] dO and Dt of a query tile
+  uint64_t* do_empty = bars + 9;   // [2] dO read by dP^T and dV
+  uint64_t* s_full = bars + 11;    // S^T(n) computed
+  uint64_t* dp_full = bars + 12;   // dP^T(n) computed
+  uint64_t* p_ready = bars + 13;   // P^T(n) stored by all 8 warps
+  uint64_t* rp_free = bars + 14;   // dP^T(n) read by all 8 warps: R_P(n) may take S^T(n+1)
+  uint64_t* ds_ready = bars + 15;  // dS^T(n) stored by all 8 warps
+  uint64_t* dkv_full = bars + 16;
+  uint64_t* drain = bars + 17;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   constexpr uint32_t T_DV = 256, T_DK = 256 + D;
 
@@ -253,9 +265,11 @@ __global__ void __launch_bounds__(384, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < QST; ++i) {
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&do_full[i], 1);
       mbar_init(&do_empty[i], 1);
     }
@@ -289,32 +303,32 @@ __global__ void __launch_bounds__(384, 1)
       mbar_arrive_expect_tx(kv_full, 2 * TILE);
       tma_load_rows<D>(sK, &tmK, kv_full, j0, kvz);
       tma_load_rows<D>(sV, &tmV, kv_full, j0, kvz);
-      // Q (with lse2) and dO (with Dt) have rings of their own: Q(n) is released by dK(n),
-      // a third of a tile before dV(n) releases dO(n), and Q(n+2) is needed first.
+      // Q (with lse2) and dO (with Dt) have rings of their own, Q three deep: Q(n+3) loads
+      // once dK(n) has read Q(n), a whole tile before S^T(n+3) needs it.
       uint32_t qiss = 0, qpar = 0, diss = 0, dpar = 0;
       bool ok = true;
       for (int n = 0; n < n_iter && ok; ++n) {
         const int g = n / iters_per_head, it = it0 + n % iters_per_head;
         const int bh = b * p.Hq + hk * group + g;
-        const int st = n & 1;
-        const uint32_t ph = (n >> 1) & 1;
+        const int st = n & 1, qs = n % QST;
+        const uint32_t ph = (n >> 1) & 1, qph = (uint32_t)(n / QST) & 1u;
         const long long srow = (long long)bh * p.S_pad + it * 128;
-        if (!mbar_wait(&q_empty[st], ph ^ 1u, abort_flag, kSiteBwdQDEmpty)) {
+        if (!mbar_wait(&q_empty[qs], qph ^ 1u, abort_flag, kSiteBwdQDEmpty)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&q_full[st], TILE + Cfg::STATS_BYTES / 2);
-        tma_load_rows<D>(sQ + st * TILE, &tmQ, &q_full[st], it * 128, bh);
-        bulk_load(sStats + st * 256, p.lse2 + srow, 512, &q_full[st]);
-        qiss |= 1u << st;
-        qpar = (qpar & ~(1u << st)) | (ph << st);
+        mbar_arrive_expect_tx(&q_full[qs], TILE + Cfg::STATS_BYTES / 2);
+        tma_load_rows<D>(sQ + qs * TILE, &tmQ, &q_full[qs], it * 128, bh);
+        bulk_load(sLse + qs * 128, p.lse2 + srow, 512, &q_full[qs]);
+        qiss |= 1u << qs;
+        qpar = (qpar & ~(1u << qs)) | (qph << qs);
         if (!mbar_wait(&do_empty[st], ph ^ 1u, abort_flag, kSiteBwdQDEmpty)) {
           ok = false;
           break;
         }
         mbar_arrive_expect_tx(&do_full[st], TILE + Cfg::STATS_BYTES / 2);
         tma_load_rows<D>(sdO + st * TILE, &tmdO, &do_full[st], it * 128, bh);
-        bulk_load(sStats + st * 256 + 128, p.dt + srow, 512, &do_full[st]);
+        bulk_load(sDt + st * 128, p.dt + srow, 512, &do_full[st]);
         diss |= 1u << st;
         dpar = (dpar & ~(1u << st)) | (ph << st);
         if (n + 1 < n_iter) {  // the tile after: into L2 now, so its load finds it there
@@ -327,10 +341,10 @@ __global__ void __launch_bounds__(384, 1)
       if (!ok) {
         volatile int no_abort = 0;
         mbar_wait(kv_full, 0, &no_abort, kSiteBwdDrain);
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < QST; ++s)
           if (qiss & (1u << s)) mbar_wait(&q_full[s], (qpar >> s) & 1u, &no_abort, kSiteBwdDrain);
+        for (int s = 0; s < 2; ++s)
           if (diss & (1u << s)) mbar_wait(&do_full[s], (dpar >> s) & 1u, &no_abort, kSiteBwdDrain);
-        }
       }
     } else if (warp == 1) {
       // ---------------------------------------------------------------- MMA issuer (whole warp, one elected lane issues)
@@ -364,7 +378,8 @@ __global__ void __launch_bounds__(384, 1)
         const uint32_t par = (uint32_t)n & 1u;
         const bool more = n + 1 < n_iter;
         const uint32_t rs = (n & 1) ? 128u : 0u, rp = 128u - rs;  // R_S(n), R_P(n)
-        const uint32_t q_addr = smem_u32(sQ + st * TILE), do_addr = smem_u32(sdO + st * TILE);
+        const int qs = n % QST, qs1 = (n + 1) % QST;
+        const uint32_t q_addr = smem_u32(sQ + qs * TILE), do_addr = smem_u32(sdO + st * TILE);
         // dV(n) as soon as P^T(n) is stored (the warps then wait for dP^T(n) and read it);
         // S^T(n+1) as soon as R_P(n) is free (the warps' next P phase waits for it); dK(n)
         // and dP^T(n+1) once dS^T(n) is stored, so dP^T(n+1) is done early in the next P phase.
@@ -374,15 +389,15 @@ __global__ void __launch_bounds__(384, 1)
         if (leader) umma_commit(&do_empty[st]);  // dO(n) read by dP^T(n) and dV(n)
         if (!warp_wait(rp_free, par, abort_flag, kSiteBwdDsFull)) break;
         if (more) {
-          if (!warp_wait(&q_full[st1], ((n + 1) >> 1) & 1, abort_flag, kSiteBwdQDFull)) break;
+          if (!warp_wait(&q_full[qs1], (uint32_t)((n + 1) / QST) & 1u, abort_flag, kSiteBwdQDFull)) break;
           tc_fence_after();
-          issue_score_tile<D>(leader, tmem + rp, k_addr, smem_u32(sQ + st1 * TILE));
+          issue_score_tile<D>(leader, tmem + rp, k_addr, smem_u32(sQ + qs1 * TILE));
           if (leader) umma_commit(s_full);
         }
         if (!warp_wait(ds_ready, par, abort_flag, kSiteBwdDsFull)) break;
         tc_fence_after();
         issue_kv(T_DK, rs + 32, q_addr, n == 0);
-        if (leader) umma_commit(&q_empty[st]);  // Q(n) read by S^T(n) and dK(n)
+        if (leader) umma_commit(&q_empty[qs]);  // Q(n) read by S^T(n) and dK(n)
         if (more) {  // into R_S(n), behind dV(n) and dK(n), which read P^T / dS^T(n) from it
           if (!warp_wait(&do_full[st1], ((n + 1) >> 1) & 1, abort_flag, kSiteBwdQDFull)) break;
           tc_fence_after();
@@ -415,12 +430,13 @@ __global__ void __launch_bounds__(384, 1)
       // off-diagonal tiles need no mask: every key < S and every query >= every key
       const bool masked = !keys_full || (p.causal && it == jt);
       const int qmin = p.causal ? kj - q0 : -1;
-      const uint32_t lse2_addr = smem_u32(sStats + st * 256 + 64 * g), dt_addr = lse2_addr + 512;
+      const int qs = n % QST;
+      const uint32_t lse2_addr = smem_u32(sLse + qs * 128 + 64 * g), dt_addr = smem_u32(sDt + st * 128 + 64 * g);
       // first of this warp's 64 query columns that the key sees (64: none)
       const int first_ok = key_ok ? max(qmin - 64 * g, 0) : 64;
       // s_full: the scores; q_full: makes the TMA-written lse2 visible to this thread
       if (!__all_sync(0xffffffffu, mbar_wait(s_full, par, abort_flag, kSiteBwdStFull) &&
-                                       mbar_wait(&q_full[st], (n >> 1) & 1, abort_flag, kSiteBwdQDFull))) {
+                                       mbar_wait(&q_full[qs], (uint32_t)(n / QST) & 1u, abort_flag, kSiteBwdQDFull))) {
         ok = false;
         break;
       }

@@ -26,6 +26,7 @@ __device__ unsigned int g_beacon_status[4];
 enum FaultCode : unsigned int {
   kFaultNone = 0,
   kFaultWaitTimeout = 1,
+  kFaultSmemAlign = 2,  // the dynamic shared-memory window is not placed as the kernel needs
 };
 
 __device__ __forceinline__ void record_fault(unsigned int code, unsigned int site) {
