@@ -72,6 +72,21 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// Work order of the attention kernels: heads in groups of kHeadGroup; within a group the
+// heaviest causal tiles of all its heads first (rank 0 = heaviest), then the next rank.
+// The CTAs in flight then share few heads, so K/V (or Q/dO) tiles come from HBM about once
+// and from L2 after that, and each group still ends with its lightest tiles (a balanced
+// tail).  Linear index w -> (rank, head) for `n_heads` heads of `n_ranks` tiles each.
+constexpr int kHeadGroup = 8;
+__device__ __forceinline__ void grouped_order(int w, int n_heads, int n_ranks, int& rank, int& head) {
+  const int per_group = kHeadGroup * n_ranks;
+  const int g = w / per_group, base = g * kHeadGroup;
+  const int in_group = min(kHeadGroup, n_heads - base);
+  const int r = w - g * per_group;
+  rank = r / in_group;
+  head = base + r % in_group;
+}
+
 // Loads one 128-row x D tile (rows `row0..row0+127` of head `z`) as D/64 swizzled
 // column blocks of 128 rows x 128 bytes.
 template <int D>
@@ -173,11 +188,9 @@ __global__ void __launch_bounds__(384, 1)
 
   const uint32_t warp = warp_id(), lane = lane_id();
   const int n_bh = p.B * p.Hq;
-  // Head-major order: the CTAs that run at the same time share few heads, so each K/V tile
-  // comes from HBM about once and from L2 for the other query tiles of its head; within a
-  // head the heaviest causal pairs go first.
-  const int pair = p.n_pairs - 1 - (int)(blockIdx.x % p.n_pairs);
-  const int bh = (int)(blockIdx.x / p.n_pairs);
+  int pair, bh;  // grouped head order, the heaviest causal pairs of a group first
+  grouped_order((int)blockIdx.x, n_bh, p.n_pairs, pair, bh);
+  pair = p.n_pairs - 1 - pair;
   const int b = bh / p.Hq, h = bh % p.Hq;
   const int kvz = b * p.Hkv + h / (p.Hq / p.Hkv);
   const int n_ktiles = (p.S + Cfg::BN - 1) / Cfg::BN;

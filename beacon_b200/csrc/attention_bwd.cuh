@@ -249,12 +249,9 @@ __global__ void __launch_bounds__(384, 1)
 
   const uint32_t warp = warp_id(), lane = lane_id();
   const int n_kvh = p.B * p.Hkv;
-  // Head-major order: the CTAs that run at the same time share few heads, so each Q/dO tile
-  // comes from HBM about once and from L2 for the other key tiles of its head; within a
-  // head key tile 0 (the most causal work) goes first.
-  const int n_kt = (p.S + 127) / 128;
-  const int jt = (int)(blockIdx.x % n_kt);
-  const int kvz = (int)(blockIdx.x / n_kt);
+  // grouped head order (Q/dO tiles re-read from L2), key tile 0 (the most causal work) first
+  int jt, kvz;
+  grouped_order((int)blockIdx.x, n_kvh, (p.S + 127) / 128, jt, kvz);
   const int b = kvz / p.Hkv, hk = kvz % p.Hkv;
   const int group = p.Hq / p.Hkv;
   const int j0 = jt * 128;
@@ -559,10 +556,15 @@ __device__ __forceinline__ DqItem dq_item(const AttnBwdParams& p, int w, int ci)
   x.w = w;
   x.ci = ci;
   x.j = 0;
-  // head-major (the items in flight share few heads, so K/V tiles are re-read from L2, not
-  // HBM); within a head the last query tile (most causal work) first
-  x.it = n_qt - 1 - w % n_qt;
-  x.bh = w / n_qt;
+  // grouped head order (K/V tiles re-read from L2), the last query tile (most causal work)
+  // first
+  if (x.valid) {
+    grouped_order(w, n_bh, n_qt, x.it, x.bh);
+    x.it = n_qt - 1 - x.it;
+  } else {
+    x.it = 0;
+    x.bh = 0;
+  }
   x.kvz = (x.bh / p.Hq) * p.Hkv + (x.bh % p.Hq) / (p.Hq / p.Hkv);
   x.n_kt = p.causal ? x.it + 1 : n_qt;
   return x;
