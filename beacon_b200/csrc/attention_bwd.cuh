@@ -492,10 +492,14 @@ __global__ void __launch_bounds__(384, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(ds_ready);
     }
-    // final dV (g = 0) / dK (g = 1) rows
+    // final dV (g = 0) / dK (g = 1) rows, staged in the idle Q ring (272-byte row stride:
+    // conflict-free 16-byte stores) and written with one 256-byte bulk copy per row.
+    // Stored straight from registers, a warp's 16-byte stores hit 32 rows 256 bytes apart,
+    // half a sector each, and the epilogue took ~5k cycles per CTA.
     if (ok && __all_sync(0xffffffffu, mbar_wait(dkv_full, 0, abort_flag, kSiteBwdDkvFull))) {
       tc_fence_after();
-      __nv_bfloat16* row = (g == 0 ? p.dv : p.dk) + ((long long)kvz * p.S + kj) * D;
+      constexpr uint32_t kRowStage = D * 2 + 16;
+      uint8_t* srow = sQ + (uint32_t)g * 128u * kRowStage + (uint32_t)r * kRowStage;
       const float sc = g == 0 ? 1.0f : p.scale;
       const uint32_t col = g == 0 ? T_DV : T_DK;
 #pragma unroll 1
@@ -503,17 +507,21 @@ __global__ void __launch_bounds__(384, 1)
         uint32_t a[32];
         tmem_ld32(tmem + lane_base + col + c * 32, a);
         tmem_wait_ld();
-        if (key_ok) {
 #pragma unroll
-          for (int e = 0; e < 32; e += 8) {
-            uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(a[e + 0]) * sc, __uint_as_float(a[e + 1]) * sc);
-            w.y = pack_bf16x2(__uint_as_float(a[e + 2]) * sc, __uint_as_float(a[e + 3]) * sc);
-            w.z = pack_bf16x2(__uint_as_float(a[e + 4]) * sc, __uint_as_float(a[e + 5]) * sc);
-            w.w = pack_bf16x2(__uint_as_float(a[e + 6]) * sc, __uint_as_float(a[e + 7]) * sc);
-            *reinterpret_cast<uint4*>(row + c * 32 + e) = w;
-          }
+        for (int e = 0; e < 32; e += 8) {
+          uint4 w;
+          w.x = pack_bf16x2(__uint_as_float(a[e + 0]) * sc, __uint_as_float(a[e + 1]) * sc);
+          w.y = pack_bf16x2(__uint_as_float(a[e + 2]) * sc, __uint_as_float(a[e + 3]) * sc);
+          w.z = pack_bf16x2(__uint_as_float(a[e + 4]) * sc, __uint_as_float(a[e + 5]) * sc);
+          w.w = pack_bf16x2(__uint_as_float(a[e + 6]) * sc, __uint_as_float(a[e + 7]) * sc);
+          *reinterpret_cast<uint4*>(srow + (c * 32 + e) * 2) = w;
         }
+      }
+      fence_proxy_async_smem();  // generic-proxy stores -> the bulk copy's async proxy
+      if (key_ok) {
+        bulk_store((g == 0 ? p.dv : p.dk) + ((long long)kvz * p.S + kj) * D, srow, D * 2);
+        bulk_commit_group();
+        bulk_wait_group_read0();  // the stage must outlive the copy's reads
       }
     }
   }

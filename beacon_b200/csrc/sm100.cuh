@@ -296,6 +296,13 @@ __device__ __forceinline__ void bulk_reduce_add_f32(float* dst, const void* src,
                "r"(smem_u32(src)), "r"(bytes)
                : "memory");
 }
+// Bulk copy shared -> global (both 16-byte aligned, a multiple of 16 bytes), in the
+// thread's current bulk group.
+__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_u32(src)),
+               "r"(bytes)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Waits until the shared-memory sources of every committed bulk group have been read.
 __device__ __forceinline__ void bulk_wait_group_read0() {
