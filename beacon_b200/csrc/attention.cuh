@@ -418,6 +418,7 @@ __global__ void __launch_bounds__(384, 1)
     if (ok && nkv[t] > 0 && __all_sync(0xffffffffu, mbar_wait(&o_full[t], 0, abort_flag, kSiteAttnOFull))) {
       tc_fence_after();
       const float inv = 1.0f / l;
+      const bool out32 = (reinterpret_cast<uintptr_t>(p.out) & 31u) == 0;
       __nv_bfloat16* orow = p.out + (p.out_tokens ? (((long long)b * p.S + qi) * p.Hq + h) * D
                                                   : ((long long)bh * p.S + qi) * D);
 #pragma unroll 1
@@ -425,15 +426,19 @@ __global__ void __launch_bounds__(384, 1)
         uint32_t u[32];
         tmem_ld32(tmem + lane_base + o_col + c * 32, u);
         tmem_wait_ld();
-        if (qi < p.S) {
+        if (qi < p.S) {  // 32-byte stores where `out` allows: each fills a whole sector of the row
 #pragma unroll
-          for (int e = 0; e < 32; e += 8) {
-            uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(u[e + 0]) * inv, __uint_as_float(u[e + 1]) * inv);
-            w.y = pack_bf16x2(__uint_as_float(u[e + 2]) * inv, __uint_as_float(u[e + 3]) * inv);
-            w.z = pack_bf16x2(__uint_as_float(u[e + 4]) * inv, __uint_as_float(u[e + 5]) * inv);
-            w.w = pack_bf16x2(__uint_as_float(u[e + 6]) * inv, __uint_as_float(u[e + 7]) * inv);
-            *reinterpret_cast<uint4*>(orow + c * 32 + e) = w;
+          for (int e = 0; e < 32; e += 16) {
+            uint32_t w[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              w[i] = pack_bf16x2(__uint_as_float(u[e + 2 * i]) * inv, __uint_as_float(u[e + 2 * i + 1]) * inv);
+            if (out32) {
+              stg256(orow + c * 32 + e, w[0], w[1], w[2], w[3], w[4], w[5], w[6], w[7]);
+            } else {  // out only 16-byte aligned
+              *reinterpret_cast<uint4*>(orow + c * 32 + e) = make_uint4(w[0], w[1], w[2], w[3]);
+              *reinterpret_cast<uint4*>(orow + c * 32 + e + 8) = make_uint4(w[4], w[5], w[6], w[7]);
+            }
           }
         }
       }

@@ -860,18 +860,23 @@ __global__ void __launch_bounds__(384, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_free);  // the next item's dQ may start
-      if (qi < p.S) {
+      if (qi < p.S) {  // 32-byte stores where dQ allows: each fills a whole sector of the row
+        const bool dq32 = (reinterpret_cast<uintptr_t>(p.dq) & 31u) == 0;
         __nv_bfloat16* row = p.dq + ((long long)x.bh * p.S + qi) * D + g * (D / 2);
 #pragma unroll
         for (int c = 0; c < D / 64; ++c)
 #pragma unroll
-          for (int e = 0; e < 32; e += 8) {
-            uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(a[c][e + 0]) * p.scale, __uint_as_float(a[c][e + 1]) * p.scale);
-            w.y = pack_bf16x2(__uint_as_float(a[c][e + 2]) * p.scale, __uint_as_float(a[c][e + 3]) * p.scale);
-            w.z = pack_bf16x2(__uint_as_float(a[c][e + 4]) * p.scale, __uint_as_float(a[c][e + 5]) * p.scale);
-            w.w = pack_bf16x2(__uint_as_float(a[c][e + 6]) * p.scale, __uint_as_float(a[c][e + 7]) * p.scale);
-            *reinterpret_cast<uint4*>(row + c * 32 + e) = w;
+          for (int e = 0; e < 32; e += 16) {
+            uint32_t w[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              w[i] = pack_bf16x2(__uint_as_float(a[c][e + 2 * i]) * p.scale, __uint_as_float(a[c][e + 2 * i + 1]) * p.scale);
+            if (dq32) {
+              stg256(row + c * 32 + e, w[0], w[1], w[2], w[3], w[4], w[5], w[6], w[7]);
+            } else {  // dQ only 16-byte aligned
+              *reinterpret_cast<uint4*>(row + c * 32 + e) = make_uint4(w[0], w[1], w[2], w[3]);
+              *reinterpret_cast<uint4*>(row + c * 32 + e + 8) = make_uint4(w[4], w[5], w[6], w[7]);
+            }
           }
       }
     }

@@ -296,6 +296,14 @@ __device__ __forceinline__ void bulk_reduce_add_f32(float* dst, const void* src,
                "r"(smem_u32(src)), "r"(bytes)
                : "memory");
 }
+// 32-byte global store (a full sector; `p` 32-byte aligned).
+__device__ __forceinline__ void stg256(void* p, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t a4,
+                                       uint32_t a5, uint32_t a6, uint32_t a7) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(a0), "r"(a1), "r"(a2), "r"(a3),
+               "r"(a4), "r"(a5), "r"(a6), "r"(a7)
+               : "memory");
+}
+
 // Bulk copy shared -> global (both 16-byte aligned, a multiple of 16 bytes), in the
 // thread's current bulk group.
 __device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
