@@ -158,3 +158,38 @@ def test_backward_gqa_group4_bf16():
     refs = O.attention_bwd(do, q, k, v, rl)
     for a, r in zip(g, refs):
         assert rel_err(to_np(a), r) <= BF16_TOL
+
+
+def test_outputs_only_16_byte_aligned():
+    """Outputs that are 16- but not 32-byte aligned (views 8 bf16 into a buffer) take the
+    16-byte store path and give the same bits as aligned outputs."""
+    import torch
+    from beacon_b200 import _lib
+    from beacon_b200.errors import check
+    ops = _ops()
+    B, H, S, D = 1, 2, 256, 128
+    q, k, v, do = _qkv(B, H, H, S, D, 9)
+    t = lambda a: to_dev(a, torch.bfloat16)
+    q, k, v, do = t(q), t(k), t(v), t(do)
+    n = B * H * S * D
+
+    def view16(like):
+        buf = torch.empty(n + 16, dtype=torch.bfloat16, device=like.device)
+        out = buf[8:8 + n].view_as(like)
+        assert out.data_ptr() % 32 == 16
+        return out
+
+    ref_out, lse = ops.attention_fwd(q, k, v)
+    out = view16(q)
+    ops.attention_fwd(q, k, v, out=out)
+    assert torch.equal(out, ref_out)
+
+    rq, rk, rv = ops.attention_bwd(do, q, k, v, lse)
+    dq, dk, dv = view16(q), view16(k), view16(v)
+    L = _lib.lib()
+    rc = L.beacon_attention_adjoint_bwd(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), do.data_ptr(), q.data_ptr(),
+                                        k.data_ptr(), v.data_ptr(), lse.data_ptr(), B, H, S, D, 1, _lib.BF16, None, 0,
+                                        torch.cuda.current_stream().cuda_stream)
+    check(rc)
+    torch.cuda.synchronize()
+    assert torch.equal(dq, rq) and torch.equal(dk, rk) and torch.equal(dv, rv)
