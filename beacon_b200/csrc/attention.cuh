@@ -95,13 +95,6 @@ __device__ __forceinline__ void tma_load_rows(uint8_t* dst, const CUtensorMap* m
   for (int b = 0; b < D / 64; ++b) tma_load_3d(dst + b * 128 * 128, m, bar, b * 64, row0, z);
 }
 
-// Prefetches the same 128-row tile into L2.
-template <int D>
-__device__ __forceinline__ void tma_prefetch_rows(const CUtensorMap* m, int row0, int z) {
-#pragma unroll
-  for (int b = 0; b < D / 64; ++b) tma_prefetch_l2_3d(m, b * 64, row0, z);
-}
-
 // 2^a for a pair of arguments without the MUFU unit: a = n + f with n = rint(a) (1.5 x 2^23
 // added and subtracted in fp32 round-to-nearest, n then sits in the low mantissa bits),
 // a cubic in f in [-0.5, 0.5] fitted to 2^f by iteratively reweighted least squares on the

@@ -328,12 +328,6 @@ __global__ void __launch_bounds__(384, 1)
         bulk_load(sDt + st * 128, p.dt + srow, 512, &do_full[st]);
         diss |= 1u << st;
         dpar = (dpar & ~(1u << st)) | (ph << st);
-        if (n + 1 < n_iter) {  // the tile after: into L2 now, so its load finds it there
-          const int g1 = (n + 1) / iters_per_head, it1 = it0 + (n + 1) % iters_per_head;
-          const int bh1 = b * p.Hq + hk * group + g1;
-          tma_prefetch_rows<D>(&tmQ, it1 * 128, bh1);
-          tma_prefetch_rows<D>(&tmdO, it1 * 128, bh1);
-        }
       }
       if (!ok) {
         volatile int no_abort = 0;
