@@ -60,7 +60,7 @@ DKDV_FLOPS = 2.0 * FWD_FLOPS
 DQ_FLOPS = 1.5 * FWD_FLOPS
 # k_attn_bwd_dkdv DRAM traffic per launch from the ncu capture summarised in
 # profiles/k_attn_bwd_dkdv_h32s4096.md (B*H=32 heads captured, scaled by the head count).
-DKDV_TRAFFIC_PER_HEAD = (187.7e6 + 39.4e6) / 32
+DKDV_TRAFFIC_PER_HEAD = (135.5e6 + 39.7e6) / 32
 
 # pre-norm Llama block forward
 BLK_B, BLK_S, BLK_DM, BLK_H, BLK_D, BLK_F = 4, 2048, 4096, 32, 128, 14336
