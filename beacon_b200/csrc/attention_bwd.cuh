@@ -231,19 +231,22 @@ __global__ void __launch_bounds__(384, 1)
   float* sLse = reinterpret_cast<float*>(sdO + 2 * TILE);  // [QST][128] lse2, with Q
   float* sDt = sLse + QST * 128;                            // [2][128] Dt, with dO
   uint64_t* bars = reinterpret_cast<uint64_t*>(sDt + 2 * 128);
+  constexpr int NB = D / 64;        // 64-column blocks of a tile
   uint64_t* kv_full = bars + 0;
-  uint64_t* q_full = bars + 1;     // [3] Q and lse2 of a query tile
-  uint64_t* q_empty = bars + 4;    // [3] Q read by S^T and dK
-  uint64_t* do_full = bars + 7;    // [2] dO and Dt of a query tile
-  uint64_t* do_empty = bars + 9;   // [2] dO read by dP^T and dV
-  uint64_t* s_full = bars + 11;    // S^T(n) computed
-  uint64_t* dp_full = bars + 12;   // dP^T(n) computed
-  uint64_t* p_ready = bars + 13;   // P^T(n) stored by all 8 warps
-  uint64_t* rp_free = bars + 14;   // dP^T(n) read by all 8 warps: R_P(n) may take S^T(n+1)
-  uint64_t* ds_ready = bars + 15;  // dS^T(n) stored by all 8 warps
-  uint64_t* dkv_full = bars + 16;
-  uint64_t* drain = bars + 17;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  // [3][2] per Q stage and column block (the last block's barrier also carries lse2): the
+  // score MMAs of block 0 start while block 1 is still landing
+  uint64_t* q_full = bars + 1;
+  uint64_t* q_empty = bars + 7;    // [3] Q read by S^T and dK
+  uint64_t* do_full = bars + 10;   // [2] dO and Dt of a query tile
+  uint64_t* do_empty = bars + 12;  // [2] dO read by dP^T and dV
+  uint64_t* s_full = bars + 14;    // S^T(n) computed
+  uint64_t* dp_full = bars + 15;   // dP^T(n) computed
+  uint64_t* p_ready = bars + 16;   // P^T(n) stored by all 8 warps
+  uint64_t* rp_free = bars + 17;   // dP^T(n) read by all 8 warps: R_P(n) may take S^T(n+1)
+  uint64_t* ds_ready = bars + 18;  // dS^T(n) stored by all 8 warps
+  uint64_t* dkv_full = bars + 19;
+  uint64_t* drain = bars + 20;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   constexpr uint32_t T_DV = 256, T_DK = 256 + D;
 
@@ -263,7 +266,8 @@ __global__ void __launch_bounds__(384, 1)
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
     for (int i = 0; i < QST; ++i) {
-      mbar_init(&q_full[i], 1);
+      mbar_init(&q_full[2 * i], 1);
+      mbar_init(&q_full[2 * i + 1], 1);
       mbar_init(&q_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -314,9 +318,12 @@ __global__ void __launch_bounds__(384, 1)
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&q_full[qs], TILE + Cfg::STATS_BYTES / 2);
-        tma_load_rows<D>(sQ + qs * TILE, &tmQ, &q_full[qs], it * 128, bh);
-        bulk_load(sLse + qs * 128, p.lse2 + srow, 512, &q_full[qs]);
+#pragma unroll
+        for (int cb = 0; cb < NB; ++cb) {
+          mbar_arrive_expect_tx(&q_full[2 * qs + cb], 128 * 128 + (cb == NB - 1 ? Cfg::STATS_BYTES / 2 : 0));
+          tma_load_3d(sQ + qs * TILE + cb * 128 * 128, &tmQ, &q_full[2 * qs + cb], cb * 64, it * 128, bh);
+        }
+        bulk_load(sLse + qs * 128, p.lse2 + srow, 512, &q_full[2 * qs + NB - 1]);
         qiss |= 1u << qs;
         qpar = (qpar & ~(1u << qs)) | (qph << qs);
         if (!mbar_wait(&do_empty[st], ph ^ 1u, abort_flag, kSiteBwdQDEmpty)) {
@@ -333,7 +340,8 @@ __global__ void __launch_bounds__(384, 1)
         volatile int no_abort = 0;
         mbar_wait(kv_full, 0, &no_abort, kSiteBwdDrain);
         for (int s = 0; s < QST; ++s)
-          if (qiss & (1u << s)) mbar_wait(&q_full[s], (qpar >> s) & 1u, &no_abort, kSiteBwdDrain);
+          if (qiss & (1u << s))
+            for (int cb = 0; cb < NB; ++cb) mbar_wait(&q_full[2 * s + cb], (qpar >> s) & 1u, &no_abort, kSiteBwdDrain);
         for (int s = 0; s < 2; ++s)
           if (diss & (1u << s)) mbar_wait(&do_full[s], (dpar >> s) & 1u, &no_abort, kSiteBwdDrain);
       }
@@ -352,13 +360,30 @@ __global__ void __launch_bounds__(384, 1)
                         (!first || kk > 0) ? 1u : 0u);
         }
       };
+      // S^T = K Q(n)^T from Q stage qs: each 64-column block's K-steps once that block landed
+      auto issue_st = [&](uint32_t d_col, int qs, uint32_t par) -> bool {
+        constexpr uint32_t idesc = make_idesc_f16(128, 128, false, false);
+        const uint32_t q_addr = smem_u32(sQ + qs * TILE);
+#pragma unroll
+        for (int cb = 0; cb < NB; ++cb) {
+          if (!warp_wait(&q_full[2 * qs + cb], par, abort_flag, kSiteBwdQDFull)) return false;
+          tc_fence_after();
+#pragma unroll
+          for (int k4 = 0; k4 < 4; ++k4) {
+            const uint32_t off = cb * 16384 + k4 * 32;
+            if (leader)
+              umma_f16_ss(tmem + d_col, make_sdesc_sw128(k_addr + off, 16, 1024), make_sdesc_sw128(q_addr + off, 16, 1024),
+                          idesc, (cb | k4) != 0 ? 1u : 0u);
+          }
+        }
+        return true;
+      };
       bool ok = warp_wait(kv_full, 0, abort_flag, kSiteBwdKV);
       if (ok && n_iter > 0) {
-        if (!warp_wait(&q_full[0], 0, abort_flag, kSiteBwdQDFull) || !warp_wait(&do_full[0], 0, abort_flag, kSiteBwdQDFull)) {
+        if (!issue_st(0, 0, 0) || !warp_wait(&do_full[0], 0, abort_flag, kSiteBwdQDFull)) {
           ok = false;
         } else {
           tc_fence_after();
-          issue_score_tile<D>(leader, tmem + 0, k_addr, smem_u32(sQ));
           if (leader) umma_commit(s_full);
           issue_score_tile<D>(leader, tmem + 128, v_addr, smem_u32(sdO));
           if (leader) umma_commit(dp_full);
@@ -380,9 +405,7 @@ __global__ void __launch_bounds__(384, 1)
         if (leader) umma_commit(&do_empty[st]);  // dO(n) read by dP^T(n) and dV(n)
         if (!warp_wait(rp_free, par, abort_flag, kSiteBwdDsFull)) break;
         if (more) {
-          if (!warp_wait(&q_full[qs1], (uint32_t)((n + 1) / QST) & 1u, abort_flag, kSiteBwdQDFull)) break;
-          tc_fence_after();
-          issue_score_tile<D>(leader, tmem + rp, k_addr, smem_u32(sQ + qs1 * TILE));
+          if (!issue_st(rp, qs1, (uint32_t)((n + 1) / QST) & 1u)) break;
           if (leader) umma_commit(s_full);
         }
         if (!warp_wait(ds_ready, par, abort_flag, kSiteBwdDsFull)) break;
@@ -427,7 +450,8 @@ __global__ void __launch_bounds__(384, 1)
       const int first_ok = key_ok ? max(qmin - 64 * g, 0) : 64;
       // s_full: the scores; q_full: makes the TMA-written lse2 visible to this thread
       if (!__all_sync(0xffffffffu, mbar_wait(s_full, par, abort_flag, kSiteBwdStFull) &&
-                                       mbar_wait(&q_full[qs], (uint32_t)(n / QST) & 1u, abort_flag, kSiteBwdQDFull))) {
+                                       mbar_wait(&q_full[2 * qs + NB - 1], (uint32_t)(n / QST) & 1u, abort_flag,
+                                                 kSiteBwdQDFull))) {
         ok = false;
         break;
       }
