@@ -351,9 +351,9 @@ __global__ void __launch_bounds__(384, 1)
       constexpr uint32_t idesc_kv = make_idesc_f16(128, D, false, true);  // dV, dK: A in TMEM, B MN-major
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
       // dV += P^T dO or dK += dS^T Q: A at TMEM columns `a_col` + [64g, 64g+32) for g = 0, 1
-      auto issue_kv = [&](uint32_t d_col, uint32_t a_col, uint32_t b_addr, bool first) {
+      auto issue_kv = [&](uint32_t d_col, uint32_t a_col, uint32_t b_addr, bool first, int kk0 = 0, int kk1 = 8) {
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {  // 16 queries per K-step
+        for (int kk = kk0; kk < kk1; ++kk) {  // 16 queries per K-step
           const uint32_t col = a_col + (uint32_t)(64 * (kk >> 2) + 8 * (kk & 3));
           if (leader)
             umma_f16_ts(tmem + d_col, tmem + col, make_sdesc_sw128(b_addr + kk * 2048, 16384, 1024), idesc_kv,
@@ -399,15 +399,18 @@ __global__ void __launch_bounds__(384, 1)
         // dV(n) as soon as P^T(n) is stored (the warps then wait for dP^T(n) and read it);
         // S^T(n+1) as soon as R_P(n) is free (the warps' next P phase waits for it); dK(n)
         // and dP^T(n+1) once dS^T(n) is stored, so dP^T(n+1) is done early in the next P phase.
+        // (dV(n) in two halves around S^T(n+1): the issuing warp, which blocks while the
+        // tensor pipe's queue is full, gets to S^T(n+1) sooner)
         if (!warp_wait(p_ready, par, abort_flag, kSiteBwdDsFull)) break;
         tc_fence_after();
-        issue_kv(T_DV, rs, do_addr, n == 0);
-        if (leader) umma_commit(&do_empty[st]);  // dO(n) read by dP^T(n) and dV(n)
+        issue_kv(T_DV, rs, do_addr, n == 0, 0, 4);
         if (!warp_wait(rp_free, par, abort_flag, kSiteBwdDsFull)) break;
         if (more) {
           if (!issue_st(rp, qs1, (uint32_t)((n + 1) / QST) & 1u)) break;
           if (leader) umma_commit(s_full);
         }
+        issue_kv(T_DV, rs, do_addr, false, 4, 8);
+        if (leader) umma_commit(&do_empty[st]);  // dO(n) read by dP^T(n) and dV(n)
         if (!warp_wait(ds_ready, par, abort_flag, kSiteBwdDsFull)) break;
         tc_fence_after();
         issue_kv(T_DK, rs + 32, q_addr, n == 0);
