@@ -212,6 +212,20 @@ __global__ void __launch_bounds__(384, 1)
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbarrier_init();
+    // the producer's first copies (Q_A, Q_B, K_0, V_0) go out before the TMEM allocation
+    // and the CTA barrier, so they overlap the set-up
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    mbar_arrive_expect_tx(q_full, 2 * Cfg::Q_BYTES);
+    tma_load_rows<D>(sQ, &tmQ, q_full, q0[0], bh);
+    tma_load_rows<D>(sQ + Cfg::Q_BYTES, &tmQ, q_full, q0[1], bh);  // rows >= S read as zeros
+    if (n_j > 0) {
+      mbar_arrive_expect_tx(&k_full[0], Cfg::KV_BYTES);
+      tma_load_rows<D>(sK, &tmK, &k_full[0], 0, kvz);
+      mbar_arrive_expect_tx(&v_full[0], Cfg::KV_BYTES);
+      tma_load_rows<D>(sV, &tmV, &v_full[0], 0, kvz);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
@@ -229,15 +243,10 @@ __global__ void __launch_bounds__(384, 1)
     if (warp == 0) {
       // ---------------------------------------------------------------- producer
       if (lane == 0) {
-        tma_prefetch_desc(&tmQ);
-        tma_prefetch_desc(&tmK);
-        tma_prefetch_desc(&tmV);
-        mbar_arrive_expect_tx(q_full, 2 * Cfg::Q_BYTES);
-        tma_load_rows<D>(sQ, &tmQ, q_full, q0[0], bh);
-        tma_load_rows<D>(sQ + Cfg::Q_BYTES, &tmQ, q_full, q0[1], bh);  // rows >= S read as zeros
-        uint32_t kissued = 0, vissued = 0, kpar = 0, vpar = 0;
+        // Q and K_0 / V_0 were issued at set-up
+        uint32_t kissued = n_j > 0 ? 1u : 0u, vissued = kissued, kpar = 0, vpar = 0;
         bool ok = true;
-        for (int j = 0; j < n_j && ok; ++j) {
+        for (int j = 1; j < n_j && ok; ++j) {
           const int st = j & 1;
           const uint32_t ph = (j >> 1) & 1;
           if (!mbar_wait(&k_empty[st], ph ^ 1u, abort_flag, kSiteAttnKEmpty)) { ok = false; break; }
