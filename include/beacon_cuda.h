@@ -81,7 +81,7 @@ int beacon_device_status(int device, unsigned int out[3]);
 uint64_t beacon_launch_count(void);
 
 /* Device timing of the tensor-core kernels (k_gemm_bf16_tc, k_attn_fwd_tc,
- * k_attn_bwd_tc): while enabled, each launch is bracketed by CUDA events on its
+ * k_attn_bwd_dkdv, k_attn_bwd_dq): while enabled, each launch is bracketed by CUDA events on its
  * own stream.  beacon_profile_read(name, ...) waits for those events and returns the
  * accumulated milliseconds and launch count for `name`; name == NULL resets.
  * No reference counterpart (the reference bench is a stub,
