@@ -37,6 +37,7 @@ EXPORTS = (
     "beacon_attention_adjoint_fwd", "beacon_attention_adjoint_bwd", "beacon_attention_bwd_workspace_size",
     "beacon_attention_gqa_fwd", "beacon_attention_gqa_bwd", "beacon_attention_bwd_with_out",
     "beacon_rmsnorm_adjoint_fwd", "beacon_rmsnorm_adjoint_bwd", "beacon_rmsnorm_adjoint_bwd_noalloc",
+    "beacon_layernorm_adjoint_fwd", "beacon_layernorm_adjoint_bwd",
     "beacon_swiglu_adjoint_fwd", "beacon_swiglu_adjoint_bwd", "beacon_swiglu_workspace_size",
     "beacon_llama_block_fwd", "beacon_llama_block_workspace_size",
     "beacon_residual_add_fwd", "beacon_residual_add_bwd", "beacon_cast",
@@ -107,6 +108,10 @@ def lib():
     _sig(L, "beacon_rmsnorm_adjoint_fwd", _int, [_vp, _vp, _vp, _vp, _i64, _i64, ctypes.c_float, _int, _vp])
     _sig(L, "beacon_rmsnorm_adjoint_bwd", _int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _int, _vp, _sz, _vp])
     _sig(L, "beacon_rmsnorm_adjoint_bwd_noalloc", _int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _int, _vp])
+    _sig(L, "beacon_layernorm_adjoint_fwd", _int,
+         [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, ctypes.c_float, _int, _vp])
+    _sig(L, "beacon_layernorm_adjoint_bwd", _int,
+         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _int, _vp, _sz, _vp])
     _sig(L, "beacon_swiglu_adjoint_fwd", _int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp, _sz, _vp])
     _sig(L, "beacon_swiglu_adjoint_bwd", _int,
          [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp, _sz, _vp])

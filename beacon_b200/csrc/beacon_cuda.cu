@@ -835,6 +835,112 @@ extern "C" int beacon_rmsnorm_adjoint_bwd(void* dx, void* dweight, const void* d
 }
 
 // ===========================================================================
+// LayerNorm
+// ===========================================================================
+extern "C" int beacon_layernorm_adjoint_fwd(void* out, const void* x, const void* weight, const void* bias,
+                                            float* mean, float* invstd, int64_t tokens, int64_t dim, float eps,
+                                            int dtype, void* stream) {
+  if (tokens < 0 || dim <= 0 || dim > INT32_MAX)
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "layernorm_fwd: bad shape tokens=%lld dim=%lld",
+                (long long)tokens, (long long)dim);
+  if (dtype != BEACON_BF16 && dtype != BEACON_F32)
+    return fail(BEACON_ERR_UNIMPLEMENTED, "layernorm_fwd: dtype %d", dtype);
+  if (tokens == 0) return BEACON_OK;
+  if (!out || !x || !weight || !bias || !mean || !invstd)
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "layernorm_fwd: null pointer");
+  int dev;
+  DeviceInfo* di;
+  BEACON_TRY(current_device(&dev, &di));
+  cudaStream_t st = as_stream(stream);
+  const int grid = (int)std::min<int64_t>(tokens, (int64_t)di->sms * 16);
+  const bool vec = aligned16(out) && aligned16(x) && aligned16(weight) && aligned16(bias) && dim % 8 == 0;
+  const int d = (int)dim;
+#define LN_FWD(T, V)                                                                                          \
+  k_layernorm_fwd<T, V><<<grid, 256, 0, st>>>((T*)out, mean, invstd, (const T*)x, (const T*)weight,           \
+                                              (const T*)bias, tokens, d, eps)
+#define LN_FWD_ANY(T)                                                                                         \
+  k_layernorm_fwd_any<T><<<grid, 256, 0, st>>>((T*)out, mean, invstd, (const T*)x, (const T*)weight,          \
+                                               (const T*)bias, tokens, d, eps)
+  if (dtype == BEACON_BF16) {
+    if (vec && dim <= 256 * 8 * 1) LN_FWD(bf16, 1);
+    else if (vec && dim <= 256 * 8 * 2) LN_FWD(bf16, 2);
+    else if (vec && dim <= 256 * 8 * 4) LN_FWD(bf16, 4);
+    else if (vec && dim <= 256 * 8 * 8) LN_FWD(bf16, 8);
+    else LN_FWD_ANY(bf16);
+  } else {
+    if (vec && dim <= 256 * 8 * 1) LN_FWD(float, 1);
+    else if (vec && dim <= 256 * 8 * 2) LN_FWD(float, 2);
+    else if (vec && dim <= 256 * 8 * 4) LN_FWD(float, 4);
+    else LN_FWD_ANY(float);
+  }
+#undef LN_FWD
+#undef LN_FWD_ANY
+  return check_launch("layernorm_fwd");
+}
+
+extern "C" int beacon_layernorm_adjoint_bwd(void* dx, void* dweight, void* dbias, const void* dy, const void* x,
+                                            const float* mean, const float* invstd, const void* weight,
+                                            int64_t tokens, int64_t dim, int dtype, void* workspace,
+                                            size_t workspace_bytes, void* stream) {
+  if (tokens < 0 || dim <= 0 || dim > INT32_MAX)
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "layernorm_bwd: bad shape tokens=%lld dim=%lld",
+                (long long)tokens, (long long)dim);
+  if (dtype != BEACON_BF16 && dtype != BEACON_F32)
+    return fail(BEACON_ERR_UNIMPLEMENTED, "layernorm_bwd: dtype %d", dtype);
+  int dev;
+  DeviceInfo* di;
+  BEACON_TRY(current_device(&dev, &di));
+  cudaStream_t st = as_stream(stream);
+  const int es = dtype == BEACON_F32 ? 4 : 2;
+  if (tokens == 0) {  // empty sums
+    if (dweight) BEACON_TRY(zero_fill(dweight, (size_t)dim * es, st));
+    if (dbias) BEACON_TRY(zero_fill(dbias, (size_t)dim * es, st));
+    return BEACON_OK;
+  }
+  if (!dx || !dy || !x || !mean || !invstd || !weight)
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "layernorm_bwd: null pointer");
+  const bool vec = aligned16(dx) && aligned16(dy) && aligned16(x) && aligned16(weight) && dim % 8 == 0;
+  const int grid = (int)std::min<int64_t>(tokens, (int64_t)di->sms * 4);
+  const size_t part_bytes = (size_t)grid * dim * 4;
+  const int nparts = (dweight ? 1 : 0) + (dbias ? 1 : 0);
+  float *part_w = nullptr, *part_b = nullptr;
+  if (nparts) {
+    void* ws = nullptr;
+    BEACON_TRY(get_workspace(dev, part_bytes * nparts, workspace, workspace_bytes, &ws));
+    float* p = reinterpret_cast<float*>(ws);
+    if (dweight) part_w = p, p += (size_t)grid * dim;
+    if (dbias) part_b = p;
+  }
+  const unsigned cgrid = (unsigned)((dim + 255) / 256);
+  if (dtype == BEACON_BF16) {
+    k_layernorm_bwd<bf16><<<grid, 256, 0, st>>>((bf16*)dx, part_w, part_b, (const bf16*)dy, (const bf16*)x, mean,
+                                                invstd, (const bf16*)weight, tokens, (int)dim, vec);
+    BEACON_TRY(check_launch("layernorm_bwd"));
+    if (dweight) {
+      k_colsum<bf16><<<cgrid, 256, 0, st>>>((bf16*)dweight, part_w, grid, (int)dim);
+      BEACON_TRY(check_launch("layernorm_bwd dweight colsum"));
+    }
+    if (dbias) {
+      k_colsum<bf16><<<cgrid, 256, 0, st>>>((bf16*)dbias, part_b, grid, (int)dim);
+      BEACON_TRY(check_launch("layernorm_bwd dbias colsum"));
+    }
+  } else {
+    k_layernorm_bwd<float><<<grid, 256, 0, st>>>((float*)dx, part_w, part_b, (const float*)dy, (const float*)x,
+                                                 mean, invstd, (const float*)weight, tokens, (int)dim, vec);
+    BEACON_TRY(check_launch("layernorm_bwd"));
+    if (dweight) {
+      k_colsum<float><<<cgrid, 256, 0, st>>>((float*)dweight, part_w, grid, (int)dim);
+      BEACON_TRY(check_launch("layernorm_bwd dweight colsum"));
+    }
+    if (dbias) {
+      k_colsum<float><<<cgrid, 256, 0, st>>>((float*)dbias, part_b, grid, (int)dim);
+      BEACON_TRY(check_launch("layernorm_bwd dbias colsum"));
+    }
+  }
+  return BEACON_OK;
+}
+
+// ===========================================================================
 // RMSNorm backward without any allocation.
 //
 // For callers that cannot allocate device memory on their own: a launcher that

@@ -360,6 +360,186 @@ __global__ void __launch_bounds__(256) k_colsum_partial(float* __restrict__ part
 }
 
 // ---------------------------------------------------------------------------
+// LayerNorm (norm.rs:55-95): y = (x - mean) * invstd * w + b with the biased
+// variance; mean and invstd are saved per row as f32 (adjoint lib.rs:78-85).
+// ---------------------------------------------------------------------------
+
+// Two block-wide sums at once for blockDim.x == 256; `red` holds 16 floats.
+__device__ __forceinline__ void block_sum2_256(float& a, float& b, float* red) {
+  a = warp_sum(a);
+  b = warp_sum(b);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) {
+    red[w] = a;
+    red[8 + w] = b;
+  }
+  __syncthreads();
+  a = warp_sum(l < 8 ? red[l] : 0.0f);
+  b = warp_sum(l < 8 ? red[8 + l] : 0.0f);
+}
+
+// One CTA of 256 threads per row (norm.rs:5-9 `rowwise`), grid-stride over rows.
+// The row stays in registers from the load to the store: the variance is taken
+// about the mean (two reductions, no E[x^2] - E[x]^2 cancellation) at one HBM
+// read and one write per element.  dim % 8 == 0, dim <= 256 * 8 * VEC and
+// 16-byte aligned pointers (the host picks k_layernorm_fwd_any otherwise).
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) k_layernorm_fwd(T* __restrict__ y, float* __restrict__ mean,
+                                                       float* __restrict__ invstd, const T* __restrict__ x,
+                                                       const T* __restrict__ w, const T* __restrict__ b,
+                                                       long long rows, int dim, float eps) {
+  __shared__ float red[8];
+  const int nvec = dim / 8;
+  for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
+    const T* xr = x + r * dim;
+    float v[VEC][8];
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const int vi = threadIdx.x + i * 256;
+      if (vi < nvec) {
+        load8(xr + vi * 8, v[i]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s += v[i][j];
+      }
+    }
+    const float mu = block_sum_256(s, red) / (float)dim;
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const int vi = threadIdx.x + i * 256;
+      if (vi < nvec) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          v[i][j] -= mu;
+          ss = fmaf(v[i][j], v[i][j], ss);
+        }
+      }
+    }
+    const float is = 1.0f / sqrtf(block_sum_256(ss, red) / (float)dim + eps);
+    if (threadIdx.x == 0) {
+      mean[r] = mu;
+      invstd[r] = is;
+    }
+    T* yr = y + r * dim;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const int vi = threadIdx.x + i * 256;
+      if (vi < nvec) {
+        float g[8], c[8], o[8];
+        load8(w + vi * 8, g);
+        load8(b + vi * 8, c);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = fmaf(v[i][j] * is, g[j], c[j]);
+        store8(yr + vi * 8, o);
+      }
+    }
+  }
+}
+
+// Any dim and alignment: three passes over the row (the second and third from L1/L2).
+template <typename T>
+__global__ void __launch_bounds__(256) k_layernorm_fwd_any(T* __restrict__ y, float* __restrict__ mean,
+                                                           float* __restrict__ invstd, const T* __restrict__ x,
+                                                           const T* __restrict__ w, const T* __restrict__ b,
+                                                           long long rows, int dim, float eps) {
+  __shared__ float red[8];
+  for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
+    const T* xr = x + r * dim;
+    float s = 0.0f;
+    for (int e = threadIdx.x; e < dim; e += 256) s += ldf(xr + e);
+    const float mu = block_sum_256(s, red) / (float)dim;
+    float ss = 0.0f;
+    for (int e = threadIdx.x; e < dim; e += 256) {
+      const float t = ldf(xr + e) - mu;
+      ss = fmaf(t, t, ss);
+    }
+    const float is = 1.0f / sqrtf(block_sum_256(ss, red) / (float)dim + eps);
+    if (threadIdx.x == 0) {
+      mean[r] = mu;
+      invstd[r] = is;
+    }
+    for (int e = threadIdx.x; e < dim; e += 256)
+      stf(y + r * dim + e, fmaf((ldf(xr + e) - mu) * is, ldf(w + e), ldf(b + e)));
+  }
+}
+
+// Backward, with xh = (x - mean) invstd and e = w dy:
+//   dx = invstd (e - mean_d e - xh mean_d(e xh))
+// and per-CTA partial column sums of dy xh (dweight) and dy (dbias) into
+// part_w / part_b [gridDim.x, dim] (f32; either may be null), summed by k_colsum.
+// `vec`: dim % 8 == 0 and every pointer 16-byte aligned.
+template <typename T>
+__global__ void __launch_bounds__(256) k_layernorm_bwd(T* __restrict__ dx, float* __restrict__ part_w,
+                                                       float* __restrict__ part_b, const T* __restrict__ dy,
+                                                       const T* __restrict__ x, const float* __restrict__ mean,
+                                                       const float* __restrict__ invstd, const T* __restrict__ w,
+                                                       long long rows, int dim, bool vec) {
+  __shared__ float red[16];
+  float* pw = part_w ? part_w + (long long)blockIdx.x * dim : nullptr;
+  float* pb = part_b ? part_b + (long long)blockIdx.x * dim : nullptr;
+  for (int e = threadIdx.x; e < dim; e += 256) {
+    if (pw) pw[e] = 0.0f;
+    if (pb) pb[e] = 0.0f;
+  }
+  __syncthreads();
+  for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
+    const T* xr = x + r * dim;
+    const T* dyr = dy + r * dim;
+    const float mu = mean[r], is = invstd[r];
+    float sg = 0.0f, sgx = 0.0f;
+    if (vec) {
+      for (int vi = threadIdx.x; vi < dim / 8; vi += 256) {
+        float a[8], d[8], g[8];
+        load8(xr + vi * 8, a);
+        load8(dyr + vi * 8, d);
+        load8(w + vi * 8, g);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float e = g[j] * d[j];
+          sg += e;
+          sgx = fmaf(e, (a[j] - mu) * is, sgx);
+        }
+      }
+    } else {
+      for (int i = threadIdx.x; i < dim; i += 256) {
+        const float e = ldf(w + i) * ldf(dyr + i);
+        sg += e;
+        sgx = fmaf(e, (ldf(xr + i) - mu) * is, sgx);
+      }
+    }
+    block_sum2_256(sg, sgx, red);
+    const float mg = sg / (float)dim, mgx = sgx / (float)dim;
+    T* dxr = dx + r * dim;
+    if (vec) {
+      for (int vi = threadIdx.x; vi < dim / 8; vi += 256) {
+        float a[8], d[8], g[8], o[8];
+        load8(xr + vi * 8, a);
+        load8(dyr + vi * 8, d);
+        load8(w + vi * 8, g);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float xh = (a[j] - mu) * is;
+          o[j] = is * (g[j] * d[j] - mg - xh * mgx);
+          if (pw) pw[vi * 8 + j] += d[j] * xh;
+          if (pb) pb[vi * 8 + j] += d[j];
+        }
+        store8(dxr + vi * 8, o);
+      }
+    } else {
+      for (int i = threadIdx.x; i < dim; i += 256) {
+        const float a = ldf(xr + i), d = ldf(dyr + i);
+        const float xh = (a - mu) * is;
+        stf(dxr + i, is * (ldf(w + i) * d - mg - xh * mgx));
+        if (pw) pw[i] += d * xh;
+        if (pb) pb[i] += d;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // SwiGLU elementwise pieces (mlp.rs:12-52); silu(z) = z * sigmoid(z)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float sigmoid_f(float z) { return 1.0f / (1.0f + expf(-z)); }

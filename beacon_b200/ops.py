@@ -184,6 +184,31 @@ def rmsnorm_bwd(dy, x, rms, weight):
     return dx, dw
 
 
+# ---------------------------------------------------------------- LayerNorm
+
+def layernorm_fwd(x, weight, bias, eps=1e-5):
+    """(out, mean, invstd), biased variance  (norm.rs:56-73)."""
+    T, dim = x.shape
+    dt = _dtype(x, weight, bias)
+    out = torch.empty_like(x)
+    mean = torch.empty(T, dtype=torch.float32, device=x.device)
+    invstd = torch.empty(T, dtype=torch.float32, device=x.device)
+    check(_lib.lib().beacon_layernorm_adjoint_fwd(_p(out), _p(x), _p(weight), _p(bias), _p(mean), _p(invstd), T,
+                                                  dim, eps, dt, _stream()))
+    return out, mean, invstd
+
+
+def layernorm_bwd(dy, x, mean, invstd, weight):
+    """(dx, dweight, dbias)  (norm.rs:75-94)."""
+    T, dim = x.shape
+    dt = _dtype(dy, x, weight)
+    dx = torch.empty_like(x)
+    dw, db = torch.empty_like(weight), torch.empty_like(weight)
+    check(_lib.lib().beacon_layernorm_adjoint_bwd(_p(dx), _p(dw), _p(db), _p(dy), _p(x), _p(mean), _p(invstd),
+                                                  _p(weight), T, dim, dt, None, 0, _stream()))
+    return dx, dw, db
+
+
 # ---------------------------------------------------------------- SwiGLU MLP
 
 def swiglu_fwd(x, gate_proj, up_proj, down_proj):

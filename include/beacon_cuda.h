@@ -191,6 +191,24 @@ int beacon_rmsnorm_adjoint_bwd(void* dx, void* dweight, const void* dy, const vo
 int beacon_rmsnorm_adjoint_bwd_noalloc(void* dx, void* dweight, const void* dy, const void* x, const float* rms,
                                        const void* weight, int64_t tokens, int64_t dim, int dtype, void* stream);
 
+/* ---- LayerNorm: crates/beacon-cuda/src/norm.rs:55-95 ----------------------- */
+
+/* layernorm_fwd (norm.rs:56-73): mean[t] = mean_d x[t, d],
+ * invstd[t] = 1 / sqrt(mean_d (x[t, d] - mean[t])^2 + eps) (biased variance; both float32),
+ * out = (x - mean) * invstd * weight + bias.  The reference signature has no eps; 1e-5 is
+ * the convention of the RMSNorm above.  The saved statistics are mean and invstd
+ * (adjoint crates/beacon-adjoint-table/src/lib.rs:78-85). */
+int beacon_layernorm_adjoint_fwd(void* out, const void* x, const void* weight, const void* bias, float* mean,
+                                 float* invstd, int64_t tokens, int64_t dim, float eps, int dtype, void* stream);
+
+/* layernorm_bwd (norm.rs:75-94): with xh = (x - mean) invstd and e = weight dy,
+ * dx = invstd (e - mean_d e - xh mean_d(e xh)); dweight = sum_t dy xh; dbias = sum_t dy
+ * (either may be NULL).  Workspace as for attention: 4 * min(tokens, 4 * SMs) * dim bytes
+ * for each of dweight and dbias requested. */
+int beacon_layernorm_adjoint_bwd(void* dx, void* dweight, void* dbias, const void* dy, const void* x,
+                                 const float* mean, const float* invstd, const void* weight, int64_t tokens,
+                                 int64_t dim, int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- SwiGLU MLP: crates/beacon-cuda/src/mlp.rs:12-52 ----------------------- */
 
 /* swiglu_fwd (mlp.rs:12-29): out[t, dm] = (silu(x Wg) * (x Wu)) Wd;

@@ -71,6 +71,8 @@ def lib():
                                        _i64, ctypes.c_int, ctypes.c_float]
         L.bo_rmsnorm_fwd.argtypes = [_f, _f, _f, _f, _i64, _i64, ctypes.c_float]
         L.bo_rmsnorm_bwd.argtypes = [_f, _f, _f, _f, _f, _f, _i64, _i64]
+        L.bo_layernorm_fwd.argtypes = [_f, _f, _f, _f, _f, _f, _i64, _i64, ctypes.c_float]
+        L.bo_layernorm_bwd.argtypes = [_f, _f, _f, _f, _f, _f, _f, _f, _i64, _i64]
         L.bo_swiglu_fwd.argtypes = [_f, _f, _f, _f, _f, _i64, _i64, _i64]
         L.bo_swiglu_bwd.argtypes = [_f, _f, _f, _f, _f, _f, _f, _f, _f, _i64, _i64, _i64]
         L.bo_residual_add_fwd.argtypes = [_f, _f, _f, _i64]
@@ -218,6 +220,20 @@ def rmsnorm_bwd(dy, x, rms, g):
     dx, dg = _empty(T, dim), _empty(dim)
     lib().bo_rmsnorm_bwd(_p(dx), _p(dg), _p(dy), _p(x), _p(rms), _p(g), T, dim)
     return dx, dg
+
+
+def layernorm_fwd(x, g, b, eps=1e-5):
+    T, dim = x.shape
+    y, mean, invstd = _empty(T, dim), _empty(T), _empty(T)
+    lib().bo_layernorm_fwd(_p(y), _p(mean), _p(invstd), _p(x), _p(g), _p(b), T, dim, eps)
+    return y, mean, invstd
+
+
+def layernorm_bwd(dy, x, mean, invstd, g):
+    T, dim = x.shape
+    dx, dg, db = _empty(T, dim), _empty(dim), _empty(dim)
+    lib().bo_layernorm_bwd(_p(dx), _p(dg), _p(db), _p(dy), _p(x), _p(mean), _p(invstd), _p(g), T, dim)
+    return dx, dg, db
 
 
 def swiglu_fwd(x, wg, wu, wd):

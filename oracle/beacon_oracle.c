@@ -403,6 +403,62 @@ void bo_rmsnorm_bwd(float* dx, float* dg, const float* dy, const float* x, const
 }
 
 /* ------------------------------------------------------------------------- */
+/* LayerNorm                                                                 */
+/* ------------------------------------------------------------------------- */
+
+void bo_layernorm_fwd(float* y, float* mean, float* invstd, const float* x, const float* g, const float* b,
+                      int64_t T, int64_t dim, float eps) {
+#pragma omp parallel for schedule(static)
+    for (int64_t t = 0; t < T; ++t) {
+        const float* xt = x + t * dim;
+        double s = 0.0;
+        for (int64_t d = 0; d < dim; ++d) s += (double)xt[d];
+        const double mu = s / (double)dim;
+        double ss = 0.0;
+        for (int64_t d = 0; d < dim; ++d) ss += ((double)xt[d] - mu) * ((double)xt[d] - mu);
+        const double is = 1.0 / sqrt(ss / (double)dim + (double)eps);
+        mean[t] = (float)mu;
+        invstd[t] = (float)is;
+        for (int64_t d = 0; d < dim; ++d)
+            y[t * dim + d] = (float)(((double)xt[d] - mu) * is * (double)g[d] + (double)b[d]);
+    }
+}
+
+void bo_layernorm_bwd(float* dx, float* dg, float* db, const float* dy, const float* x, const float* mean,
+                      const float* invstd, const float* g, int64_t T, int64_t dim) {
+#pragma omp parallel for schedule(static)
+    for (int64_t t = 0; t < T; ++t) {
+        const float* xt = x + t * dim;
+        const float* dyt = dy + t * dim;
+        const double mu = (double)mean[t], is = (double)invstd[t];
+        double sg = 0.0, sgx = 0.0;
+        for (int64_t d = 0; d < dim; ++d) {
+            const double gd = (double)g[d] * (double)dyt[d];
+            sg += gd;
+            sgx += gd * ((double)xt[d] - mu) * is;
+        }
+        const double mg = sg / (double)dim, mgx = sgx / (double)dim;
+        for (int64_t d = 0; d < dim; ++d) {
+            const double xh = ((double)xt[d] - mu) * is;
+            dx[t * dim + d] = (float)(is * ((double)g[d] * (double)dyt[d] - mg - xh * mgx));
+        }
+    }
+    if (dg || db) {
+#pragma omp parallel for schedule(static)
+        for (int64_t d = 0; d < dim; ++d) {
+            double sw = 0.0, sb = 0.0;
+            for (int64_t t = 0; t < T; ++t) {
+                const double e = (double)dy[t * dim + d];
+                sw += e * ((double)x[t * dim + d] - (double)mean[t]) * (double)invstd[t];
+                sb += e;
+            }
+            if (dg) dg[d] = (float)sw;
+            if (db) db[d] = (float)sb;
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------- */
 /* SwiGLU MLP                                                                */
 /* ------------------------------------------------------------------------- */
 

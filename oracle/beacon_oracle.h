@@ -95,6 +95,18 @@ void bo_rmsnorm_fwd(float* y, float* rms, const float* x, const float* g, int64_
 void bo_rmsnorm_bwd(float* dx, float* dg, const float* dy, const float* x, const float* rms,
                     const float* g, int64_t T, int64_t dim);
 
+/* ---- LayerNorm (crates/beacon-cuda/src/norm.rs:55-95; adjoint lib.rs:78-85) ----
+ * mean[t] = mean_d x[t,d]; invstd[t] = 1 / sqrt(mean_d (x[t,d] - mean[t])^2 + eps)
+ * (biased variance); y = (x - mean) * invstd * g + b.  The saved statistics are mean, invstd.
+ * bwd, with xh = (x - mean) invstd and e = g dy:
+ *   dx = invstd * (e - mean_d e - xh * mean_d(e xh)); dg = sum_t dy xh; db = sum_t dy.
+ * dg or db may be NULL.
+ */
+void bo_layernorm_fwd(float* y, float* mean, float* invstd, const float* x, const float* g, const float* b,
+                      int64_t T, int64_t dim, float eps);
+void bo_layernorm_bwd(float* dx, float* dg, float* db, const float* dy, const float* x, const float* mean,
+                      const float* invstd, const float* g, int64_t T, int64_t dim);
+
 /* ---- SwiGLU MLP (crates/beacon-cuda/src/mlp.rs:12-52; adjoint lib.rs:100-107) ----
  * out[T,dm] = (silu(x Wg) * (x Wu)) Wd, Wg/Wu [dm, F], Wd [F, dm], silu(z) = z / (1 + e^-z).
  * bwd recomputes gate and up and returns dx, dWg, dWu, dWd.

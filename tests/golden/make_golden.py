@@ -76,6 +76,16 @@ def main():
     y.backward(torch.tensor(dy, dtype=torch.float64))
     G["rms_y"], G["rms_rms"], G["rms_dx"], G["rms_dw"] = (y.detach().numpy(), r.detach().numpy()[:, 0],
                                                           tx.grad.numpy(), tw.grad.numpy())
+    # LayerNorm (biased variance, eps 1e-5)
+    x, w, bb, dy = O.normal((8, 96), 13), O.normal((96,), 14), O.normal((96,), 15), O.normal((8, 96), 16)
+    tx, tw, tb = f64(x), f64(w), f64(bb)
+    mu = tx.mean(-1, keepdim=True)
+    inv = 1.0 / torch.sqrt(((tx - mu) ** 2).mean(-1, keepdim=True) + 1e-5)
+    y = (tx - mu) * inv * tw + tb
+    y.backward(torch.tensor(dy, dtype=torch.float64))
+    G["ln_y"], G["ln_mean"], G["ln_invstd"] = (y.detach().numpy(), mu.detach().numpy()[:, 0],
+                                               inv.detach().numpy()[:, 0])
+    G["ln_dx"], G["ln_dw"], G["ln_db"] = tx.grad.numpy(), tw.grad.numpy(), tb.grad.numpy()
     # SwiGLU MLP
     x = O.normal((16, 32), 8)
     wg, wu, wd = O.normal((32, 48), 9, std=0.2), O.normal((32, 48), 10, std=0.2), O.normal((48, 32), 11, std=0.2)

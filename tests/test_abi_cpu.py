@@ -66,8 +66,8 @@ def _launch(kernel, args, scalars):
 
 def test_arena_dispatch_host_checks():
     # IDs outside the hot path answer Unimplemented with their name, like runtime.rs:41
-    assert _launch(b"layernorm_adjoint_fwd", [(0, 16)] * 6, [4, 4]) == _lib.ERR_UNIMPLEMENTED
-    assert "layernorm_adjoint_fwd" in _lib.last_error()
+    assert _launch(b"dropout_fwd", [(0, 16)] * 3, [4]) == _lib.ERR_UNIMPLEMENTED
+    assert "dropout_fwd" in _lib.last_error()
     assert _launch(b"no_such_kernel", [(0, 16)], []) == _lib.ERR_FUNCTION_NOT_FOUND
     # an argument reaching past the arena
     assert _launch(b"matmul_fwd", [(4000, 512), (0, 128), (0, 128)], [8, 4, 8, _lib.BF16]) == \
@@ -78,3 +78,7 @@ def test_arena_dispatch_host_checks():
     # attention scalars must describe the tensors
     assert _launch(b"attention_adjoint_fwd", [(0, 8)] * 5, [1, 1, 4, 0, 1, _lib.BF16]) == \
         _lib.ERR_INVALID_LAUNCH_CONFIG
+    # layernorm: bad scalars, then an argument smaller than the stated rows x dim
+    assert _launch(b"layernorm_adjoint_fwd", [(0, 16)] * 6, [4]) == _lib.ERR_INVALID_LAUNCH_CONFIG
+    assert _launch(b"layernorm_adjoint_bwd", [(0, 64)] * 8, [4, 16, _lib.BF16]) == _lib.ERR_SHAPE_MISMATCH
+    assert "layernorm_adjoint_bwd" in _lib.last_error()

@@ -1,4 +1,4 @@
-"""RMSNorm (norm.rs:19-51), SwiGLU MLP (mlp.rs:12-52), residual add and casts
+"""RMSNorm (norm.rs:19-51), LayerNorm (norm.rs:55-95), SwiGLU MLP (mlp.rs:12-52), residual add and casts
 (elementwise.rs) through the C ABI against the CPU oracle."""
 import numpy as np
 import pytest
@@ -31,6 +31,49 @@ def test_rmsnorm(T, dim, dt):
     rdx, rdg = O.rmsnorm_bwd(dy, x, rr, g)
     assert rel_err(to_np(dx), rdx) <= tol
     assert rel_err(to_np(dg), rdg) <= tol
+
+
+# (2000, 768): more rows than CTAs, so each CTA's dweight / dbias partials cover several rows;
+# (5, 100) and (7, 20) reach the any-dim forward and the scalar backward loop.
+@pytest.mark.parametrize("T,dim,dt", [(64, 4096, "bf16"), (8, 14336, "bf16"), (2000, 768, "bf16"),
+                                      (33, 1000, "f32"), (16, 256, "f32"), (5, 100, "bf16"), (7, 20, "f32")])
+def test_layernorm(T, dim, dt):
+    import torch
+    ops = _ops()
+    tdt = torch.bfloat16 if dt == "bf16" else torch.float32
+    tol = BF16_TOL if dt == "bf16" else F32_TOL
+    r = as_bf16 if dt == "bf16" else (lambda a: a)
+    x, g, b, dy = r(normal((T, dim), 6)), r(normal((dim,), 7)), r(normal((dim,), 8)), r(normal((T, dim), 9))
+    y, mu, inv = ops.layernorm_fwd(to_dev(x, tdt), to_dev(g, tdt), to_dev(b, tdt))
+    ry, rmu, rinv = O.layernorm_fwd(x, g, b)
+    assert rel_err(to_np(y), ry) <= tol
+    assert rel_err(to_np(mu), rmu) <= 1e-5 and rel_err(to_np(inv), rinv) <= 1e-5
+    dx, dg, db = ops.layernorm_bwd(to_dev(dy, tdt), to_dev(x, tdt), mu, inv, to_dev(g, tdt))
+    rdx, rdg, rdb = O.layernorm_bwd(dy, x, rmu, rinv, g)
+    assert rel_err(to_np(dx), rdx) <= tol
+    assert rel_err(to_np(dg), rdg) <= tol
+    assert rel_err(to_np(db), rdb) <= tol
+
+
+def test_layernorm_edges():
+    import torch
+    ops = _ops()
+    dev = "cuda"
+    # constant rows: zero variance, so out = bias up to float32 rounding
+    x = torch.full((4, 512), 2.5, dtype=torch.float32, device=dev)
+    g = torch.randn(512, device=dev)
+    b = torch.randn(512, device=dev)
+    y, mu, inv = ops.layernorm_fwd(x, g, b)
+    assert torch.allclose(y, b.expand_as(y), atol=1e-6)
+    assert torch.allclose(mu, torch.full_like(mu, 2.5))
+    # no rows: the parameter gradients are empty sums
+    x0 = torch.empty((0, 64), dtype=torch.bfloat16, device=dev)
+    g0 = torch.ones(64, dtype=torch.bfloat16, device=dev)
+    y0, mu0, inv0 = ops.layernorm_fwd(x0, g0, g0)
+    assert y0.shape == (0, 64)
+    dx0, dg0, db0 = ops.layernorm_bwd(x0, x0, mu0, inv0, g0)
+    torch.cuda.synchronize()
+    assert dx0.shape == (0, 64) and not dg0.float().any() and not db0.float().any()
 
 
 @pytest.mark.parametrize("T,dm,F,dt", [(128, 256, 512, "bf16"), (200, 128, 320, "bf16"), (64, 64, 96, "f32")])
