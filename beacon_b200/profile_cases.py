@@ -3,10 +3,15 @@
     python -m beacon_b200.profile_cases attn_bwd --heads 32
     python -m beacon_b200.profile_cases attn_fwd --heads 32
     python -m beacon_b200.profile_cases gemm --m 4096 --n 4096 --k 4096
+    python -m beacon_b200.profile_cases layernorm_bwd --tokens 16384 --width 4096
 
 Each case runs `--warmup` untimed launches and then `--iters` launches timed with
 CUDA events, printing the per-launch time and TFLOP/s (algorithmic FLOPs: causal
-attention forward 2*H*S^2*D, backward 2.5x that; GEMM 2*M*N*K).  Sizes default to
+attention forward 2*H*S^2*D, backward 2.5x that; GEMM 2*M*N*K).  The LayerNorm
+cases are HBM-bound and print GB/s of algorithmic bytes instead: the forward reads x
+and writes out (2 * tokens * width * 2 B, bf16) plus 8 B of statistics per row; the
+backward reads x and dy and writes dx (3 * tokens * width * 2 B) plus the statistics
+read, timed over the whole call (row kernel and the two column sums).  Sizes default to
 a case larger than the 126 MB L2 but a few hundred MB on the device, the size an
 ncu capture of a single launch (-k <kernel> -s <warmup launches> -c 1) should use.
 """
@@ -18,7 +23,10 @@ import sys
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["attn_fwd", "attn_bwd", "attn_bwd_recompute", "gemm"])
+    ap.add_argument("case", choices=["attn_fwd", "attn_bwd", "attn_bwd_recompute", "gemm", "layernorm_fwd",
+                                     "layernorm_bwd"])
+    ap.add_argument("--tokens", type=int, default=16384)
+    ap.add_argument("--width", type=int, default=4096)
     ap.add_argument("--heads", type=int, default=32)
     ap.add_argument("--kv-heads", type=int, default=0)
     ap.add_argument("--seq", type=int, default=4096)
@@ -36,6 +44,8 @@ def main(argv=None):
 
     torch.manual_seed(0)
     dev = torch.device("cuda", 0)
+    if a.case.startswith("layernorm"):
+        return _layernorm(a, torch, ops, dev)
     if a.case.startswith("attn"):
         H, S, D = a.heads, a.seq, a.dim
         Hkv = a.kv_heads or H
@@ -78,6 +88,33 @@ def main(argv=None):
         qms /= max(qn, 1)
         print(f"{a.case}: k_attn_bwd_dq {qms:.4f} ms/launch {0.6 * flops / (qms * 1e-3) / 1e12:.1f} TFLOP/s executed",
               flush=True)
+    ops.device_status(0)
+    return 0
+
+
+def _layernorm(a, torch, ops, dev):
+    T, W = a.tokens, a.width
+    x = torch.randn(T, W, device=dev).bfloat16()
+    dy = torch.randn(T, W, device=dev).bfloat16()
+    g = torch.randn(W, device=dev).bfloat16()
+    b = torch.randn(W, device=dev).bfloat16()
+    out, mean, invstd = ops.layernorm_fwd(x, g, b)
+    if a.case == "layernorm_fwd":
+        fn, nbytes = (lambda: ops.layernorm_fwd(x, g, b)), 2.0 * T * W * 2 + 8.0 * T
+    else:
+        fn, nbytes = (lambda: ops.layernorm_bwd(dy, x, mean, invstd, g)), 3.0 * T * W * 2 + 8.0 * T
+    for _ in range(a.warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.iters
+    print(f"{a.case}: tokens {T} width {W} bf16 {ms:.4f} ms/call {nbytes / (ms * 1e-3) / 1e9:.0f} GB/s algorithmic",
+          flush=True)
     ops.device_status(0)
     return 0
 
