@@ -900,21 +900,49 @@ extern "C" int beacon_layernorm_adjoint_bwd(void* dx, void* dweight, void* dbias
   if (!dx || !dy || !x || !mean || !invstd || !weight)
     return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "layernorm_bwd: null pointer");
   const bool vec = aligned16(dx) && aligned16(dy) && aligned16(x) && aligned16(weight) && dim % 8 == 0;
-  const int grid = (int)std::min<int64_t>(tokens, (int64_t)di->sms * 4);
+  // Register-resident rows (k_layernorm_bwd_rows) up to 8192 bf16 / 4096 f32 columns;
+  // beyond that, or with a misaligned workspace, the partials go through global memory.
+  int rows_vec = 0;
+  if (vec) {
+    if (dim <= 256 * 8) rows_vec = 1;
+    else if (dim <= 256 * 8 * 2) rows_vec = 2;
+    else if (dim <= 256 * 8 * 4 && dtype == BEACON_BF16) rows_vec = 4;
+  }
+  const void* rows_fn = nullptr;
+  if (rows_vec == 1) rows_fn = dtype == BEACON_BF16 ? (const void*)k_layernorm_bwd_rows<bf16, 1>
+                                                    : (const void*)k_layernorm_bwd_rows<float, 1>;
+  if (rows_vec == 2) rows_fn = dtype == BEACON_BF16 ? (const void*)k_layernorm_bwd_rows<bf16, 2>
+                                                    : (const void*)k_layernorm_bwd_rows<float, 2>;
+  if (rows_vec == 4) rows_fn = (const void*)k_layernorm_bwd_rows<bf16, 4>;
+  int per_sm = 4;  // resident CTAs per SM for the grid (one wave)
+  if (rows_fn) {
+    int nb = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, rows_fn, 256, 0) == cudaSuccess && nb > 0) per_sm = nb;
+    cudaGetLastError();
+  }
+  const int grid = (int)std::min<int64_t>(tokens, (int64_t)di->sms * per_sm);
   const size_t part_bytes = (size_t)grid * dim * 4;
   const int nparts = (dweight ? 1 : 0) + (dbias ? 1 : 0);
   float *part_w = nullptr, *part_b = nullptr;
   if (nparts) {
     void* ws = nullptr;
     BEACON_TRY(get_workspace(dev, part_bytes * nparts, workspace, workspace_bytes, &ws));
+    if (!aligned16(ws)) rows_fn = nullptr;
     float* p = reinterpret_cast<float*>(ws);
     if (dweight) part_w = p, p += (size_t)grid * dim;
     if (dbias) part_b = p;
   }
   const unsigned cgrid = (unsigned)((dim + 255) / 256);
+#define LN_BWD_ROWS(T, V)                                                                                       \
+  k_layernorm_bwd_rows<T, V><<<grid, 256, 0, st>>>((T*)dx, part_w, part_b, (const T*)dy, (const T*)x, mean,     \
+                                                   invstd, (const T*)weight, tokens, (int)dim)
   if (dtype == BEACON_BF16) {
-    k_layernorm_bwd<bf16><<<grid, 256, 0, st>>>((bf16*)dx, part_w, part_b, (const bf16*)dy, (const bf16*)x, mean,
-                                                invstd, (const bf16*)weight, tokens, (int)dim, vec);
+    if (rows_fn && rows_vec == 1) LN_BWD_ROWS(bf16, 1);
+    else if (rows_fn && rows_vec == 2) LN_BWD_ROWS(bf16, 2);
+    else if (rows_fn && rows_vec == 4) LN_BWD_ROWS(bf16, 4);
+    else
+      k_layernorm_bwd<bf16><<<grid, 256, 0, st>>>((bf16*)dx, part_w, part_b, (const bf16*)dy, (const bf16*)x, mean,
+                                                  invstd, (const bf16*)weight, tokens, (int)dim, vec);
     BEACON_TRY(check_launch("layernorm_bwd"));
     if (dweight) {
       k_colsum<bf16><<<cgrid, 256, 0, st>>>((bf16*)dweight, part_w, grid, (int)dim);
@@ -925,8 +953,11 @@ extern "C" int beacon_layernorm_adjoint_bwd(void* dx, void* dweight, void* dbias
       BEACON_TRY(check_launch("layernorm_bwd dbias colsum"));
     }
   } else {
-    k_layernorm_bwd<float><<<grid, 256, 0, st>>>((float*)dx, part_w, part_b, (const float*)dy, (const float*)x,
-                                                 mean, invstd, (const float*)weight, tokens, (int)dim, vec);
+    if (rows_fn && rows_vec == 1) LN_BWD_ROWS(float, 1);
+    else if (rows_fn && rows_vec == 2) LN_BWD_ROWS(float, 2);
+    else
+      k_layernorm_bwd<float><<<grid, 256, 0, st>>>((float*)dx, part_w, part_b, (const float*)dy, (const float*)x,
+                                                   mean, invstd, (const float*)weight, tokens, (int)dim, vec);
     BEACON_TRY(check_launch("layernorm_bwd"));
     if (dweight) {
       k_colsum<float><<<cgrid, 256, 0, st>>>((float*)dweight, part_w, grid, (int)dim);
@@ -937,6 +968,7 @@ extern "C" int beacon_layernorm_adjoint_bwd(void* dx, void* dweight, void* dbias
       BEACON_TRY(check_launch("layernorm_bwd dbias colsum"));
     }
   }
+#undef LN_BWD_ROWS
   return BEACON_OK;
 }
 

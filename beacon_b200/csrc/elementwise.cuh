@@ -539,6 +539,76 @@ __global__ void __launch_bounds__(256) k_layernorm_bwd(T* __restrict__ dx, float
   }
 }
 
+// Backward for dim % 8 == 0, dim <= 256 * 8 * VEC and 16-byte aligned pointers
+// (part_w / part_b included).  Same arithmetic as k_layernorm_bwd, but a thread
+// owns the same 8 * VEC columns of every row its CTA visits, so the weight, the row
+// (x and dy, read once from HBM) and the dweight / dbias partial sums all stay in
+// registers; each CTA writes its two partial rows once, at the end.
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) k_layernorm_bwd_rows(T* __restrict__ dx, float* __restrict__ part_w,
+                                                            float* __restrict__ part_b, const T* __restrict__ dy,
+                                                            const T* __restrict__ x, const float* __restrict__ mean,
+                                                            const float* __restrict__ invstd,
+                                                            const T* __restrict__ w, long long rows, int dim) {
+  __shared__ float red[16];
+  const int nvec = dim / 8;
+  float g[VEC][8], aw[VEC][8], ab[VEC][8];
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    const int vi = threadIdx.x + i * 256;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) aw[i][j] = ab[i][j] = g[i][j] = 0.0f;
+    if (vi < nvec) load8(w + vi * 8, g[i]);
+  }
+  for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
+    const T* xr = x + r * dim;
+    const T* dyr = dy + r * dim;
+    const float mu = mean[r], is = invstd[r];
+    float xh[VEC][8], d[VEC][8];
+    float sg = 0.0f, sgx = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const int vi = threadIdx.x + i * 256;
+      if (vi < nvec) {
+        load8(xr + vi * 8, xh[i]);
+        load8(dyr + vi * 8, d[i]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          xh[i][j] = (xh[i][j] - mu) * is;
+          const float e = g[i][j] * d[i][j];
+          sg += e;
+          sgx = fmaf(e, xh[i][j], sgx);
+        }
+      }
+    }
+    block_sum2_256(sg, sgx, red);
+    const float mg = sg / (float)dim, mgx = sgx / (float)dim;
+    T* dxr = dx + r * dim;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const int vi = threadIdx.x + i * 256;
+      if (vi < nvec) {
+        float o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          o[j] = is * (g[i][j] * d[i][j] - mg - xh[i][j] * mgx);
+          aw[i][j] = fmaf(d[i][j], xh[i][j], aw[i][j]);
+          ab[i][j] += d[i][j];
+        }
+        store8(dxr + vi * 8, o);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    const int vi = threadIdx.x + i * 256;
+    if (vi < nvec) {
+      if (part_w) store8(part_w + (long long)blockIdx.x * dim + vi * 8, aw[i]);
+      if (part_b) store8(part_b + (long long)blockIdx.x * dim + vi * 8, ab[i]);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // SwiGLU elementwise pieces (mlp.rs:12-52); silu(z) = z * sigmoid(z)
 // ---------------------------------------------------------------------------

@@ -34,8 +34,10 @@ def test_rmsnorm(T, dim, dt):
 
 
 # (2000, 768): more rows than CTAs, so each CTA's dweight / dbias partials cover several rows;
-# (5, 100) and (7, 20) reach the any-dim forward and the scalar backward loop.
-@pytest.mark.parametrize("T,dim,dt", [(64, 4096, "bf16"), (8, 14336, "bf16"), (2000, 768, "bf16"),
+# widths up to 8192 (bf16) / 4096 (f32) take the register-resident backward, (8, 14336) the
+# one with partials in global memory; (5, 100) and (7, 20) reach the any-dim forward and the
+# scalar backward loop.
+@pytest.mark.parametrize("T,dim,dt", [(64, 4096, "bf16"), (8, 14336, "bf16"), (2000, 768, "bf16"), (40, 6144, "bf16"),
                                       (33, 1000, "f32"), (16, 256, "f32"), (5, 100, "bf16"), (7, 20, "f32")])
 def test_layernorm(T, dim, dt):
     import torch
