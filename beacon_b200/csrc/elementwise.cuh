@@ -1,4 +1,4 @@
-// elementwise.cuh -- residual add, casts, RMSNorm forward/backward.
+// elementwise.cuh -- residual add, casts, RMSNorm and LayerNorm forward/backward.
 //
 // All HBM-bound: 128-bit vectorised, coalesced loads and stores, fp32 math,
 // warp-shuffle reductions.  The dtype codecs restate the reference's bit-level
@@ -364,6 +364,36 @@ __global__ void __launch_bounds__(256) k_colsum_partial(float* __restrict__ part
 // variance; mean and invstd are saved per row as f32 (adjoint lib.rs:78-85).
 // ---------------------------------------------------------------------------
 
+// 8 elements held as their raw 16-byte words (one uint4 for bf16, two for f32), so a
+// row can be fetched one iteration ahead at half (bf16) the registers of floats.
+template <typename T>
+struct Raw8 {
+  uint4 u[sizeof(T) / 2];
+};
+template <typename T>
+__device__ __forceinline__ void ldraw(const T* p, Raw8<T>& r) {
+#pragma unroll
+  for (int k = 0; k < (int)(sizeof(T) / 2); ++k) r.u[k] = reinterpret_cast<const uint4*>(p)[k];
+}
+__device__ __forceinline__ void unraw(const Raw8<__nv_bfloat16>& r, float (&v)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r.u[0]);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = __bfloat1622float2(h[j]);
+    v[2 * j] = f.x;
+    v[2 * j + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void unraw(const Raw8<float>& r, float (&v)[8]) {
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    v[4 * k] = __uint_as_float(r.u[k].x);
+    v[4 * k + 1] = __uint_as_float(r.u[k].y);
+    v[4 * k + 2] = __uint_as_float(r.u[k].z);
+    v[4 * k + 3] = __uint_as_float(r.u[k].w);
+  }
+}
+
 // Two block-wide sums at once for blockDim.x == 256; `red` holds 16 floats.
 __device__ __forceinline__ void block_sum2_256(float& a, float& b, float* red) {
   a = warp_sum(a);
@@ -382,8 +412,10 @@ __device__ __forceinline__ void block_sum2_256(float& a, float& b, float* red) {
 // One CTA of 256 threads per row (norm.rs:5-9 `rowwise`), grid-stride over rows.
 // The row stays in registers from the load to the store: the variance is taken
 // about the mean (two reductions, no E[x^2] - E[x]^2 cancellation) at one HBM
-// read and one write per element.  dim % 8 == 0, dim <= 256 * 8 * VEC and
-// 16-byte aligned pointers (the host picks k_layernorm_fwd_any otherwise).
+// read and one write per element.  The next row's words are fetched before this
+// row's reductions, so each CTA keeps a row of loads in flight while it waits at
+// the barriers.  dim % 8 == 0, dim <= 256 * 8 * VEC and 16-byte aligned pointers
+// (the host picks k_layernorm_fwd_any otherwise).
 template <typename T, int VEC>
 __global__ void __launch_bounds__(256) k_layernorm_fwd(T* __restrict__ y, float* __restrict__ mean,
                                                        float* __restrict__ invstd, const T* __restrict__ x,
@@ -391,17 +423,33 @@ __global__ void __launch_bounds__(256) k_layernorm_fwd(T* __restrict__ y, float*
                                                        long long rows, int dim, float eps) {
   __shared__ float red[8];
   const int nvec = dim / 8;
-  for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
-    const T* xr = x + r * dim;
+  Raw8<T> nx[VEC];
+  long long r = blockIdx.x;
+  if (r < rows) {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const int vi = threadIdx.x + i * 256;
+      if (vi < nvec) ldraw(x + r * dim + vi * 8, nx[i]);
+    }
+  }
+  for (; r < rows; r += gridDim.x) {
     float v[VEC][8];
     float s = 0.0f;
 #pragma unroll
     for (int i = 0; i < VEC; ++i) {
       const int vi = threadIdx.x + i * 256;
       if (vi < nvec) {
-        load8(xr + vi * 8, v[i]);
+        unraw(nx[i], v[i]);
 #pragma unroll
         for (int j = 0; j < 8; ++j) s += v[i][j];
+      }
+    }
+    const long long rn = r + gridDim.x;
+    if (rn < rows) {
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        const int vi = threadIdx.x + i * 256;
+        if (vi < nvec) ldraw(x + rn * dim + vi * 8, nx[i]);
       }
     }
     const float mu = block_sum_256(s, red) / (float)dim;
@@ -541,41 +589,73 @@ __global__ void __launch_bounds__(256) k_layernorm_bwd(T* __restrict__ dx, float
 
 // Backward for dim % 8 == 0, dim <= 256 * 8 * VEC and 16-byte aligned pointers
 // (part_w / part_b included).  Same arithmetic as k_layernorm_bwd, but a thread
-// owns the same 8 * VEC columns of every row its CTA visits, so the weight, the row
-// (x and dy, read once from HBM) and the dweight / dbias partial sums all stay in
-// registers; each CTA writes its two partial rows once, at the end.
+// owns the same 8 * VEC columns of every row its CTA visits, so the row (x and dy,
+// read once from HBM) and the dweight / dbias partial sums stay in registers, and
+// each CTA writes its two partial rows once, at the end.  The next row's x and dy
+// words are fetched before this row's reduction; the weight is re-read per row
+// (an L1 hit) to leave registers for them.
 template <typename T, int VEC>
-__global__ void __launch_bounds__(256) k_layernorm_bwd_rows(T* __restrict__ dx, float* __restrict__ part_w,
-                                                            float* __restrict__ part_b, const T* __restrict__ dy,
-                                                            const T* __restrict__ x, const float* __restrict__ mean,
-                                                            const float* __restrict__ invstd,
-                                                            const T* __restrict__ w, long long rows, int dim) {
+__global__ void __launch_bounds__(256, VEC <= 2 ? 2 : 1)
+    k_layernorm_bwd_rows(T* __restrict__ dx, float* __restrict__ part_w, float* __restrict__ part_b,
+                         const T* __restrict__ dy, const T* __restrict__ x, const float* __restrict__ mean,
+                         const float* __restrict__ invstd, const T* __restrict__ w, long long rows, int dim) {
   __shared__ float red[16];
   const int nvec = dim / 8;
-  float g[VEC][8], aw[VEC][8], ab[VEC][8];
+  float aw[VEC][8], ab[VEC][8];
 #pragma unroll
-  for (int i = 0; i < VEC; ++i) {
-    const int vi = threadIdx.x + i * 256;
+  for (int i = 0; i < VEC; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) aw[i][j] = ab[i][j] = g[i][j] = 0.0f;
-    if (vi < nvec) load8(w + vi * 8, g[i]);
+    for (int j = 0; j < 8; ++j) aw[i][j] = ab[i][j] = 0.0f;
+  Raw8<T> nx[VEC], nd[VEC];
+  float nmu = 0.0f, nis = 0.0f;
+  long long r = blockIdx.x;
+  if (r < rows) {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const int vi = threadIdx.x + i * 256;
+      if (vi < nvec) {
+        ldraw(x + r * dim + vi * 8, nx[i]);
+        ldraw(dy + r * dim + vi * 8, nd[i]);
+      }
+    }
+    nmu = mean[r];
+    nis = invstd[r];
   }
-  for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
-    const T* xr = x + r * dim;
-    const T* dyr = dy + r * dim;
-    const float mu = mean[r], is = invstd[r];
+  for (; r < rows; r += gridDim.x) {
+    const float mu = nmu, is = nis;
     float xh[VEC][8], d[VEC][8];
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const int vi = threadIdx.x + i * 256;
+      if (vi < nvec) {
+        unraw(nx[i], xh[i]);
+        unraw(nd[i], d[i]);
+      }
+    }
+    const long long rn = r + gridDim.x;
+    if (rn < rows) {
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        const int vi = threadIdx.x + i * 256;
+        if (vi < nvec) {
+          ldraw(x + rn * dim + vi * 8, nx[i]);
+          ldraw(dy + rn * dim + vi * 8, nd[i]);
+        }
+      }
+      nmu = mean[rn];
+      nis = invstd[rn];
+    }
     float sg = 0.0f, sgx = 0.0f;
 #pragma unroll
     for (int i = 0; i < VEC; ++i) {
       const int vi = threadIdx.x + i * 256;
       if (vi < nvec) {
-        load8(xr + vi * 8, xh[i]);
-        load8(dyr + vi * 8, d[i]);
+        float g[8];
+        load8(w + vi * 8, g);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           xh[i][j] = (xh[i][j] - mu) * is;
-          const float e = g[i][j] * d[i][j];
+          const float e = g[j] * d[i][j];
           sg += e;
           sgx = fmaf(e, xh[i][j], sgx);
         }
@@ -588,10 +668,11 @@ __global__ void __launch_bounds__(256) k_layernorm_bwd_rows(T* __restrict__ dx, 
     for (int i = 0; i < VEC; ++i) {
       const int vi = threadIdx.x + i * 256;
       if (vi < nvec) {
-        float o[8];
+        float g[8], o[8];
+        load8(w + vi * 8, g);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          o[j] = is * (g[i][j] * d[i][j] - mg - xh[i][j] * mgx);
+          o[j] = is * (g[j] * d[i][j] - mg - xh[i][j] * mgx);
           aw[i][j] = fmaf(d[i][j], xh[i][j], aw[i][j]);
           ab[i][j] += d[i][j];
         }
