@@ -932,7 +932,7 @@ extern "C" int beacon_layernorm_adjoint_bwd(void* dx, void* dweight, void* dbias
     if (dweight) part_w = p, p += (size_t)grid * dim;
     if (dbias) part_b = p;
   }
-  const unsigned cgrid = (unsigned)((dim + 255) / 256);
+  const dim3 cgrid((unsigned)((dim + 31) / 32), 2);
 #define LN_BWD_ROWS(T, V)                                                                                       \
   k_layernorm_bwd_rows<T, V><<<grid, 256, 0, st>>>((T*)dx, part_w, part_b, (const T*)dy, (const T*)x, mean,     \
                                                    invstd, (const T*)weight, tokens, (int)dim)
@@ -944,14 +944,8 @@ extern "C" int beacon_layernorm_adjoint_bwd(void* dx, void* dweight, void* dbias
       k_layernorm_bwd<bf16><<<grid, 256, 0, st>>>((bf16*)dx, part_w, part_b, (const bf16*)dy, (const bf16*)x, mean,
                                                   invstd, (const bf16*)weight, tokens, (int)dim, vec);
     BEACON_TRY(check_launch("layernorm_bwd"));
-    if (dweight) {
-      k_colsum<bf16><<<cgrid, 256, 0, st>>>((bf16*)dweight, part_w, grid, (int)dim);
-      BEACON_TRY(check_launch("layernorm_bwd dweight colsum"));
-    }
-    if (dbias) {
-      k_colsum<bf16><<<cgrid, 256, 0, st>>>((bf16*)dbias, part_b, grid, (int)dim);
-      BEACON_TRY(check_launch("layernorm_bwd dbias colsum"));
-    }
+    if (nparts)
+      k_colsum_split2<bf16><<<cgrid, 256, 0, st>>>((bf16*)dweight, part_w, (bf16*)dbias, part_b, grid, (int)dim);
   } else {
     if (rows_fn && rows_vec == 1) LN_BWD_ROWS(float, 1);
     else if (rows_fn && rows_vec == 2) LN_BWD_ROWS(float, 2);
@@ -959,15 +953,10 @@ extern "C" int beacon_layernorm_adjoint_bwd(void* dx, void* dweight, void* dbias
       k_layernorm_bwd<float><<<grid, 256, 0, st>>>((float*)dx, part_w, part_b, (const float*)dy, (const float*)x,
                                                    mean, invstd, (const float*)weight, tokens, (int)dim, vec);
     BEACON_TRY(check_launch("layernorm_bwd"));
-    if (dweight) {
-      k_colsum<float><<<cgrid, 256, 0, st>>>((float*)dweight, part_w, grid, (int)dim);
-      BEACON_TRY(check_launch("layernorm_bwd dweight colsum"));
-    }
-    if (dbias) {
-      k_colsum<float><<<cgrid, 256, 0, st>>>((float*)dbias, part_b, grid, (int)dim);
-      BEACON_TRY(check_launch("layernorm_bwd dbias colsum"));
-    }
+    if (nparts)
+      k_colsum_split2<float><<<cgrid, 256, 0, st>>>((float*)dweight, part_w, (float*)dbias, part_b, grid, (int)dim);
   }
+  if (nparts) BEACON_TRY(check_launch("layernorm_bwd colsum"));
 #undef LN_BWD_ROWS
   return BEACON_OK;
 }

@@ -690,6 +690,33 @@ __global__ void __launch_bounds__(256, VEC <= 2 ? 2 : 1)
   }
 }
 
+// out{0,1}[d] = sum_i part{0,1}[i, d] for the LayerNorm parameter gradients, both in
+// one launch (blockIdx.y picks the pair; a null `out` skips it).  A CTA owns 32
+// columns and its 8 warps split the partial rows, so each thread issues
+// nparts / 8 coalesced loads instead of nparts.
+template <typename T>
+__global__ void __launch_bounds__(256) k_colsum_split2(T* __restrict__ out0, const float* __restrict__ part0,
+                                                       T* __restrict__ out1, const float* __restrict__ part1,
+                                                       int nparts, int dim) {
+  __shared__ float red[8][33];
+  T* out = blockIdx.y ? out1 : out0;
+  const float* part = blockIdx.y ? part1 : part0;
+  if (out == nullptr) return;  // uniform across the CTA
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  const int d = blockIdx.x * 32 + lane;
+  float s = 0.0f;
+  if (d < dim)
+    for (int i = wp; i < nparts; i += 8) s += part[(long long)i * dim + d];
+  red[wp][lane] = s;
+  __syncthreads();
+  if (wp == 0 && d < dim) {
+    float t = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += red[k][lane];
+    stf(out + d, t);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // SwiGLU elementwise pieces (mlp.rs:12-52); silu(z) = z * sigmoid(z)
 // ---------------------------------------------------------------------------
