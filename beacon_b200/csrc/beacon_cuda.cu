@@ -812,24 +812,60 @@ extern "C" int beacon_rmsnorm_adjoint_bwd(void* dx, void* dweight, const void* d
   }
   const bool vec = aligned16(dx) && aligned16(x) && aligned16(dy) && aligned16(weight);
   if (!vec) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "rmsnorm_bwd: pointers must be 16-byte aligned");
-  const int grid = (int)std::min<int64_t>(tokens, (int64_t)di->sms * 4);
+  // Register-resident rows (k_rmsnorm_bwd_rows) up to 8192 bf16 / 4096 f32 columns;
+  // beyond that, for dim % 8 != 0 or with a misaligned workspace, k_rmsnorm_bwd.
+  int rows_vec = 0;
+  if (dim % 8 == 0) {
+    if (dim <= 256 * 8) rows_vec = 1;
+    else if (dim <= 256 * 8 * 2) rows_vec = 2;
+    else if (dim <= 256 * 8 * 4 && dtype == BEACON_BF16) rows_vec = 4;
+  }
+  const void* rows_fn = nullptr;
+  if (rows_vec == 1) rows_fn = dtype == BEACON_BF16 ? (const void*)k_rmsnorm_bwd_rows<bf16, 1>
+                                                    : (const void*)k_rmsnorm_bwd_rows<float, 1>;
+  if (rows_vec == 2) rows_fn = dtype == BEACON_BF16 ? (const void*)k_rmsnorm_bwd_rows<bf16, 2>
+                                                    : (const void*)k_rmsnorm_bwd_rows<float, 2>;
+  if (rows_vec == 4) rows_fn = (const void*)k_rmsnorm_bwd_rows<bf16, 4>;
+  int per_sm = 4;  // resident CTAs per SM for the grid (one wave)
+  if (rows_fn) {
+    int nb = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, rows_fn, 256, 0) == cudaSuccess && nb > 0) per_sm = nb;
+    cudaGetLastError();
+  }
+  const int grid = (int)std::min<int64_t>(tokens, (int64_t)di->sms * per_sm);
   float* part = nullptr;
   if (dweight) {
     void* ws = nullptr;
     BEACON_TRY(get_workspace(dev, (size_t)grid * dim * 4, workspace, workspace_bytes, &ws));
+    if (!aligned16(ws)) rows_fn = nullptr;
     part = reinterpret_cast<float*>(ws);
   }
+#define RMS_BWD_ROWS(T, V)                                                                                  \
+  k_rmsnorm_bwd_rows<T, V><<<grid, 256, 0, st>>>((T*)dx, part, (const T*)dy, (const T*)x, rms, (const T*)weight, \
+                                                 tokens, (int)dim)
   if (dtype == BEACON_BF16) {
-    k_rmsnorm_bwd<bf16><<<grid, 256, 0, st>>>((bf16*)dx, part, (const bf16*)dy, (const bf16*)x, rms,
-                                              (const bf16*)weight, tokens, (int)dim);
+    if (rows_fn && rows_vec == 1) RMS_BWD_ROWS(bf16, 1);
+    else if (rows_fn && rows_vec == 2) RMS_BWD_ROWS(bf16, 2);
+    else if (rows_fn && rows_vec == 4) RMS_BWD_ROWS(bf16, 4);
+    else
+      k_rmsnorm_bwd<bf16><<<grid, 256, 0, st>>>((bf16*)dx, part, (const bf16*)dy, (const bf16*)x, rms,
+                                                (const bf16*)weight, tokens, (int)dim);
     BEACON_TRY(check_launch("rmsnorm_bwd"));
-    if (dweight) k_colsum<bf16><<<(unsigned)((dim + 255) / 256), 256, 0, st>>>((bf16*)dweight, part, grid, (int)dim);
+    if (dweight)
+      k_colsum_split2<bf16><<<dim3((unsigned)((dim + 31) / 32), 1), 256, 0, st>>>((bf16*)dweight, part, nullptr,
+                                                                                  nullptr, grid, (int)dim);
   } else {
-    k_rmsnorm_bwd<float><<<grid, 256, 0, st>>>((float*)dx, part, (const float*)dy, (const float*)x, rms,
-                                               (const float*)weight, tokens, (int)dim);
+    if (rows_fn && rows_vec == 1) RMS_BWD_ROWS(float, 1);
+    else if (rows_fn && rows_vec == 2) RMS_BWD_ROWS(float, 2);
+    else
+      k_rmsnorm_bwd<float><<<grid, 256, 0, st>>>((float*)dx, part, (const float*)dy, (const float*)x, rms,
+                                                 (const float*)weight, tokens, (int)dim);
     BEACON_TRY(check_launch("rmsnorm_bwd"));
-    if (dweight) k_colsum<float><<<(unsigned)((dim + 255) / 256), 256, 0, st>>>((float*)dweight, part, grid, (int)dim);
+    if (dweight)
+      k_colsum_split2<float><<<dim3((unsigned)((dim + 31) / 32), 1), 256, 0, st>>>((float*)dweight, part, nullptr,
+                                                                                   nullptr, grid, (int)dim);
   }
+#undef RMS_BWD_ROWS
   if (dweight) BEACON_TRY(check_launch("rmsnorm_bwd colsum"));
   return BEACON_OK;
 }

@@ -717,6 +717,97 @@ __global__ void __launch_bounds__(256) k_colsum_split2(T* __restrict__ out0, con
   }
 }
 
+// RMSNorm backward for dim % 8 == 0, dim <= 256 * 8 * VEC and 16-byte aligned
+// pointers (part included): the arithmetic of k_rmsnorm_bwd with the row layout of
+// k_layernorm_bwd_rows (row and dweight partials in registers, next row fetched
+// before the reduction, one partial row per CTA written at the end).
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256, VEC <= 2 ? 2 : 1)
+    k_rmsnorm_bwd_rows(T* __restrict__ dx, float* __restrict__ part, const T* __restrict__ dy,
+                       const T* __restrict__ x, const float* __restrict__ rms, const T* __restrict__ w,
+                       long long rows, int dim) {
+  __shared__ float red[8];
+  const int nvec = dim / 8;
+  float aw[VEC][8];
+#pragma unroll
+  for (int i = 0; i < VEC; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) aw[i][j] = 0.0f;
+  Raw8<T> nx[VEC], nd[VEC];
+  float nr = 1.0f;
+  long long r = blockIdx.x;
+  if (r < rows) {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const int vi = threadIdx.x + i * 256;
+      if (vi < nvec) {
+        ldraw(x + r * dim + vi * 8, nx[i]);
+        ldraw(dy + r * dim + vi * 8, nd[i]);
+      }
+    }
+    nr = rms[r];
+  }
+  for (; r < rows; r += gridDim.x) {
+    const float inv = 1.0f / nr;
+    float a[VEC][8], d[VEC][8];
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const int vi = threadIdx.x + i * 256;
+      if (vi < nvec) {
+        unraw(nx[i], a[i]);
+        unraw(nd[i], d[i]);
+      }
+    }
+    const long long rn = r + gridDim.x;
+    if (rn < rows) {
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        const int vi = threadIdx.x + i * 256;
+        if (vi < nvec) {
+          ldraw(x + rn * dim + vi * 8, nx[i]);
+          ldraw(dy + rn * dim + vi * 8, nd[i]);
+        }
+      }
+      nr = rms[rn];
+    }
+    float dot = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const int vi = threadIdx.x + i * 256;
+      if (vi < nvec) {
+        float g[8];
+        load8(w + vi * 8, g);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dot = fmaf(g[j] * d[i][j], a[i][j], dot);
+      }
+    }
+    dot = block_sum_256(dot, red);
+    const float c = dot * inv * inv * inv / (float)dim;
+    T* dxr = dx + r * dim;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const int vi = threadIdx.x + i * 256;
+      if (vi < nvec) {
+        float g[8], o[8];
+        load8(w + vi * 8, g);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          o[j] = g[j] * d[i][j] * inv - a[i][j] * c;
+          aw[i][j] += d[i][j] * a[i][j] * inv;
+        }
+        store8(dxr + vi * 8, o);
+      }
+    }
+  }
+  if (part) {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const int vi = threadIdx.x + i * 256;
+      if (vi < nvec) store8(part + (long long)blockIdx.x * dim + vi * 8, aw[i]);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // SwiGLU elementwise pieces (mlp.rs:12-52); silu(z) = z * sigmoid(z)
 // ---------------------------------------------------------------------------

@@ -8,7 +8,8 @@
 Each case runs `--warmup` untimed launches and then `--iters` launches timed with
 CUDA events, printing the per-launch time and TFLOP/s (algorithmic FLOPs: causal
 attention forward 2*H*S^2*D, backward 2.5x that; GEMM 2*M*N*K).  The LayerNorm
-cases are HBM-bound and print GB/s of algorithmic bytes instead: the forward reads x
+and RMSNorm backward cases are HBM-bound and print GB/s of algorithmic bytes instead
+(RMSNorm backward: x, dy in, dx out, 4 B of rms per row): the LayerNorm forward reads x
 and writes out (2 * tokens * width * 2 B, bf16) plus 8 B of statistics per row; the
 backward reads x and dy and writes dx (3 * tokens * width * 2 B) plus the statistics
 read, timed over the whole call (row kernel and the two column sums).  Sizes default to
@@ -24,7 +25,7 @@ import sys
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["attn_fwd", "attn_bwd", "attn_bwd_recompute", "gemm", "layernorm_fwd",
-                                     "layernorm_bwd"])
+                                     "layernorm_bwd", "rmsnorm_bwd"])
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--width", type=int, default=4096)
     ap.add_argument("--heads", type=int, default=32)
@@ -44,7 +45,7 @@ def main(argv=None):
 
     torch.manual_seed(0)
     dev = torch.device("cuda", 0)
-    if a.case.startswith("layernorm"):
+    if a.case.startswith(("layernorm", "rmsnorm")):
         return _layernorm(a, torch, ops, dev)
     if a.case.startswith("attn"):
         H, S, D = a.heads, a.seq, a.dim
@@ -101,6 +102,9 @@ def _layernorm(a, torch, ops, dev):
     out, mean, invstd = ops.layernorm_fwd(x, g, b)
     if a.case == "layernorm_fwd":
         fn, nbytes = (lambda: ops.layernorm_fwd(x, g, b)), 2.0 * T * W * 2 + 8.0 * T
+    elif a.case == "rmsnorm_bwd":
+        _, rms = ops.rmsnorm_fwd(x, g)
+        fn, nbytes = (lambda: ops.rmsnorm_bwd(dy, x, rms, g)), 3.0 * T * W * 2 + 4.0 * T
     else:
         fn, nbytes = (lambda: ops.layernorm_bwd(dy, x, mean, invstd, g)), 3.0 * T * W * 2 + 8.0 * T
     for _ in range(a.warmup):

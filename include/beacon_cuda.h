@@ -10,7 +10,8 @@
  *
  * Conventions
  *  - Row-major contiguous tensors: matrices [rows, cols]; attention tensors
- *    [B, H, S, D]; LSE [B, H, S] float32; RMSNorm statistic rms [tokens] float32.
+ *    [B, H, S, D]; LSE [B, H, S] float32; RMSNorm statistic rms and LayerNorm
+ *    statistics mean, invstd: [tokens] float32.
  *  - `dtype` is a beacon_dtype (crates/beacon-core/src/dtype.rs:1-6 order).
  *    BEACON_BF16: bf16 operands, fp32 accumulation on tcgen05 tensor cores.
  *    BEACON_F32 : exact fp32 FFMA (no TF32) -- the 1e-5 parity path.
@@ -182,7 +183,8 @@ int beacon_rmsnorm_adjoint_bwd(void* dx, void* dweight, const void* dy, const vo
  * for callers that cannot allocate device memory themselves (a launcher that only
  * hands out pointers into one preallocated arena, a path that cannot afford the
  * first-call cudaMalloc and device synchronisation of the library's own workspace).
- * Same results as beacon_rmsnorm_adjoint_bwd; the dweight partial sums live in a
+ * Same arithmetic as beacon_rmsnorm_adjoint_bwd (results agree up to the float32
+ * summation order of dweight); the dweight partial sums live in a
  * fixed 4 MiB (1,048,576-float) array compiled into the library, which every GPU
  * that loads the library holds until exit.  dim above 1,048,576 is rejected with
  * BEACON_ERR_INVALID_LAUNCH_CONFIG.  The array's address is looked up on the first
