@@ -249,14 +249,14 @@ class RmsNormLaunch:
 
 
 class LayerNormLaunch:
-    """norm.rs:55-95 (outside the hot path: the library answers Unimplemented, as the reference does)"""
+    """norm.rs:55-95"""
 
-    def layernorm_fwd(self, out, x, weight, bias, mean, invstd, tokens, dim):
-        self.launch(kid.LAYERNORM_FWD, rowwise(tokens), [out, x, weight, bias, mean, invstd], (tokens, dim))
+    def layernorm_fwd(self, out, x, weight, bias, mean, invstd, tokens, dim, dtype=BF16):
+        self.launch(kid.LAYERNORM_FWD, rowwise(tokens), [out, x, weight, bias, mean, invstd], (tokens, dim, dtype))
 
-    def layernorm_bwd(self, dx, dweight, dbias, dy, x, mean, invstd, weight, tokens, dim):
+    def layernorm_bwd(self, dx, dweight, dbias, dy, x, mean, invstd, weight, tokens, dim, dtype=BF16):
         self.launch(kid.LAYERNORM_BWD, rowwise(tokens), [dx, dweight, dbias, dy, x, mean, invstd, weight],
-                    (tokens, dim))
+                    (tokens, dim, dtype))
 
 
 class SwigluLaunch:
