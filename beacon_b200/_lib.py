@@ -31,6 +31,7 @@ F32, F16, BF16, FP8E4M3 = 0, 1, 2, 3
 # Every symbol include/beacon_cuda.h declares.
 EXPORTS = (
     "beacon_version", "beacon_last_error", "beacon_device_status", "beacon_launch_count",
+    "beacon_diag_wait_timeout", "beacon_diag_exp2_poly",
     "beacon_profile_enable", "beacon_profile_read",
     "beacon_matmul_fwd", "beacon_matmul_bwd", "beacon_linear_fwd", "beacon_linear_bwd",
     "beacon_matmul_fp8w_fwd", "beacon_linear_fp8w_fwd",
@@ -86,6 +87,8 @@ def lib():
     _sig(L, "beacon_last_error", _int, [ctypes.c_char_p, _sz])
     _sig(L, "beacon_device_status", _int, [_int, ctypes.POINTER(ctypes.c_uint)])
     _sig(L, "beacon_launch_count", ctypes.c_uint64, [])
+    _sig(L, "beacon_diag_wait_timeout", _int, [ctypes.c_uint64, _vp, _vp])
+    _sig(L, "beacon_diag_exp2_poly", _int, [_vp, _vp, _i64, _vp])
     _sig(L, "beacon_profile_enable", None, [_int])
     _sig(L, "beacon_profile_read", _int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_double),
                                           ctypes.POINTER(ctypes.c_uint64)])

@@ -23,6 +23,7 @@
 #include "../../include/beacon_cuda.h"
 #include "attention.cuh"
 #include "attention_bwd.cuh"
+#include "diag.cuh"
 #include "elementwise.cuh"
 #include "gemm.cuh"
 #include "sm100.cuh"
@@ -586,6 +587,28 @@ extern "C" int beacon_device_status(int device, unsigned int out[3]) {
   return BEACON_OK;
 }
 
+extern "C" int beacon_diag_wait_timeout(uint64_t limit_ns, unsigned int* out, void* stream) {
+  if (!out) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "diag_wait_timeout: null pointer");
+  if (limit_ns == 0 || limit_ns > 1000000000ull)
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "diag_wait_timeout: limit must be in (0, 1 s]");
+  int dev;
+  DeviceInfo* di;
+  BEACON_TRY(current_device(&dev, &di));
+  k_diag_wait_timeout<<<1, 32, 0, as_stream(stream)>>>(limit_ns, reinterpret_cast<uint32_t*>(out));
+  return check_launch("k_diag_wait_timeout");
+}
+
+extern "C" int beacon_diag_exp2_poly(float* out, const float* in, int64_t n, void* stream) {
+  if (n < 0 || (n & 1)) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "diag_exp2_poly: n must be even");
+  if (n == 0) return BEACON_OK;
+  if (!out || !in) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "diag_exp2_poly: null pointer");
+  int dev;
+  DeviceInfo* di;
+  BEACON_TRY(current_device(&dev, &di));
+  k_diag_exp2_poly<<<grid_for(n / 2, 256, di->sms), 256, 0, as_stream(stream)>>>(out, in, n);
+  return check_launch("k_diag_exp2_poly");
+}
+
 // ===========================================================================
 // matmul / linear
 // ===========================================================================
@@ -597,11 +620,11 @@ namespace {
 int gemm_fp8w(void* out, const void* lhs, const void* rhs_fp8, float scale, const void* bias, int64_t m, int64_t k,
               int64_t n, cudaStream_t st) {
   BEACON_TRY(check_dims("fp8-weight GEMM", m, k, n));
+  if (m == 0 || n == 0) return BEACON_OK;
+  if (!out || (k && (!lhs || !rhs_fp8))) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "fp8-weight GEMM: null pointer");
   int dev;
   DeviceInfo* di;
   BEACON_TRY(current_device(&dev, &di));
-  if (m == 0 || n == 0) return BEACON_OK;
-  if (!out || (k && (!lhs || !rhs_fp8))) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "fp8-weight GEMM: null pointer");
   void* ws = nullptr;
   const size_t wbytes = align256((size_t)k * n * 2);
   BEACON_TRY(get_workspace(dev, wbytes, nullptr, 0, &ws));
@@ -648,6 +671,8 @@ extern "C" int beacon_matmul_bwd(void* dlhs, void* drhs, const void* dout, const
                                  int64_t m, int64_t k, int64_t n, int dtype, void* stream) {
   BEACON_TRY(check_dtype_gemm(dtype));
   BEACON_TRY(check_dims("matmul_bwd", m, k, n));
+  if ((dlhs && m && k && n && (!dout || !rhs)) || (drhs && k && n && m && (!lhs || !dout)))
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "matmul_bwd: null pointer");
   cudaStream_t st = as_stream(stream);
   const bool f32 = dtype == BEACON_F32;
   if (dlhs) {  // dlhs[m,k] = dout[m,n] . rhs[k,n]^T   (B stored [N=k][K=n]: K-major)
@@ -666,6 +691,8 @@ extern "C" int beacon_linear_fwd(void* out, const void* x, const void* weight, c
   if (dtype == BEACON_FP8E4M3) return gemm_fp8w(out, x, weight, 1.0f, bias, m, k, n, as_stream(stream));
   BEACON_TRY(check_dtype_gemm(dtype));
   BEACON_TRY(check_dims("linear_fwd", m, k, n));
+  if (m && n && (!out || (k && (!x || !weight))))
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "linear_fwd: null pointer");
   GemmParams p = gemm_params(m, n, k, out, n, dtype == BEACON_F32);
   if (bias) {
     p.epi = kEpiBias;
@@ -678,6 +705,7 @@ extern "C" int beacon_linear_bwd(void* dx, void* dweight, void* dbias, const voi
                                  const void* weight, int64_t m, int64_t k, int64_t n, int dtype, void* stream) {
   BEACON_TRY(check_dtype_gemm(dtype));
   BEACON_TRY(check_dims("linear_bwd", m, k, n));
+  if (dbias && n > 0 && m > 0 && !dout) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "linear_bwd: null pointer");
   BEACON_TRY(beacon_matmul_bwd(dx, dweight, dout, x, weight, m, k, n, dtype, stream));
   if (dbias && n > 0) {
     int dev;
@@ -711,6 +739,8 @@ extern "C" int beacon_residual_add_fwd(void* out, const void* a, const void* b, 
                                        void* stream) {
   if (n < 0) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "residual_add: negative n");
   if (n == 0) return BEACON_OK;
+  if (dtype != BEACON_BF16 && dtype != BEACON_F32) return fail(BEACON_ERR_UNIMPLEMENTED, "residual_add: dtype %d", dtype);
+  if (!out || !a || !b) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "residual_add: null pointer");
   int dev;
   DeviceInfo* di;
   BEACON_TRY(current_device(&dev, &di));
@@ -736,11 +766,12 @@ extern "C" int beacon_residual_add_bwd(void* d_a, void* d_b, const void* d_out, 
   if (n == 0) return BEACON_OK;
   if (dtype < 0 || dtype > 3) return fail(BEACON_ERR_UNIMPLEMENTED, "residual_add_bwd: dtype %d", dtype);
   const int es[4] = {4, 2, 2, 1};
+  if (!d_out) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "residual_add_bwd: null pointer");
+  if (!aligned16(d_out) || (d_a && !aligned16(d_a)) || (d_b && !aligned16(d_b)))
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "residual_add_bwd: pointers must be 16-byte aligned");
   int dev;
   DeviceInfo* di;
   BEACON_TRY(current_device(&dev, &di));
-  if (!aligned16(d_out) || (d_a && !aligned16(d_a)) || (d_b && !aligned16(d_b)))
-    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "residual_add_bwd: pointers must be 16-byte aligned");
   const long long nbytes = n * es[dtype];
   k_fanout2<<<grid_for(nbytes / 16 + 1, 256, di->sms), 256, 0, as_stream(stream)>>>(
       reinterpret_cast<uint8_t*>(d_a), reinterpret_cast<uint8_t*>(d_b), reinterpret_cast<const uint8_t*>(d_out),
@@ -752,6 +783,7 @@ extern "C" int beacon_cast(void* dst, const void* src, int64_t n, int kind, void
   if (n < 0) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "cast: negative n");
   if (kind < 0 || kind > 3) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "cast: unknown kind %d", kind);
   if (n == 0) return BEACON_OK;
+  if (!dst || !src) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "cast: null pointer");
   int dev;
   DeviceInfo* di;
   BEACON_TRY(current_device(&dev, &di));
@@ -767,7 +799,9 @@ extern "C" int beacon_rmsnorm_adjoint_fwd(void* out, const void* x, const void* 
   if (tokens < 0 || dim <= 0 || dim > INT32_MAX)
     return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "rmsnorm_fwd: bad shape tokens=%lld dim=%lld",
                 (long long)tokens, (long long)dim);
+  if (dtype != BEACON_BF16 && dtype != BEACON_F32) return fail(BEACON_ERR_UNIMPLEMENTED, "rmsnorm_fwd: dtype %d", dtype);
   if (tokens == 0) return BEACON_OK;
+  if (!out || !x || !weight || !rms) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "rmsnorm_fwd: null pointer");
   int dev;
   DeviceInfo* di;
   BEACON_TRY(current_device(&dev, &di));
@@ -801,6 +835,10 @@ extern "C" int beacon_rmsnorm_adjoint_bwd(void* dx, void* dweight, const void* d
   if (tokens < 0 || dim <= 0 || dim > INT32_MAX)
     return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "rmsnorm_bwd: bad shape");
   if (dtype != BEACON_BF16 && dtype != BEACON_F32) return fail(BEACON_ERR_UNIMPLEMENTED, "rmsnorm_bwd: dtype %d", dtype);
+  if (tokens > 0 && (!dx || !dy || !x || !rms || !weight))
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "rmsnorm_bwd: null pointer");
+  const bool vec = aligned16(dx) && aligned16(x) && aligned16(dy) && aligned16(weight);
+  if (!vec) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "rmsnorm_bwd: pointers must be 16-byte aligned");
   int dev;
   DeviceInfo* di;
   BEACON_TRY(current_device(&dev, &di));
@@ -810,8 +848,6 @@ extern "C" int beacon_rmsnorm_adjoint_bwd(void* dx, void* dweight, const void* d
     if (dweight) return zero_fill(dweight, (size_t)dim * es, st);
     return BEACON_OK;
   }
-  const bool vec = aligned16(dx) && aligned16(x) && aligned16(dy) && aligned16(weight);
-  if (!vec) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "rmsnorm_bwd: pointers must be 16-byte aligned");
   // Register-resident rows (k_rmsnorm_bwd_rows) up to 8192 bf16 / 4096 f32 columns;
   // beyond that, for dim % 8 != 0 or with a misaligned workspace, k_rmsnorm_bwd.
   int rows_vec = 0;
@@ -923,6 +959,8 @@ extern "C" int beacon_layernorm_adjoint_bwd(void* dx, void* dweight, void* dbias
                 (long long)tokens, (long long)dim);
   if (dtype != BEACON_BF16 && dtype != BEACON_F32)
     return fail(BEACON_ERR_UNIMPLEMENTED, "layernorm_bwd: dtype %d", dtype);
+  if (tokens > 0 && (!dx || !dy || !x || !mean || !invstd || !weight))
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "layernorm_bwd: null pointer");
   int dev;
   DeviceInfo* di;
   BEACON_TRY(current_device(&dev, &di));
@@ -933,8 +971,6 @@ extern "C" int beacon_layernorm_adjoint_bwd(void* dx, void* dweight, void* dbias
     if (dbias) BEACON_TRY(zero_fill(dbias, (size_t)dim * es, st));
     return BEACON_OK;
   }
-  if (!dx || !dy || !x || !mean || !invstd || !weight)
-    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "layernorm_bwd: null pointer");
   const bool vec = aligned16(dx) && aligned16(dy) && aligned16(x) && aligned16(weight) && dim % 8 == 0;
   // Register-resident rows (k_layernorm_bwd_rows) up to 8192 bf16 / 4096 f32 columns;
   // beyond that, or with a misaligned workspace, the partials go through global memory.
@@ -1055,6 +1091,10 @@ extern "C" int beacon_rmsnorm_adjoint_bwd_noalloc(void* dx, void* dweight, const
                 (long long)dim, kNoAllocScratchFloats);
   if (dtype != BEACON_BF16 && dtype != BEACON_F32)
     return fail(BEACON_ERR_UNIMPLEMENTED, "rmsnorm_bwd_noalloc: dtype %d", dtype);
+  if (tokens > 0 && (!dx || !dy || !x || !rms || !weight))
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "rmsnorm_bwd_noalloc: null pointer");
+  if (!(aligned16(dx) && aligned16(x) && aligned16(dy) && aligned16(weight)))
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "rmsnorm_bwd_noalloc: pointers must be 16-byte aligned");
   int dev;
   DeviceInfo* di;
   BEACON_TRY(current_device(&dev, &di));
@@ -1063,8 +1103,6 @@ extern "C" int beacon_rmsnorm_adjoint_bwd_noalloc(void* dx, void* dweight, const
     if (dweight) return zero_fill(dweight, (size_t)dim * (dtype == BEACON_F32 ? 4 : 2), st);
     return BEACON_OK;
   }
-  if (!(aligned16(dx) && aligned16(x) && aligned16(dy) && aligned16(weight)))
-    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "rmsnorm_bwd_noalloc: pointers must be 16-byte aligned");
   // partial rows: as many CTAs as the fixed scratch holds rows of `dim` floats
   const int64_t cap_rows = (int64_t)(kNoAllocScratchFloats / (size_t)dim);
   const int grid = (int)std::min<int64_t>(std::min<int64_t>(tokens, (int64_t)di->sms * 4), cap_rows);

@@ -94,10 +94,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity.  `abort_flag` (shared) lets
-// one role that gave up release every other role quickly.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          unsigned int site) {
+// Bounded wait for the phase with the given parity, giving up after `limit_ns`.
+// `abort_flag` (shared) lets one role that gave up release every other role quickly.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                              unsigned int site, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
@@ -105,12 +105,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > BEACON_WAIT_LIMIT_NS) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       record_fault(kFaultWaitTimeout, site);
       *abort_flag = 1;
       return false;
     }
   }
+}
+
+// The wait every kernel of the library uses: limit BEACON_WAIT_LIMIT_NS.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          unsigned int site) {
+  return mbar_wait_for(bar, parity, abort_flag, site, BEACON_WAIT_LIMIT_NS);
 }
 
 // The whole warp waits; the outcome is warp-uniform.  MMA-issuing warps run their loop
@@ -143,15 +149,6 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* m, uin
           smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
-}
-
-// Brings a tile of a 3-D tensor into L2 ahead of its tma_load_3d (no shared memory, no
-// completion to wait for).
-__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* m, int x, int y, int z) {
-  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
-                   reinterpret_cast<uint64_t>(m)),
-               "r"(x), "r"(y), "r"(z)
-               : "memory");
 }
 
 // Untiled bulk copy global -> shared (both 16-byte aligned, bytes a multiple of 16),
@@ -288,14 +285,6 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8])
                : "memory");
 }
 
-// Bulk (non-tensor) TMA reduction: global[dst .. dst+bytes) += shared[src ..] as fp32.
-// Both addresses 16-byte aligned, bytes a multiple of 16.  Tracked by the issuing
-// thread's bulk async-group.
-__device__ __forceinline__ void bulk_reduce_add_f32(float* dst, const void* src, uint32_t bytes) {
-  asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(dst),
-               "r"(smem_u32(src)), "r"(bytes)
-               : "memory");
-}
 // 32-byte global store (a full sector; `p` 32-byte aligned).
 __device__ __forceinline__ void stg256(void* p, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t a4,
                                        uint32_t a5, uint32_t a6, uint32_t a7) {
@@ -318,21 +307,6 @@ __device__ __forceinline__ void bulk_wait_group_read0() {
 }
 // Waits until every committed bulk group has completed (its global writes done).
 __device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-
-// Fire-and-forget fp32 reduction into global memory.
-__device__ __forceinline__ void red_add_f32(float* addr, float a) {
-  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(addr), "f"(a) : "memory");
-}
-
-__device__ __forceinline__ void prefetch_l1(const void* p) {
-  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
-}
-
-// Fire-and-forget fp32 vector reduction into global memory (16-byte aligned).
-__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
-}
 
 // Warpgroup register rebalancing (all 4 warps of a warpgroup execute it).  The
 // per-thread counts of all warpgroups must add up to at most the registers the

@@ -55,6 +55,46 @@ def gather_checksums(t, world: int):
     return torch.stack(out)
 
 
+def owner(unit: int, total: int, world: int) -> int:
+    """The rank whose even_shard block holds `unit`."""
+    for r in range(world):
+        s, c = even_shard(total, world, r)
+        if s <= unit < s + c:
+            return r
+    raise ValueError(f"unit {unit} outside [0, {total})")
+
+
+def gather_units(local, start: int, total: int, wanted, world: int):
+    """Bring the `wanted` units (global indices) of a sharded tensor to every rank.
+
+    `local` is this rank's block [count, ...] of units start .. start+count-1 of `total`.
+    Every rank fills one slot per wanted unit (zeros where it does not own the unit)
+    and the slots are all-gathered, so all ranks take the same collective step whatever
+    they own; each unit is then read from its owner's slots.  Returns [len(wanted), ...].
+    Used after timing, to verify sampled heads / columns / rows on rank 0."""
+    import torch
+    count = local.shape[0]
+    slots = torch.zeros((len(wanted),) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+    for i, u in enumerate(wanted):
+        if start <= u < start + count:
+            slots[i] = local[u - start]
+    if world == 1:
+        return slots
+    import torch.distributed as dist
+    parts = [torch.empty_like(slots) for _ in range(world)]
+    dist.all_gather(parts, slots)
+    return torch.stack([parts[owner(u, total, world)][i] for i, u in enumerate(wanted)])
+
+
+def unit_generator(seed: int, unit: int, device):
+    """A torch generator for one unit (head, KV group, weight) of a global seeded tensor:
+    the unit's values depend on (seed, unit) only, never on how many ranks share the work."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed * 1_000_003 + unit)
+    return g
+
+
 def gather_rows(t, world: int):
     """All-gather equally shaped per-rank tensors along dim 0 (verification of
     small cases)."""

@@ -24,6 +24,14 @@ Also reported on the same JSON line:
   "gqa":       long-context grouped-query causal forward (64 query heads, 8 KV heads,
                S=32768, D=128), KV groups sharded across ranks.
 
+After timing, rank 0 checks the timed runs' outputs against the oracle (the CPU
+restatement of the path, used here only as the checker): sampled heads of the
+attention step (gathered from the ranks that own them over NCCL), sampled rows of
+the GEMM (every rank's column block gathered), sampled rows of two long GQA heads,
+and sampled rows of one block sequence.  Every input is generated from a global
+seed per unit (head, KV group, weight), so the data do not depend on the number of
+ranks.  The worst norm-wise relative error is printed as "max_rel_err".
+
 `--impl reference` times the reference's CPU path for this op (the oracle: the
 reference itself has no numeric implementation) on rank 0 with all host threads.
 """
@@ -244,6 +252,47 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------- inputs and checks
+
+ATTN_SEED, GEMM_SEED, BLOCK_SEED, GQA_SEED = 2, 1, 3, 4
+CHECK_TOL = 2e-2  # bf16 inputs, fp32 accumulation, gradients included (norm-wise)
+
+
+def attn_head_inputs(t, h0, nh, dev):
+    """Tensor t (0 Q, 1 K, 2 V, 3 dO) of global heads h0 .. h0+nh-1: [1, nh, S, D] bf16,
+    each head N(0, 1) from its own generator."""
+    import torch
+    from beacon_b200.shard import unit_generator
+    out = torch.empty(1, nh, S, D, dtype=torch.bfloat16, device=dev)
+    for i in range(nh):
+        g = unit_generator(ATTN_SEED, 4 * (h0 + i) + t, dev)
+        out[0, i] = torch.randn(S, D, generator=g, device=dev).to(torch.bfloat16)
+    return out
+
+
+def check_attention(world, h0, nh, out, lse, dq, dk, dv, dev):
+    """Heads 0 and B*H-1 of the timed step (gathered from their owners) against the oracle:
+    out, lse, dq, dk, dv over every query and key row of each head.  Rank 0 returns
+    {quantity: worst relative error}; the other ranks None."""
+    import numpy as np
+    import torch
+    from beacon_b200.shard import gather_units
+    wanted = [0, B * H - 1]
+    got = {name: gather_units(t[0], h0, B * H, wanted, world).float().cpu().numpy()
+           for name, t in (("out", out), ("lse", lse), ("dq", dq), ("dk", dk), ("dv", dv))}
+    if h0 != 0:
+        return None
+    import oracle as O
+    errs = {"out": 0.0, "lse": 0.0, "dq": 0.0, "dk": 0.0, "dv": 0.0}
+    for i, gh in enumerate(wanted):
+        qh, kh, vh, doh = (attn_head_inputs(t, gh, 1, dev)[0, 0].float().cpu().numpy() for t in range(4))
+        ro, rl = O.attention_fwd_rows(qh, kh, vh, np.arange(S))
+        rq, rk, rv = O.attention_bwd_head(doh, qh, kh, vh, rl)
+        for name, r in (("out", ro), ("lse", rl), ("dq", rq), ("dk", rk), ("dv", rv)):
+            errs[name] = max(errs[name], O.rel_err(got[name][i], r))
+    return {"heads": wanted, **errs}
+
+
 # --------------------------------------------------------------------------- GPU arm
 
 def run_beacon(args, rank, world, local):
@@ -253,6 +302,7 @@ def run_beacon(args, rank, world, local):
     if (B * H) % world != 0:
         raise SystemExit(f"{B * H} heads do not shard over {world} ranks")
     nh = B * H // world
+    h0 = rank * nh  # first global (b*H + h) head of this rank
     dev = torch.device("cuda", local)
     uuid = None
     try:
@@ -261,11 +311,10 @@ def run_beacon(args, rank, world, local):
         uuid = str(local)
     burst, sustained, peak_kind = peaks()
 
-    # inputs: pinned host buffers (used by e2e), copied once for the device-resident loop
-    g = torch.Generator().manual_seed(2 + 1000 * rank)
-    host = [torch.randn(1, nh, S, D, generator=g, dtype=torch.float32).to(torch.bfloat16).pin_memory()
-            for _ in range(4)]
-    q, k, v, do = [h.to(dev) for h in host]
+    # inputs: head gh's Q, K, V, dO come from seed 2 and gh alone (the global tensors do not
+    # depend on the rank count); pinned host copies feed the e2e step
+    q, k, v, do = (attn_head_inputs(t, h0, nh, dev) for t in range(4))
+    host = [t.cpu().pin_memory() for t in (q, k, v, do)]
     out = torch.empty_like(q)
     lse = torch.empty(1, nh, S, dtype=torch.float32, device=dev)
     L = ops._lib.lib()
@@ -330,14 +379,18 @@ def run_beacon(args, rank, world, local):
     achieved = bwd_flops_local / (bwd_avg_ms * 1e-3) / 1e12
     traffic = None if DKDV_TRAFFIC_PER_HEAD is None else DKDV_TRAFFIC_PER_HEAD * nh
     dq_avg_ms = dq_ms / max(dq_n, 1)
-    roofline = {"kernel": "k_attn_bwd_dkdv", "bound": "tensor", "achieved": achieved, "peak": sustained,
-                "unit": "TFLOP/s", "frac": achieved / sustained, "traffic": traffic,
-                "peak_kind": f"{peak_kind} bf16_tflops_sustained (kernel timed inside a multi-second loop)",
+    roofline = {"kernel": "k_attn_bwd_dkdv", "bound": "tensor", "achieved": achieved, "peak": burst,
+                "unit": "TFLOP/s", "frac": achieved / burst, "traffic": traffic,
+                "peak_kind": f"{peak_kind} bf16_tflops (burst: the timed region is well under a second)",
+                "frac_of_sustained_peak": achieved / sustained, "sustained_peak": sustained,
                 "avg_launch_ms": bwd_avg_ms, "launches": bwd_n,
                 "dq_kernel": {"kernel": "k_attn_bwd_dq", "avg_launch_ms": dq_avg_ms,
                               "tflops_executed": DQ_FLOPS * nh / (B * H) / (dq_avg_ms * 1e-3) / 1e12},
                 "fwd_kernel": {"kernel": "k_attn_fwd_tc", "avg_launch_ms": fwd_ms / max(fwd_n, 1),
                                "launches_per_step": fwd_n / max(args.steps, 1)}}
+
+    # ---- the timed step's outputs (deterministic: every step writes the same values)
+    check_attn = check_attention(world, h0, nh, out, lse, dq, dk, dv, dev)
 
     # ---- with_out variant
     ms_wo = max_over_ranks(timed(step_with_out, args.steps, 2), world)
@@ -422,11 +475,17 @@ def run_beacon(args, rank, world, local):
 
     # ---- GEMM 4096^3, columns of B sharded
     gemm = None
+    check_gemm = None
     if not args.no_gemm:
+        from beacon_b200.shard import gather_rows, unit_generator
         ncols = GEMM_N // world
-        gg = torch.Generator(device=dev).manual_seed(1 + rank)
-        a = (torch.rand(GEMM_N, GEMM_N, generator=gg, device=dev) * 2 - 1).to(torch.bfloat16)
-        bm = (torch.rand(GEMM_N, ncols, generator=gg, device=dev) * 2 - 1).to(torch.bfloat16)
+        # A and B entries U(-1, 1) from the GEMM seed (A: unit 0, B: unit 1); every rank
+        # holds A and its own column block of B
+        a = (torch.rand(GEMM_N, GEMM_N, generator=unit_generator(GEMM_SEED, 0, dev), device=dev) * 2 - 1
+             ).to(torch.bfloat16)
+        b_full = (torch.rand(GEMM_N, GEMM_N, generator=unit_generator(GEMM_SEED, 1, dev), device=dev) * 2 - 1
+                  ).to(torch.bfloat16)
+        bm = b_full[:, rank * ncols:(rank + 1) * ncols].contiguous()
         c = torch.empty(GEMM_N, ncols, dtype=torch.bfloat16, device=dev)
         flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
         for _ in range(3):
@@ -448,22 +507,37 @@ def run_beacon(args, rank, world, local):
         gemm = {"value": gt, "unit": "TFLOP/s", "ms": gms, "frac_of_burst_peak": gt / burst / world,
                 "config": f"bf16 {GEMM_N}^3, B columns sharded {world}-way, L2 flushed between iterations",
                 "per_gpu_tflops": gt / world}
-        del a, bm, c, flush
+        # 16 sampled rows of C: every rank's column block gathered to rank 0
+        rows = torch.arange(0, GEMM_N, GEMM_N // 16, device=dev)
+        c_rows = gather_rows(c[rows].t().contiguous(), world).t()  # [16, GEMM_N]
+        if rank == 0:
+            import oracle as O
+            ref = O.matmul_fwd(a[rows].float().cpu().numpy(), b_full.float().cpu().numpy())
+            check_gemm = {"rows": 16, "c": O.rel_err(c_rows.float().cpu().numpy(), ref)}
+        del a, bm, b_full, c, flush
 
-    block = None if args.no_block else bench_block(args, rank, world, dev, stream)
-    gqa = None if args.no_gqa else bench_gqa(args, rank, world, dev, stream)
+    block, check_block = (None, None) if args.no_block else bench_block(args, rank, world, dev, stream)
+    gqa, check_gqa = (None, None) if args.no_gqa else bench_gqa(args, rank, world, dev, stream)
 
     if rank != 0:
         return
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         cpu, _ = cpu_attention_sample()
+    checks = {"attention": check_attn, "gemm": check_gemm, "gqa": check_gqa, "block": check_block}
+    worst = 0.0
+    for c in checks.values():
+        if c:
+            worst = max([worst] + [float(x) for k_, x in c.items() if isinstance(x, float)])
+    max_rel_err = {"value": worst, "tolerance": CHECK_TOL, "ok": worst <= CHECK_TOL,
+                   "measure": "max |x - ref| / max |ref| per checked tensor, oracle on sampled units", **checks}
     line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic: i.i.d. N(0,1) Q/K/V/dO, seeded",
-            "config": CONFIG, "frac_of_peak": value / (sustained * world),
-            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "with_out": with_out, "gemm": gemm,
-            "block": block, "gqa": gqa,
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic: i.i.d. N(0,1) Q/K/V/dO, seeded per head",
+            "config": CONFIG, "frac_of_peak": value / (burst * world),
+            "frac_of_sustained_peak": value / (sustained * world),
+            "roofline": roofline, "max_rel_err": max_rel_err, "cpu_baseline": cpu, "e2e": e2e,
+            "with_out": with_out, "gemm": gemm, "block": block, "gqa": gqa,
             "clocks": clk, "gpu_launches": int(n_launch), "impl": "beacon"}
     print(json.dumps(line), flush=True)
 
@@ -486,16 +560,17 @@ def bench_block(args, rank, world, dev, stream):
     """One pre-norm Llama block forward per rank (replicas), weights N(0, 0.02), x N(0, 1)."""
     import torch
     from beacon_b200 import ops
-    g = torch.Generator(device=dev).manual_seed(3 + 1000 * rank)
+    from beacon_b200.shard import unit_generator
 
-    def w(*shape, std=0.02):
-        return (torch.randn(*shape, generator=g, device=dev) * std).to(torch.bfloat16)
+    def w(unit, *shape, std=0.02):
+        return (torch.randn(*shape, generator=unit_generator(BLOCK_SEED, unit, dev), device=dev) * std
+                ).to(torch.bfloat16)
 
-    x = torch.randn(BLK_T, BLK_DM, generator=g, device=dev).to(torch.bfloat16)
+    x = w(0, BLK_T, BLK_DM, std=1.0)
     n1 = torch.ones(BLK_DM, device=dev, dtype=torch.bfloat16)
     n2 = torch.ones(BLK_DM, device=dev, dtype=torch.bfloat16)
-    wqkv, wo = w(BLK_DM, 3 * BLK_H * BLK_D), w(BLK_H * BLK_D, BLK_DM)
-    wg, wu, wd = w(BLK_DM, BLK_F), w(BLK_DM, BLK_F), w(BLK_F, BLK_DM)
+    wqkv, wo = w(1, BLK_DM, 3 * BLK_H * BLK_D), w(2, BLK_H * BLK_D, BLK_DM)
+    wg, wu, wd = w(3, BLK_DM, BLK_F), w(4, BLK_DM, BLK_F), w(5, BLK_F, BLK_DM)
     out = torch.empty_like(x)
     ws = torch.empty(ops.llama_block_workspace_bytes(BLK_B, BLK_S, BLK_DM, BLK_H, BLK_H, BLK_D, BLK_F),
                      dtype=torch.uint8, device=dev)
@@ -504,30 +579,53 @@ def bench_block(args, rank, world, dev, stream):
         ops.llama_block_fwd(x, n1, wqkv, wo, n2, wg, wu, wd, BLK_B, BLK_S, BLK_H, BLK_H, out=out, workspace=ws)
 
     barrier(world)
-    ms = max_over_ranks(_time_calls(fn, stream, max(5, args.steps // 3), 2), world)
+    ms = max_over_ranks(_time_calls(fn, stream, max(10, args.steps // 2), 3), world)
     torch.cuda.synchronize()
-    ok = bool(torch.isfinite(out.float()).all().item())
+    check = None
+    if rank == 0:  # rows of sequence 1 of the timed replica against the sampled-row block oracle
+        import numpy as np
+        import oracle as O
+        seq = 1
+        rows = np.array([0, 1, 127, 128, 777, 1500, BLK_S - 2, BLK_S - 1])
+        h = lambda t: t.float().cpu().numpy()
+        xs = h(x[seq * BLK_S:(seq + 1) * BLK_S])
+        ones = np.ones(BLK_DM, dtype=np.float32)
+        ref = O.llama_block_fwd_rows(xs, ones, h(wqkv), h(wo), ones, h(wg), h(wu), h(wd), BLK_H, BLK_H, rows)
+        got = h(out[seq * BLK_S + torch.from_numpy(rows).to(dev)])
+        check = {"sequence": seq, "rows": rows.tolist(), "out": O.rel_err(got, ref),
+                 "branch": O.rel_err(got - xs[rows], ref - xs[rows])}
     del x, wqkv, wo, wg, wu, wd, out, ws
     torch.cuda.empty_cache()
     return {"value": BLK_FLOPS * world / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": ms,
-            "per_gpu_tflops": BLK_FLOPS / (ms * 1e-3) / 1e12, "flops_per_block": BLK_FLOPS, "finite": ok,
+            "per_gpu_tflops": BLK_FLOPS / (ms * 1e-3) / 1e12, "flops_per_block": BLK_FLOPS,
             "config": f"pre-norm Llama block forward, batch {BLK_B} x seq {BLK_S}, d_model {BLK_DM}, "
                       f"{BLK_H} x {BLK_D} heads, SwiGLU {BLK_F}, bf16; one replica per rank",
-            "api": "beacon_llama_block_fwd (7 launches)"}
+            "api": "beacon_llama_block_fwd (7 launches)"}, check
 
 
 def bench_gqa(args, rank, world, dev, stream):
     """Causal GQA forward, S=32768; the 8 KV groups (8 query heads each) sharded across ranks."""
     import torch
     from beacon_b200 import ops
+    from beacon_b200.shard import gather_units, unit_generator
     if GQA_HKV % world != 0:
-        return None
+        return None, None
     hkv = GQA_HKV // world
-    hq = hkv * (GQA_HQ // GQA_HKV)
-    g = torch.Generator(device=dev).manual_seed(4 + 1000 * rank)
-    q = torch.randn(1, hq, GQA_S, GQA_D, generator=g, device=dev).to(torch.bfloat16)
-    k = torch.randn(1, hkv, GQA_S, GQA_D, generator=g, device=dev).to(torch.bfloat16)
-    v = torch.randn(1, hkv, GQA_S, GQA_D, generator=g, device=dev).to(torch.bfloat16)
+    grp = GQA_HQ // GQA_HKV
+    hq = hkv * grp
+    kv0, q0 = rank * hkv, rank * hkv * grp  # first global KV head / query head of this rank
+
+    def gen(unit, n):  # n heads [1, n, S, D], head i from unit + i
+        t = torch.empty(1, n, GQA_S, GQA_D, dtype=torch.bfloat16, device=dev)
+        for i in range(n):
+            t[0, i] = torch.randn(GQA_S, GQA_D, generator=unit_generator(GQA_SEED, unit + i, dev),
+                                  device=dev).to(torch.bfloat16)
+        return t
+
+    # units: query head h -> h, KV head g -> GQA_HQ + g (K), GQA_HQ + GQA_HKV + g (V)
+    q = gen(q0, hq)
+    k = gen(GQA_HQ + kv0, hkv)
+    v = gen(GQA_HQ + GQA_HKV + kv0, hkv)
     out = torch.empty_like(q)
     lse = torch.empty(1, hq, GQA_S, dtype=torch.float32, device=dev)
     L = ops._lib.lib()
@@ -538,14 +636,34 @@ def bench_gqa(args, rank, world, dev, stream):
                                              GQA_S, GQA_D, 1, ops._lib.BF16, sp))
 
     barrier(world)
-    ms = max_over_ranks(_time_calls(fn, stream, 3, 1), world)
+    ms = max_over_ranks(_time_calls(fn, stream, 10, 3), world)
+    # query heads 0 and 63 (KV groups 0 and 7): the last 128 rows (all 256 key tiles deep)
+    # and 128 rows spread over the sequence, gathered from their owners
+    import numpy as np
+    rows = np.unique(np.concatenate([np.linspace(0, GQA_S - 129, 128).astype(np.int64),
+                                     np.arange(GQA_S - 128, GQA_S)]))
+    ridx = torch.from_numpy(rows).to(dev)
+    wanted = [0, GQA_HQ - 1]
+    got = gather_units(out[0][:, ridx], q0, GQA_HQ, wanted, world).float().cpu().numpy()
+    check = None
+    if rank == 0:
+        import oracle as O
+        err = 0.0
+        for i, h in enumerate(wanted):
+            g = h // grp
+            qh = gen(h, 1)[0, 0].float().cpu().numpy()
+            kh = gen(GQA_HQ + g, 1)[0, 0].float().cpu().numpy()
+            vh = gen(GQA_HQ + GQA_HKV + g, 1)[0, 0].float().cpu().numpy()
+            ro, _ = O.attention_fwd_rows(qh, kh, vh, rows)
+            err = max(err, O.rel_err(got[i], ro))
+        check = {"query_heads": wanted, "rows": int(rows.size), "out": err}
     del q, k, v, out, lse
     torch.cuda.empty_cache()
     return {"value": GQA_FLOPS / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": ms,
             "per_gpu_tflops": GQA_FLOPS / world / (ms * 1e-3) / 1e12,
             "config": f"causal GQA forward B=1, {GQA_HQ} query / {GQA_HKV} KV heads, S={GQA_S}, D={GQA_D}, bf16; "
                       f"{hq} query heads ({hkv} KV groups) per rank",
-            "api": "beacon_attention_gqa_fwd"}
+            "api": "beacon_attention_gqa_fwd"}, check
 
 
 def main():

@@ -81,6 +81,19 @@ int beacon_device_status(int device, unsigned int out[3]);
 /* Number of kernels launched by this library since load (all devices, all threads). */
 uint64_t beacon_launch_count(void);
 
+/* Self-checks of device building blocks (no reference counterpart).
+ * beacon_diag_wait_timeout: one warp on the current device waits on an mbarrier that
+ * nothing completes, with the bounded wait every kernel uses but a limit of `limit_ns`
+ * (at most 1 s); the wait gives up, records fault code 1 at site 0x501 (read it with
+ * beacon_device_status), the bulk copy the kernel has in flight lands, its TMEM is freed
+ * and it returns.  out: 3 device words = {gave up (1), first word of the copy (1),
+ * TMEM released (1)}.
+ * beacon_diag_exp2_poly: out[i] = 2^in[i] by the FMA-pipe polynomial the attention
+ * softmax uses for part of its exponentials (n even); its stated bound is a relative
+ * error below 7.5e-5 on [-126, 8]. */
+int beacon_diag_wait_timeout(uint64_t limit_ns, unsigned int* out, void* stream);
+int beacon_diag_exp2_poly(float* out, const float* in, int64_t n, void* stream);
+
 /* Device timing of the tensor-core kernels (k_gemm_bf16_tc, k_attn_fwd_tc,
  * k_attn_bwd_dkdv, k_attn_bwd_dq): while enabled, each launch is bracketed by CUDA events on its
  * own stream.  beacon_profile_read(name, ...) waits for those events and returns the
@@ -188,8 +201,12 @@ int beacon_rmsnorm_adjoint_bwd(void* dx, void* dweight, const void* dy, const vo
  * fixed 4 MiB (1,048,576-float) array compiled into the library, which every GPU
  * that loads the library holds until exit.  dim above 1,048,576 is rejected with
  * BEACON_ERR_INVALID_LAUNCH_CONFIG.  The array's address is looked up on the first
- * call made on each device (make that call before any stream capture).  All calls
- * share the array: calls that overlap on the GPU race and must be serialised. */
+ * call made on each device (make that call before any stream capture).  With CUDA's
+ * lazy module loading (the default), the first call into this library on a device --
+ * whichever entry point it is -- loads the library's module there, which places the
+ * array and may synchronise; make one such call outside any latency-critical region,
+ * or load eagerly with CUDA_MODULE_LOADING=EAGER.  All calls share the array: calls
+ * that overlap on the GPU race and must be serialised. */
 int beacon_rmsnorm_adjoint_bwd_noalloc(void* dx, void* dweight, const void* dy, const void* x, const float* rms,
                                        const void* weight, int64_t tokens, int64_t dim, int dtype, void* stream);
 
@@ -265,8 +282,14 @@ int beacon_cast(void* dst, const void* src, int64_t n, int kind, void* stream);
  * crates/beacon-cuda/src/runtime.rs:31-47 (Launcher::launch) and
  * crates/beacon-cuda/src/launcher.rs:21-63 (KernelArg = byte offset into one arena).
  * A Rust `Launcher` implements KernelLauncher::launch by forwarding here; the
- * typed traits' shapes, which they drop before launch, travel in `scalars`
- * (see INTEGRATION.md for the order per kernel).  */
+ * typed traits' shapes, which they drop before launch, travel in `scalars`, in
+ * this order per kernel ID (args in the typed trait's order):
+ *   matmul_fwd/_bwd, linear_fwd/_bwd          m, k, n, dtype
+ *   attention_adjoint_fwd/_bwd                batch, heads, seqlen, head_dim, causal, dtype[, kv_heads]
+ *   rmsnorm_ / layernorm_adjoint_fwd/_bwd     tokens, dim, dtype[, eps as float32 bits]
+ *   swiglu_adjoint_fwd/_bwd                   tokens, d_model, d_ff, dtype
+ *   residual_add_fwd/_bwd                     n, dtype
+ *   cast_*                                    n                                            */
 typedef struct beacon_arena beacon_arena;
 
 typedef struct beacon_kernel_arg {

@@ -69,6 +69,10 @@ def lib():
                                              ctypes.POINTER(ctypes.c_int64), _i64]
         L.bo_attention_bwd.argtypes = [_f, _f, _f, _f, _f, _f, _f, _f, _i64, _i64, _i64, _i64,
                                        _i64, ctypes.c_int, ctypes.c_float]
+        L.bo_attention_fwd_rows.argtypes = [_f, _f, _f, _f, _f, _i64, _i64, ctypes.c_int, ctypes.c_float,
+                                            ctypes.POINTER(ctypes.c_int64), _i64]
+        L.bo_attention_bwd_head.argtypes = [_f, _f, _f, _f, _f, _f, _f, _f, _i64, _i64, ctypes.c_int,
+                                            ctypes.c_float]
         L.bo_rmsnorm_fwd.argtypes = [_f, _f, _f, _f, _i64, _i64, ctypes.c_float]
         L.bo_rmsnorm_bwd.argtypes = [_f, _f, _f, _f, _f, _f, _i64, _i64]
         L.bo_layernorm_fwd.argtypes = [_f, _f, _f, _f, _f, _f, _i64, _i64, ctypes.c_float]
@@ -199,6 +203,27 @@ def attention_fwd_heads(q, k, v, heads, causal=True, scale=0.0):
     return out, lse
 
 
+def attention_fwd_rows(q, k, v, rows, causal=True, scale=0.0):
+    """Forward of one head (q, k, v: [S, D]) for the listed query rows: (out [n, D], lse [n])."""
+    S, D = q.shape
+    rs = np.ascontiguousarray(np.asarray(rows, dtype=np.int64))
+    out, lse = _empty(rs.size, D), _empty(rs.size)
+    lib().bo_attention_fwd_rows(_p(out), _p(lse), _p(np.ascontiguousarray(q)), _p(np.ascontiguousarray(k)),
+                                _p(np.ascontiguousarray(v)), S, D, int(causal), scale,
+                                rs.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)), rs.size)
+    return out, lse
+
+
+def attention_bwd_head(dout, q, k, v, lse, causal=True, scale=0.0):
+    """Backward of one head ([S, D] each, lse [S]), rows spread over the threads: (dq, dk, dv)."""
+    S, D = q.shape
+    dq, dk, dv = _empty(S, D), _empty(S, D), _empty(S, D)
+    c = np.ascontiguousarray
+    lib().bo_attention_bwd_head(_p(dq), _p(dk), _p(dv), _p(c(dout)), _p(c(q)), _p(c(k)), _p(c(v)), _p(c(lse)),
+                                S, D, int(causal), scale)
+    return dq, dk, dv
+
+
 def attention_bwd(dout, q, k, v, lse, causal=True, scale=0.0):
     B, Hq, S, D = q.shape
     Hkv = k.shape[1]
@@ -286,6 +311,48 @@ def llama_block_fwd(x, attn_norm, w_qkv, w_o, ffn_norm, w_gate, w_up, w_down, ba
     hn, _ = rmsnorm_fwd(h, ffn_norm, eps)
     f = swiglu_fwd(rnd(hn), w_gate, w_up, w_down)
     return residual_add_fwd(rnd(f), h)
+
+
+def llama_block_fwd_rows(x_seq, attn_norm, w_qkv, w_o, ffn_norm, w_gate, w_up, w_down, heads, kv_heads, rows,
+                         eps=1e-5):
+    """The pre-norm block of llama_block_fwd for ONE sequence (x_seq [S, dm]), evaluated
+    only at the listed rows: the full-size check of the block (batch 4 x seq 2048,
+    d_model 4096) in seconds.  Every row's keys and values are computed (attention needs
+    them); queries, the output projection and the MLP only for `rows`.  The operators
+    are the same restatements -- rmsnorm_fwd (crates/beacon-cuda/src/norm.rs:19-31),
+    linear_fwd (crates/beacon-cuda/src/matmul.rs:46-58) as float64 matrix products,
+    attention_fwd (crates/beacon-cuda/src/attention.rs:21-40) on the sampled rows,
+    residual_add (crates/beacon-cuda/src/elementwise.rs:47-55) and swiglu_fwd
+    (crates/beacon-cuda/src/mlp.rs:12-29) -- with every operator output rounded to bf16
+    as bf16 operators store it.  Returns out[rows] [len(rows), dm]."""
+    S, dm = x_seq.shape
+    hd = w_o.shape[0] // heads
+    rows = np.asarray(rows, dtype=np.int64)
+    f64 = lambda a: np.asarray(a, dtype=np.float64)
+    xn, _ = rmsnorm_fwd(np.ascontiguousarray(x_seq), attn_norm, eps)
+    xn = f64(round_bf16(xn))
+    nq, nkv = heads * hd, kv_heads * hd
+    kv = round_bf16((xn @ f64(w_qkv[:, nq:nq + 2 * nkv])).astype(np.float32))
+    q = round_bf16((xn[rows] @ f64(w_qkv[:, :nq])).astype(np.float32))
+    ao = np.empty((rows.size, nq), dtype=np.float32)
+    group = heads // kv_heads
+    for h in range(heads):
+        g = h // group
+        kh = np.ascontiguousarray(kv[:, g * hd:(g + 1) * hd])
+        vh = np.ascontiguousarray(kv[:, nkv + g * hd:nkv + (g + 1) * hd])
+        # a query row stands alone: put row r of the sample at position rows[r] of a
+        # copy of the head, so the causal limit is its own position
+        qh = np.zeros((S, hd), dtype=np.float32)
+        qh[rows] = q[:, h * hd:(h + 1) * hd]
+        o, _ = attention_fwd_rows(qh, kh, vh, rows, causal=True)
+        ao[:, h * hd:(h + 1) * hd] = o
+    ao = f64(round_bf16(ao))
+    hres = f64(round_bf16((ao @ f64(w_o) + f64(x_seq[rows])).astype(np.float32)))
+    hn, _ = rmsnorm_fwd(np.ascontiguousarray(hres.astype(np.float32)), ffn_norm, eps)
+    hn = f64(round_bf16(hn))
+    gate, up = hn @ f64(w_gate), hn @ f64(w_up)
+    act = f64(round_bf16((gate / (1.0 + np.exp(-gate)) * up).astype(np.float32)))
+    return (act @ f64(w_down) + hres).astype(np.float32)
 
 
 def num_threads() -> int:

@@ -363,6 +363,95 @@ void bo_attention_bwd(float* dq, float* dk, float* dv, const float* dout,
     }
 }
 
+void bo_attention_fwd_rows(float* out, float* lse, const float* q, const float* k, const float* v,
+                           int64_t S, int64_t D, int causal, float scale, const int64_t* rows, int64_t nrows) {
+    const double sc = attn_scale(scale, D);
+#pragma omp parallel
+    {
+        double* s = (double*)malloc(sizeof(double) * (size_t)(S + D));
+#pragma omp for schedule(dynamic, 1)
+        for (int64_t t = 0; t < nrows; ++t) {
+            const int64_t i = rows[t];
+            const int64_t jend = causal ? i + 1 : S;
+            const float* qi = q + i * D;
+            double m = -INFINITY;
+            for (int64_t j = 0; j < jend; ++j) {
+                const float* kj = k + j * D;
+                double acc = 0.0;
+                for (int64_t d = 0; d < D; ++d) acc += (double)qi[d] * (double)kj[d];
+                s[j] = acc * sc;
+                if (s[j] > m) m = s[j];
+            }
+            double l = 0.0;
+            for (int64_t j = 0; j < jend; ++j) { s[j] = exp(s[j] - m); l += s[j]; }
+            double* o = s + S;
+            for (int64_t d = 0; d < D; ++d) o[d] = 0.0;
+            for (int64_t j = 0; j < jend; ++j)
+                for (int64_t d = 0; d < D; ++d) o[d] += s[j] * (double)v[j * D + d];
+            for (int64_t d = 0; d < D; ++d) out[t * D + d] = (float)(o[d] / l);
+            lse[t] = (float)(m + log(l));
+        }
+        free(s);
+    }
+}
+
+void bo_attention_bwd_head(float* dq, float* dk, float* dv, const float* dout, const float* q,
+                           const float* k, const float* v, const float* lse, int64_t S, int64_t D, int causal,
+                           float scale) {
+    const double sc = attn_scale(scale, D);
+    double* dks = (double*)calloc((size_t)(S * D), sizeof(double));
+    double* dvs = (double*)calloc((size_t)(S * D), sizeof(double));
+#pragma omp parallel
+    {
+        double* p = (double*)malloc(sizeof(double) * (size_t)(S + D));
+        double* dp = (double*)malloc(sizeof(double) * (size_t)S);
+        double* dka = (double*)calloc((size_t)(S * D), sizeof(double));
+        double* dva = (double*)calloc((size_t)(S * D), sizeof(double));
+        /* one query row at a time: attn_bwd_head's arithmetic for rows [i, i+1) */
+#pragma omp for schedule(dynamic, 16)
+        for (int64_t i = 0; i < S; ++i) {
+            const float* qi = q + i * D;
+            const float* doi = dout + i * D;
+            const int64_t jend = causal ? i + 1 : S;
+            double dterm = 0.0;
+            for (int64_t j = 0; j < jend; ++j) {
+                double acc = 0.0, accp = 0.0;
+                for (int64_t d = 0; d < D; ++d) {
+                    acc += (double)qi[d] * (double)k[j * D + d];
+                    accp += (double)doi[d] * (double)v[j * D + d];
+                }
+                p[j] = exp(acc * sc - (double)lse[i]);
+                dp[j] = accp;
+                dterm += p[j] * dp[j];
+            }
+            double* dqi = p + S;
+            for (int64_t d = 0; d < D; ++d) dqi[d] = 0.0;
+            for (int64_t j = 0; j < jend; ++j) {
+                const double ds = p[j] * (dp[j] - dterm);
+                for (int64_t d = 0; d < D; ++d) {
+                    dqi[d] += ds * (double)k[j * D + d];
+                    dka[j * D + d] += sc * ds * (double)qi[d];
+                    dva[j * D + d] += p[j] * (double)doi[d];
+                }
+            }
+            for (int64_t d = 0; d < D; ++d) dq[i * D + d] = (float)(sc * dqi[d]);
+        }
+#pragma omp critical
+        {
+            for (int64_t e = 0; e < S * D; ++e) {
+                dks[e] += dka[e];
+                dvs[e] += dva[e];
+            }
+        }
+        free(p); free(dp); free(dka); free(dva);
+    }
+    for (int64_t e = 0; e < S * D; ++e) {
+        dk[e] = (float)dks[e];
+        dv[e] = (float)dvs[e];
+    }
+    free(dks); free(dvs);
+}
+
 /* ------------------------------------------------------------------------- */
 /* RMSNorm                                                                   */
 /* ------------------------------------------------------------------------- */

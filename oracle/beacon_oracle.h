@@ -86,6 +86,17 @@ void bo_attention_bwd(float* dq, float* dk, float* dv, const float* dout,
 void bo_attention_fwd_heads(float* out, float* lse, const float* q, const float* k, const float* v,
                             int64_t B, int64_t Hq, int64_t Hkv, int64_t S, int64_t D, int causal,
                             float scale, const int64_t* heads, int64_t nheads);
+/* Forward of one query head for the listed query rows only, the rows spread over the
+ * threads (a long head is checked on sampled rows in seconds).  q, k, v point at that
+ * head's [S, D] rows; out [nrows, D], lse [nrows]. */
+void bo_attention_fwd_rows(float* out, float* lse, const float* q, const float* k, const float* v,
+                           int64_t S, int64_t D, int causal, float scale, const int64_t* rows, int64_t nrows);
+/* Backward of one query head, its query rows spread over the threads (dk/dv summed from
+ * per-thread double accumulators).  Same arithmetic as bo_attention_bwd for one head;
+ * all pointers are that head's [S, D] / [S] rows. */
+void bo_attention_bwd_head(float* dq, float* dk, float* dv, const float* dout, const float* q,
+                           const float* k, const float* v, const float* lse, int64_t S, int64_t D, int causal,
+                           float scale);
 
 /* ---- RMSNorm (crates/beacon-cuda/src/norm.rs:19-51; adjoint lib.rs:70-77) ----
  * rms[t] = sqrt(mean_d x[t,d]^2 + eps); y = x * g / rms.  The saved statistic is rms.

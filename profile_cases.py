@@ -1,9 +1,9 @@
 """Small, self-contained launches of one hot-path kernel, for ncu captures and quick timing.
 
-    python -m beacon_b200.profile_cases attn_bwd --heads 32
-    python -m beacon_b200.profile_cases attn_fwd --heads 32
-    python -m beacon_b200.profile_cases gemm --m 4096 --n 4096 --k 4096
-    python -m beacon_b200.profile_cases layernorm_bwd --tokens 16384 --width 4096
+    python profile_cases.py attn_bwd --heads 32
+    python profile_cases.py attn_fwd --heads 32
+    python profile_cases.py gemm --m 4096 --n 4096 --k 4096
+    python profile_cases.py layernorm_bwd --tokens 16384 --width 4096
 
 Each case runs `--warmup` untimed launches and then `--iters` launches timed with
 CUDA events, printing the per-launch time and TFLOP/s (algorithmic FLOPs: causal
@@ -19,7 +19,12 @@ ncu capture of a single launch (-k <kernel> -s <warmup launches> -c 1) should us
 from __future__ import annotations
 
 import argparse
+import os
 import sys
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
 
 
 def main(argv=None):
@@ -41,7 +46,7 @@ def main(argv=None):
 
     import torch
 
-    from . import ops
+    from beacon_b200 import ops
 
     torch.manual_seed(0)
     dev = torch.device("cuda", 0)

@@ -82,3 +82,52 @@ def test_arena_dispatch_host_checks():
     assert _launch(b"layernorm_adjoint_fwd", [(0, 16)] * 6, [4]) == _lib.ERR_INVALID_LAUNCH_CONFIG
     assert _launch(b"layernorm_adjoint_bwd", [(0, 64)] * 8, [4, 16, _lib.BF16]) == _lib.ERR_SHAPE_MISMATCH
     assert "layernorm_adjoint_bwd" in _lib.last_error()
+
+
+# Every entry point validates its pointers before it asks for a device: each case below
+# passes one required pointer as NULL (the rest point at a 16-byte aligned host buffer,
+# never dereferenced) and must be answered with InvalidLaunchConfig.  Without a GPU,
+# an entry that reached the device first would answer Cuda or ModuleLoad instead.
+_BUF = ctypes.create_string_buffer(1 << 16)
+_H = (ctypes.addressof(_BUF) + 255) & ~255  # 256-byte aligned host address
+
+
+def _null_cases():
+    b, f = _lib.BF16, _lib.F32
+    h = _H
+    return [
+        # name, args with None at the position of each required pointer to try, positions
+        ("beacon_matmul_fwd", [h, h, h, 8, 8, 8, b, None], [0, 1, 2]),
+        ("beacon_matmul_bwd", [h, h, h, h, h, 8, 8, 8, b, None], [2, 3, 4]),
+        ("beacon_linear_fwd", [h, h, h, None, 8, 8, 8, b, None], [0, 1, 2]),
+        ("beacon_linear_bwd", [None, None, h, h, h, h, 8, 8, 8, b, None], [3]),
+        ("beacon_matmul_fp8w_fwd", [h, h, h, 1.0, 8, 8, 8, None], [0, 1, 2]),
+        ("beacon_attention_adjoint_fwd", [h, h, h, h, h, 1, 2, 128, 64, 1, b, None], [0, 1, 2, 3, 4]),
+        ("beacon_attention_adjoint_bwd",
+         [h, h, h, h, h, h, h, h, 1, 2, 128, 64, 1, b, None, 0, None], [0, 1, 2, 3, 4, 5, 6, 7]),
+        ("beacon_attention_gqa_fwd", [h, h, h, h, h, 1, 4, 2, 128, 64, 1, b, None], [0, 1, 2, 3, 4]),
+        ("beacon_rmsnorm_adjoint_fwd", [h, h, h, h, 4, 64, 1e-5, b, None], [0, 1, 2, 3]),
+        ("beacon_rmsnorm_adjoint_bwd", [h, h, h, h, h, h, 4, 64, f, None, 0, None], [0, 2, 3, 4, 5]),
+        ("beacon_rmsnorm_adjoint_bwd_noalloc", [h, h, h, h, h, h, 4, 64, b, None], [0, 2, 3, 4, 5]),
+        ("beacon_layernorm_adjoint_fwd", [h, h, h, h, h, h, 4, 64, 1e-5, b, None], [0, 1, 2, 3, 4, 5]),
+        ("beacon_layernorm_adjoint_bwd", [h, h, h, h, h, h, h, h, 4, 64, b, None, 0, None], [0, 3, 4, 5, 6, 7]),
+        ("beacon_swiglu_adjoint_fwd", [h, h, h, h, h, 8, 16, 32, b, None, 0, None], [0, 1, 2, 3, 4]),
+        ("beacon_swiglu_adjoint_bwd", [h, h, h, h, h, h, h, h, h, 8, 16, 32, b, None, 0, None], [4, 5, 6, 7, 8]),
+        ("beacon_llama_block_fwd",
+         [h] * 9 + [1, 128, 128, 2, 1, 64, 256, 1e-5, b, None, 0, None], list(range(9))),
+        ("beacon_residual_add_fwd", [h, h, h, 64, b, None], [0, 1, 2]),
+        ("beacon_residual_add_bwd", [h, h, h, 64, b, None], [2]),
+        ("beacon_cast", [h, h, 64, 2, None], [0, 1]),
+    ]
+
+
+@pytest.mark.parametrize("name,args,positions", _null_cases(), ids=lambda v: v if isinstance(v, str) else "")
+def test_null_pointers_rejected_before_any_device_call(name, args, positions):
+    L = _lib.lib()
+    fn = getattr(L, name)
+    for pos in positions:
+        a = list(args)
+        a[pos] = None
+        rc = fn(*a)
+        assert rc == _lib.ERR_INVALID_LAUNCH_CONFIG, (name, pos, rc, _lib.last_error())
+        assert "null pointer" in _lib.last_error(), (name, pos, _lib.last_error())

@@ -75,3 +75,42 @@ def test_two_gloo_ranks_shard_and_gather():
     err, gathered_sum, ref_sum = q.get(timeout=5)
     assert err == 0.0
     assert abs(gathered_sum - ref_sum) <= 1e-6 * max(1.0, abs(ref_sum))
+
+
+def _worker_units(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+
+    from beacon_b200.shard import even_shard, gather_units, unit_generator
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        total = 10
+        start, count = even_shard(total, world, rank)
+        # each rank generates only its units, from (seed, unit): the global tensor is the
+        # same whatever the world size
+        local = torch.stack([torch.randn(3, 4, generator=unit_generator(7, u, "cpu")) for u in
+                             range(start, start + count)])
+        wanted = [0, 4, 9]
+        got = gather_units(local, start, total, wanted, world)
+        if rank == 0:
+            ref = torch.stack([torch.randn(3, 4, generator=unit_generator(7, u, "cpu")) for u in wanted])
+            q.put(bool(torch.equal(got, ref)))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_gather_sampled_units_from_their_owners():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_units, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert q.get(timeout=5) is True

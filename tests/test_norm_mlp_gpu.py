@@ -15,7 +15,7 @@ def _ops():
 
 
 @pytest.mark.parametrize("T,dim,dt", [(64, 4096, "bf16"), (8, 14336, "bf16"), (33, 1000, "f32"), (16, 256, "f32"),
-                                      (5, 100, "bf16")])
+                                      (5, 100, "bf16"), (64, 4096, "f32")])
 def test_rmsnorm(T, dim, dt):
     import torch
     ops = _ops()
@@ -38,7 +38,8 @@ def test_rmsnorm(T, dim, dt):
 # one with partials in global memory; (5, 100) and (7, 20) reach the any-dim forward and the
 # scalar backward loop.
 @pytest.mark.parametrize("T,dim,dt", [(64, 4096, "bf16"), (8, 14336, "bf16"), (2000, 768, "bf16"), (40, 6144, "bf16"),
-                                      (33, 1000, "f32"), (16, 256, "f32"), (5, 100, "bf16"), (7, 20, "f32")])
+                                      (33, 1000, "f32"), (16, 256, "f32"), (5, 100, "bf16"), (7, 20, "f32"),
+                                      (64, 4096, "f32")])
 def test_layernorm(T, dim, dt):
     import torch
     ops = _ops()
@@ -55,6 +56,36 @@ def test_layernorm(T, dim, dt):
     assert rel_err(to_np(dx), rdx) <= tol
     assert rel_err(to_np(dg), rdg) <= tol
     assert rel_err(to_np(db), rdb) <= tol
+
+
+@pytest.mark.parametrize("skip", ["dweight", "dbias"])
+def test_layernorm_bwd_one_parameter_gradient(skip):
+    """dweight or dbias alone (the other NULL): the column-sum kernel writes only the one asked for."""
+    import ctypes
+    import torch
+    from beacon_b200 import _lib
+    from beacon_b200.errors import check
+    ops = _ops()
+    T, dim = 300, 2048
+    x, g, b, dy = (as_bf16(normal(s, 20 + i)) for i, s in enumerate([(T, dim), (dim,), (dim,), (T, dim)]))
+    t = lambda a: to_dev(a, torch.bfloat16)
+    _, mu, inv = ops.layernorm_fwd(t(x), t(g), t(b))
+    rdx, rdg, rdb = O.layernorm_bwd(dy, x, to_np(mu), to_np(inv), g)
+    dx = torch.empty(T, dim, dtype=torch.bfloat16, device="cuda")
+    dw = torch.full((dim,), float("nan"), dtype=torch.bfloat16, device="cuda")
+    db = torch.full((dim,), float("nan"), dtype=torch.bfloat16, device="cuda")
+    p = lambda a: None if a is None else ctypes.c_void_p(a.data_ptr())
+    dyt, xt, gt = t(dy), t(x), t(g)
+    check(_lib.lib().beacon_layernorm_adjoint_bwd(p(dx), None if skip == "dweight" else p(dw),
+                                                  None if skip == "dbias" else p(db), p(dyt), p(xt), p(mu), p(inv),
+                                                  p(gt), T, dim, _lib.BF16, None, 0,
+                                                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    torch.cuda.synchronize()
+    assert rel_err(to_np(dx), rdx) <= BF16_TOL
+    if skip == "dweight":
+        assert torch.isnan(dw.float()).all() and rel_err(to_np(db), rdb) <= BF16_TOL
+    else:
+        assert torch.isnan(db.float()).all() and rel_err(to_np(dw), rdg) <= BF16_TOL
 
 
 def test_layernorm_edges():
