@@ -38,9 +38,10 @@ EXPORTS = (
     "beacon_attention_adjoint_fwd", "beacon_attention_adjoint_bwd", "beacon_attention_bwd_workspace_size",
     "beacon_attention_gqa_fwd", "beacon_attention_gqa_bwd", "beacon_attention_bwd_with_out",
     "beacon_rmsnorm_adjoint_fwd", "beacon_rmsnorm_adjoint_bwd", "beacon_rmsnorm_adjoint_bwd_noalloc",
+    "beacon_rmsnorm_fold_weight", "beacon_rmsnorm_linear_fwd",
     "beacon_layernorm_adjoint_fwd", "beacon_layernorm_adjoint_bwd",
     "beacon_swiglu_adjoint_fwd", "beacon_swiglu_adjoint_bwd", "beacon_swiglu_workspace_size",
-    "beacon_llama_block_fwd", "beacon_llama_block_workspace_size",
+    "beacon_llama_block_fwd", "beacon_llama_block_workspace_size", "beacon_llama_block_fwd_folded",
     "beacon_residual_add_fwd", "beacon_residual_add_bwd", "beacon_cast",
     "beacon_arena_create", "beacon_arena_destroy", "beacon_arena_base", "beacon_arena_size", "beacon_launch",
 )
@@ -111,6 +112,9 @@ def lib():
     _sig(L, "beacon_rmsnorm_adjoint_fwd", _int, [_vp, _vp, _vp, _vp, _i64, _i64, ctypes.c_float, _int, _vp])
     _sig(L, "beacon_rmsnorm_adjoint_bwd", _int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _int, _vp, _sz, _vp])
     _sig(L, "beacon_rmsnorm_adjoint_bwd_noalloc", _int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _int, _vp])
+    _sig(L, "beacon_rmsnorm_fold_weight", _int, [_vp, _vp, _vp, _i64, _i64, _int, _vp])
+    _sig(L, "beacon_rmsnorm_linear_fwd", _int,
+         [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, ctypes.c_float, _int, _vp])
     _sig(L, "beacon_layernorm_adjoint_fwd", _int,
          [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, ctypes.c_float, _int, _vp])
     _sig(L, "beacon_layernorm_adjoint_bwd", _int,
@@ -121,6 +125,7 @@ def lib():
     _sig(L, "beacon_swiglu_workspace_size", _sz, [_i64, _i64, _i64, _int, _int])
     _sig(L, "beacon_llama_block_fwd", _int, [_vp] * 9 + [_i64] * 7 + [ctypes.c_float, _int, _vp, _sz, _vp])
     _sig(L, "beacon_llama_block_workspace_size", _sz, [_i64] * 7 + [_int])
+    _sig(L, "beacon_llama_block_fwd_folded", _int, [_vp] * 7 + [_i64] * 7 + [ctypes.c_float, _int, _vp, _sz, _vp])
     _sig(L, "beacon_residual_add_fwd", _int, [_vp, _vp, _vp, _i64, _int, _vp])
     _sig(L, "beacon_residual_add_bwd", _int, [_vp, _vp, _vp, _i64, _int, _vp])
     _sig(L, "beacon_cast", _int, [_vp, _vp, _i64, _int, _vp])

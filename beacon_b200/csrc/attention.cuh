@@ -98,7 +98,7 @@ __device__ __forceinline__ void tma_load_rows(uint8_t* dst, const CUtensorMap* m
 // 2^a for a pair of arguments without the MUFU unit: a = n + f with n = rint(a) (1.5 x 2^23
 // added and subtracted in fp32 round-to-nearest, n then sits in the low mantissa bits),
 // a cubic in f in [-0.5, 0.5] fitted to 2^f by iteratively reweighted least squares on the
-// relative error (max relative error 7.5e-5, far below the bf16 rounding P receives), and n
+// relative error (max relative error 7.5e-5 on [-125.5, 8], far below the bf16 rounding P receives), and n
 // shifted into the exponent field.  Arguments are clamped at -126, which returns less than
 // 2^-125 instead of 0, so callers use it only where no element is masked to -inf.
 __device__ __forceinline__ void exp2_poly2(float& r0, float& r1, float a0, float a1) {

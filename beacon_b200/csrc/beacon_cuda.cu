@@ -359,17 +359,22 @@ int choose_bn(int64_t M, int64_t Nout, bool swiglu, int sms) {
   return best;
 }
 
-// C[M,N] = A . B (+ epilogue) with bf16 operands.  `B2` is the up-projection for kEpiSwiglu.
+// C[M,N] = A . B (+ epilogue) with bf16 operands.  `B2` is the up-projection for the tile-pair
+// (SwiGLU) epilogues, or the second K range of B when p.k_split > 0 (C = A . [B ; B2]).
 int gemm_bf16(const Operand& A, const Operand& B, const Operand* B2, GemmParams p, cudaStream_t st, int force_bn = 0) {
   int dev;
   DeviceInfo* di;
   BEACON_TRY(current_device(&dev, &di));
   if (p.M == 0 || p.N == 0) return BEACON_OK;
-  const bool swiglu = p.epi == kEpiSwiglu;
+  const bool swiglu = epi_tile_pairs(p.epi);
+  const bool two_b = swiglu || p.k_split > 0;
+  if (p.k_split > 0 && (p.k_split % 64 != 0 || p.k_split >= p.K || swiglu))
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "K-split GEMM: split %d of K %d must be a multiple of 64", p.k_split,
+                p.K);
   const bool tma_ok = aligned16(A.ptr) && aligned16(B.ptr) && (A.ld % 8 == 0) && (B.ld % 8 == 0) &&
-                      (!swiglu || (aligned16(B2->ptr) && B2->ld % 8 == 0)) && p.K > 0;
+                      (!two_b || (aligned16(B2->ptr) && B2->ld % 8 == 0)) && p.K > 0;
   if (!tma_ok) {
-    if (swiglu || p.sc_hd > 0)
+    if (two_b || p.sc_hd > 0 || p.epi == kEpiSwigluBwd || p.out2 != nullptr)
       return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "fused GEMM epilogue needs 16-byte aligned rows");
     // exact SIMT path for shapes TMA cannot describe
     const long long sam = A.mn_major ? 1 : A.ld, sak = A.mn_major ? A.ld : 1;
@@ -401,14 +406,17 @@ int gemm_bf16(const Operand& A, const Operand& B, const Operand* B2, GemmParams 
       BEACON_TRY(make_map_2d(&ta, A.ptr, (uint64_t)p.K, (uint64_t)p.M, (uint64_t)A.ld, 64, 128));
     else
       BEACON_TRY(make_map_2d(&ta, A.ptr, (uint64_t)p.M, (uint64_t)p.K, (uint64_t)A.ld, 64, 64));
-    auto map_b2 = [&](CUtensorMap* m, const Operand& op) -> int {
-      if (op.mn_major) return make_map_2d(m, op.ptr, (uint64_t)p.N, (uint64_t)p.K, (uint64_t)op.ld, 64, 64);
-      return make_map_2d(m, op.ptr, (uint64_t)p.K, (uint64_t)p.N, (uint64_t)op.ld, 64, 128);
+    // with a K split each B tensor holds its own K range (extent k_split / K - k_split)
+    const uint64_t k1 = p.k_split > 0 ? (uint64_t)p.k_split : (uint64_t)p.K;
+    const uint64_t k2 = p.k_split > 0 ? (uint64_t)(p.K - p.k_split) : (uint64_t)p.K;
+    auto map_b2 = [&](CUtensorMap* m, const Operand& op, uint64_t kext) -> int {
+      if (op.mn_major) return make_map_2d(m, op.ptr, (uint64_t)p.N, kext, (uint64_t)op.ld, 64, 64);
+      return make_map_2d(m, op.ptr, kext, (uint64_t)p.N, (uint64_t)op.ld, 64, 128);
     };
-    BEACON_TRY(map_b2(&tb, B));
-    if (swiglu) {
-      if (B2->mn_major != B.mn_major) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "swiglu operands differ in major");
-      BEACON_TRY(map_b2(&tb2, *B2));
+    BEACON_TRY(map_b2(&tb, B, k1));
+    if (two_b) {
+      if (B2->mn_major != B.mn_major) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "B operands differ in major");
+      BEACON_TRY(map_b2(&tb2, *B2, k2));
     } else {
       tb2 = tb;
     }
@@ -427,15 +435,18 @@ int gemm_bf16(const Operand& A, const Operand& B, const Operand* B2, GemmParams 
     BEACON_TRY(make_map_2d(&ta, A.ptr, (uint64_t)p.K, (uint64_t)p.M, (uint64_t)A.ld, 64, 128));
   else
     BEACON_TRY(make_map_2d(&ta, A.ptr, (uint64_t)p.M, (uint64_t)p.K, (uint64_t)A.ld, 64, 64));
-  // B logical [K,N]; for SwiGLU the tensor's N is the hidden width F
-  auto map_b = [&](CUtensorMap* m, const Operand& op) -> int {
-    if (op.mn_major) return make_map_2d(m, op.ptr, (uint64_t)p.N, (uint64_t)p.K, (uint64_t)op.ld, 64, 64);
-    return make_map_2d(m, op.ptr, (uint64_t)p.K, (uint64_t)p.N, (uint64_t)op.ld, 64, (uint32_t)cols);
+  // B logical [K,N]; for SwiGLU the tensor's N is the hidden width F; with a K split each
+  // B tensor holds its own K range
+  const uint64_t k1 = p.k_split > 0 ? (uint64_t)p.k_split : (uint64_t)p.K;
+  const uint64_t k2 = p.k_split > 0 ? (uint64_t)(p.K - p.k_split) : (uint64_t)p.K;
+  auto map_b = [&](CUtensorMap* m, const Operand& op, uint64_t kext) -> int {
+    if (op.mn_major) return make_map_2d(m, op.ptr, (uint64_t)p.N, kext, (uint64_t)op.ld, 64, 64);
+    return make_map_2d(m, op.ptr, kext, (uint64_t)p.N, (uint64_t)op.ld, 64, (uint32_t)cols);
   };
-  BEACON_TRY(map_b(&tb, B));
-  if (swiglu) {
-    if (B2->mn_major != B.mn_major) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "swiglu operands differ in major");
-    BEACON_TRY(map_b(&tb2, *B2));
+  BEACON_TRY(map_b(&tb, B, k1));
+  if (two_b) {
+    if (B2->mn_major != B.mn_major) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "B operands differ in major");
+    BEACON_TRY(map_b(&tb2, *B2, k2));
   } else {
     tb2 = tb;
   }
@@ -904,6 +915,72 @@ extern "C" int beacon_rmsnorm_adjoint_bwd(void* dx, void* dweight, const void* d
 #undef RMS_BWD_ROWS
   if (dweight) BEACON_TRY(check_launch("rmsnorm_bwd colsum"));
   return BEACON_OK;
+}
+
+// ===========================================================================
+// RMSNorm folded into the GEMM that follows it
+//   rmsnorm(x, g) . W = diag(1 / rms) . x . (diag(g) . W)
+// The gain is folded into W's rows once per weight version (beacon_rmsnorm_fold_weight);
+// each call then runs one row-statistics pass over x (k_rms_stats: reads x, writes rms)
+// and the GEMM on raw x with 1 / rms applied to the accumulator in its epilogue, instead
+// of writing and re-reading a normalised copy of x.
+// ===========================================================================
+namespace {
+
+int rms_stats(float* rms, float* sumsq, const void* x, int64_t T, int64_t dim, float eps, int dtype, int sms,
+              cudaStream_t st) {
+  const int grid = (int)std::min<int64_t>((T + 7) / 8, (int64_t)sms * 16);
+  const int vec = aligned16(x) && dim % 8 == 0;
+  if (dtype == BEACON_BF16)
+    k_rms_stats<bf16><<<grid, 256, 0, st>>>(rms, sumsq, (const bf16*)x, T, (int)dim, eps, vec);
+  else
+    k_rms_stats<float><<<grid, 256, 0, st>>>(rms, sumsq, (const float*)x, T, (int)dim, eps, vec);
+  return check_launch("k_rms_stats");
+}
+
+}  // namespace
+
+extern "C" int beacon_rmsnorm_fold_weight(void* w_out, const void* gain, const void* w, int64_t k, int64_t n,
+                                          int dtype, void* stream) {
+  BEACON_TRY(check_dims("rmsnorm_fold_weight", k, n, 1));
+  if (dtype != BEACON_BF16 && dtype != BEACON_F32)
+    return fail(BEACON_ERR_UNIMPLEMENTED, "rmsnorm_fold_weight: dtype %d", dtype);
+  if (k == 0 || n == 0) return BEACON_OK;
+  if (!w_out || !gain || !w) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "rmsnorm_fold_weight: null pointer");
+  int dev;
+  DeviceInfo* di;
+  BEACON_TRY(current_device(&dev, &di));
+  const int grid = grid_for(k * n, 256, di->sms);
+  if (dtype == BEACON_BF16)
+    k_fold_gain<bf16><<<grid, 256, 0, as_stream(stream)>>>((bf16*)w_out, (const bf16*)gain, (const bf16*)w, k, n);
+  else
+    k_fold_gain<float><<<grid, 256, 0, as_stream(stream)>>>((float*)w_out, (const float*)gain, (const float*)w, k,
+                                                            n);
+  return check_launch("k_fold_gain");
+}
+
+extern "C" int beacon_rmsnorm_linear_fwd(void* out, float* rms, const void* x, const void* w_folded,
+                                         const void* bias, int64_t m, int64_t k, int64_t n, float eps, int dtype,
+                                         void* stream) {
+  BEACON_TRY(check_dtype_gemm(dtype));
+  BEACON_TRY(check_dims("rmsnorm_linear_fwd", m, k, n));
+  if (k == 0) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "rmsnorm_linear_fwd: k (the normalised width) is 0");
+  if (m == 0) return BEACON_OK;
+  if (!rms || !x || (n && (!out || !w_folded)))
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "rmsnorm_linear_fwd: null pointer");
+  int dev;
+  DeviceInfo* di;
+  BEACON_TRY(current_device(&dev, &di));
+  cudaStream_t st = as_stream(stream);
+  BEACON_TRY(rms_stats(rms, nullptr, x, m, k, eps, dtype, di->sms, st));
+  if (n == 0) return BEACON_OK;
+  GemmParams p = gemm_params(m, n, k, out, n, dtype == BEACON_F32);
+  p.row_rms = rms;
+  if (bias) {
+    p.epi = kEpiBias;
+    p.bias = bias;
+  }
+  return gemm_any(dtype, Operand{x, false, k}, Operand{w_folded, true, n}, p, st);
 }
 
 // ===========================================================================

@@ -259,6 +259,65 @@ __global__ void __launch_bounds__(256) k_rmsnorm_fwd(T* __restrict__ y, float* _
   }
 }
 
+// Row statistics of an RMSNorm whose scaling is folded into the GEMM that consumes the
+// rows (rmsnorm(x) W = diag(1/rms) x (diag(g) W)): reads x once and writes only
+// rms[r] = sqrt(mean(x[r]^2) + eps) (when rms != null) and the sum of squares (when
+// sumsq != null), 4 or 8 bytes per row instead of a normalised copy of x.  One warp per
+// row, vectors of 8 elements (16 bytes of bf16) four deep; `vec` rows are 16-byte aligned
+// with dim % 8 == 0.
+template <typename T>
+__global__ void __launch_bounds__(256) k_rms_stats(float* __restrict__ rms, float* __restrict__ sumsq,
+                                                   const T* __restrict__ x, long long rows, int dim, float eps,
+                                                   int vec) {
+  constexpr int EPV = 8;
+  const int lane = threadIdx.x & 31;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long r = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
+    const T* xr = x + r * dim;
+    float ss = 0.0f;
+    if (vec) {
+      const int nv = dim / EPV;
+      int vi = lane;
+      for (; vi + 96 < nv; vi += 128) {
+        float a[4][8];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) load8(xr + (vi + 32 * u) * EPV, a[u]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int j = 0; j < EPV; ++j) ss = fmaf(a[u][j], a[u][j], ss);
+      }
+      for (; vi < nv; vi += 32) {
+        float a[8];
+        load8(xr + vi * EPV, a);
+#pragma unroll
+        for (int j = 0; j < EPV; ++j) ss = fmaf(a[j], a[j], ss);
+      }
+    } else {
+      for (int e = lane; e < dim; e += 32) {
+        const float t = ldf(xr + e);
+        ss = fmaf(t, t, ss);
+      }
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) {
+      if (rms) rms[r] = sqrtf(ss / (float)dim + eps);
+      if (sumsq) sumsq[r] = ss;
+    }
+  }
+}
+
+// w_out[i, j] = gain[i] * w[i, j], rounded to T: the RMSNorm gain folded into the rows
+// (the input dimension) of the weight that follows the norm.  Once per weight version.
+template <typename T>
+__global__ void k_fold_gain(T* __restrict__ w_out, const T* __restrict__ gain, const T* __restrict__ w, long long k,
+                            long long n) {
+  const long long total = k * n;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x)
+    stf(w_out + i, ldf(gain + i / n) * ldf(w + i));
+}
+
 // Generic fallback for any dim (two passes over the row, second from L1/L2).
 template <typename T>
 __global__ void __launch_bounds__(256) k_rmsnorm_fwd_any(T* __restrict__ y, float* __restrict__ rms,

@@ -11,7 +11,8 @@
 //   warp 1      TMEM allocator + tcgen05.mma issuer (M=128, N=BN, K=16): the whole warp runs
 //               the loop, one elected lane issues.
 //   warps 2-5   epilogue: tcgen05.ld of the fp32 accumulator (one TMEM lane per
-//               thread), fused bias / row-scale / residual / SwiGLU, bf16 or f32 store.
+//               thread), fused RMSNorm row scale / bias / residual / SwiGLU, bf16 or f32
+//               store, optionally the row sums of squares of what it stored.
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
 // of tile i overlaps the main loop of tile i+1.
 #pragma once
@@ -20,13 +21,20 @@
 
 namespace beacon {
 
+// Every accumulator of row r is first multiplied by out_scale and, when the GEMM carries
+// an RMSNorm (row_rms or row_sumsq set), by 1 / rms[r]; then the epilogue applies.
 enum GemmEpilogue : int {
-  kEpiStore = 0,     // out = acc
-  kEpiBias = 1,      // out = acc + bias[col]
-  kEpiRowScale = 2,  // out = acc * row_scale[row] (+ bias[col] when bias != null)
-  kEpiResidual = 3,  // out = acc + residual[row, col]
-  kEpiSwiglu = 4,    // out[:, j] = silu(acc_gate[:, j]) * acc_up[:, j]; B = [Wg | Wu] per tile
+  kEpiStore = 0,       // out = acc
+  kEpiBias = 1,        // out = acc + bias[col]
+  kEpiResidual = 3,    // out = acc + residual[row, col]
+  kEpiSwiglu = 4,      // out[:, j] = silu(acc_gate[:, j]) * acc_up[:, j]; B = [Wg | Wu] per tile
+  kEpiSwigluSave = 5,  // kEpiSwiglu, and the gate and up values themselves to aux_g, aux_u
+  // SwiGLU derivative of acc = dh = dy Wd^T, with g, u read from aux_g, aux_u:
+  //   out[row, col]          = dgate = dh * u * s * (1 + g (1 - s)),  s = sigmoid(g)
+  //   out[row, dup_off + col] = dup  = dh * g * s
+  kEpiSwigluBwd = 6,
 };
+__host__ __device__ constexpr bool epi_tile_pairs(int epi) { return epi == kEpiSwiglu || epi == kEpiSwigluSave; }
 
 struct GemmParams {
   int M, N, K;            // N: output columns (SwiGLU: F, the hidden width)
@@ -37,10 +45,32 @@ struct GemmParams {
   int epi;
   int aux_f32;            // 1: bias / residual are float32, 0: bf16
   const void* bias;       // [N]
-  const float* row_scale; // [M]
   const void* residual;   // [M, ldr]
   long long ldr;
   float out_scale;        // every accumulator is multiplied by it first (dequantisation scale; 1 = none)
+  // RMSNorm folded into the GEMM: rmsnorm(x) W = diag(1 / rms) . x . (diag(g) W), so the
+  // GEMM reads raw x and the gain-folded weights and scales row r by 1 / rms[r], with
+  //   rms[r] = row_rms[r]                                  when row_rms is set, else
+  //   rms[r] = sqrt(row_sumsq[r] / row_dim + row_eps)      when row_sumsq is set.
+  const float* row_rms;
+  const float* row_sumsq;
+  float row_dim, row_eps;
+  // When set, the epilogue adds the sum of squares of the values it stores in row r
+  // (after bf16 rounding) to out_sumsq[r]: the statistic of the next RMSNorm, accumulated
+  // over the column tiles with one atomic add per row and tile.
+  float* out_sumsq;
+  // SwiGLU backward (bf16): kEpiSwigluSave writes gate / up here, kEpiSwigluBwd reads
+  // them; [M, ld_aux].  kEpiSwigluBwd writes dup at column offset dup_off of out.
+  void* aux_g;
+  void* aux_u;
+  long long ld_aux;
+  long long dup_off;
+  // Column split of the output: columns >= n_split go to out2 (column - n_split), same ldo.
+  int n_split;
+  void* out2;
+  // K split of B: K-tiles at k >= k_split read the second B tensor map at k - k_split
+  // (C = [A1 | A2] . [B1 ; B2] as one GEMM; k_split a multiple of 64).
+  int k_split;
   // Head scatter (hd > 0): output column c of row r = b*seq + s is stored head-major,
   // [B, heads, seq, hd], into `out` for c < hq*hd, then `out_k`, then `out_v` (kv heads
   // each).  hd is a multiple of 32, so every 32-column chunk lands contiguously.
@@ -69,19 +99,22 @@ struct GemmCfg {
 
 __device__ __forceinline__ float silu_f(float z) { return z / (1.0f + __expf(-z)); }
 
-// Apply the epilogue to 32 consecutive columns [col0, col0+32) of one row and store.
-__device__ __forceinline__ void gemm_store_chunk(const GemmParams& p, int row, int col0, float (&v)[32]) {
-  if (row >= p.M) return;
-  if (p.out_scale != 1.0f) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] *= p.out_scale;
+// The factor every accumulator of `row` is multiplied by before the epilogue.
+__device__ __forceinline__ float gemm_row_factor(const GemmParams& p, int row) {
+  float s = p.out_scale;
+  if (row < p.M) {
+    if (p.row_rms != nullptr) s *= 1.0f / p.row_rms[row];
+    else if (p.row_sumsq != nullptr) s *= 1.0f / sqrtf(p.row_sumsq[row] / p.row_dim + p.row_eps);
   }
-  if (p.epi == kEpiRowScale) {
-    const float s = p.row_scale[row];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] *= s;
-  }
-  if ((p.epi == kEpiBias || p.epi == kEpiRowScale) && p.bias != nullptr) {
+  return s;
+}
+
+// Apply the epilogue to 32 consecutive columns [col0, col0+32) of one row (already
+// scaled by gemm_row_factor) and store; returns the sum of squares of the stored values
+// when p.out_sumsq is set (0 otherwise).
+__device__ __forceinline__ float gemm_store_chunk(const GemmParams& p, int row, int col0, float (&v)[32]) {
+  if (row >= p.M) return 0.0f;
+  if (p.epi == kEpiBias && p.bias != nullptr) {
 #pragma unroll
     for (int j = 0; j < 32; ++j)
       if (col0 + j < p.N) v[j] += gemm_aux(p.bias, col0 + j, p.aux_f32);
@@ -111,6 +144,10 @@ __device__ __forceinline__ void gemm_store_chunk(const GemmParams& p, int row, i
   void* base = p.out;
   long long off = (long long)row * p.ldo + col0;
   long long ld = p.ldo;
+  if (p.out2 != nullptr && col0 >= p.n_split) {  // chunks never straddle n_split (a multiple of 32)
+    base = p.out2;
+    off -= p.n_split;
+  }
   if (p.sc_hd > 0) {
     int head = col0 / p.sc_hd, nh = p.sc_hq;
     if (head >= p.sc_hq) {
@@ -127,6 +164,7 @@ __device__ __forceinline__ void gemm_store_chunk(const GemmParams& p, int row, i
     ld = 0;  // chunks never straddle a head: the vector path's alignment holds
     full = true;
   }
+  float ss = 0.0f;
   if (p.out_f32) {
     float* o = reinterpret_cast<float*>(base) + off;
     if (full && ((ld & 3) == 0)) {
@@ -137,8 +175,19 @@ __device__ __forceinline__ void gemm_store_chunk(const GemmParams& p, int row, i
       for (int j = 0; j < 32; ++j)
         if (col0 + j < p.N) o[j] = v[j];
     }
+    if (p.out_sumsq != nullptr)
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < p.N) ss = fmaf(v[j], v[j], ss);
   } else {
     __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(base) + off;
+    if (p.out_sumsq != nullptr) {  // the statistic of what is stored: bf16-rounded values
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        v[j] = __bfloat162float(__float2bfloat16_rn(v[j]));
+        if (col0 + j < p.N) ss = fmaf(v[j], v[j], ss);
+      }
+    }
     if (full && ((ld & 7) == 0)) {
 #pragma unroll
       for (int j = 0; j < 32; j += 8) {
@@ -154,6 +203,118 @@ __device__ __forceinline__ void gemm_store_chunk(const GemmParams& p, int row, i
         if (col0 + j < p.N) o[j] = __float2bfloat16_rn(v[j]);
     }
   }
+  return ss;
+}
+
+// 32 bf16 values of row `row` at [col0, col0+32) of `base` (row stride ld), zero past n.
+__device__ __forceinline__ void gemm_load_bf16_chunk(const void* base, long long ld, int row, int col0, int n,
+                                                     float (&v)[32]) {
+  const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(base) + (long long)row * ld + col0;
+  if (col0 + 32 <= n) {  // rows 16-byte aligned (ld % 8 == 0, col0 % 32 == 0)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 w = __ldg(reinterpret_cast<const uint4*>(src) + q);
+      const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        v[8 * q + 2 * e] = __uint_as_float(u[e] << 16);
+        v[8 * q + 2 * e + 1] = __uint_as_float(u[e] & 0xffff0000u);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = (col0 + j < n) ? __bfloat162float(src[j]) : 0.0f;
+  }
+}
+
+// 32 values to row `row`, columns [col0, col0+32) of a bf16 matrix (row stride ld), rounded;
+// columns at or past n are not written.
+__device__ __forceinline__ void gemm_store_bf16_chunk(void* base, long long ld, int row, int col0, int n,
+                                                      const float (&v)[32]) {
+  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(base) + (long long)row * ld + col0;
+  if (col0 + 32 <= n) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      uint4 w;
+      w.x = pack_bf16x2(v[j + 0], v[j + 1]);
+      w.y = pack_bf16x2(v[j + 2], v[j + 3]);
+      w.z = pack_bf16x2(v[j + 4], v[j + 5]);
+      w.w = pack_bf16x2(v[j + 6], v[j + 7]);
+      *reinterpret_cast<uint4*>(dst + j) = w;
+    }
+  } else {
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j < n) dst[j] = __float2bfloat16_rn(v[j]);
+  }
+}
+
+// kEpiSwigluBwd for 32 columns of dh = dy Wd^T (already scaled): the SwiGLU derivative
+// with the recomputed gate / up, dgate to out and dup to out + dup_off (bf16).
+__device__ __forceinline__ void gemm_store_swiglu_bwd(const GemmParams& p, int row, int col0, const float (&dh)[32]) {
+  if (row >= p.M) return;
+  float g[32], u[32];
+  gemm_load_bf16_chunk(p.aux_g, p.ld_aux, row, col0, p.N, g);
+  gemm_load_bf16_chunk(p.aux_u, p.ld_aux, row, col0, p.N, u);
+  float dg[32], du[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const float s = 1.0f / (1.0f + __expf(-g[j]));
+    dg[j] = dh[j] * u[j] * s * (1.0f + g[j] * (1.0f - s));
+    du[j] = dh[j] * g[j] * s;
+  }
+  gemm_store_bf16_chunk(p.out, p.ldo, row, col0, p.N, dg);
+  gemm_store_bf16_chunk(reinterpret_cast<__nv_bfloat16*>(p.out) + p.dup_off, p.ldo, row, col0, p.N, du);
+}
+
+// The epilogue of one accumulator tile for one thread (one TMEM lane = output row `row`):
+// BN fp32 columns at TMEM address `tbase`, column tile `tn`.  With tile pairs (SwiGLU) the
+// first BN/2 columns are the gate and the last BN/2 the up projection of BN/2 outputs.
+template <int BN>
+__device__ __forceinline__ void gemm_epilogue_tile(const GemmParams& p, int row, uint32_t tbase, int tn, bool pairs) {
+  const float rs = gemm_row_factor(p, row);
+  float ss = 0.0f;
+  if (!pairs) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(tbase + c * 32, r);
+      tmem_wait_ld();
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * rs;
+      const int col0 = tn * BN + c * 32;
+      if (col0 < p.N) {
+        if (p.epi == kEpiSwigluBwd)
+          gemm_store_swiglu_bwd(p, row, col0, v);
+        else
+          ss += gemm_store_chunk(p, row, col0, v);
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int c = 0; c < BN / 64; ++c) {
+      uint32_t g[32], u[32];
+      tmem_ld32(tbase + c * 32, g);
+      tmem_ld32(tbase + BN / 2 + c * 32, u);
+      tmem_wait_ld();
+      float gv[32], uv[32], v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        gv[j] = __uint_as_float(g[j]) * rs;
+        uv[j] = __uint_as_float(u[j]) * rs;
+        v[j] = silu_f(gv[j]) * uv[j];
+      }
+      const int col0 = tn * (BN / 2) + c * 32;
+      if (col0 < p.N && row < p.M) {
+        if (p.epi == kEpiSwigluSave) {
+          gemm_store_bf16_chunk(p.aux_g, p.ld_aux, row, col0, p.N, gv);
+          gemm_store_bf16_chunk(p.aux_u, p.ld_aux, row, col0, p.N, uv);
+        }
+        ss += gemm_store_chunk(p, row, col0, v);
+      }
+    }
+  }
+  if (p.out_sumsq != nullptr && row < p.M) atomicAdd(p.out_sumsq + row, ss);
 }
 
 // Fault-site codes (g_beacon_status[1]) for the GEMM's waits.
@@ -200,7 +361,7 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    if (p.epi == kEpiSwiglu) tma_prefetch_desc(&tmB2);
+    if (epi_tile_pairs(p.epi) || p.k_split > 0) tma_prefetch_desc(&tmB2);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
@@ -213,7 +374,7 @@ __global__ void __launch_bounds__(192, 1)
 
   const int num_tiles = p.tiles_m * p.tiles_n;
   const int ktiles = (p.K + BK - 1) / BK;
-  const bool swiglu = (p.epi == kEpiSwiglu);
+  const bool swiglu = epi_tile_pairs(p.epi);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -241,11 +402,15 @@ __global__ void __launch_bounds__(192, 1)
             tma_load_2d(a + 64 * BK * 2, &tmA, fb, tm * BM + 64, k0);
           }
           if (!swiglu) {
+            // K split: the second half of K reads the second B tensor
+            const bool second = p.k_split > 0 && k0 >= p.k_split;
+            const CUtensorMap* mb = second ? &tmB2 : &tmB;
+            const int kb = second ? k0 - p.k_split : k0;
             if constexpr (!B_MN) {
-              tma_load_2d(b, &tmB, fb, k0, tn * BN);
+              tma_load_2d(b, mb, fb, kb, tn * BN);
             } else {
 #pragma unroll
-              for (int j = 0; j < BN / 64; ++j) tma_load_2d(b + j * 64 * BK * 2, &tmB, fb, tn * BN + j * 64, k0);
+              for (int j = 0; j < BN / 64; ++j) tma_load_2d(b + j * 64 * BK * 2, mb, fb, tn * BN + j * 64, kb);
             }
           } else {
             const int n0 = tn * (BN / 2);
@@ -334,33 +499,7 @@ __global__ void __launch_bounds__(192, 1)
       if (!__all_sync(0xffffffffu, got)) break;  // warp-uniform: tcgen05.ld below is warp-collective
       tc_fence_after();
       const int row = tm * BM + (int)(q * 32 + lane);
-      const uint32_t tbase = tmem_base + ((q * 32u) << 16) + (uint32_t)(acc * BN);
-      if (!swiglu) {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tbase + c * 32, r);
-          tmem_wait_ld();
-          float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          const int col0 = tn * BN + c * 32;
-          if (col0 < p.N) gemm_store_chunk(p, row, col0, v);
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN / 64; ++c) {
-          uint32_t g[32], u[32];
-          tmem_ld32(tbase + c * 32, g);
-          tmem_ld32(tbase + BN / 2 + c * 32, u);
-          tmem_wait_ld();
-          float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = silu_f(__uint_as_float(g[j])) * __uint_as_float(u[j]);
-          const int col0 = tn * (BN / 2) + c * 32;
-          if (col0 < p.N) gemm_store_chunk(p, row, col0, v);
-        }
-      }
+      gemm_epilogue_tile<BN>(p, row, tmem_base + ((q * 32u) << 16) + (uint32_t)(acc * BN), tn, swiglu);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -434,7 +573,7 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    if (p.epi == kEpiSwiglu) tma_prefetch_desc(&tmB2);
+    if (epi_tile_pairs(p.epi) || p.k_split > 0) tma_prefetch_desc(&tmB2);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
@@ -447,7 +586,7 @@ __global__ void __launch_bounds__(192, 1)
 
   const int num_tiles = p.tiles_m * p.tiles_n;  // tiles of 256 x 256 (SwiGLU: 256 x 128 outputs)
   const int ktiles = (p.K + BK - 1) / BK;
-  const bool swiglu = (p.epi == kEpiSwiglu);
+  const bool swiglu = epi_tile_pairs(p.epi);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer (both CTAs)
@@ -459,7 +598,7 @@ __global__ void __launch_bounds__(192, 1)
       for (int tile = cluster; tile < num_tiles && ok; tile += n_clusters) {
         const int tm = tile / p.tiles_n, tn = tile % p.tiles_n;
         const int m0 = tm * 256 + 128 * (int)rank;
-        const CUtensorMap* mb = (swiglu && rank == 1) ? &tmB2 : &tmB;
+        const CUtensorMap* mb_tile = (swiglu && rank == 1) ? &tmB2 : &tmB;
         const int n0 = swiglu ? tn * 128 : tn * 256 + 128 * (int)rank;
         for (int kt = 0; kt < ktiles; ++kt) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteGemmEmpty)) {
@@ -477,11 +616,15 @@ __global__ void __launch_bounds__(192, 1)
             tma_load_2d_pair(a, &tmA, lb, m0, k0);
             tma_load_2d_pair(a + 64 * BK * 2, &tmA, lb, m0 + 64, k0);
           }
+          // K split: the second half of K reads the second B tensor
+          const bool second = !swiglu && p.k_split > 0 && k0 >= p.k_split;
+          const CUtensorMap* mb = second ? &tmB2 : mb_tile;
+          const int kb = second ? k0 - p.k_split : k0;
           if constexpr (!B_MN) {
-            tma_load_2d_pair(b, mb, lb, k0, n0);
+            tma_load_2d_pair(b, mb, lb, kb, n0);
           } else {
-            tma_load_2d_pair(b, mb, lb, n0, k0);
-            tma_load_2d_pair(b + 64 * BK * 2, mb, lb, n0 + 64, k0);
+            tma_load_2d_pair(b, mb, lb, n0, kb);
+            tma_load_2d_pair(b + 64 * BK * 2, mb, lb, n0 + 64, kb);
           }
           issued |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -556,33 +699,7 @@ __global__ void __launch_bounds__(192, 1)
       if (!__all_sync(0xffffffffu, got)) break;  // warp-uniform: tcgen05.ld below is warp-collective
       tc_fence_after();
       const int row = tm * 256 + 128 * (int)rank + (int)(q * 32 + lane);
-      const uint32_t tbase = tmem_base + ((q * 32u) << 16) + (uint32_t)(acc * Cfg::BN);
-      if (!swiglu) {
-#pragma unroll 1
-        for (int c = 0; c < Cfg::BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tbase + c * 32, r);
-          tmem_wait_ld();
-          float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          const int col0 = tn * Cfg::BN + c * 32;
-          if (col0 < p.N) gemm_store_chunk(p, row, col0, v);
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < Cfg::BN / 64; ++c) {
-          uint32_t g[32], u[32];
-          tmem_ld32(tbase + c * 32, g);
-          tmem_ld32(tbase + Cfg::BN / 2 + c * 32, u);
-          tmem_wait_ld();
-          float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = silu_f(__uint_as_float(g[j])) * __uint_as_float(u[j]);
-          const int col0 = tn * (Cfg::BN / 2) + c * 32;
-          if (col0 < p.N) gemm_store_chunk(p, row, col0, v);
-        }
-      }
+      gemm_epilogue_tile<Cfg::BN>(p, row, tmem_base + ((q * 32u) << 16) + (uint32_t)(acc * Cfg::BN), tn, swiglu);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
@@ -650,9 +767,8 @@ __global__ void __launch_bounds__(256)
     for (int j = 0; j < 4; ++j) {
       const int n = n0 + tx * 4 + j;
       if (n >= p.N) continue;
-      float v = acc[i][j] * p.out_scale;
-      if (p.epi == kEpiRowScale) v *= p.row_scale[m];
-      if ((p.epi == kEpiBias || p.epi == kEpiRowScale) && p.bias) v += gemm_aux(p.bias, n, p.aux_f32);
+      float v = acc[i][j] * gemm_row_factor(p, m);
+      if (p.epi == kEpiBias && p.bias) v += gemm_aux(p.bias, n, p.aux_f32);
       if (p.epi == kEpiResidual) v += gemm_aux(p.residual, m * p.ldr + n, p.aux_f32);
       if (p.out_f32)
         reinterpret_cast<float*>(p.out)[m * p.ldo + n] = v;

@@ -184,6 +184,30 @@ def rmsnorm_bwd(dy, x, rms, weight):
     return dx, dw
 
 
+def rmsnorm_fold_weight(gain, weight):
+    """diag(gain) . weight: the RMSNorm gain folded into the rows of the weight that follows
+    the norm (once per weight version)."""
+    k, n = weight.shape
+    dt = _dtype(weight, gain)
+    out = torch.empty_like(weight)
+    check(_lib.lib().beacon_rmsnorm_fold_weight(_p(out), _p(gain), _p(weight), k, n, dt, _stream()))
+    return out
+
+
+def rmsnorm_linear_fwd(x, weight_folded, bias=None, eps=1e-5, out=None):
+    """(out, rms): rmsnorm(x, g) . W + bias with W folded as diag(g) . W
+    (norm.rs:20-31 then matmul.rs:46-58 in one pass over x plus one GEMM)."""
+    m, k = x.shape
+    n = weight_folded.shape[1]
+    dt = _dtype(x, weight_folded, bias)
+    if out is None:
+        out = torch.empty(m, n, dtype=x.dtype, device=x.device)
+    rms = torch.empty(m, dtype=torch.float32, device=x.device)
+    check(_lib.lib().beacon_rmsnorm_linear_fwd(_p(out), _p(rms), _p(x), _p(weight_folded), _p(bias), m, k, n, eps,
+                                               dt, _stream()))
+    return out, rms
+
+
 # ---------------------------------------------------------------- LayerNorm
 
 def layernorm_fwd(x, weight, bias, eps=1e-5):
@@ -259,6 +283,30 @@ def llama_block_fwd(x, attn_norm, w_qkv, w_o, ffn_norm, w_gate, w_up, w_down, ba
     check(_lib.lib().beacon_llama_block_fwd(_p(out), _p(x), _p(attn_norm), _p(w_qkv), _p(w_o), _p(ffn_norm),
                                             _p(w_gate), _p(w_up), _p(w_down), batch, seq, dm, heads, kv_heads, hd, F,
                                             eps, dt, ws, wsb, _stream()))
+    return out
+
+
+def llama_block_fold_weights(attn_norm, w_qkv, ffn_norm, w_gate, w_up):
+    """(w_qkv_folded, w_gate_folded, w_up_folded) for llama_block_fwd_folded."""
+    return (rmsnorm_fold_weight(attn_norm, w_qkv), rmsnorm_fold_weight(ffn_norm, w_gate),
+            rmsnorm_fold_weight(ffn_norm, w_up))
+
+
+def llama_block_fwd_folded(x, w_qkv_folded, w_o, w_gate_folded, w_up_folded, w_down, batch, seq, heads,
+                           kv_heads=None, eps=1e-5, out=None, workspace=None):
+    """llama_block_fwd with both RMSNorm gains folded into the weights that follow them
+    (llama_block_fold_weights): the norms run as row statistics and GEMM row scales."""
+    kv_heads = heads if kv_heads is None else kv_heads
+    T, dm = x.shape
+    hd = w_o.shape[0] // heads
+    F = w_gate_folded.shape[1]
+    dt = _dtype(x, w_qkv_folded, w_o, w_gate_folded, w_up_folded, w_down)
+    if out is None:
+        out = torch.empty_like(x)
+    ws, wsb = (None, 0) if workspace is None else (_p(workspace), workspace.numel() * workspace.element_size())
+    check(_lib.lib().beacon_llama_block_fwd_folded(_p(out), _p(x), _p(w_qkv_folded), _p(w_o), _p(w_gate_folded),
+                                                   _p(w_up_folded), _p(w_down), batch, seq, dm, heads, kv_heads, hd,
+                                                   F, eps, dt, ws, wsb, _stream()))
     return out
 
 

@@ -90,7 +90,7 @@ uint64_t beacon_launch_count(void);
  * TMEM released (1)}.
  * beacon_diag_exp2_poly: out[i] = 2^in[i] by the FMA-pipe polynomial the attention
  * softmax uses for part of its exponentials (n even); its stated bound is a relative
- * error below 7.5e-5 on [-126, 8]. */
+ * error below 7.5e-5 on [-125.5, 8] and an absolute error below 2^-125 beneath it. */
 int beacon_diag_wait_timeout(uint64_t limit_ns, unsigned int* out, void* stream);
 int beacon_diag_exp2_poly(float* out, const float* in, int64_t n, void* stream);
 
@@ -210,6 +210,21 @@ int beacon_rmsnorm_adjoint_bwd(void* dx, void* dweight, const void* dy, const vo
 int beacon_rmsnorm_adjoint_bwd_noalloc(void* dx, void* dweight, const void* dy, const void* x, const float* rms,
                                        const void* weight, int64_t tokens, int64_t dim, int dtype, void* stream);
 
+/* RMSNorm fused into the linear layer that consumes it: rmsnorm_fwd (norm.rs:20-31)
+ * followed by linear_fwd (matmul.rs:46-58) as
+ *     rmsnorm(x, g) . W + b = diag(1 / rms) . x . (diag(g) . W) + b.
+ * beacon_rmsnorm_fold_weight writes w_out[i, j] = g[i] * w[i, j] (rounded to dtype), once
+ * per weight version.  beacon_rmsnorm_linear_fwd then reads x once for its row statistic
+ * rms[t] = sqrt(mean(x[t]^2) + eps) (written: the value rmsnorm_fwd saves for the
+ * backward) and runs the GEMM on raw x and the folded weight with 1 / rms[t] applied to
+ * each accumulator row in the epilogue (+ bias, may be NULL): no normalised copy of x is
+ * written or read.  x [m, k], w_folded [k, n], out [m, n]; f32 or bf16.
+ * No reference counterpart as one call (the reference has the two operators). */
+int beacon_rmsnorm_fold_weight(void* w_out, const void* gain, const void* w, int64_t k, int64_t n, int dtype,
+                               void* stream);
+int beacon_rmsnorm_linear_fwd(void* out, float* rms, const void* x, const void* w_folded, const void* bias,
+                              int64_t m, int64_t k, int64_t n, float eps, int dtype, void* stream);
+
 /* ---- LayerNorm: crates/beacon-cuda/src/norm.rs:55-95 ----------------------- */
 
 /* layernorm_fwd (norm.rs:56-73): mean[t] = mean_d x[t, d],
@@ -268,6 +283,18 @@ int beacon_llama_block_fwd(void* out, const void* x, const void* attn_norm, cons
                            size_t workspace_bytes, void* stream);
 size_t beacon_llama_block_workspace_size(int64_t batch, int64_t seq, int64_t d_model, int64_t heads,
                                          int64_t kv_heads, int64_t head_dim, int64_t d_ff, int dtype);
+
+/* The same block with both RMSNorms folded into the GEMMs that consume them (six
+ * launches and a 4-byte-per-row memset, no normalised activations written or read):
+ * w_qkv_folded = diag(attn_norm) . w_qkv, w_gate_folded = diag(ffn_norm) . w_gate,
+ * w_up_folded = diag(ffn_norm) . w_up, each made once per weight version with
+ * beacon_rmsnorm_fold_weight.  The first norm's statistic is one read of x; the second's
+ * is summed in the output projection's epilogue from the h it stores.  Same workspace. */
+int beacon_llama_block_fwd_folded(void* out, const void* x, const void* w_qkv_folded, const void* w_o,
+                                  const void* w_gate_folded, const void* w_up_folded, const void* w_down,
+                                  int64_t batch, int64_t seq, int64_t d_model, int64_t heads, int64_t kv_heads,
+                                  int64_t head_dim, int64_t d_ff, float eps, int dtype, void* workspace,
+                                  size_t workspace_bytes, void* stream);
 
 /* ---- elementwise: crates/beacon-cuda/src/elementwise.rs -------------------- */
 

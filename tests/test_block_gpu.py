@@ -66,3 +66,32 @@ def test_llama_block_fwd_caller_workspace_and_errors():
     with pytest.raises(errors.LaunchError):
         ops.llama_block_fwd(x, w["attn_norm"], w["w_qkv"], w["w_o"], w["ffn_norm"], w["w_gate"], w["w_up"],
                             w["w_down"], Bt, S, Hq, Hkv, workspace=ws[: need // 2])
+
+
+@pytest.mark.parametrize("Bt,S,dm,Hq,Hkv,D,F", [
+    (2, 200, 256, 4, 2, 64, 384),
+    (1, 512, 1024, 8, 2, 128, 2816),
+])
+def test_llama_block_fwd_folded(Bt, S, dm, Hq, Hkv, D, F):
+    """The block with both RMSNorms folded into the GEMMs after them (gains folded into the
+    weights, statistics as row scales, the second statistic summed in the output
+    projection's epilogue) against the operator-by-operator oracle and the unfused block."""
+    import torch
+    from beacon_b200 import ops
+    w = _weights(dm, Hq, Hkv, D, F, 40, std=0.05)
+    x = as_bf16(normal((Bt * S, dm), 3))
+    ref = O.llama_block_fwd(x, w["attn_norm"], w["w_qkv"], w["w_o"], w["ffn_norm"], w["w_gate"], w["w_up"],
+                            w["w_down"], Bt, S, Hq, Hkv)
+    dev = {k: to_dev(v, torch.bfloat16) for k, v in w.items()}
+    xd = to_dev(x, torch.bfloat16)
+    wq, wg, wu = ops.llama_block_fold_weights(dev["attn_norm"], dev["w_qkv"], dev["ffn_norm"], dev["w_gate"],
+                                              dev["w_up"])
+    out = ops.llama_block_fwd_folded(xd, wq, dev["w_o"], wg, wu, dev["w_down"], Bt, S, Hq, Hkv)
+    unfused = ops.llama_block_fwd(xd, dev["attn_norm"], dev["w_qkv"], dev["w_o"], dev["ffn_norm"], dev["w_gate"],
+                                  dev["w_up"], dev["w_down"], Bt, S, Hq, Hkv)
+    torch.cuda.synchronize()
+    got = to_np(out)
+    assert np.isfinite(got).all()
+    assert rel_err(got, ref) <= BF16_TOL
+    assert rel_err(got - x, ref - x) <= BF16_TOL
+    assert rel_err(got - x, to_np(unfused) - x) <= BF16_TOL

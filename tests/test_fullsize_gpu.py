@@ -108,4 +108,11 @@ def test_llama_block_benchmark_shape_sampled_rows():
     g = got[seq * S + rows]
     assert rel_err(g, ref) <= BF16_TOL
     assert rel_err(g - xs[rows], ref - xs[rows]) <= BF16_TOL
+    # the same block with both norms folded into the GEMMs after them
+    wq, wg, wu = ops.llama_block_fold_weights(n1, dev["w_qkv"], n1, dev["w_gate"], dev["w_up"])
+    folded = to_np(ops.llama_block_fwd_folded(to_dev(x, torch.bfloat16), wq, dev["w_o"], wg, wu, dev["w_down"], Bt,
+                                              S, H, H))
+    gf = folded[seq * S + rows]
+    assert rel_err(gf, ref) <= BF16_TOL
+    assert rel_err(gf - xs[rows], ref - xs[rows]) <= BF16_TOL
     assert ops.device_status(0)[0] == 0

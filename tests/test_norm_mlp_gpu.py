@@ -109,7 +109,10 @@ def test_layernorm_edges():
     assert dx0.shape == (0, 64) and not dg0.float().any() and not db0.float().any()
 
 
-@pytest.mark.parametrize("T,dm,F,dt", [(128, 256, 512, "bf16"), (200, 128, 320, "bf16"), (64, 64, 96, "f32")])
+# bf16 backward: F % 64 == 0 takes the fused five-GEMM path (K = 2F dx GEMM, N = 2F weight
+# gradient GEMM); (64, 64, 96) the N-split but two dx GEMMs; (100, 128, 200) two GEMMs for each
+@pytest.mark.parametrize("T,dm,F,dt", [(128, 256, 512, "bf16"), (200, 128, 320, "bf16"), (64, 64, 96, "f32"),
+                                      (64, 64, 96, "bf16"), (100, 128, 200, "bf16")])
 def test_swiglu(T, dm, F, dt):
     import torch
     ops = _ops()
@@ -163,3 +166,26 @@ def test_no_device_fault_recorded():
     ops = _ops()
     code, site, count = ops.device_status(0)
     assert (code, count) == (0, 0)
+
+
+@pytest.mark.parametrize("m,k,n,dt,bias", [(256, 512, 384, "bf16", False), (200, 136, 328, "bf16", True),
+                                           (4096, 4096, 1024, "bf16", False), (64, 96, 48, "f32", True),
+                                           (33, 40, 24, "bf16", True)])
+def test_rmsnorm_folded_into_linear(m, k, n, dt, bias):
+    """rmsnorm_fwd then linear_fwd (norm.rs:20-31, matmul.rs:46-58) as one statistics pass
+    and one GEMM on raw x with the gain folded into W and 1/rms applied in the epilogue."""
+    import torch
+    ops = _ops()
+    tdt = torch.bfloat16 if dt == "bf16" else torch.float32
+    tol = BF16_TOL if dt == "bf16" else F32_TOL
+    r = as_bf16 if dt == "bf16" else (lambda a: a)
+    x, g = r(normal((m, k), 61)), r(1.0 + 0.1 * normal((k,), 62))
+    w, b = r(normal((k, n), 63, std=0.05)), (r(normal((n,), 64)) if bias else None)
+    dev = lambda a: None if a is None else to_dev(a, tdt)
+    wf = ops.rmsnorm_fold_weight(dev(g), dev(w))
+    assert rel_err(to_np(wf), r(g[:, None] * w)) <= (F32_TOL if dt == "f32" else 0.0)
+    out, rms = ops.rmsnorm_linear_fwd(dev(x), wf, dev(b))
+    y, rr = O.rmsnorm_fwd(x, g)
+    ref = O.linear_fwd(r(y), w, b)
+    assert rel_err(to_np(rms), rr) <= 1e-5
+    assert rel_err(to_np(out), ref) <= tol
