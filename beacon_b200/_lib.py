@@ -34,7 +34,8 @@ EXPORTS = (
     "beacon_diag_wait_timeout", "beacon_diag_exp2_poly",
     "beacon_profile_enable", "beacon_profile_read",
     "beacon_matmul_fwd", "beacon_matmul_bwd", "beacon_linear_fwd", "beacon_linear_bwd",
-    "beacon_matmul_fp8w_fwd", "beacon_linear_fp8w_fwd",
+    "beacon_matmul_fp8w_fwd", "beacon_linear_fp8w_fwd", "beacon_linear_fp8w_fwd_devscale",
+    "beacon_quantize_fp8e4m3",
     "beacon_attention_adjoint_fwd", "beacon_attention_adjoint_bwd", "beacon_attention_bwd_workspace_size",
     "beacon_attention_gqa_fwd", "beacon_attention_gqa_bwd", "beacon_attention_bwd_with_out",
     "beacon_rmsnorm_adjoint_fwd", "beacon_rmsnorm_adjoint_bwd", "beacon_rmsnorm_adjoint_bwd_noalloc",
@@ -99,6 +100,8 @@ def lib():
     _sig(L, "beacon_linear_bwd", _int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp])
     _sig(L, "beacon_matmul_fp8w_fwd", _int, [_vp, _vp, _vp, ctypes.c_float, _i64, _i64, _i64, _vp])
     _sig(L, "beacon_linear_fp8w_fwd", _int, [_vp, _vp, _vp, ctypes.c_float, _vp, _i64, _i64, _i64, _vp])
+    _sig(L, "beacon_linear_fp8w_fwd_devscale", _int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp])
+    _sig(L, "beacon_quantize_fp8e4m3", _int, [_vp, _vp, _vp, _vp, _i64, _vp])
     _sig(L, "beacon_attention_adjoint_fwd", _int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int, _vp])
     _sig(L, "beacon_attention_adjoint_bwd", _int,
          [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int, _vp, _sz, _vp])

@@ -26,6 +26,7 @@
 #include "diag.cuh"
 #include "elementwise.cuh"
 #include "gemm.cuh"
+#include "gemm_fp8.cuh"
 #include "sm100.cuh"
 
 using namespace beacon;
@@ -168,9 +169,11 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// bf16 tensor of `rank` dims (dims[0] innermost, contiguous), 128-byte swizzle.
+// Tensor of `rank` dims (dims[0] innermost, contiguous); bf16 with 128-byte swizzle unless
+// given another element type / swizzle.
 int make_map(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
-             const uint32_t* box) {
+             const uint32_t* box, CUtensorMapDataType type = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+             CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(BEACON_ERR_MODULE_LOAD, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t d[5], s[4];
@@ -181,9 +184,8 @@ int make_map(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, c
     es[i] = 1;
   }
   for (int i = 0; i + 1 < rank; ++i) s[i] = strides_bytes[i];
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void*>(base), d, s, b, es,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(m, type, (cuuint32_t)rank, const_cast<void*>(base), d, s, b, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return BEACON_OK;
 }
@@ -625,17 +627,73 @@ extern "C" int beacon_diag_exp2_poly(float* out, const float* in, int64_t n, voi
 // ===========================================================================
 namespace {
 
-// fp8 e4m3 weights [k, n] (crates/beacon-core/src/dtype.rs:134-195) dequantised to bf16 in
-// the library workspace, then the bf16 tensor-core GEMM with `scale` folded into its
-// epilogue: out = (lhs . decode(rhs)) * scale (+ bias).
-int gemm_fp8w(void* out, const void* lhs, const void* rhs_fp8, float scale, const void* bias, int64_t m, int64_t k,
-              int64_t n, cudaStream_t st) {
+int launch_gemm_fp8w_tc2(const void* lhs, const void* rhs_fp8, GemmParams p, int sms, cudaStream_t st) {
+  using Cfg = GemmFp8Cfg;
+  CUtensorMap ta, tw;
+  BEACON_TRY(make_map_2d(&ta, lhs, (uint64_t)p.K, (uint64_t)p.M, (uint64_t)p.K, 64, 128));
+  {  // the fp8 weight [K][N] as bytes: boxes of 128 columns x 64 K rows, not swizzled
+    const uint64_t dims[2] = {(uint64_t)p.N, (uint64_t)p.K};
+    const uint64_t strides[1] = {(uint64_t)p.N};
+    const uint32_t box[2] = {128, 64};
+    BEACON_TRY(make_map(&tw, rhs_fp8, 2, dims, strides, box, CU_TENSOR_MAP_DATA_TYPE_UINT8,
+                        CU_TENSOR_MAP_SWIZZLE_NONE));
+  }
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_fp8w_tc2, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return fail(BEACON_ERR_CUDA, "fp8 gemm smem attribute: %s", cudaGetErrorString(e));
+    attr_set[dev] = true;
+  }
+  p.tiles_m = (p.M + 255) / 256;
+  p.tiles_n = (p.N + 255) / 256;
+  const int pairs = std::min(p.tiles_m * p.tiles_n, sms / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * pairs));
+  cfg.blockDim = dim3(Cfg::THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  {
+    ProfScope prof("k_gemm_fp8w_tc2", st);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_fp8w_tc2, ta, tw, p);
+    if (e != cudaSuccess) return fail(BEACON_ERR_CUDA, "k_gemm_fp8w_tc2 launch: %s", cudaGetErrorString(e));
+  }
+  return check_launch("k_gemm_fp8w_tc2");
+}
+
+// fp8 e4m3 weights [k, n] (crates/beacon-core/src/dtype.rs:134-195):
+// out = (lhs . decode(rhs)) * scale (* *scale_dev) (+ bias).  Where TMA can describe the
+// operands (16-byte aligned, k % 8 == 0, n % 16 == 0) the weights are decoded inside the
+// GEMM pipeline (k_gemm_fp8w_tc2: each weight byte is read from HBM once); otherwise they
+// are decoded to a bf16 copy in the library workspace and the bf16 GEMM runs on that.
+int gemm_fp8w(void* out, const void* lhs, const void* rhs_fp8, float scale, const float* scale_dev,
+              const void* bias, int64_t m, int64_t k, int64_t n, cudaStream_t st) {
   BEACON_TRY(check_dims("fp8-weight GEMM", m, k, n));
   if (m == 0 || n == 0) return BEACON_OK;
   if (!out || (k && (!lhs || !rhs_fp8))) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "fp8-weight GEMM: null pointer");
   int dev;
   DeviceInfo* di;
   BEACON_TRY(current_device(&dev, &di));
+  if (k > 0 && k % 8 == 0 && n % 16 == 0 && aligned16(lhs) && aligned16(rhs_fp8) && aligned16(out) &&
+      gemm_path_override() != 1) {
+    GemmParams p = gemm_params(m, n, k, out, n, false);
+    p.out_scale = scale;
+    p.out_scale_dev = scale_dev;
+    if (bias) {
+      p.epi = kEpiBias;
+      p.bias = bias;
+    }
+    return launch_gemm_fp8w_tc2(lhs, rhs_fp8, p, di->sms, st);
+  }
   void* ws = nullptr;
   const size_t wbytes = align256((size_t)k * n * 2);
   BEACON_TRY(get_workspace(dev, wbytes, nullptr, 0, &ws));
@@ -648,6 +706,7 @@ int gemm_fp8w(void* out, const void* lhs, const void* rhs_fp8, float scale, cons
   }
   GemmParams p = gemm_params(m, n, k, out, n, false);
   p.out_scale = scale;
+  p.out_scale_dev = scale_dev;
   if (bias) {
     p.epi = kEpiBias;
     p.bias = bias;
@@ -659,17 +718,43 @@ int gemm_fp8w(void* out, const void* lhs, const void* rhs_fp8, float scale, cons
 
 extern "C" int beacon_matmul_fp8w_fwd(void* out, const void* lhs, const void* rhs_fp8, float rhs_scale, int64_t m,
                                       int64_t k, int64_t n, void* stream) {
-  return gemm_fp8w(out, lhs, rhs_fp8, rhs_scale, nullptr, m, k, n, as_stream(stream));
+  return gemm_fp8w(out, lhs, rhs_fp8, rhs_scale, nullptr, nullptr, m, k, n, as_stream(stream));
 }
 
 extern "C" int beacon_linear_fp8w_fwd(void* out, const void* x, const void* weight_fp8, float weight_scale,
                                       const void* bias, int64_t m, int64_t k, int64_t n, void* stream) {
-  return gemm_fp8w(out, x, weight_fp8, weight_scale, bias, m, k, n, as_stream(stream));
+  return gemm_fp8w(out, x, weight_fp8, weight_scale, nullptr, bias, m, k, n, as_stream(stream));
+}
+
+extern "C" int beacon_linear_fp8w_fwd_devscale(void* out, const void* x, const void* weight_fp8,
+                                               const float* weight_scale_dev, const void* bias, int64_t m, int64_t k,
+                                               int64_t n, void* stream) {
+  if (!weight_scale_dev) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "linear_fp8w_fwd_devscale: null pointer");
+  return gemm_fp8w(out, x, weight_fp8, 1.0f, weight_scale_dev, bias, m, k, n, as_stream(stream));
+}
+
+extern "C" int beacon_quantize_fp8e4m3(void* out_fp8, float* scale, float* amax, const float* src, int64_t n,
+                                       void* stream) {
+  if (n < 0) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "quantize_fp8e4m3: negative n");
+  if (!scale || !amax || (n > 0 && (!out_fp8 || !src)))
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "quantize_fp8e4m3: null pointer");
+  int dev;
+  DeviceInfo* di;
+  BEACON_TRY(current_device(&dev, &di));
+  cudaStream_t st = as_stream(stream);
+  BEACON_TRY(zero_fill(amax, 4, st));
+  if (n > 0) {
+    k_absmax<<<grid_for(n / 4 + 1, 256, di->sms), 256, 0, st>>>(reinterpret_cast<unsigned int*>(amax), src, n);
+    BEACON_TRY(check_launch("k_absmax"));
+  }
+  k_quantize_fp8<<<grid_for(std::max<int64_t>(n, 1), 256, di->sms), 256, 0, st>>>(
+      reinterpret_cast<uint8_t*>(out_fp8), scale, amax, src, n);
+  return check_launch("k_quantize_fp8");
 }
 
 extern "C" int beacon_matmul_fwd(void* out, const void* lhs, const void* rhs, int64_t m, int64_t k, int64_t n,
                                  int dtype, void* stream) {
-  if (dtype == BEACON_FP8E4M3) return gemm_fp8w(out, lhs, rhs, 1.0f, nullptr, m, k, n, as_stream(stream));
+  if (dtype == BEACON_FP8E4M3) return gemm_fp8w(out, lhs, rhs, 1.0f, nullptr, nullptr, m, k, n, as_stream(stream));
   BEACON_TRY(check_dtype_gemm(dtype));
   BEACON_TRY(check_dims("matmul_fwd", m, k, n));
   if (m && n && (!out || (k && (!lhs || !rhs))))
@@ -699,7 +784,7 @@ extern "C" int beacon_matmul_bwd(void* dlhs, void* drhs, const void* dout, const
 
 extern "C" int beacon_linear_fwd(void* out, const void* x, const void* weight, const void* bias, int64_t m,
                                  int64_t k, int64_t n, int dtype, void* stream) {
-  if (dtype == BEACON_FP8E4M3) return gemm_fp8w(out, x, weight, 1.0f, bias, m, k, n, as_stream(stream));
+  if (dtype == BEACON_FP8E4M3) return gemm_fp8w(out, x, weight, 1.0f, nullptr, bias, m, k, n, as_stream(stream));
   BEACON_TRY(check_dtype_gemm(dtype));
   BEACON_TRY(check_dims("linear_fwd", m, k, n));
   if (m && n && (!out || (k && (!x || !weight))))

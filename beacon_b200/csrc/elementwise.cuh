@@ -142,6 +142,47 @@ __global__ void k_cast(void* __restrict__ dst, const void* __restrict__ src, lon
   }
 }
 
+// ---------------------------------------------------------------------------
+// fp32 master -> fp8 e4m3 weights with one scale per tensor
+//   amax = max |x| (NaN ignored), scale = amax / 448 (1 when amax is 0),
+//   q = F8E4M3::from_f32(x * (448 / amax)), so that x ~ decode(q) * scale.
+// k_absmax folds each CTA's maximum into *amax_bits (the float's bits: for values >= 0
+// the unsigned order is the float order; the word starts at 0); k_quantize_fp8 reads it.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_absmax(unsigned int* __restrict__ amax_bits, const float* __restrict__ x,
+                                                long long n) {
+  __shared__ float red[8];
+  float m = 0.0f;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const long long nvec = ((reinterpret_cast<uintptr_t>(x) & 15) == 0) ? n / 4 : 0;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+    const float4 v = reinterpret_cast<const float4*>(x)[i];
+    m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  }
+  for (long long i = nvec * 4 + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    m = fmaxf(m, fabsf(x[i]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = red[0];
+    for (int w = 1; w < 8; ++w) b = fmaxf(b, red[w]);
+    atomicMax(amax_bits, __float_as_uint(b));
+  }
+}
+
+__global__ void __launch_bounds__(256) k_quantize_fp8(uint8_t* __restrict__ q, float* __restrict__ scale,
+                                                      const float* __restrict__ amax, const float* __restrict__ x,
+                                                      long long n) {
+  const float a = *amax;
+  const float inv = a > 0.0f ? 448.0f / a : 1.0f;
+  if (blockIdx.x == 0 && threadIdx.x == 0) *scale = a > 0.0f ? a / 448.0f : 1.0f;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    q[i] = fp8e4m3_from_f32(x[i] * inv);
+}
+
 // fp8 e4m3 -> bf16, 16 elements per thread-step (every e4m3 value is exact in bf16).
 __global__ void k_fp8_to_bf16(uint16_t* __restrict__ dst, const uint8_t* __restrict__ src, long long n) {
   const long long stride = (long long)gridDim.x * blockDim.x;

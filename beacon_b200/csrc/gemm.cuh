@@ -48,6 +48,7 @@ struct GemmParams {
   const void* residual;   // [M, ldr]
   long long ldr;
   float out_scale;        // every accumulator is multiplied by it first (dequantisation scale; 1 = none)
+  const float* out_scale_dev;  // when set, also by *out_scale_dev (a scale the device produced)
   // RMSNorm folded into the GEMM: rmsnorm(x) W = diag(1 / rms) . x . (diag(g) W), so the
   // GEMM reads raw x and the gain-folded weights and scales row r by 1 / rms[r], with
   //   rms[r] = row_rms[r]                                  when row_rms is set, else
@@ -102,6 +103,7 @@ __device__ __forceinline__ float silu_f(float z) { return z / (1.0f + __expf(-z)
 // The factor every accumulator of `row` is multiplied by before the epilogue.
 __device__ __forceinline__ float gemm_row_factor(const GemmParams& p, int row) {
   float s = p.out_scale;
+  if (p.out_scale_dev != nullptr) s *= *p.out_scale_dev;
   if (row < p.M) {
     if (p.row_rms != nullptr) s *= 1.0f / p.row_rms[row];
     else if (p.row_sumsq != nullptr) s *= 1.0f / sqrtf(p.row_sumsq[row] / p.row_dim + p.row_eps);

@@ -94,16 +94,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// The same with cluster-scope acquire: for a barrier that threads of the peer CTA arrive on
+// (release.cluster) after writing shared memory that this CTA's tensor core then reads.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred P;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2;\n"
+      " selp.b32 %0, 1, 0, P;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait for the phase with the given parity, giving up after `limit_ns`.
 // `abort_flag` (shared) lets one role that gave up release every other role quickly.
+template <bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                               unsigned int site, uint64_t limit_ns) {
-  if (mbar_try_wait(bar, parity)) return true;
+  auto try_wait = [&]() { return CLUSTER ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity); };
+  if (try_wait()) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
+      if (try_wait()) return true;
     if (*abort_flag) return false;
     if (globaltimer_ns() - t0 > limit_ns) {
       record_fault(kFaultWaitTimeout, site);
@@ -126,6 +141,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           unsigned int site) {
   return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, site));
+}
+__device__ __forceinline__ bool warp_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                  unsigned int site) {
+  return __all_sync(0xffffffffu, mbar_wait_for<true>(bar, parity, abort_flag, site, BEACON_WAIT_LIMIT_NS));
 }
 
 // ---------------------------------------------------------------------------

@@ -113,6 +113,33 @@ def matmul_fp8w_fwd(lhs, rhs_fp8, scale=1.0, bias=None, out=None):
     return out
 
 
+def quantize_fp8e4m3(src):
+    """fp32 master -> (fp8 e4m3 bytes, scale, amax): one scale per tensor, scale = amax / 448,
+    q = F8E4M3::from_f32(src * 448 / amax) (crates/beacon-core/src/dtype.rs:163-195).
+    scale and amax are one-element float32 device tensors."""
+    if src.dtype != torch.float32 or not src.is_cuda or not src.is_contiguous():
+        raise InvalidLaunchConfig("quantize_fp8e4m3: src must be a contiguous float32 CUDA tensor")
+    q = torch.empty(src.shape, dtype=torch.uint8, device=src.device)
+    scale = torch.empty(1, dtype=torch.float32, device=src.device)
+    amax = torch.empty(1, dtype=torch.float32, device=src.device)
+    check(_lib.lib().beacon_quantize_fp8e4m3(_p(q), _p(scale), _p(amax), _p(src), src.numel(), _stream()))
+    return q, scale, amax
+
+
+def linear_fp8w_fwd_devscale(x, weight_fp8, scale_dev, bias=None, out=None):
+    """(x . decode(weight_fp8)) * scale_dev[0] (+ bias), the scale read on the device."""
+    m, k = x.shape
+    n = weight_fp8.shape[1]
+    if weight_fp8.dtype != torch.uint8 or x.dtype != torch.bfloat16 or scale_dev.dtype != torch.float32:
+        raise InvalidLaunchConfig("linear_fp8w_fwd_devscale: x bf16, weight uint8 (e4m3), scale float32")
+    _dtype(x, bias)
+    if out is None:
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
+    check(_lib.lib().beacon_linear_fp8w_fwd_devscale(_p(out), _p(x), _p(weight_fp8), _p(scale_dev), _p(bias), m, k,
+                                                     n, _stream()))
+    return out
+
+
 # ---------------------------------------------------------------- attention
 
 def attention_fwd(q, k, v, causal=True, out=None, lse=None):

@@ -123,13 +123,28 @@ int beacon_linear_fwd(void* out, const void* x, const void* weight, const void* 
  * crates/beacon-train/Cargo.toml:7).  `dtype = BEACON_FP8E4M3` in beacon_matmul_fwd /
  * beacon_linear_fwd means: lhs / x, bias and out are bf16, rhs / weight is fp8 e4m3 [k, n]
  * with scale 1.  The _fp8w_ entry points take the per-tensor dequantisation scale:
- * out = (lhs . decode(rhs)) * scale (+ bias).  The weights are decoded to bf16 (exactly) in
- * the library workspace and multiplied on the bf16 tensor cores, the scale folded into
- * the GEMM epilogue. */
+ * out = (lhs . decode(rhs)) * scale (+ bias).  The weights are decoded to bf16 (exactly)
+ * inside the GEMM pipeline -- TMA brings the fp8 bytes into shared memory, converter warps
+ * decode them into the tensor core's operand layout -- so each weight byte is read from
+ * HBM once; the scale is applied in the epilogue.  (lhs 16-byte aligned with k % 8 == 0,
+ * weights 16-byte aligned with n % 16 == 0; other shapes decode to a bf16 copy in the
+ * library workspace first.) */
 int beacon_matmul_fp8w_fwd(void* out, const void* lhs, const void* rhs_fp8, float rhs_scale, int64_t m, int64_t k,
                            int64_t n, void* stream);
 int beacon_linear_fp8w_fwd(void* out, const void* x, const void* weight_fp8, float weight_scale, const void* bias,
                            int64_t m, int64_t k, int64_t n, void* stream);
+/* The same with the scale read from device memory (as beacon_quantize_fp8e4m3 writes it),
+ * so no host round trip sits between quantising and using the weights; bias may be NULL. */
+int beacon_linear_fp8w_fwd_devscale(void* out, const void* x, const void* weight_fp8, const float* weight_scale_dev,
+                                    const void* bias, int64_t m, int64_t k, int64_t n, void* stream);
+
+/* fp32 master -> fp8 e4m3 weights, one scale per tensor (the reference's "fp32 master ->
+ * fp8 weights", crates/beacon-train/Cargo.toml:7; no scale convention is fixed there):
+ *   amax = max |src| (NaN ignored), scale = amax / 448 (1 when amax is 0),
+ *   out[i] = F8E4M3::from_f32(src[i] * (448 / amax))  (crates/beacon-core/src/dtype.rs:163-195,
+ *   bit-exact, float32 arithmetic), so src ~ decode(out) * scale.
+ * amax and scale are single floats in device memory (written on the stream). */
+int beacon_quantize_fp8e4m3(void* out_fp8, float* scale, float* amax, const float* src, int64_t n, void* stream);
 
 /* linear_bwd (matmul.rs:60-78): dx = dout . weight^T ; dweight = x^T . dout ; dbias = sum_rows dout.
  * Any gradient pointer may be NULL to skip it. */

@@ -141,6 +141,21 @@ def to_fp8_bits(x: np.ndarray) -> np.ndarray:
     return out
 
 
+def quantize_fp8e4m3(x: np.ndarray):
+    """fp32 master -> fp8 e4m3 with one scale per tensor, in float32 arithmetic:
+    amax = max |x| (NaN ignored), scale = amax / 448 (1 when amax is 0),
+    q = F8E4M3::from_f32(x * (448 / amax)) (the encode of crates/beacon-core/src/dtype.rs:163-195).
+    The reference names the step ("fp32 master -> fp8 weights", crates/beacon-train/Cargo.toml:7)
+    but fixes no scale convention; this is the one the library implements.
+    Returns (codes uint8, scale float32, amax float32)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    finite = np.abs(x[~np.isnan(x)])
+    a = np.float32(finite.max()) if finite.size else np.float32(0.0)
+    inv = np.float32(448.0) / a if a > 0 else np.float32(1.0)
+    scale = a / np.float32(448.0) if a > 0 else np.float32(1.0)
+    return to_fp8_bits((x * inv).astype(np.float32)), np.float32(scale), np.float32(a)
+
+
 def from_fp8_bits(b: np.ndarray) -> np.ndarray:
     b = np.ascontiguousarray(b, dtype=np.uint8)
     out = _empty(*b.shape)
@@ -276,6 +291,32 @@ def swiglu_bwd(dy, x, wg, wu, wd):
     lib().bo_swiglu_bwd(_p(dx), _p(dwg), _p(dwu), _p(dwd), _p(dy), _p(x), _p(wg), _p(wu), _p(wd),
                         T, dm, F)
     return dx, dwg, dwu, dwd
+
+
+def swiglu_bwd_sampled(dy, x, wg, wu, wd, rows, cols):
+    """swiglu_bwd (crates/beacon-cuda/src/mlp.rs:31-52; adjoint
+    crates/beacon-adjoint-table/src/lib.rs:100-107: x stored, gate and up recomputed) at
+    sampled rows of dx and sampled hidden columns of the weight gradients, in float64:
+        g = x Wg, u = x Wu, s = sigmoid(g), h = g s u, dh = dy Wd^T,
+        dgate = dh u s (1 + g (1 - s)), dup = dh g s,
+        dx = dgate Wg^T + dup Wu^T, dWg = x^T dgate, dWu = x^T dup, dWd = h^T dy.
+    Each sampled quantity needs only its own rows / columns of the intermediates, so the
+    block-sized backward (T = 8192, d_model = 4096, d_ff = 14336) is checked in seconds.
+    Returns (dx[rows], dWg[:, cols], dWu[:, cols], dWd[cols, :])."""
+    f = lambda a: np.asarray(a, dtype=np.float64)
+    x64, dy64 = f(x), f(dy)
+    rows, cols = np.asarray(rows), np.asarray(cols)
+
+    def parts(xr, dyr, wg_, wu_, wd_t):
+        g, u, dh = xr @ wg_, xr @ wu_, dyr @ wd_t
+        s = 1.0 / (1.0 + np.exp(-g))
+        return g, u, s, dh * u * s * (1.0 + g * (1.0 - s)), dh * g * s
+
+    _, _, _, dgr, dur = parts(x64[rows], dy64[rows], f(wg), f(wu), f(wd).T)
+    dx = dgr @ f(wg).T + dur @ f(wu).T
+    g, u, s, dgc, duc = parts(x64, dy64, f(wg[:, cols]), f(wu[:, cols]), f(wd[cols, :]).T)
+    return (dx.astype(np.float32), (x64.T @ dgc).astype(np.float32), (x64.T @ duc).astype(np.float32),
+            ((g * s * u).T @ dy64).astype(np.float32))
 
 
 def residual_add_fwd(a, b):

@@ -4,6 +4,8 @@
     python profile_cases.py attn_fwd --heads 32
     python profile_cases.py gemm --m 4096 --n 4096 --k 4096
     python profile_cases.py layernorm_bwd --tokens 16384 --width 4096
+    python profile_cases.py gemm_fp8 --m 4096 --n 4096 --k 4096
+    python profile_cases.py swiglu_bwd --tokens 16384 --width 4096 --n 14336
 
 Each case runs `--warmup` untimed launches and then `--iters` launches timed with
 CUDA events, printing the per-launch time and TFLOP/s (algorithmic FLOPs: causal
@@ -29,8 +31,8 @@ if ROOT not in sys.path:
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["attn_fwd", "attn_bwd", "attn_bwd_recompute", "gemm", "layernorm_fwd",
-                                     "layernorm_bwd", "rmsnorm_bwd"])
+    ap.add_argument("case", choices=["attn_fwd", "attn_bwd", "attn_bwd_recompute", "gemm", "gemm_fp8", "swiglu_bwd",
+                                     "layernorm_fwd", "layernorm_bwd", "rmsnorm_fwd", "rmsnorm_bwd"])
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--width", type=int, default=4096)
     ap.add_argument("--heads", type=int, default=32)
@@ -67,6 +69,20 @@ def main(argv=None):
             fn, flops, kname = (lambda: ops.attention_bwd(do, q, k, v, lse, out=out)), 2.5 * fwd, "k_attn_bwd_dkdv"
         else:
             fn, flops, kname = (lambda: ops.attention_bwd(do, q, k, v, lse)), 2.5 * fwd, "k_attn_bwd_dkdv"
+    elif a.case == "gemm_fp8":
+        A = (torch.rand(a.m, a.k, device=dev) * 2 - 1).bfloat16()
+        W8, scale, _ = ops.quantize_fp8e4m3(torch.randn(a.k, a.n, device=dev))
+        C = torch.empty(a.m, a.n, device=dev, dtype=torch.bfloat16)
+        fn = lambda: ops.linear_fp8w_fwd_devscale(A, W8, scale, out=C)
+        flops, kname = 2.0 * a.m * a.n * a.k, "k_gemm_fp8w_tc2"
+    elif a.case == "swiglu_bwd":
+        T, dm, F = a.tokens // 2, a.width, a.n
+        x = torch.randn(T, dm, device=dev).bfloat16()
+        dy = torch.randn(T, dm, device=dev).bfloat16()
+        wg, wu = ((torch.randn(dm, F, device=dev) * 0.02).bfloat16() for _ in range(2))
+        wd = (torch.randn(F, dm, device=dev) * 0.02).bfloat16()
+        fn = lambda: ops.swiglu_bwd(dy, x, wg, wu, wd)
+        flops, kname = 12.0 * T * dm * F, "k_gemm_bf16_tc"  # dWd, dh, dWg, dWu, dx (recompute not counted)
     else:
         A = (torch.rand(a.m, a.k, device=dev) * 2 - 1).bfloat16()
         Bm = (torch.rand(a.k, a.n, device=dev) * 2 - 1).bfloat16()
@@ -87,8 +103,13 @@ def main(argv=None):
     ops.profile_enable(False)
     ms, n = ops.profile_read(kname)
     kms = ms / max(n, 1)
-    print(f"{a.case}: {kname} {kms:.4f} ms/launch {flops / (kms * 1e-3) / 1e12:.1f} TFLOP/s; "
-          f"call {e0.elapsed_time(e1) / a.iters:.4f} ms", flush=True)
+    call_ms = e0.elapsed_time(e1) / a.iters
+    if a.case == "swiglu_bwd":  # five GEMM launches per call: the whole call against the algorithmic FLOPs
+        print(f"{a.case}: {call_ms:.4f} ms/call {flops / (call_ms * 1e-3) / 1e12:.1f} TFLOP/s algorithmic "
+              f"({n // max(a.iters, 1)} GEMM launches per call, {kms:.4f} ms each on average)", flush=True)
+    else:
+        print(f"{a.case}: {kname} {kms:.4f} ms/launch {flops / (kms * 1e-3) / 1e12:.1f} TFLOP/s; "
+              f"call {call_ms:.4f} ms", flush=True)
     if a.case.startswith("attn_bwd"):  # the dQ kernel of the same calls: 3 of the backward's 5 products
         qms, qn = ops.profile_read("k_attn_bwd_dq")
         qms /= max(qn, 1)
@@ -107,6 +128,8 @@ def _layernorm(a, torch, ops, dev):
     out, mean, invstd = ops.layernorm_fwd(x, g, b)
     if a.case == "layernorm_fwd":
         fn, nbytes = (lambda: ops.layernorm_fwd(x, g, b)), 2.0 * T * W * 2 + 8.0 * T
+    elif a.case == "rmsnorm_fwd":
+        fn, nbytes = (lambda: ops.rmsnorm_fwd(x, g)), 2.0 * T * W * 2 + 4.0 * T
     elif a.case == "rmsnorm_bwd":
         _, rms = ops.rmsnorm_fwd(x, g)
         fn, nbytes = (lambda: ops.rmsnorm_bwd(dy, x, rms, g)), 3.0 * T * W * 2 + 4.0 * T

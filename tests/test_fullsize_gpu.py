@@ -116,3 +116,44 @@ def test_llama_block_benchmark_shape_sampled_rows():
     assert rel_err(gf, ref) <= BF16_TOL
     assert rel_err(gf - xs[rows], ref - xs[rows]) <= BF16_TOL
     assert ops.device_status(0)[0] == 0
+
+
+def test_block_backward_shapes_sampled():
+    """The backward operators at the block's shapes (tokens 8192, d_model 4096, SwiGLU hidden
+    14336, QKV width 12288): swiglu_bwd (mlp.rs:31-52), linear_bwd (matmul.rs:60-78) and
+    rmsnorm_bwd (norm.rs:33-50) on the GPU in full, the oracle on sampled rows of dx and
+    sampled columns of the weight gradients (rmsnorm_bwd and dbias in full)."""
+    import torch
+    from beacon_b200 import ops
+    T, dm, F, N = 8192, 4096, 14336, 12288
+    t = lambda a: to_dev(a, torch.bfloat16)
+    rng = np.random.default_rng(1)
+    rows = np.sort(rng.choice(T, 16, replace=False))
+    # SwiGLU MLP backward
+    x, dy = as_bf16(normal((T, dm), 81)), as_bf16(normal((T, dm), 82))
+    wg, wu = as_bf16(normal((dm, F), 83, std=0.02)), as_bf16(normal((dm, F), 84, std=0.02))
+    wd = as_bf16(normal((F, dm), 85, std=0.02))
+    dx, dwg, dwu, dwd = (to_np(a) for a in ops.swiglu_bwd(t(dy), t(x), t(wg), t(wu), t(wd)))
+    cols = np.sort(rng.choice(F, 16, replace=False))
+    rdx, rdwg, rdwu, rdwd = O.swiglu_bwd_sampled(dy, x, wg, wu, wd, rows, cols)
+    assert rel_err(dx[rows], rdx) <= BF16_TOL
+    assert rel_err(dwg[:, cols], rdwg) <= BF16_TOL and rel_err(dwu[:, cols], rdwu) <= BF16_TOL
+    assert rel_err(dwd[cols, :], rdwd) <= BF16_TOL
+    del dx, dwg, dwu, dwd, wg, wu, wd
+    # linear backward of the QKV projection
+    w = as_bf16(normal((dm, N), 86, std=0.02))
+    dout = as_bf16(normal((T, N), 87))
+    ldx, ldw, ldb = (to_np(a) for a in ops.linear_bwd(t(dout), t(x), t(w)))
+    lcols = np.sort(rng.choice(N, 16, replace=False))
+    f64 = lambda a: np.asarray(a, dtype=np.float64)
+    assert rel_err(ldx[rows], f64(dout[rows]) @ f64(w).T) <= BF16_TOL
+    assert rel_err(ldw[:, lcols], f64(x).T @ f64(dout[:, lcols])) <= BF16_TOL
+    assert rel_err(ldb, f64(dout).sum(axis=0)) <= BF16_TOL
+    del ldx, ldw, ldb, dout, w
+    # RMSNorm backward, in full
+    g = as_bf16(1.0 + 0.1 * normal((dm,), 88))
+    _, rms = ops.rmsnorm_fwd(t(x), t(g))
+    rdx, rdg = O.rmsnorm_bwd(dy, x, to_np(rms), g)
+    ndx, ndg = ops.rmsnorm_bwd(t(dy), t(x), rms, t(g))
+    assert rel_err(to_np(ndx), rdx) <= BF16_TOL and rel_err(to_np(ndg), rdg) <= BF16_TOL
+    assert ops.device_status(0)[0] == 0

@@ -112,8 +112,11 @@ def test_no_device_fault_recorded():
     assert (code, count) == (0, 0)
 
 
+# n % 16 == 0 with aligned rows: decoded inside the GEMM pipeline (k_gemm_fp8w_tc2);
+# (72, 200, 200): n % 16 != 0, decoded to a bf16 copy first
 @pytest.mark.parametrize("m,k,n,scale,with_bias", [(256, 512, 384, 1.0, False), (4096, 4096, 4096, 0.03125, True),
-                                                   (100, 64, 48, 2.5, True)])
+                                                   (100, 64, 48, 2.5, True), (300, 136, 336, 1.0, False),
+                                                   (72, 200, 200, 0.5, True)])
 def test_fp8_weight_gemm(m, k, n, scale, with_bias):
     """fp8 e4m3 weights (reference codec) dequantised in the GEMM path; bf16 activations."""
     import torch
@@ -149,3 +152,49 @@ def test_fp8_dtype_through_matmul_fwd_entry():
                                       ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == 0, _lib.last_error()
     assert rel_err(to_np(out), O.matmul_fwd(a, O.from_fp8_bits(w8))) <= BF16_TOL
+
+
+def test_fp8_in_gemm_decode_of_every_code_is_exact():
+    """All 256 e4m3 codes through the in-pipeline decoder: column j of the weight holds code
+    j at row j % 64 and zeros elsewhere, the activations are the identity, so out[i, j] is
+    exactly the decoded code at i == j % 64 (0 elsewhere), or NaN down the whole column of a
+    NaN code.  Compared with the reference codec (crates/beacon-core/src/dtype.rs:138-161)."""
+    import torch
+    ops = _ops()
+    k, n = 64, 256
+    w8 = np.zeros((k, n), dtype=np.uint8)
+    codes = np.arange(256, dtype=np.uint8)
+    w8[np.arange(n) % k, np.arange(n)] = codes
+    eye = np.eye(k, dtype=np.float32)
+    out = to_np(ops.matmul_fp8w_fwd(to_dev(eye, torch.bfloat16), torch.from_numpy(w8).cuda(), 1.0))
+    dec = O.from_fp8_bits(codes)
+    ref = np.zeros((k, n), dtype=np.float32)
+    ref[np.arange(n) % k, np.arange(n)] = dec
+    ref[:, np.isnan(dec)] = np.nan
+    assert np.array_equal(out, ref, equal_nan=True)
+
+
+def test_fp8_quantizer_is_bit_exact_and_feeds_the_gemm():
+    """fp32 master -> fp8 weights (amax, scale = amax / 448, encode of x * 448 / amax)
+    against the oracle bit for bit, then the device-scale GEMM on those weights against the
+    oracle and against the host-scale GEMM (same bits)."""
+    import torch
+    ops = _ops()
+    k, n, m = 1024, 768, 256
+    w = normal((k, n), 26, std=0.3)
+    w[3, 5] = 7.25  # the tensor's maximum
+    q, scale, amax = ops.quantize_fp8e4m3(torch.from_numpy(w).cuda())
+    rq, rscale, ramax = O.quantize_fp8e4m3(w)
+    assert np.array_equal(q.cpu().numpy(), rq)
+    assert float(scale.item()) == float(rscale) and float(amax.item()) == float(ramax)
+    a = as_bf16(normal((m, k), 27))
+    ad = to_dev(a, torch.bfloat16)
+    out = ops.linear_fp8w_fwd_devscale(ad, q, scale)
+    ref = O.matmul_fwd(a, (O.from_fp8_bits(rq) * rscale).astype(np.float32))
+    assert rel_err(to_np(out), ref) <= BF16_TOL
+    assert rel_err(to_np(out), O.matmul_fwd(a, w)) <= 0.1  # the quantisation error itself stays small
+    host = ops.matmul_fp8w_fwd(ad, q, float(scale.item()))
+    assert torch.equal(out, host)
+    # all zeros: scale 1, codes 0
+    q0, s0, a0 = ops.quantize_fp8e4m3(torch.zeros(64, device="cuda"))
+    assert not q0.any() and float(s0.item()) == 1.0 and float(a0.item()) == 0.0
