@@ -45,6 +45,7 @@ EXPORTS = (
     "beacon_llama_block_fwd", "beacon_llama_block_workspace_size", "beacon_llama_block_fwd_folded",
     "beacon_residual_add_fwd", "beacon_residual_add_bwd", "beacon_cast",
     "beacon_arena_create", "beacon_arena_destroy", "beacon_arena_base", "beacon_arena_size", "beacon_launch",
+    "beacon_workspace_create",
 )
 
 _lib = None
@@ -136,6 +137,7 @@ def lib():
     _sig(L, "beacon_arena_destroy", None, [_vp])
     _sig(L, "beacon_arena_base", _vp, [_vp])
     _sig(L, "beacon_arena_size", ctypes.c_uint64, [_vp])
+    _sig(L, "beacon_workspace_create", _int, [_vp, ctypes.c_uint64])
     _sig(L, "beacon_launch", _int, [_vp, ctypes.c_char_p, ctypes.POINTER(KernelArgC), _sz,
                                     ctypes.POINTER(ctypes.c_int64), _sz, _vp])
     _lib = L

@@ -210,6 +210,16 @@ struct Workspace {
 std::mutex g_ws_mu;
 Workspace g_ws[64];
 
+// While beacon_launch dispatches a kernel ID, the arena's own workspace stands in for the
+// library's: an entry point that needs scratch and was given none takes the arena's, and
+// fails with OutOfMemory instead of allocating when the arena has too little.
+struct ArenaScope {
+  bool active = false;
+  void* ws = nullptr;
+  size_t bytes = 0;
+};
+thread_local ArenaScope t_arena;
+
 int get_workspace(int dev, size_t need, void* user, size_t user_bytes, void** out) {
   if (need == 0) {
     *out = user;
@@ -219,6 +229,15 @@ int get_workspace(int dev, size_t need, void* user, size_t user_bytes, void** ou
     if (user_bytes < need)
       return fail(BEACON_ERR_OUT_OF_MEMORY, "workspace of %zu bytes given, %zu needed", user_bytes, need);
     *out = user;
+    return BEACON_OK;
+  }
+  if (t_arena.active) {
+    if (t_arena.bytes < need)
+      return fail(BEACON_ERR_OUT_OF_MEMORY,
+                  "out of device memory: requested %zu bytes of arena workspace, %zu available "
+                  "(reserve it once with beacon_workspace_create)",
+                  need, t_arena.bytes);
+    *out = t_arena.ws;
     return BEACON_OK;
   }
   std::lock_guard<std::mutex> lk(g_ws_mu);

@@ -327,6 +327,7 @@ class Launcher(KernelLauncher, AllLaunch):
 
     ordinal: int = 0
     arena_bytes: int = 1 << 20
+    workspace_bytes: int = 0
     _arena: int = field(default=0, init=False, repr=False)
 
     def __post_init__(self):
@@ -334,10 +335,17 @@ class Launcher(KernelLauncher, AllLaunch):
         self._arena = L.beacon_arena_create(self.ordinal, self.arena_bytes)
         if not self._arena:
             raise MemoryError(_lib.last_error())
+        if self.workspace_bytes:
+            self.reserve_workspace(self.workspace_bytes)
 
     @staticmethod
-    def on_device(ordinal: int, arena_bytes: int = 1 << 20) -> "Launcher":
-        return Launcher(ordinal, arena_bytes)
+    def on_device(ordinal: int, arena_bytes: int = 1 << 20, workspace_bytes: int = 0) -> "Launcher":
+        return Launcher(ordinal, arena_bytes, workspace_bytes)
+
+    def reserve_workspace(self, nbytes: int) -> None:
+        """The launcher's scratch, made once (kernels launched through it never allocate)."""
+        check(_lib.lib().beacon_workspace_create(self._arena, int(nbytes)))
+        self.workspace_bytes = int(nbytes)
 
     def device(self) -> int:
         return self.ordinal

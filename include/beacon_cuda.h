@@ -344,6 +344,15 @@ typedef struct beacon_kernel_arg {
  * regions are the caller's business, crates/beacon-core/src/arena.rs:7). */
 beacon_arena* beacon_arena_create(int device, uint64_t bytes);
 void beacon_arena_destroy(beacon_arena* arena);
+
+/* The launcher's workspace (crates/beacon-cuda/src/runtime.rs:6-48 keeps one Launcher per
+ * device; "kernels never allocate"): `bytes` of device memory owned by the arena, made once
+ * at set-up (a second call replaces it, after a device synchronisation).  beacon_launch
+ * hands it to every kernel ID that needs scratch (the attention, RMSNorm, LayerNorm and
+ * SwiGLU backward, linear_bwd's dbias, the SwiGLU forward) and never allocates: when the
+ * workspace is missing or too small the launch fails with BEACON_ERR_OUT_OF_MEMORY
+ * ("requested / available").  Size it with the beacon_*_workspace_size functions. */
+int beacon_workspace_create(beacon_arena* arena, uint64_t bytes);
 void* beacon_arena_base(beacon_arena* arena);
 uint64_t beacon_arena_size(beacon_arena* arena);
 

@@ -131,3 +131,37 @@ def test_null_pointers_rejected_before_any_device_call(name, args, positions):
         rc = fn(*a)
         assert rc == _lib.ERR_INVALID_LAUNCH_CONFIG, (name, pos, rc, _lib.last_error())
         assert "null pointer" in _lib.last_error(), (name, pos, _lib.last_error())
+
+
+def _launch_access(kernel, args, scalars):
+    """beacon_launch over a host-memory stand-in arena; args are (offset, len, access)."""
+    L = _lib.lib()
+    buf = ctypes.create_string_buffer(4096)
+    arena = _FakeArena(0, ctypes.cast(buf, ctypes.c_void_p), 4096)
+    arr = (_lib.KernelArgC * len(args))(*[_lib.KernelArgC(o, n, acc) for o, n, acc in args])
+    sc = (ctypes.c_int64 * max(len(scalars), 1))(*scalars)
+    return L.beacon_launch(ctypes.byref(arena), kernel, arr, len(args), sc, len(scalars), None)
+
+
+def test_arena_dispatch_checks_access_modes():
+    """A kernel never writes through an argument declared Read (launcher.rs:14-19); the
+    check runs on the host before any device call."""
+    R, W, RW = 0, 1, 2
+    mm = [8, 4, 8, _lib.BF16]  # out 128 B, lhs 64 B, rhs 64 B
+    rc = _launch_access(b"matmul_fwd", [(0, 128, R), (128, 64, R), (256, 64, R)], mm)
+    assert rc == _lib.ERR_INVALID_LAUNCH_CONFIG and "declared Read" in _lib.last_error()
+    rc = _launch_access(b"matmul_fwd", [(0, 128, 7), (128, 64, R), (256, 64, R)], mm)
+    assert rc == _lib.ERR_INVALID_LAUNCH_CONFIG and "access 7" in _lib.last_error()
+    # attention backward writes dq, dk, dv (arguments 0-2)
+    at = [1, 1, 16, 16, 1, _lib.BF16]
+    q = 16 * 16 * 2
+    args = [(0, q, W), (q, q, RW), (2 * q, q, R)] + [(3 * q, q, R)] * 4 + [(3 * q, 64, R)]
+    rc = _launch_access(b"attention_adjoint_bwd", args, at)
+    assert rc == _lib.ERR_INVALID_LAUNCH_CONFIG and "argument 2" in _lib.last_error()
+    # with Write / ReadWrite outputs the host checks pass and the call goes on to the
+    # device (none in this container: the answer is then a CUDA-side error).  The stand-in
+    # arena is host memory, so this step runs only where no GPU could receive the launch.
+    import torch
+    if not torch.cuda.is_available():
+        rc = _launch_access(b"matmul_fwd", [(0, 128, W), (128, 64, R), (256, 64, RW)], mm)
+        assert rc not in (_lib.OK, _lib.ERR_INVALID_LAUNCH_CONFIG, _lib.ERR_SHAPE_MISMATCH), _lib.last_error()
