@@ -514,7 +514,31 @@ def run_beacon(args, rank, world, local):
             import oracle as O
             ref = O.matmul_fwd(a[rows].float().cpu().numpy(), b_full.float().cpu().numpy())
             check_gemm = {"rows": 16, "c": O.rel_err(c_rows.float().cpu().numpy(), ref)}
-        del a, bm, b_full, c, flush
+        # the same GEMM with fp8 e4m3 weights (fp32 master quantised per tensor on the device,
+        # decoded inside the GEMM pipeline, the scale read on the device)
+        w8, wscale, _ = ops.quantize_fp8e4m3(b_full[:, rank * ncols:(rank + 1) * ncols].float().contiguous())
+        c8 = torch.empty_like(c)
+        times8 = []
+        for i in range(max(args.steps, 5) + 3):
+            flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            ops.linear_fp8w_fwd_devscale(a, w8, wscale, out=c8)
+            e1.record(stream)
+            e1.synchronize()
+            if i >= 3:
+                times8.append(e0.elapsed_time(e1))
+        barrier(world)
+        g8ms = max_over_ranks(statistics.median(times8), world)
+        gemm["fp8_weights"] = {"value": 2.0 * GEMM_N ** 3 / (g8ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": g8ms,
+                               "api": "beacon_quantize_fp8e4m3 then beacon_linear_fp8w_fwd_devscale "
+                                      "(k_gemm_fp8w_tc2: e4m3 decoded inside the GEMM pipeline)"}
+        if rank == 0:
+            import oracle as O
+            wq = (O.from_fp8_bits(w8.cpu().numpy()) * float(wscale.item())).astype("float32")
+            ref8 = O.matmul_fwd(a[rows].float().cpu().numpy(), wq)
+            check_gemm["c_fp8_weights_local_columns"] = O.rel_err(c8[rows].float().cpu().numpy(), ref8)
+        del a, bm, b_full, c, flush, w8, c8
 
     block, check_block = (None, None) if args.no_block else bench_block(args, rank, world, dev, stream)
     gqa, check_gqa = (None, None) if args.no_gqa else bench_gqa(args, rank, world, dev, stream)

@@ -80,11 +80,20 @@ def test_attention_and_matmul_through_the_arena_launcher():
     torch.cuda.synchronize()
 
     R, W = KernelArg.read, KernelArg.write
+
+    def step():
+        la.attention_fwd(W(o_out, tb), R(o_q, tb), R(o_k, tb), R(o_v, tb), W(o_lse, B * H * S * 4), B, H, S, D,
+                         True)
+        la.attention_bwd(W(o_dq, tb), W(o_dk, tb), W(o_dv, tb), R(o_do, tb), R(o_q, tb), R(o_k, tb), R(o_v, tb),
+                         R(o_lse, B * H * S * 4), B, H, S, D, True)
+        la.matmul_fwd(W(o_c, m * n * 2), R(o_a, m * kk * 2), R(o_b, kk * n * 2), m, kk, n)
+
+    # The first launch of a kernel in a process loads the library's module onto the device
+    # (CUDA's lazy loading), which takes device memory once; the second pass is measured.
+    step()
+    torch.cuda.synchronize()
     free0, _ = torch.cuda.mem_get_info()
-    la.attention_fwd(W(o_out, tb), R(o_q, tb), R(o_k, tb), R(o_v, tb), W(o_lse, B * H * S * 4), B, H, S, D, True)
-    la.attention_bwd(W(o_dq, tb), W(o_dk, tb), W(o_dv, tb), R(o_do, tb), R(o_q, tb), R(o_k, tb), R(o_v, tb),
-                     R(o_lse, B * H * S * 4), B, H, S, D, True)
-    la.matmul_fwd(W(o_c, m * n * 2), R(o_a, m * kk * 2), R(o_b, kk * n * 2), m, kk, n)
+    step()
     torch.cuda.synchronize()
     free1, _ = torch.cuda.mem_get_info()
     assert free1 == free0  # the launches took their scratch from the launcher's workspace
