@@ -44,6 +44,7 @@ EXPORTS = (
     "beacon_swiglu_adjoint_fwd", "beacon_swiglu_adjoint_bwd", "beacon_swiglu_workspace_size",
     "beacon_llama_block_fwd", "beacon_llama_block_workspace_size", "beacon_llama_block_fwd_folded",
     "beacon_residual_add_fwd", "beacon_residual_add_bwd", "beacon_cast",
+    "beacon_embedding_lookup_fwd", "beacon_embedding_lookup_bwd", "beacon_dropout_fwd", "beacon_dropout_bwd",
     "beacon_arena_create", "beacon_arena_destroy", "beacon_arena_base", "beacon_arena_size", "beacon_launch",
     "beacon_workspace_create",
 )
@@ -133,6 +134,10 @@ def lib():
     _sig(L, "beacon_residual_add_fwd", _int, [_vp, _vp, _vp, _i64, _int, _vp])
     _sig(L, "beacon_residual_add_bwd", _int, [_vp, _vp, _vp, _i64, _int, _vp])
     _sig(L, "beacon_cast", _int, [_vp, _vp, _i64, _int, _vp])
+    _sig(L, "beacon_embedding_lookup_fwd", _int, [_vp, _vp, _vp, _i64, _i64, _i64, _int, _vp])
+    _sig(L, "beacon_embedding_lookup_bwd", _int, [_vp, _vp, _vp, _i64, _i64, _i64, _int, _vp])
+    _sig(L, "beacon_dropout_fwd", _int, [_vp, _vp, _vp, _i64, ctypes.c_float, ctypes.c_uint64, _int, _vp])
+    _sig(L, "beacon_dropout_bwd", _int, [_vp, _vp, _vp, _i64, _int, _vp])
     _sig(L, "beacon_arena_create", _vp, [_int, ctypes.c_uint64])
     _sig(L, "beacon_arena_destroy", None, [_vp])
     _sig(L, "beacon_arena_base", _vp, [_vp])

@@ -907,6 +907,95 @@ extern "C" int beacon_cast(void* dst, const void* src, int64_t n, int kind, void
 }
 
 // ===========================================================================
+// embedding lookup / dropout
+// ===========================================================================
+namespace {
+constexpr unsigned int kSiteEmbFwd = 0x601, kSiteEmbBwd = 0x602;
+
+int embedding_check(const char* what, const void* a, const void* b, const void* idx, int64_t tokens, int64_t dim,
+                    int64_t vocab, int dtype) {
+  if (tokens < 0 || dim <= 0 || dim > INT32_MAX || vocab < 0)
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "%s: bad shape tokens=%lld dim=%lld vocab=%lld", what,
+                (long long)tokens, (long long)dim, (long long)vocab);
+  if (dtype != BEACON_BF16 && dtype != BEACON_F32) return fail(BEACON_ERR_UNIMPLEMENTED, "%s: dtype %d", what, dtype);
+  if (tokens > 0 && (!a || !b || !idx)) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "%s: null pointer", what);
+  return BEACON_OK;
+}
+}  // namespace
+
+extern "C" int beacon_embedding_lookup_fwd(void* out, const void* table, const uint32_t* indices, int64_t tokens,
+                                           int64_t dim, int64_t vocab, int dtype, void* stream) {
+  BEACON_TRY(embedding_check("embedding_lookup_fwd", out, table, indices, tokens, dim, vocab, dtype));
+  if (tokens == 0) return BEACON_OK;
+  int dev;
+  DeviceInfo* di;
+  BEACON_TRY(current_device(&dev, &di));
+  const int es = dtype == BEACON_F32 ? 4 : 2;
+  const int vec = aligned16(out) && aligned16(table) && (dim * es) % 16 == 0;
+  const int grid = grid_for(tokens * 32, 256, di->sms);
+  if (dtype == BEACON_BF16)
+    k_embedding_fwd<bf16><<<grid, 256, 0, as_stream(stream)>>>((bf16*)out, (const bf16*)table, indices, tokens,
+                                                                 (int)dim, vocab, vec, kSiteEmbFwd);
+  else
+    k_embedding_fwd<float><<<grid, 256, 0, as_stream(stream)>>>((float*)out, (const float*)table, indices, tokens,
+                                                                  (int)dim, vocab, vec, kSiteEmbFwd);
+  return check_launch("k_embedding_fwd");
+}
+
+extern "C" int beacon_embedding_lookup_bwd(void* d_table, const void* d_out, const uint32_t* indices, int64_t tokens,
+                                           int64_t dim, int64_t vocab, int dtype, void* stream) {
+  BEACON_TRY(embedding_check("embedding_lookup_bwd", d_table, d_out, indices, tokens, dim, vocab, dtype));
+  if (tokens == 0) return BEACON_OK;
+  int dev;
+  DeviceInfo* di;
+  BEACON_TRY(current_device(&dev, &di));
+  const int grid = grid_for(tokens * 32, 256, di->sms);
+  if (dtype == BEACON_BF16)
+    k_embedding_bwd<bf16><<<grid, 256, 0, as_stream(stream)>>>((bf16*)d_table, (const bf16*)d_out, indices, tokens,
+                                                                 (int)dim, vocab, kSiteEmbBwd);
+  else
+    k_embedding_bwd<float><<<grid, 256, 0, as_stream(stream)>>>((float*)d_table, (const float*)d_out, indices,
+                                                                  tokens, (int)dim, vocab, kSiteEmbBwd);
+  return check_launch("k_embedding_bwd");
+}
+
+extern "C" int beacon_dropout_fwd(void* out, const void* input, void* mask, int64_t n, float p, uint64_t seed,
+                                  int dtype, void* stream) {
+  if (n < 0 || !(p >= 0.0f)) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "dropout_fwd: n %lld, p %g", (long long)n, p);
+  if (dtype != BEACON_BF16 && dtype != BEACON_F32) return fail(BEACON_ERR_UNIMPLEMENTED, "dropout_fwd: dtype %d", dtype);
+  if (n == 0) return BEACON_OK;
+  if (!out || !input || !mask) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "dropout_fwd: null pointer");
+  int dev;
+  DeviceInfo* di;
+  BEACON_TRY(current_device(&dev, &di));
+  const int grid = grid_for(n, 256, di->sms);
+  if (dtype == BEACON_BF16)
+    k_dropout_fwd<bf16><<<grid, 256, 0, as_stream(stream)>>>((bf16*)out, (bf16*)mask, (const bf16*)input, n, p, seed);
+  else
+    k_dropout_fwd<float><<<grid, 256, 0, as_stream(stream)>>>((float*)out, (float*)mask, (const float*)input, n, p,
+                                                               seed);
+  return check_launch("k_dropout_fwd");
+}
+
+extern "C" int beacon_dropout_bwd(void* d_in, const void* d_out, const void* mask, int64_t n, int dtype,
+                                  void* stream) {
+  if (n < 0) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "dropout_bwd: negative n");
+  if (dtype != BEACON_BF16 && dtype != BEACON_F32) return fail(BEACON_ERR_UNIMPLEMENTED, "dropout_bwd: dtype %d", dtype);
+  if (n == 0) return BEACON_OK;
+  if (!d_in || !d_out || !mask) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "dropout_bwd: null pointer");
+  int dev;
+  DeviceInfo* di;
+  BEACON_TRY(current_device(&dev, &di));
+  const int grid = grid_for(n, 256, di->sms);
+  if (dtype == BEACON_BF16)
+    k_dropout_bwd<bf16><<<grid, 256, 0, as_stream(stream)>>>((bf16*)d_in, (const bf16*)d_out, (const bf16*)mask, n);
+  else
+    k_dropout_bwd<float><<<grid, 256, 0, as_stream(stream)>>>((float*)d_in, (const float*)d_out, (const float*)mask,
+                                                               n);
+  return check_launch("k_dropout_bwd");
+}
+
+// ===========================================================================
 // RMSNorm
 // ===========================================================================
 extern "C" int beacon_rmsnorm_adjoint_fwd(void* out, const void* x, const void* weight, float* rms,

@@ -143,6 +143,106 @@ __global__ void k_cast(void* __restrict__ dst, const void* __restrict__ src, lon
 }
 
 // ---------------------------------------------------------------------------
+// Embedding lookup (crates/beacon-cuda/src/elementwise.rs:67-95): out[t, :] = table[idx[t], :]
+// with u32 indices; the backward adds d_out[t, :] into d_table[idx[t], :] (d_table is
+// ReadWrite in the reference's own test, elementwise.rs:185).  An index at or beyond
+// `vocab` is not followed: its output row is written as zeros (forward) or skipped
+// (backward), and the fault word records kFaultIndex once per launch site.
+// ---------------------------------------------------------------------------
+constexpr unsigned int kFaultIndex = 3;
+
+__device__ __forceinline__ float elem_ld(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+__device__ __forceinline__ float elem_ld(const float* p) { return *p; }
+__device__ __forceinline__ void elem_st(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+__device__ __forceinline__ void elem_st(float* p, float v) { *p = v; }
+
+// One warp per token row; 16-byte vectors when `vec` (rows 16-byte aligned, dim * es % 16 == 0).
+template <typename T>
+__global__ void __launch_bounds__(256) k_embedding_fwd(T* __restrict__ out, const T* __restrict__ table,
+                                                       const uint32_t* __restrict__ idx, long long tokens, int dim,
+                                                       long long vocab, int vec, unsigned int site) {
+  const int lane = threadIdx.x & 31;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long t = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < tokens; t += warps) {
+    const uint32_t r = idx[t];
+    T* o = out + t * dim;
+    if ((long long)r >= vocab) {
+      if (lane == 0) record_fault(kFaultIndex, site);
+      for (int e = lane; e < dim; e += 32) o[e] = T(0.0f);
+      continue;
+    }
+    const T* src = table + (long long)r * dim;
+    if (vec) {
+      const int nv = dim * (int)sizeof(T) / 16;
+      for (int v = lane; v < nv; v += 32) reinterpret_cast<uint4*>(o)[v] = reinterpret_cast<const uint4*>(src)[v];
+    } else {
+      for (int e = lane; e < dim; e += 32) o[e] = src[e];
+    }
+  }
+}
+
+__device__ __forceinline__ void atomic_add_elem(float* p, float v) { atomicAdd(p, v); }
+__device__ __forceinline__ void atomic_add_elem(__nv_bfloat16* p, float v) { atomicAdd(p, __float2bfloat16_rn(v)); }
+
+// One warp per token row: d_table[idx[t], e] += d_out[t, e] (atomic adds: tokens sharing an
+// index add in any order).
+template <typename T>
+__global__ void __launch_bounds__(256) k_embedding_bwd(T* __restrict__ d_table, const T* __restrict__ d_out,
+                                                       const uint32_t* __restrict__ idx, long long tokens, int dim,
+                                                       long long vocab, unsigned int site) {
+  const int lane = threadIdx.x & 31;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long t = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < tokens; t += warps) {
+    const uint32_t r = idx[t];
+    if ((long long)r >= vocab) {
+      if (lane == 0) record_fault(kFaultIndex, site);
+      continue;
+    }
+    T* dst = d_table + (long long)r * dim;
+    const T* src = d_out + t * dim;
+    for (int e = lane; e < dim; e += 32) atomic_add_elem(dst + e, elem_ld(src + e));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Dropout (crates/beacon-cuda/src/elementwise.rs:97-118).  Element i is kept when
+// u_i >= p, u_i = (splitmix64(seed, i) >> 40) / 2^24 (the counter-based generator the
+// synthetic inputs use, so the mask depends on (seed, i) only, not on the launch shape).
+// mask[i] holds the multiplier, 1 / (1 - p) for a kept element and 0 for a dropped one,
+// rounded to the data type; out = input * mask and the backward, which the reference
+// calls without p (elementwise.rs:110-118), is d_in = d_out * mask.  p >= 1 drops all.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t splitmix64_at(uint64_t seed, uint64_t i) {
+  uint64_t z = seed + (i + 1) * 0x9E3779B97F4A7C15ULL;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+  return z ^ (z >> 31);
+}
+
+template <typename T>
+__global__ void k_dropout_fwd(T* __restrict__ out, T* __restrict__ mask, const T* __restrict__ in, long long n,
+                              float p, unsigned long long seed) {
+  const float keep_scale = p < 1.0f ? 1.0f / (1.0f - p) : 0.0f;
+  const T m_keep = T(keep_scale);
+  const float mk = elem_ld(&m_keep);
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const float u = (float)(splitmix64_at(seed, (uint64_t)i) >> 40) * (1.0f / 16777216.0f);
+    const bool keep = p < 1.0f && u >= p;
+    mask[i] = keep ? m_keep : T(0.0f);
+    elem_st(out + i, keep ? elem_ld(in + i) * mk : 0.0f);
+  }
+}
+
+template <typename T>
+__global__ void k_dropout_bwd(T* __restrict__ d_in, const T* __restrict__ d_out, const T* __restrict__ mask,
+                              long long n) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    elem_st(d_in + i, elem_ld(d_out + i) * elem_ld(mask + i));
+}
+
+// ---------------------------------------------------------------------------
 // fp32 master -> fp8 e4m3 weights with one scale per tensor
 //   amax = max |x| (NaN ignored), scale = amax / 448 (1 when amax is 0),
 //   q = F8E4M3::from_f32(x * (448 / amax)), so that x ~ decode(q) * scale.

@@ -18,6 +18,7 @@ trailing `scalars` tuple; the typed methods' own parameter lists are unchanged.
 from __future__ import annotations
 
 import ctypes
+import struct
 from abc import ABC, abstractmethod
 from dataclasses import dataclass, field
 from enum import Enum
@@ -282,17 +283,19 @@ class ElementwiseLaunch:
     def residual_add_backward(self, d_a, d_b, d_out, n, dtype=BF16):
         self.launch(kid.RESIDUAL_ADD_BWD, elementwise_grid(n), [d_a, d_b, d_out], (n, dtype))
 
-    def embedding_lookup(self, out, table, indices, tokens, dim):
-        self.launch(kid.EMBEDDING_FWD, elementwise_grid(tokens * dim), [out, table, indices], (tokens, dim))
+    def embedding_lookup(self, out, table, indices, tokens, dim, dtype=BF16):
+        self.launch(kid.EMBEDDING_FWD, elementwise_grid(tokens * dim), [out, table, indices], (tokens, dim, dtype))
 
-    def embedding_backward(self, d_table, d_out, indices, tokens, dim):
-        self.launch(kid.EMBEDDING_BWD, elementwise_grid(tokens * dim), [d_table, d_out, indices], (tokens, dim))
+    def embedding_backward(self, d_table, d_out, indices, tokens, dim, dtype=BF16):
+        self.launch(kid.EMBEDDING_BWD, elementwise_grid(tokens * dim), [d_table, d_out, indices],
+                    (tokens, dim, dtype))
 
-    def dropout_forward(self, out, inp, mask, n, p, seed):
-        self.launch(kid.DROPOUT_FWD, elementwise_grid(n), [out, inp, mask], (n,))
+    def dropout_forward(self, out, inp, mask, n, p, seed, dtype=BF16):
+        p_bits = struct.unpack("<I", struct.pack("<f", float(p)))[0]
+        self.launch(kid.DROPOUT_FWD, elementwise_grid(n), [out, inp, mask], (n, p_bits, seed, dtype))
 
-    def dropout_backward(self, d_in, d_out, mask, n):
-        self.launch(kid.DROPOUT_BWD, elementwise_grid(n), [d_in, d_out, mask], (n,))
+    def dropout_backward(self, d_in, d_out, mask, n, dtype=BF16):
+        self.launch(kid.DROPOUT_BWD, elementwise_grid(n), [d_in, d_out, mask], (n, dtype))
 
     def cast(self, dst, src, n, kind: CastKind):
         self.launch(kind.kernel(), elementwise_grid(n), [dst, src], (n,))

@@ -355,6 +355,43 @@ def residual_add_bwd(dout):
     return da, db
 
 
+def embedding_lookup(table, indices):
+    """out[t] = table[indices[t]] (elementwise.rs:67-80); indices int32/uint32 on the device."""
+    vocab, dim = table.shape
+    dt = _dtype(table)
+    if indices.dtype not in (torch.int32, torch.uint32) or not indices.is_cuda or not indices.is_contiguous():
+        raise InvalidLaunchConfig("embedding_lookup: indices must be a contiguous 32-bit CUDA tensor")
+    out = torch.empty(indices.numel(), dim, dtype=table.dtype, device=table.device)
+    check(_lib.lib().beacon_embedding_lookup_fwd(_p(out), _p(table), _p(indices), indices.numel(), dim, vocab, dt,
+                                                 _stream()))
+    return out
+
+
+def embedding_backward(d_table, d_out, indices):
+    """d_table[indices[t]] += d_out[t] in place (elementwise.rs:82-95)."""
+    vocab, dim = d_table.shape
+    dt = _dtype(d_table, d_out)
+    check(_lib.lib().beacon_embedding_lookup_bwd(_p(d_table), _p(d_out), _p(indices), indices.numel(), dim, vocab,
+                                                 dt, _stream()))
+    return d_table
+
+
+def dropout_fwd(x, p, seed):
+    """(out, mask) with mask = 1/(1-p) on kept elements, 0 on dropped (elementwise.rs:97-108)."""
+    dt = _dtype(x)
+    out, mask = torch.empty_like(x), torch.empty_like(x)
+    check(_lib.lib().beacon_dropout_fwd(_p(out), _p(x), _p(mask), x.numel(), float(p), int(seed), dt, _stream()))
+    return out, mask
+
+
+def dropout_bwd(d_out, mask):
+    """d_in = d_out * mask (elementwise.rs:110-118)."""
+    dt = _dtype(d_out, mask)
+    d_in = torch.empty_like(d_out)
+    check(_lib.lib().beacon_dropout_bwd(_p(d_in), _p(d_out), _p(mask), d_out.numel(), dt, _stream()))
+    return d_in
+
+
 CAST_F32_TO_FP8E4M3, CAST_FP8E4M3_TO_F32, CAST_F32_TO_BF16, CAST_BF16_TO_F32 = 0, 1, 2, 3
 
 

@@ -320,6 +320,27 @@ int beacon_residual_add_bwd(void* d_a, void* d_b, const void* d_out, int64_t n, 
 /* cast (elementwise.rs:120-128) with the reference's rounding rules (dtype.rs:58-66, 163-195). */
 int beacon_cast(void* dst, const void* src, int64_t n, int kind, void* stream);
 
+/* embedding_lookup (elementwise.rs:67-80): out[t, :] = table[indices[t], :], u32 indices.
+ * embedding_backward (elementwise.rs:82-95): d_table[indices[t], :] += d_out[t, :] (atomic
+ * adds; d_table is accumulated into, as its ReadWrite access in the reference's test says).
+ * `vocab` (table rows) bounds the indices: an index >= vocab is not followed -- the forward
+ * writes a zero row, the backward skips the token -- and the device fault word records code 3
+ * (read it with beacon_device_status).  f32 or bf16 (bf16 adds round at every add). */
+int beacon_embedding_lookup_fwd(void* out, const void* table, const uint32_t* indices, int64_t tokens, int64_t dim,
+                                int64_t vocab, int dtype, void* stream);
+int beacon_embedding_lookup_bwd(void* d_table, const void* d_out, const uint32_t* indices, int64_t tokens,
+                                int64_t dim, int64_t vocab, int dtype, void* stream);
+
+/* dropout_forward (elementwise.rs:97-108): element i is kept when u_i >= p, with
+ * u_i = (splitmix64(seed, i) >> 40) / 2^24 (SplitMix64: z = seed + (i + 1) * 0x9E3779B97F4A7C15,
+ * then the usual two xor-shift-multiply rounds), so the mask depends on (seed, i) only.
+ * mask[i] = 1 / (1 - p) rounded to dtype for a kept element, 0 for a dropped one;
+ * out = input * mask.  dropout_backward (elementwise.rs:110-118, no p): d_in = d_out * mask.
+ * p >= 1 drops everything.  f32 or bf16; mask has the data type. */
+int beacon_dropout_fwd(void* out, const void* input, void* mask, int64_t n, float p, uint64_t seed, int dtype,
+                       void* stream);
+int beacon_dropout_bwd(void* d_in, const void* d_out, const void* mask, int64_t n, int dtype, void* stream);
+
 /* ---- arena launcher: the KernelLauncher::launch boundary ------------------
  * crates/beacon-cuda/src/runtime.rs:31-47 (Launcher::launch) and
  * crates/beacon-cuda/src/launcher.rs:21-63 (KernelArg = byte offset into one arena).
@@ -331,7 +352,10 @@ int beacon_cast(void* dst, const void* src, int64_t n, int kind, void* stream);
  *   rmsnorm_ / layernorm_adjoint_fwd/_bwd     tokens, dim, dtype[, eps as float32 bits]
  *   swiglu_adjoint_fwd/_bwd                   tokens, d_model, d_ff, dtype
  *   residual_add_fwd/_bwd                     n, dtype
- *   cast_*                                    n                                            */
+ *   cast_*                                    n
+ *   embedding_lookup_fwd/_bwd                 tokens, dim[, dtype]  (vocab = table extent / row)
+ *   dropout_fwd                               n, p as float32 bits, seed[, dtype]
+ *   dropout_bwd                               n[, dtype]                                   */
 typedef struct beacon_arena beacon_arena;
 
 typedef struct beacon_kernel_arg {

@@ -319,6 +319,54 @@ def swiglu_bwd_sampled(dy, x, wg, wu, wd, rows, cols):
             ((g * s * u).T @ dy64).astype(np.float32))
 
 
+def embedding_lookup_fwd(table, indices):
+    """embedding_lookup (crates/beacon-cuda/src/elementwise.rs:67-80): out[t] = table[indices[t]];
+    an index at or beyond the table gives a zero row (the library's rule for that case)."""
+    idx = np.asarray(indices, dtype=np.int64)
+    out = np.zeros((idx.size, table.shape[1]), dtype=np.float32)
+    ok = idx < table.shape[0]
+    out[ok] = table[idx[ok]]
+    return out
+
+
+def embedding_lookup_bwd(d_table, d_out, indices):
+    """embedding_backward (elementwise.rs:82-95): d_table[indices[t]] += d_out[t] (float64 sums,
+    indices beyond the table skipped).  Returns the updated copy of d_table."""
+    idx = np.asarray(indices, dtype=np.int64)
+    acc = np.asarray(d_table, dtype=np.float64).copy()
+    ok = idx < acc.shape[0]
+    np.add.at(acc, idx[ok], np.asarray(d_out, dtype=np.float64)[ok])
+    return acc.astype(np.float32)
+
+
+def _splitmix64(seed: int, i: np.ndarray) -> np.ndarray:
+    """SplitMix64 at counters i (the same stream as bo_splitmix64), vectorised in uint64."""
+    with np.errstate(over="ignore"):
+        z = np.uint64(seed) + (i.astype(np.uint64) + np.uint64(1)) * np.uint64(0x9E3779B97F4A7C15)
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+        return z ^ (z >> np.uint64(31))
+
+
+def dropout_fwd(x, p, seed, bf16=False):
+    """dropout_forward (elementwise.rs:97-108) with the library's mask rule: element i is kept
+    when (splitmix64(seed, i) >> 40) / 2^24 >= p; mask = 1 / (1 - p) (float32, rounded to bf16
+    for bf16 data) where kept, 0 where dropped; out = x * mask in float32 (rounded to bf16 for
+    bf16 data).  Returns (out, mask)."""
+    x = np.asarray(x, dtype=np.float32).ravel()
+    u = (_splitmix64(seed, np.arange(x.size)) >> np.uint64(40)).astype(np.float32) * np.float32(1.0 / 16777216.0)
+    p32 = np.float32(p)
+    keep = (u >= p32) & (p32 < np.float32(1.0))
+    scale = np.float32(1.0) / (np.float32(1.0) - p32) if p32 < 1 else np.float32(0.0)
+    if bf16:
+        scale = round_bf16(np.array([scale], dtype=np.float32))[0]
+    mask = np.where(keep, scale, np.float32(0.0)).astype(np.float32)
+    out = np.where(keep, x * scale, np.float32(0.0)).astype(np.float32)
+    if bf16:
+        out = round_bf16(out)
+    return out, mask
+
+
 def residual_add_fwd(a, b):
     out = _empty(*a.shape)
     lib().bo_residual_add_fwd(_p(out), _p(a), _p(b), a.size)

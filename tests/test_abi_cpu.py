@@ -66,8 +66,12 @@ def _launch(kernel, args, scalars):
 
 def test_arena_dispatch_host_checks():
     # IDs outside the hot path answer Unimplemented with their name, like runtime.rs:41
-    assert _launch(b"dropout_fwd", [(0, 16)] * 3, [4]) == _lib.ERR_UNIMPLEMENTED
+    # dropout_fwd needs p and the seed among its scalars
+    assert _launch(b"dropout_fwd", [(0, 16)] * 3, [4]) == _lib.ERR_INVALID_LAUNCH_CONFIG
     assert "dropout_fwd" in _lib.last_error()
+    # embedding: the indices (u32) must cover the tokens
+    assert _launch_access(b"embedding_lookup_fwd", [(0, 64, 1), (64, 64, 0), (128, 8, 0)], [4, 8, _lib.BF16]) == \
+        _lib.ERR_SHAPE_MISMATCH
     assert _launch(b"no_such_kernel", [(0, 16)], []) == _lib.ERR_FUNCTION_NOT_FOUND
     # an argument reaching past the arena
     assert _launch(b"matmul_fwd", [(4000, 512), (0, 128), (0, 128)], [8, 4, 8, _lib.BF16]) == \
