@@ -24,6 +24,13 @@
 //               maximum, so O / l is exact either way).
 //
 // TMEM: S_A [0,128), S_B [128,256), O_A [256,256+D), O_B [256+D,256+2D).
+//
+// RECOMP = true is the forward the drop-in backward runs, given the saved LSE: P =
+// exp2(S * scale*log2e - lse*log2e) is final as it is computed (no running maximum, no
+// rescale, no row sum), O accumulates already normalised, and the epilogue writes the
+// backward's row statistics instead of O: Dt = rowsum(dO * O) (O in fp32 from TMEM, dO
+// read from global memory) and lse2 = -lse*log2e, both padded to whole 128-row tiles
+// (0 / -inf on rows at or beyond S).
 #pragma once
 
 #include "sm100.cuh"
@@ -39,6 +46,12 @@ struct AttnParams {
   int n_qtiles;
   int n_pairs;         // ceil(n_qtiles / 2)
   int out_tokens;      // 1: out is token-major [B, S, Hq, D] (the input of an output projection)
+  // RECOMP only
+  const float* lse_in;            // [B, Hq, S] saved LSE (natural log)
+  const __nv_bfloat16* dout;      // [B, Hq, S, D]
+  float* dt;                      // [B*Hq, S_pad] rowsum(dO * O)
+  float* lse2;                    // [B*Hq, S_pad] -lse * log2(e)
+  int S_pad;
 };
 
 template <int D>
@@ -119,7 +132,10 @@ __device__ __forceinline__ void exp2_poly2(float& r0, float& r1, float a0, float
 // Pairs of S columns whose exponentials run on the FMA pipe on unmasked tiles, one bit per
 // pair index mod 8: the exponential unit (16 results per clock per SM) and the FMA pipe
 // then finish the row in about the same time.
-constexpr uint32_t kPolyPairs = 0x11u;
+#ifndef BEACON_FWD_POLY_PAIRS
+#define BEACON_FWD_POLY_PAIRS 0x11u
+#endif
+constexpr uint32_t kPolyPairs = BEACON_FWD_POLY_PAIRS;
 
 // P = 2^(x * scale_log2 - m) for one 128-wide S row, packed to bf16 pairs into the
 // 64 TMEM columns at `taddr`; returns the row sum of P (fp32, before rounding).  The
@@ -156,7 +172,7 @@ __device__ __forceinline__ float softmax_p_to_tmem(const float* x, float scale_l
   return (ls[0] + ls[1]) + (ls[2] + ls[3]);
 }
 
-template <int D>
+template <int D, bool RECOMP = false>
 __global__ void __launch_bounds__(384, 1)
     k_attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
@@ -354,6 +370,9 @@ __global__ void __launch_bounds__(384, 1)
     const uint32_t lane_base = (quarter * 32u) << 16;
     const uint32_t s_col = (Cfg::S_COL_STRIDE * t), o_col = Cfg::O_COL0 + t * D;
     float m_used = -INFINITY, l = 0.0f;
+    // RECOMP: the exponent offset of the row, from the saved LSE (rows at or beyond S: -inf)
+    const float nl2 = RECOMP ? (qi < p.S ? p.lse_in[(long long)bh * p.S + qi] * -1.4426950408889634f : -INFINITY)
+                             : 0.0f;
     bool ok = true;
     for (int j = 0; j < nkv[t]; ++j) {
       // warp-uniform outcome: the tcgen05.ld / st that follow are warp-collective
@@ -374,6 +393,13 @@ __global__ void __launch_bounds__(384, 1)
       if (!unmasked) {
 #pragma unroll
         for (int c = 0; c < 128; ++c) x[c] = (c < limit) ? x[c] : -INFINITY;
+      }
+      if constexpr (RECOMP) {
+        if (unmasked)
+          softmax_p_to_tmem<true>(x, p.scale_log2, nl2, tmem + lane_base + s_col, &p_full[2 * t]);
+        else
+          softmax_p_to_tmem<false>(x, p.scale_log2, nl2, tmem + lane_base + s_col, &p_full[2 * t]);
+        continue;
       }
       float mx;
       {  // tree reduction: 8 independent chains of three-input maxima
@@ -416,8 +442,42 @@ __global__ void __launch_bounds__(384, 1)
       else
         l += softmax_p_to_tmem<false>(x, p.scale_log2, -m_used, tmem + lane_base + s_col, &p_full[2 * t]);
     }
-    // epilogue: O / l -> bf16, LSE
-    if (ok && nkv[t] > 0 && __all_sync(0xffffffffu, mbar_wait(&o_full[t], 0, abort_flag, kSiteAttnOFull))) {
+    if constexpr (RECOMP) {
+      // epilogue: Dt = rowsum(dO * O) and lse2 for the backward
+      if (ok && nkv[t] > 0 && __all_sync(0xffffffffu, mbar_wait(&o_full[t], 0, abort_flag, kSiteAttnOFull))) {
+        tc_fence_after();
+        const bool row_ok = qi < p.S;
+        const uint4* drow = reinterpret_cast<const uint4*>(p.dout + ((long long)bh * p.S + (row_ok ? qi : 0)) * D);
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint4 dv4[4] = {};
+          if (row_ok) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dv4[i] = __ldg(drow + c * 4 + i);
+          }
+          uint32_t u[32];
+          tmem_ld32(tmem + lane_base + o_col + c * 32, u);  // warp-collective: every lane
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&dv4[i]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 d2 = __bfloat1622float2(h2[e]);
+              acc[i] = fmaf(__uint_as_float(u[8 * i + 2 * e]), d2.x, acc[i]);
+              acc[i] = fmaf(__uint_as_float(u[8 * i + 2 * e + 1]), d2.y, acc[i]);
+            }
+          }
+        }
+        if (qi < p.S_pad) {  // rows of a query tile past the last one do not exist in Dt / lse2
+          const long long r = (long long)bh * p.S_pad + qi;
+          p.dt[r] = row_ok ? (acc[0] + acc[1]) + (acc[2] + acc[3]) : 0.0f;
+          p.lse2[r] = row_ok ? nl2 : -INFINITY;
+        }
+      }
+    } else if (ok && nkv[t] > 0 && __all_sync(0xffffffffu, mbar_wait(&o_full[t], 0, abort_flag, kSiteAttnOFull))) {
+      // epilogue: O / l -> bf16, LSE
       tc_fence_after();
       const float inv = 1.0f / l;
       const bool out32 = (reinterpret_cast<uintptr_t>(p.out) & 31u) == 0;

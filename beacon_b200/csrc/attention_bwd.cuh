@@ -3,11 +3,12 @@
 // Kernel ID `attention_adjoint_bwd` (crates/beacon-cuda/src/attention.rs:42-64); the
 // adjoint entry (crates/beacon-adjoint-table/src/lib.rs:86-99) saves q, k, v, lse and
 // recomputes the scores.  Three launches:
-//   1. k_attn_bwd_prep  per query row: Dt = rowsum(dO * O), nlse2 = -lse * log2(e),
-//                       padded to whole 128-row tiles (-inf / 0), so no tile needs a row
-//                       check; P = exp2(S * scale*log2e + nlse2) is one packed FMA and MUFU.
-//                       (O is the forward output, recomputed by the forward kernel when
-//                       the caller lacks it.)
+//   1. the row statistics Dt = rowsum(dO * O) and nlse2 = -lse * log2(e), padded to whole
+//                       128-row tiles (-inf / 0), so no tile needs a row check; P =
+//                       exp2(S * scale*log2e + nlse2) is one packed FMA and MUFU.  The
+//                       drop-in entry, which has no O, runs the forward kernel's recompute
+//                       form (k_attn_fwd_tc<D, true>: O stays in TMEM, its epilogue writes
+//                       Dt and nlse2); given O, k_attn_bwd_prep reads it.
 //   2. k_attn_bwd_dkdv  one CTA per (128-key tile, KV head): dK and dV accumulate in TMEM
 //                       over the query tiles (and grouped query heads) that see the keys.
 //   3. k_attn_bwd_dq    persistent, one CTA per SM over (128-query tile, query head)
@@ -410,9 +411,11 @@ __global__ void __launch_bounds__(384, 1)
           if (leader) umma_commit(s_full);
         }
         issue_kv(T_DV, rs, do_addr, false, 4, 8);
-        if (leader) umma_commit(&do_empty[st]);  // dO(n) read by dP^T(n) and dV(n)
         if (!warp_wait(ds_ready, par, abort_flag, kSiteBwdDsFull)) break;
         tc_fence_after();
+        // dO(n) read by dP^T(n) and dV(n), and Dt(n), which shares its stage, by the warps'
+        // dS phase: the stage may take dO(n+2)
+        if (leader) umma_commit(&do_empty[st]);
         issue_kv(T_DK, rs + 32, q_addr, n == 0);
         if (leader) umma_commit(&q_empty[qs]);  // Q(n) read by S^T(n) and dK(n)
         if (more) {  // into R_S(n), behind dV(n) and dK(n), which read P^T / dS^T(n) from it

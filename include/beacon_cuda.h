@@ -162,8 +162,9 @@ int beacon_attention_adjoint_fwd(void* out, const void* q, const void* k, const 
 
 /* attention_bwd (attention.rs:42-64), kernel `attention_adjoint_bwd`; adjoint entry
  * crates/beacon-adjoint-table/src/lib.rs:86-99 (saved q, k, v, lse; scores recomputed).
- * The forward output is not an argument, so the kernel recomputes it to form
- * rowsum(dO * O).  Scratch: `workspace` of at least
+ * The forward output is not an argument: the forward kernel runs again, given the saved
+ * lse, and forms rowsum(dO * O) from O in tensor memory (O is not written).  Scratch
+ * (two fp32 values per query row): `workspace` of at least
  * beacon_attention_bwd_workspace_size(...) bytes, or NULL to use the library's
  * per-device workspace (grown with cudaMalloc on first use; the growth synchronises
  * the device). */

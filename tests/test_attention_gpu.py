@@ -94,6 +94,22 @@ def test_backward_bf16(B, H, Hkv, S, D):
     assert rel_err(to_np(dv), rv) <= BF16_TOL
 
 
+@pytest.mark.parametrize("B,H,Hkv,S,causal", [(1, 2, 2, 640, True), (2, 4, 1, 130, True), (1, 2, 2, 384, False),
+                                               (1, 2, 2, 136, False)])
+def test_backward_tile_edges_bf16(B, H, Hkv, S, causal):
+    """An odd number of key tiles, S a tile plus a few rows, a single KV head for four query
+    heads, non-causal attention with a ragged last tile."""
+    import torch
+    ops = _ops()
+    q, k, v, do = _qkv(B, H, Hkv, S, 128, 11)
+    t = lambda a: to_dev(a, torch.bfloat16)
+    _, rl = O.attention_fwd(q, k, v, causal=causal)
+    g = ops.attention_bwd(t(do), t(q), t(k), t(v), to_dev(rl, torch.float32), causal=causal)
+    refs = O.attention_bwd(do, q, k, v, rl, causal=causal)
+    for a, r in zip(g, refs):
+        assert rel_err(to_np(a), r) <= BF16_TOL
+
+
 def test_backward_f32():
     import torch
     ops = _ops()
@@ -114,7 +130,9 @@ def test_no_device_fault_recorded():
 
 
 def test_backward_with_out_matches_drop_in():
-    """beacon_attention_bwd_with_out (O given) and the drop-in backward (O recomputed) agree."""
+    """beacon_attention_bwd_with_out (O given) and the drop-in backward (O recomputed in
+    tensor memory) agree.  They differ only in rowsum(dO * O): from the bf16 output in one,
+    from the fp32 accumulator in the other."""
     import torch
     ops = _ops()
     q, k, v, do = _qkv(1, 4, 4, 384, 128, 6)
@@ -122,12 +140,13 @@ def test_backward_with_out_matches_drop_in():
     out, lse = ops.attention_fwd(t(q), t(k), t(v))
     g1 = ops.attention_bwd(t(do), t(q), t(k), t(v), lse)
     g2 = ops.attention_bwd(t(do), t(q), t(k), t(v), lse, out=out)
-    for a, b in zip(g1, g2):
-        assert torch.equal(a, b)
+    for a, b in zip(g1, g2):  # about one bf16 rounding step apart
+        assert rel_err(to_np(a), to_np(b)) <= 1e-2
     _, rl = O.attention_fwd(q, k, v)
     refs = O.attention_bwd(do, q, k, v, rl)
-    for a, r in zip(g2, refs):
-        assert rel_err(to_np(a), r) <= BF16_TOL
+    for g in (g1, g2):
+        for a, r in zip(g, refs):
+            assert rel_err(to_np(a), r) <= BF16_TOL
 
 
 @pytest.mark.parametrize("causal", [True, False])
