@@ -131,11 +131,9 @@ __device__ __forceinline__ void exp2_poly2(float& r0, float& r1, float a0, float
 
 // Pairs of S columns whose exponentials run on the FMA pipe on unmasked tiles, one bit per
 // pair index mod 8: the exponential unit (16 results per clock per SM) and the FMA pipe
-// then finish the row in about the same time.
-#ifndef BEACON_FWD_POLY_PAIRS
-#define BEACON_FWD_POLY_PAIRS 0x11u
-#endif
-constexpr uint32_t kPolyPairs = BEACON_FWD_POLY_PAIRS;
+// then finish the row in about the same time.  (A quarter measured fastest: three or four
+// eighths on the FMA pipe were 3-4% slower.)
+constexpr uint32_t kPolyPairs = 0x11u;
 
 // P = 2^(x * scale_log2 - m) for one 128-wide S row, packed to bf16 pairs into the
 // 64 TMEM columns at `taddr`; returns the row sum of P (fp32, before rounding).  The
@@ -291,16 +289,19 @@ __global__ void __launch_bounds__(384, 1)
         const bool leader = elect_one();
         constexpr uint32_t idesc_s = make_idesc_f16(128, 128, false, false);
         constexpr uint32_t idesc_o = make_idesc_f16(128, D, false, true);
-        const uint32_t q_addr = smem_u32(sQ);
+        // descriptors built once; tiles, stages and K-steps are constant offsets from them
+        const uint64_t q_desc = make_sdesc_sw128(smem_u32(sQ), 16, 1024);
+        const uint64_t k_desc = make_sdesc_sw128(smem_u32(sK), 16, 1024);
+        const uint64_t v_desc = make_sdesc_sw128(smem_u32(sV), 128 * 128, 1024);
         bool ok = warp_wait(q_full, 0, abort_flag, kSiteAttnQ);
         // S_t(j) = Q_t K_j^T into tile t's S columns
         auto issue_s = [&](int t, int j) {
-          const uint32_t k_addr = smem_u32(sK + (j & 1) * Cfg::KV_BYTES);
+          const uint64_t qd = sdesc_adv(q_desc, t * Cfg::Q_BYTES), kd = sdesc_adv(k_desc, (j & 1) * Cfg::KV_BYTES);
   #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-            if (leader) umma_f16_ss(tmem + (Cfg::S_COL_STRIDE * t), make_sdesc_sw128(q_addr + t * Cfg::Q_BYTES + off, 16, 1024),
-                        make_sdesc_sw128(k_addr + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+            if (leader) umma_f16_ss(tmem + (Cfg::S_COL_STRIDE * t), sdesc_adv(qd, off), sdesc_adv(kd, off), idesc_s,
+                                    kk > 0 ? 1u : 0u);
           }
           if (leader) umma_commit(&s_full[t]);
         };
@@ -323,7 +324,7 @@ __global__ void __launch_bounds__(384, 1)
           const uint32_t ph = (j >> 1) & 1;
           bool k_next = false;  // K_{j+1} has landed
           if (!warp_wait(&v_full[st], ph, abort_flag, kSiteAttnVFull)) { ok = false; break; }
-          const uint32_t v_addr = smem_u32(sV + st * Cfg::KV_BYTES);
+          const uint64_t vd = sdesc_adv(v_desc, st * Cfg::KV_BYTES);
           for (int t = 0; t < 2 && ok; ++t) {
             if (j >= nkv[t]) continue;
             // O_t += P_t V_j, P_t from TMEM (K = 128 keys), each 64-key half as soon as it is stored
@@ -334,7 +335,7 @@ __global__ void __launch_bounds__(384, 1)
               for (int k4 = 0; k4 < 4; ++k4) {
                 const int kk = 4 * hf + k4;
                 if (leader) umma_f16_ts(tmem + Cfg::O_COL0 + t * D, tmem + (Cfg::S_COL_STRIDE * t) + kk * 8,
-                            make_sdesc_sw128(v_addr + kk * 2048, 128 * 128, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+                                        sdesc_adv(vd, kk * 2048), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
               }
             }
             if (!ok) break;
