@@ -1,16 +1,23 @@
 // attention.cuh -- causal scaled-dot-product attention forward on tcgen05 tensor cores.
 //
 // Kernel ID `attention_adjoint_fwd` (crates/beacon-cuda/src/attention.rs:21-40).
-// One CTA per (pair of 128-row query tiles, batch*head).  The two tiles (A, B)
-// share every K/V tile and ping-pong on the tensor core: while one softmax
-// warpgroup turns S_A into P_A, the tensor core computes S_B, and so on:
+// Persistent: one CTA per SM walks work items (pair of 128-row query tiles, batch*head),
+// its first item its block index and the next ones from the launch's work counter, so
+// the SMs finish together although causal items differ in cost by up to the number of
+// key tiles.  The rings, TMEM regions and barrier phases run on across items: the next
+// item's Q loads as soon as the current item's last S has read Q, and its first S MMAs
+// follow the last PV MMAs at once, running while the softmax warps write the item's
+// output (one CTA per item spent ~5k cycles before its first S and ~6k after its last).
+// The two tiles (A, B) of an item share every K/V tile and ping-pong on the tensor core:
+// while one softmax warpgroup turns S_A into P_A, the tensor core computes S_B, and so on:
 //
 //   MMA issue order:   S_A(0) S_B(0) | O_A += P_A(j) V_j, S_A(j+1), O_B += P_B(j) V_j, S_B(j+1) | ...
 //
 // with each PV product issued in two 64-key halves, each as soon as the softmax warps have
 // stored that half of P, so the tensor core starts on P while the warps finish it.
 //
-//   warp 0      TMA producer: Q_A, Q_B once, then K_j and V_j into 2-deep rings.
+//   warp 0      TMA producer: fetches and publishes the work items (a four-slot ring in
+//               shared memory); per item Q_A, Q_B, then K_j and V_j into 2-deep rings.
 //   warp 1      TMEM allocator + tcgen05.mma issuer (the whole warp runs the issue loop,
 //               one elected lane issues).
 //   warps 2-3   idle; warps 0-3 hand most of their registers to the softmax warpgroups
@@ -46,6 +53,7 @@ struct AttnParams {
   int n_qtiles;
   int n_pairs;         // ceil(n_qtiles / 2)
   int out_tokens;      // 1: out is token-major [B, S, Hq, D] (the input of an output projection)
+  int sched_slot;      // the launch's work counter (g_sched)
   // RECOMP only
   const float* lse_in;            // [B, Hq, S] saved LSE (natural log)
   const __nv_bfloat16* dout;      // [B, Hq, S, D]
@@ -59,7 +67,7 @@ struct AttnFwdCfg {
   static constexpr int BM = 128, BN = 128;
   static constexpr uint32_t Q_BYTES = BM * D * 2;
   static constexpr uint32_t KV_BYTES = BN * D * 2;
-  static constexpr size_t SMEM_BYTES = 1024 + 2 * (size_t)Q_BYTES + 4 * (size_t)KV_BYTES + 256;
+  static constexpr size_t SMEM_BYTES = 1024 + 2 * (size_t)Q_BYTES + 4 * (size_t)KV_BYTES + 512;
   static constexpr int THREADS = 384;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t S_COL_STRIDE = 128;  // S_A at column 0, S_B at column 128
@@ -77,6 +85,7 @@ enum : unsigned int {
   kSiteAttnPFull = 0x208,
   kSiteAttnOFull = 0x20a,
   kSiteAttnDrain = 0x20b,
+  kSiteAttnItem = 0x20c,
 };
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -170,6 +179,35 @@ __device__ __forceinline__ float softmax_p_to_tmem(const float* x, float scale_l
   return (ls[0] + ls[1]) + (ls[2] + ls[3]);
 }
 
+// Work items of the persistent forward: (pair of query tiles, batch*head) in the grouped
+// head order, the heaviest causal pairs of a group first.  Published by the producer in a
+// four-slot ring in shared memory.
+constexpr int kFwdItemRing = 4;
+struct FwdItem {
+  bool valid;
+  int bh, kvz, n_j;
+  int q0[2], nkv[2];  // per tile: first query row, key tiles it attends to (0: tile beyond S)
+};
+__device__ __forceinline__ FwdItem fwd_item(const AttnParams& p, int w, int n_bh, int n_ktiles) {
+  FwdItem x;
+  x.valid = w < p.n_pairs * n_bh;
+  int pair = 0, bh = 0;
+  if (x.valid) {
+    grouped_order(w, n_bh, p.n_pairs, pair, bh);
+    pair = p.n_pairs - 1 - pair;
+  }
+  x.bh = bh;
+  x.kvz = (bh / p.Hq) * p.Hkv + (bh % p.Hq) / (p.Hq / p.Hkv);
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int qt = 2 * pair + t;
+    x.q0[t] = qt * 128;
+    x.nkv[t] = (!x.valid || x.q0[t] >= p.S) ? 0 : (p.causal ? min(qt + 1, n_ktiles) : n_ktiles);
+  }
+  x.n_j = max(x.nkv[0], x.nkv[1]);
+  return x;
+}
+
 template <int D, bool RECOMP = false>
 __global__ void __launch_bounds__(384, 1)
     k_attn_fwd_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -190,29 +228,21 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* p_full = bars + 11;   // [2][2] per tile and 64-key half: P stored by its 4 warps
   uint64_t* o_full = bars + 15;   // [2] per tile
   uint64_t* drain = bars + 17;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  uint64_t* q_empty = bars + 18;                    // Q_A, Q_B read by the item's last S
+  uint64_t* item_full = bars + 19;                  // [4] item published by the producer
+  uint64_t* item_empty = item_full + kFwdItemRing;  // [4] read by the MMA warp and the 8 softmax warps
+  int* s_item = reinterpret_cast<int*>(item_empty + kFwdItemRing);  // [4] item indices
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_item + kFwdItemRing);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const uint32_t warp = warp_id(), lane = lane_id();
   const int n_bh = p.B * p.Hq;
-  int pair, bh;  // grouped head order, the heaviest causal pairs of a group first
-  grouped_order((int)blockIdx.x, n_bh, p.n_pairs, pair, bh);
-  pair = p.n_pairs - 1 - pair;
-  const int b = bh / p.Hq, h = bh % p.Hq;
-  const int kvz = b * p.Hkv + h / (p.Hq / p.Hkv);
+  const int n_items = p.n_pairs * n_bh;
   const int n_ktiles = (p.S + Cfg::BN - 1) / Cfg::BN;
-  // per tile: first query row, number of key tiles it attends to (0: tile beyond S)
-  int q0[2], nkv[2];
-#pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    const int qt = 2 * pair + t;
-    q0[t] = qt * Cfg::BM;
-    nkv[t] = (q0[t] >= p.S) ? 0 : (p.causal ? min(qt + 1, n_ktiles) : n_ktiles);
-  }
-  const int n_j = max(nkv[0], nkv[1]);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
@@ -224,22 +254,12 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(&o_full[i], 1);
     }
     mbar_init(drain, 1);
+    for (int i = 0; i < kFwdItemRing; ++i) {
+      mbar_init(&item_full[i], 1);
+      mbar_init(&item_empty[i], 9);
+    }
     *abort_flag = 0;
     fence_mbarrier_init();
-    // the producer's first copies (Q_A, Q_B, K_0, V_0) go out before the TMEM allocation
-    // and the CTA barrier, so they overlap the set-up
-    tma_prefetch_desc(&tmQ);
-    tma_prefetch_desc(&tmK);
-    tma_prefetch_desc(&tmV);
-    mbar_arrive_expect_tx(q_full, 2 * Cfg::Q_BYTES);
-    tma_load_rows<D>(sQ, &tmQ, q_full, q0[0], bh);
-    tma_load_rows<D>(sQ + Cfg::Q_BYTES, &tmQ, q_full, q0[1], bh);  // rows >= S read as zeros
-    if (n_j > 0) {
-      mbar_arrive_expect_tx(&k_full[0], Cfg::KV_BYTES);
-      tma_load_rows<D>(sK, &tmK, &k_full[0], 0, kvz);
-      mbar_arrive_expect_tx(&v_full[0], Cfg::KV_BYTES);
-      tma_load_rows<D>(sV, &tmV, &v_full[0], 0, kvz);
-    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
@@ -249,6 +269,16 @@ __global__ void __launch_bounds__(384, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+
+  // The ci-th item of this CTA from the ring (every role but the producer): false at the
+  // end of the CTA's work or when a wait gave up.
+  auto read_item = [&](int ci, FwdItem& x) -> bool {
+    const int slot = ci % kFwdItemRing;
+    if (!mbar_wait(&item_full[slot], (uint32_t)(ci / kFwdItemRing) & 1u, abort_flag, kSiteAttnItem)) return false;
+    x = fwd_item(p, s_item[slot], n_bh, n_ktiles);
+    return x.valid;
+  };
+
   // Registers: the producer / MMA warpgroup gives up most of its share to the two
   // softmax warpgroups, which hold a whole 128-column S row per thread.
   // 128 x 72 + 256 x 216 = 384 x 168, the allocation the CTA is launched with.
@@ -257,26 +287,49 @@ __global__ void __launch_bounds__(384, 1)
     if (warp == 0) {
       // ---------------------------------------------------------------- producer
       if (lane == 0) {
-        // Q and K_0 / V_0 were issued at set-up
-        uint32_t kissued = n_j > 0 ? 1u : 0u, vissued = kissued, kpar = 0, vpar = 0;
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
+        // K/V tiles are counted over all of the CTA's items (tk): the rings run on across items
+        uint32_t tk = 0, kissued = 0, vissued = 0, kpar = 0, vpar = 0, qissued = 0, qpar = 0;
         bool ok = true;
-        for (int j = 1; j < n_j && ok; ++j) {
-          const int st = j & 1;
-          const uint32_t ph = (j >> 1) & 1;
-          if (!mbar_wait(&k_empty[st], ph ^ 1u, abort_flag, kSiteAttnKEmpty)) { ok = false; break; }
-          mbar_arrive_expect_tx(&k_full[st], Cfg::KV_BYTES);
-          tma_load_rows<D>(sK + st * Cfg::KV_BYTES, &tmK, &k_full[st], j * Cfg::BN, kvz);
-          kissued |= 1u << st;
-          kpar = (kpar & ~(1u << st)) | (ph << st);
-          if (!mbar_wait(&v_empty[st], ph ^ 1u, abort_flag, kSiteAttnVEmpty)) { ok = false; break; }
-          mbar_arrive_expect_tx(&v_full[st], Cfg::KV_BYTES);
-          tma_load_rows<D>(sV + st * Cfg::KV_BYTES, &tmV, &v_full[st], j * Cfg::BN, kvz);
-          vissued |= 1u << st;
-          vpar = (vpar & ~(1u << st)) | (ph << st);
+        for (int ci = 0; ok; ++ci) {
+          // fetch the CTA's next item and publish it (an index >= n_items ends every role)
+          const int w = ci == 0 ? (int)blockIdx.x : sched_fetch(p.sched_slot);
+          const int slot = ci % kFwdItemRing;
+          if (!mbar_wait(&item_empty[slot], ((uint32_t)(ci / kFwdItemRing) & 1u) ^ 1u, abort_flag, kSiteAttnItem)) {
+            ok = false;
+            break;
+          }
+          s_item[slot] = w < n_items ? w : n_items;
+          mbar_arrive(&item_full[slot]);
+          const FwdItem x = fwd_item(p, w, n_bh, n_ktiles);
+          if (!x.valid) break;
+          // Q_A, Q_B once the previous item's last S has read them
+          if (!mbar_wait(q_empty, ((uint32_t)ci & 1u) ^ 1u, abort_flag, kSiteAttnQ)) { ok = false; break; }
+          mbar_arrive_expect_tx(q_full, 2 * Cfg::Q_BYTES);
+          tma_load_rows<D>(sQ, &tmQ, q_full, x.q0[0], x.bh);
+          tma_load_rows<D>(sQ + Cfg::Q_BYTES, &tmQ, q_full, x.q0[1], x.bh);  // rows >= S read as zeros
+          qissued = 1;
+          qpar = (uint32_t)ci & 1u;
+          for (int j = 0; j < x.n_j; ++j, ++tk) {
+            const int st = (int)(tk & 1u);
+            const uint32_t ph = (tk >> 1) & 1u;
+            if (!mbar_wait(&k_empty[st], ph ^ 1u, abort_flag, kSiteAttnKEmpty)) { ok = false; break; }
+            mbar_arrive_expect_tx(&k_full[st], Cfg::KV_BYTES);
+            tma_load_rows<D>(sK + st * Cfg::KV_BYTES, &tmK, &k_full[st], j * Cfg::BN, x.kvz);
+            kissued |= 1u << st;
+            kpar = (kpar & ~(1u << st)) | (ph << st);
+            if (!mbar_wait(&v_empty[st], ph ^ 1u, abort_flag, kSiteAttnVEmpty)) { ok = false; break; }
+            mbar_arrive_expect_tx(&v_full[st], Cfg::KV_BYTES);
+            tma_load_rows<D>(sV + st * Cfg::KV_BYTES, &tmV, &v_full[st], j * Cfg::BN, x.kvz);
+            vissued |= 1u << st;
+            vpar = (vpar & ~(1u << st)) | (ph << st);
+          }
         }
         if (!ok) {
           volatile int no_abort = 0;
-          mbar_wait(q_full, 0, &no_abort, kSiteAttnDrain);
+          if (qissued) mbar_wait(q_full, qpar, &no_abort, kSiteAttnDrain);
           for (int s = 0; s < 2; ++s) {
             if (kissued & (1u << s)) mbar_wait(&k_full[s], (kpar >> s) & 1u, &no_abort, kSiteAttnDrain);
             if (vissued & (1u << s)) mbar_wait(&v_full[s], (vpar >> s) & 1u, &no_abort, kSiteAttnDrain);
@@ -293,10 +346,9 @@ __global__ void __launch_bounds__(384, 1)
         const uint64_t q_desc = make_sdesc_sw128(smem_u32(sQ), 16, 1024);
         const uint64_t k_desc = make_sdesc_sw128(smem_u32(sK), 16, 1024);
         const uint64_t v_desc = make_sdesc_sw128(smem_u32(sV), 128 * 128, 1024);
-        bool ok = warp_wait(q_full, 0, abort_flag, kSiteAttnQ);
-        // S_t(j) = Q_t K_j^T into tile t's S columns
-        auto issue_s = [&](int t, int j) {
-          const uint64_t qd = sdesc_adv(q_desc, t * Cfg::Q_BYTES), kd = sdesc_adv(k_desc, (j & 1) * Cfg::KV_BYTES);
+        // S_t(j) = Q_t K^T (K tile of ring count `tk`) into tile t's S columns
+        auto issue_s = [&](int t, uint32_t tk) {
+          const uint64_t qd = sdesc_adv(q_desc, t * Cfg::Q_BYTES), kd = sdesc_adv(k_desc, (tk & 1u) * Cfg::KV_BYTES);
   #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
@@ -305,56 +357,71 @@ __global__ void __launch_bounds__(384, 1)
           }
           if (leader) umma_commit(&s_full[t]);
         };
-        // Issue order: S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) | ...  tcgen05.mma
+        // Issue order per item: S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) | ...  tcgen05.mma
         // executes in issue order, so S_t(j+1) may follow PV_t(j), which reads P_t(j) from
         // the same TMEM columns, without waiting for it; each softmax warpgroup then has the
-        // other tile's PV and S (1024 tensor-core cycles) to hide behind.
-        if (ok && n_j > 0) {
-          if (!warp_wait(&k_full[0], 0, abort_flag, kSiteAttnKFull)) {
-            ok = false;
-          } else {
-            tc_fence_after();
-            for (int t = 0; t < 2; ++t)
-              if (nkv[t] > 0) issue_s(t, 0);
-            if (leader) umma_commit(&k_empty[0]);
-          }
-        }
-        for (int j = 0; j < n_j && ok; ++j) {
-          const int st = j & 1;
-          const uint32_t ph = (j >> 1) & 1;
-          bool k_next = false;  // K_{j+1} has landed
-          if (!warp_wait(&v_full[st], ph, abort_flag, kSiteAttnVFull)) { ok = false; break; }
-          const uint64_t vd = sdesc_adv(v_desc, st * Cfg::KV_BYTES);
-          for (int t = 0; t < 2 && ok; ++t) {
-            if (j >= nkv[t]) continue;
-            // O_t += P_t V_j, P_t from TMEM (K = 128 keys), each 64-key half as soon as it is stored
-            for (int hf = 0; hf < 2 && ok; ++hf) {
-              if (!warp_wait(&p_full[2 * t + hf], (uint32_t)j & 1u, abort_flag, kSiteAttnPFull)) { ok = false; break; }
-              tc_fence_after();
-  #pragma unroll
-              for (int k4 = 0; k4 < 4; ++k4) {
-                const int kk = 4 * hf + k4;
-                if (leader) umma_f16_ts(tmem + Cfg::O_COL0 + t * D, tmem + (Cfg::S_COL_STRIDE * t) + kk * 8,
-                                        sdesc_adv(vd, kk * 2048), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
-              }
-            }
-            if (!ok) break;
-            if (j == nkv[t] - 1 && leader) umma_commit(&o_full[t]);
-            if (j + 1 < nkv[t]) {
-              if (!k_next) {
-                if (!warp_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, kSiteAttnKFull)) {
+        // other tile's PV and S (1024 tensor-core cycles) to hide behind.  Across items the
+        // same holds: the next item's S_A(0), S_B(0) follow the last PV_A, PV_B at once and
+        // run while the softmax warps write the item's output; its first PV, which starts O
+        // afresh, waits for P, which the warps store only after that output has left TMEM.
+        uint32_t tk = 0;            // K/V tiles consumed over all items
+        uint32_t ns[2] = {0u, 0u};  // S tiles issued per tile slot over all items (P barrier phases)
+        bool ok = true;
+        FwdItem x;
+        for (int ci = 0; ok && __all_sync(0xffffffffu, read_item(ci, x)); ++ci) {
+          if (!warp_wait(q_full, (uint32_t)ci & 1u, abort_flag, kSiteAttnQ)) { ok = false; break; }
+          if (!warp_wait(&k_full[tk & 1u], (tk >> 1) & 1u, abort_flag, kSiteAttnKFull)) { ok = false; break; }
+          tc_fence_after();
+          for (int t = 0; t < 2; ++t)
+            if (x.nkv[t] > 0) issue_s(t, tk);
+          if (leader) umma_commit(&k_empty[tk & 1u]);
+          if (x.n_j == 1 && leader) umma_commit(q_empty);  // the item's last S has read Q
+          for (int j = 0; j < x.n_j && ok; ++j) {
+            const uint32_t tv = tk + (uint32_t)j, tn = tv + 1u;  // V_j, K_{j+1} ring counts
+            bool k_next = false;  // K_{j+1} has landed
+            if (!warp_wait(&v_full[tv & 1u], (tv >> 1) & 1u, abort_flag, kSiteAttnVFull)) { ok = false; break; }
+            const uint64_t vd = sdesc_adv(v_desc, (tv & 1u) * Cfg::KV_BYTES);
+            for (int t = 0; t < 2 && ok; ++t) {
+              if (j >= x.nkv[t]) continue;
+              // O_t += P_t V_j, P_t from TMEM (K = 128 keys), each 64-key half as soon as it is stored
+              for (int hf = 0; hf < 2 && ok; ++hf) {
+                if (!warp_wait(&p_full[2 * t + hf], (ns[t] + (uint32_t)j) & 1u, abort_flag, kSiteAttnPFull)) {
                   ok = false;
                   break;
                 }
                 tc_fence_after();
-                k_next = true;
+  #pragma unroll
+                for (int k4 = 0; k4 < 4; ++k4) {
+                  const int kk = 4 * hf + k4;
+                  if (leader) umma_f16_ts(tmem + Cfg::O_COL0 + t * D, tmem + (Cfg::S_COL_STRIDE * t) + kk * 8,
+                                          sdesc_adv(vd, kk * 2048), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+                }
               }
-              issue_s(t, j + 1);
+              if (!ok) break;
+              if (j == x.nkv[t] - 1 && leader) umma_commit(&o_full[t]);
+              if (j + 1 < x.nkv[t]) {
+                if (!k_next) {
+                  if (!warp_wait(&k_full[tn & 1u], (tn >> 1) & 1u, abort_flag, kSiteAttnKFull)) {
+                    ok = false;
+                    break;
+                  }
+                  tc_fence_after();
+                  k_next = true;
+                }
+                issue_s(t, tn);
+              }
             }
+            if (!ok) break;
+            if (leader) umma_commit(&v_empty[tv & 1u]);
+            if (k_next && leader) umma_commit(&k_empty[tn & 1u]);
+            if (j + 2 == x.n_j && leader) umma_commit(q_empty);  // S(n_j - 1) were the item's last S
           }
           if (!ok) break;
-          if (leader) umma_commit(&v_empty[st]);
-          if (k_next && leader) umma_commit(&k_empty[(j + 1) & 1]);
+          tk += (uint32_t)x.n_j;
+          ns[0] += (uint32_t)x.nkv[0];
+          ns[1] += (uint32_t)x.nkv[1];
+          __syncwarp();
+          if (leader) mbar_arrive(&item_empty[ci % kFwdItemRing]);
         }
         if (leader) umma_commit(drain);
         volatile int no_abort = 0;
@@ -367,86 +434,103 @@ __global__ void __launch_bounds__(384, 1)
     const int t = (warp < 8) ? 0 : 1;
     const uint32_t quarter = warp & 3u;
     const int r = (int)(quarter * 32 + lane);  // row within the Q tile == TMEM lane
-    const int qi = q0[t] + r;                  // query index
     const uint32_t lane_base = (quarter * 32u) << 16;
     const uint32_t s_col = (Cfg::S_COL_STRIDE * t), o_col = Cfg::O_COL0 + t * D;
-    float m_used = -INFINITY, l = 0.0f;
-    // RECOMP: the exponent offset of the row, from the saved LSE (rows at or beyond S: -inf)
-    const float nl2 = RECOMP ? (qi < p.S ? p.lse_in[(long long)bh * p.S + qi] * -1.4426950408889634f : -INFINITY)
-                             : 0.0f;
+    uint32_t ns = 0, no = 0;  // S tiles and outputs of this tile slot over all items (barrier phases)
     bool ok = true;
-    for (int j = 0; j < nkv[t]; ++j) {
-      // warp-uniform outcome: the tcgen05.ld / st that follow are warp-collective
-      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], (uint32_t)j & 1u, abort_flag, kSiteAttnSFull))) {
+    for (int ci = 0; ok; ++ci) {
+      FwdItem x;
+      const bool more = __all_sync(0xffffffffu, read_item(ci, x));
+      if (lane == 0) mbar_arrive(&item_empty[ci % kFwdItemRing]);
+      if (!more) break;
+      const int nkv = x.nkv[t];
+      const int qi = x.q0[t] + r;  // query index
+      const int bh = x.bh;
+      float m_used = -INFINITY, l = 0.0f;
+      // RECOMP: the exponent offset of the row, from the saved LSE (rows at or beyond S: -inf)
+      const float nl2 = RECOMP ? (qi < p.S ? p.lse_in[(long long)bh * p.S + qi] * -1.4426950408889634f : -INFINITY)
+                               : 0.0f;
+      for (int j = 0; j < nkv; ++j) {
+        // warp-uniform outcome: the tcgen05.ld / st that follow are warp-collective
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], (ns + (uint32_t)j) & 1u, abort_flag, kSiteAttnSFull))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t xu[128];  // the S row, loaded straight into the registers it is used from
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_base + s_col + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&xu[32 * c]));
+        tmem_wait_ld();
+        float* xs = reinterpret_cast<float*>(xu);
+        const int k0 = j * 128;
+        int limit = p.S - k0;                           // keys at or beyond S are masked
+        if (p.causal) limit = min(limit, qi - k0 + 1);  // keys after the query are masked
+        const bool unmasked = __all_sync(0xffffffffu, limit >= 128);
+        if (!unmasked) {
+#pragma unroll
+          for (int c = 0; c < 128; ++c) xs[c] = (c < limit) ? xs[c] : -INFINITY;
+        }
+        if constexpr (RECOMP) {
+          if (unmasked)
+            softmax_p_to_tmem<true>(xs, p.scale_log2, nl2, tmem + lane_base + s_col, &p_full[2 * t]);
+          else
+            softmax_p_to_tmem<false>(xs, p.scale_log2, nl2, tmem + lane_base + s_col, &p_full[2 * t]);
+          continue;
+        }
+        float mx;
+        {  // tree reduction: 8 independent chains of three-input maxima
+          float m8[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) m8[u] = fmaxf(xs[u], xs[8 + u]);
+#pragma unroll
+          for (int c = 16; c < 128; c += 16)
+#pragma unroll
+            for (int u = 0; u < 8; ++u) m8[u] = fmax3(m8[u], xs[c + u], xs[c + 8 + u]);
+          mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
+        }
+        mx *= p.scale_log2;
+        const float m_new = fmaxf(m_used, mx);
+        if (j == 0) {
+          m_used = m_new;
+        } else {
+          const bool need = m_new > m_used + 8.0f;
+          if (__any_sync(0xffffffffu, need)) {
+            // O_t holds PV(j-1) (S_t(j) was issued after it completed); no PV is in flight
+            const float alpha = need ? ex2_approx(m_used - m_new) : 1.0f;
+            if (need) {
+              l *= alpha;
+              m_used = m_new;
+            }
+#pragma unroll 1
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t u[32];
+              tmem_ld32(tmem + lane_base + o_col + c * 32, u);
+              tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * alpha);
+              tmem_st32(tmem + lane_base + o_col + c * 32, u);
+            }
+          }
+        }
+        // P = exp2(x * scale_log2 - m_used) -> bf16 pairs into TMEM columns [s_col, s_col + 64)
+        if (unmasked)
+          l += softmax_p_to_tmem<true>(xs, p.scale_log2, -m_used, tmem + lane_base + s_col, &p_full[2 * t]);
+        else
+          l += softmax_p_to_tmem<false>(xs, p.scale_log2, -m_used, tmem + lane_base + s_col, &p_full[2 * t]);
+      }
+      if (!ok) break;
+      ns += (uint32_t)nkv;
+      if (nkv == 0) continue;  // a second tile beyond S: nothing computed, nothing stored
+      // the item's output leaves TMEM before these warps store the next item's first P,
+      // which is what the next item's first PV (overwriting O_t) waits for
+      if (!__all_sync(0xffffffffu, mbar_wait(&o_full[t], no & 1u, abort_flag, kSiteAttnOFull))) {
         ok = false;
         break;
       }
+      ++no;
       tc_fence_after();
-      uint32_t xu[128];  // the S row, loaded straight into the registers it is used from
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_base + s_col + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&xu[32 * c]));
-      tmem_wait_ld();
-      float* x = reinterpret_cast<float*>(xu);
-      const int k0 = j * 128;
-      int limit = p.S - k0;                           // keys at or beyond S are masked
-      if (p.causal) limit = min(limit, qi - k0 + 1);  // keys after the query are masked
-      const bool unmasked = __all_sync(0xffffffffu, limit >= 128);
-      if (!unmasked) {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) x[c] = (c < limit) ? x[c] : -INFINITY;
-      }
       if constexpr (RECOMP) {
-        if (unmasked)
-          softmax_p_to_tmem<true>(x, p.scale_log2, nl2, tmem + lane_base + s_col, &p_full[2 * t]);
-        else
-          softmax_p_to_tmem<false>(x, p.scale_log2, nl2, tmem + lane_base + s_col, &p_full[2 * t]);
-        continue;
-      }
-      float mx;
-      {  // tree reduction: 8 independent chains of three-input maxima
-        float m8[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) m8[u] = fmaxf(x[u], x[8 + u]);
-#pragma unroll
-        for (int c = 16; c < 128; c += 16)
-#pragma unroll
-          for (int u = 0; u < 8; ++u) m8[u] = fmax3(m8[u], x[c + u], x[c + 8 + u]);
-        mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
-      }
-      mx *= p.scale_log2;
-      const float m_new = fmaxf(m_used, mx);
-      if (j == 0) {
-        m_used = m_new;
-      } else {
-        const bool need = m_new > m_used + 8.0f;
-        if (__any_sync(0xffffffffu, need)) {
-          // O_t holds PV(j-1) (S_t(j) was issued after it completed); no PV is in flight
-          const float alpha = need ? ex2_approx(m_used - m_new) : 1.0f;
-          if (need) {
-            l *= alpha;
-            m_used = m_new;
-          }
-#pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t u[32];
-            tmem_ld32(tmem + lane_base + o_col + c * 32, u);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * alpha);
-            tmem_st32(tmem + lane_base + o_col + c * 32, u);
-          }
-        }
-      }
-      // P = exp2(x * scale_log2 - m_used) -> bf16 pairs into TMEM columns [s_col, s_col + 64)
-      if (unmasked)
-        l += softmax_p_to_tmem<true>(x, p.scale_log2, -m_used, tmem + lane_base + s_col, &p_full[2 * t]);
-      else
-        l += softmax_p_to_tmem<false>(x, p.scale_log2, -m_used, tmem + lane_base + s_col, &p_full[2 * t]);
-    }
-    if constexpr (RECOMP) {
-      // epilogue: Dt = rowsum(dO * O) and lse2 for the backward
-      if (ok && nkv[t] > 0 && __all_sync(0xffffffffu, mbar_wait(&o_full[t], 0, abort_flag, kSiteAttnOFull))) {
-        tc_fence_after();
+        // epilogue: Dt = rowsum(dO * O) and lse2 for the backward
         const bool row_ok = qi < p.S;
         const uint4* drow = reinterpret_cast<const uint4*>(p.dout + ((long long)bh * p.S + (row_ok ? qi : 0)) * D);
         float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -472,45 +556,47 @@ __global__ void __launch_bounds__(384, 1)
           }
         }
         if (qi < p.S_pad) {  // rows of a query tile past the last one do not exist in Dt / lse2
-          const long long r = (long long)bh * p.S_pad + qi;
-          p.dt[r] = row_ok ? (acc[0] + acc[1]) + (acc[2] + acc[3]) : 0.0f;
-          p.lse2[r] = row_ok ? nl2 : -INFINITY;
+          const long long rr = (long long)bh * p.S_pad + qi;
+          p.dt[rr] = row_ok ? (acc[0] + acc[1]) + (acc[2] + acc[3]) : 0.0f;
+          p.lse2[rr] = row_ok ? nl2 : -INFINITY;
         }
-      }
-    } else if (ok && nkv[t] > 0 && __all_sync(0xffffffffu, mbar_wait(&o_full[t], 0, abort_flag, kSiteAttnOFull))) {
-      // epilogue: O / l -> bf16, LSE
-      tc_fence_after();
-      const float inv = 1.0f / l;
-      const bool out32 = (reinterpret_cast<uintptr_t>(p.out) & 31u) == 0;
-      __nv_bfloat16* orow = p.out + (p.out_tokens ? (((long long)b * p.S + qi) * p.Hq + h) * D
-                                                  : ((long long)bh * p.S + qi) * D);
+      } else {
+        // epilogue: O / l -> bf16, LSE
+        const float inv = 1.0f / l;
+        const bool out32 = (reinterpret_cast<uintptr_t>(p.out) & 31u) == 0;
+        const int b = bh / p.Hq, h = bh % p.Hq;
+        __nv_bfloat16* orow = p.out + (p.out_tokens ? (((long long)b * p.S + qi) * p.Hq + h) * D
+                                                    : ((long long)bh * p.S + qi) * D);
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t u[32];
-        tmem_ld32(tmem + lane_base + o_col + c * 32, u);
-        tmem_wait_ld();
-        if (qi < p.S) {  // 32-byte stores where `out` allows: each fills a whole sector of the row
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t u[32];
+          tmem_ld32(tmem + lane_base + o_col + c * 32, u);
+          tmem_wait_ld();
+          if (qi < p.S) {  // 32-byte stores where `out` allows: each fills a whole sector of the row
 #pragma unroll
-          for (int e = 0; e < 32; e += 16) {
-            uint32_t w[8];
+            for (int e = 0; e < 32; e += 16) {
+              uint32_t wv[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-              w[i] = pack_bf16x2(__uint_as_float(u[e + 2 * i]) * inv, __uint_as_float(u[e + 2 * i + 1]) * inv);
-            if (out32) {
-              stg256(orow + c * 32 + e, w[0], w[1], w[2], w[3], w[4], w[5], w[6], w[7]);
-            } else {  // out only 16-byte aligned
-              *reinterpret_cast<uint4*>(orow + c * 32 + e) = make_uint4(w[0], w[1], w[2], w[3]);
-              *reinterpret_cast<uint4*>(orow + c * 32 + e + 8) = make_uint4(w[4], w[5], w[6], w[7]);
+              for (int i = 0; i < 8; ++i)
+                wv[i] = pack_bf16x2(__uint_as_float(u[e + 2 * i]) * inv, __uint_as_float(u[e + 2 * i + 1]) * inv);
+              if (out32) {
+                stg256(orow + c * 32 + e, wv[0], wv[1], wv[2], wv[3], wv[4], wv[5], wv[6], wv[7]);
+              } else {  // out only 16-byte aligned
+                *reinterpret_cast<uint4*>(orow + c * 32 + e) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+                *reinterpret_cast<uint4*>(orow + c * 32 + e + 8) = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+              }
             }
           }
         }
+        if (qi < p.S) p.lse[(long long)bh * p.S + qi] = (m_used + __log2f(l)) * 0.69314718055994531f;
       }
-      if (qi < p.S) p.lse[(long long)bh * p.S + qi] = (m_used + __log2f(l)) * 0.69314718055994531f;
+      tc_fence_before();
     }
   }
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) sched_finish(p.sched_slot);  // every fetch of this CTA is done
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::TMEM_COLS);

@@ -43,6 +43,7 @@ struct AttnBwdParams {
   __nv_bfloat16* dq;  // [B*Hq, S, D]
   __nv_bfloat16* dk;  // [B*Hkv, S, D]
   __nv_bfloat16* dv;  // [B*Hkv, S, D]
+  int sched_slot;     // dQ kernel: its work counter (g_sched)
 };
 
 template <int D>
@@ -57,8 +58,8 @@ struct AttnBwdCfg {
   static constexpr uint32_t DKDV_BODY = (2 + DKDV_QST + 2) * TILE_BYTES + (DKDV_QST + 2) * 512 + 256;
   static constexpr uint32_t DKDV_SLACK = 256;
   static constexpr size_t DKDV_SMEM = (size_t)DKDV_BODY + DKDV_SLACK;
-  // dQ kernel: Q, dO, three K stages, two V stages.
-  static constexpr size_t DQ_SMEM = 1024 + 7 * (size_t)TILE_BYTES + 256;
+  // dQ kernel: Q, dO, three K stages, two V stages, barriers and the work-item ring.
+  static constexpr size_t DQ_SMEM = 1024 + 7 * (size_t)TILE_BYTES + 512;
   static constexpr int THREADS = 384;
   static constexpr uint32_t TMEM_COLS = 512;
 };
@@ -81,6 +82,7 @@ enum : unsigned int {
   kSiteQDqFull = 0x318,
   kSiteQDrain = 0x319,
   kSiteQQd = 0x31a,
+  kSiteQItem = 0x31b,
 };
 
 // ---------------------------------------------------------------------------
@@ -566,7 +568,11 @@ __global__ void __launch_bounds__(384, 1)
 
 // ---------------------------------------------------------------------------
 // 3. dQ.  Persistent: one CTA per SM walks work items (128-query tile, query head),
-//    heaviest causal tiles first, item w = blockIdx.x + k * gridDim.x.  Per key tile of
+//    heaviest causal tiles first; its first item is w = blockIdx.x, the next ones come from
+//    the launch's work counter (sched_fetch), so the CTAs finish together although items
+//    differ in cost by up to 32x.  The producer fetches and publishes each item in a
+//    four-slot ring in shared memory (item_full / item_empty), read by the MMA warp and
+//    the softmax warps.  Per key tile of
 //    an item (thread = query row, so lse2 and Dt are per-thread registers):
 //   S(t)  = Q K_j^T -> TMEM [128 (t&1), +128)  (double-buffered: S(t+1) is computed while
 //                                               the warps work on tile t)
@@ -586,7 +592,8 @@ struct DqItem {
   int w, ci, j, n_kt, it, bh, kvz;
 };
 
-// Work item `w` (the ci-th of this CTA), positioned at its key tile 0.
+// Work item `w` (the ci-th of this CTA), positioned at its key tile 0; w at or beyond the
+// item count is the end of the CTA's work.
 __device__ __forceinline__ DqItem dq_item(const AttnBwdParams& p, int w, int ci) {
   DqItem x;
   const int n_bh = p.B * p.Hq, n_qt = (p.S + 127) / 128;
@@ -608,11 +615,7 @@ __device__ __forceinline__ DqItem dq_item(const AttnBwdParams& p, int w, int ci)
   return x;
 }
 
-// The key tile after `x`: the next tile of the item, or tile 0 of the CTA's next item.
-__device__ __forceinline__ DqItem dq_next(const AttnBwdParams& p, DqItem x) {
-  if (++x.j < x.n_kt) return x;
-  return dq_item(p, x.w + (int)gridDim.x, x.ci + 1);
-}
+constexpr int kDqItemRing = 4;
 
 template <int D>
 __global__ void __launch_bounds__(384, 1)
@@ -646,7 +649,10 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* do_full = bars + 21;
   uint64_t* do_empty = bars + 22;  // dO read by the item's last dP
   uint64_t* dq_free = bars + 23;   // an item's dQ read out of TMEM by all 8 warps
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
+  uint64_t* item_full = bars + 24;                 // [4] item published by the producer
+  uint64_t* item_empty = item_full + kDqItemRing;  // [4] read by the MMA warp and the 8 softmax warps
+  int* s_item = reinterpret_cast<int*>(item_empty + kDqItemRing);  // [4] item indices
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_item + kDqItemRing);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   constexpr uint32_t T_S = 0, T_DP = 256, T_DQ = 384;
 
@@ -672,9 +678,22 @@ __global__ void __launch_bounds__(384, 1)
     mbar_init(dq_full, 1);
     mbar_init(dq_free, 8);
     mbar_init(drain, 1);
+    for (int i = 0; i < kDqItemRing; ++i) {
+      mbar_init(&item_full[i], 1);
+      mbar_init(&item_empty[i], 9);
+    }
     *abort_flag = 0;
     fence_mbarrier_init();
   }
+  // The ci-th item of this CTA, from the ring (every role but the producer).
+  auto read_item = [&](int ci, bool& ok) -> DqItem {
+    const int slot = ci % kDqItemRing;
+    if (!mbar_wait(&item_full[slot], (uint32_t)(ci / kDqItemRing) & 1u, abort_flag, kSiteQItem)) {
+      ok = false;
+      return dq_item(p, INT32_MAX, ci);
+    }
+    return dq_item(p, s_item[slot], ci);
+  };
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
     tmem_relinquish();
@@ -697,7 +716,19 @@ __global__ void __launch_bounds__(384, 1)
       uint32_t kiss = 0, viss = 0, kpar = 0, vpar = 0, qiss = 0, qpar = 0, diss = 0, dpar = 0;
       bool ok = true;
       uint32_t t = 0;
-      for (DqItem x = dq_item(p, (int)blockIdx.x, 0); x.valid && ok; x = dq_item(p, x.w + (int)gridDim.x, x.ci + 1)) {
+      const int n_items = p.B * p.Hq * ((p.S + 127) / 128);
+      for (int ci = 0; ok; ++ci) {
+        // fetch the CTA's next item and publish it (an index >= n_items ends every role)
+        const int w = ci == 0 ? (int)blockIdx.x : sched_fetch(p.sched_slot);
+        const int slot = ci % kDqItemRing;
+        if (!mbar_wait(&item_empty[slot], ((uint32_t)(ci / kDqItemRing) & 1u) ^ 1u, abort_flag, kSiteQItem)) {
+          ok = false;
+          break;
+        }
+        s_item[slot] = w < n_items ? w : n_items;
+        mbar_arrive(&item_full[slot]);
+        const DqItem x = dq_item(p, w, ci);
+        if (!x.valid) break;
         const uint32_t iph = (uint32_t)x.ci & 1u;
         if (!mbar_wait(q_empty, iph ^ 1u, abort_flag, kSiteQKEmpty)) {
           ok = false;
@@ -772,17 +803,24 @@ __global__ void __launch_bounds__(384, 1)
         if (x.j == x.n_kt - 1 && leader) umma_commit(do_empty);  // the item's last dP has read dO
         return true;
       };
-      DqItem xq = dq_item(p, (int)blockIdx.x, 0);  // tile t: dQ
-      DqItem xp = xq, xs = xq;                     // tiles t+1: dP, t+2: S
       bool ok = true;
+      // The key tile after `x`: the next tile of the item, or tile 0 of the CTA's next item
+      // (read from the ring: the leading cursor waits for it, the others find it there).  The
+      // end of the CTA's work stays the end: no slot is published after it.
+      auto dq_next = [&](DqItem x) -> DqItem {
+        if (!x.valid || ++x.j < x.n_kt) return x;
+        return read_item(x.ci + 1, ok);
+      };
+      DqItem xq = read_item(0, ok);  // tile t: dQ
+      DqItem xp = xq, xs = xq;       // tiles t+1: dP, t+2: S
       if (xs.valid) {
         ok = issue_s(xs, 0) && issue_dp(xp, 0);
-        xs = dq_next(p, xs);
-        xp = dq_next(p, xp);
+        xs = dq_next(xs);
+        xp = dq_next(xp);
         if (ok && xs.valid) ok = issue_s(xs, 1);
-        xs = dq_next(p, xs);
+        xs = dq_next(xs);
       }
-      for (uint32_t t = 0; xq.valid && ok; ++t, xq = dq_next(p, xq)) {
+      for (uint32_t t = 0; xq.valid && ok; ++t) {
         const uint32_t sb = T_S + 128 * (t & 1);
         const uint64_t k_mn = sdesc_adv(k_desc_mn, (t % KST) * TILE);
         if (!warp_wait(dp_free, t & 1u, abort_flag, kSiteQDpFree)) {
@@ -795,7 +833,7 @@ __global__ void __launch_bounds__(384, 1)
             ok = false;
             break;
           }
-          xp = dq_next(p, xp);
+          xp = dq_next(xp);
         }
         // the item's first dQ MMA overwrites the accumulator: the previous item's dQ must be out
         if (xq.j == 0 && xq.ci > 0 && !warp_wait(dq_free, (uint32_t)(xq.ci - 1) & 1u, abort_flag, kSiteQDqFull)) {
@@ -824,8 +862,11 @@ __global__ void __launch_bounds__(384, 1)
             ok = false;
             break;
           }
-          xs = dq_next(p, xs);
+          xs = dq_next(xs);
         }
+        // the dQ cursor leaves its item: the MMA warp is done with the ring slot
+        if (xq.j == xq.n_kt - 1 && leader) mbar_arrive(&item_empty[xq.ci % kDqItemRing]);
+        xq = dq_next(xq);
       }
       if (leader) umma_commit(drain);
       volatile int no_abort = 0;
@@ -840,7 +881,11 @@ __global__ void __launch_bounds__(384, 1)
     const uint32_t lane_base = (quarter * 32u) << 16;
     bool ok = true;
     uint32_t t = 0;
-    for (DqItem x = dq_item(p, (int)blockIdx.x, 0); x.valid && ok; x = dq_item(p, x.w + (int)gridDim.x, x.ci + 1)) {
+    for (int ci = 0; ok; ++ci) {
+      const DqItem x = read_item(ci, ok);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[ci % kDqItemRing]);
+      if (!__all_sync(0xffffffffu, ok) || !x.valid) break;
       const int qi = x.it * 128 + r;
       const long long srow = (long long)x.bh * p.S_pad + qi;  // padded rows: -lse2 = -inf, Dt = 0
       const float nl2 = __ldg(p.lse2 + srow), dtr = __ldg(p.dt + srow);
@@ -916,6 +961,7 @@ __global__ void __launch_bounds__(384, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) sched_finish(p.sched_slot);  // every fetch of this CTA is done
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::TMEM_COLS);

@@ -149,6 +149,10 @@ int current_device(int* dev, DeviceInfo** info) {
   return BEACON_OK;
 }
 
+// The work-counter slot (g_sched) of the next persistent launch on device `dev`.
+std::atomic<unsigned> g_sched_next[64];
+int sched_slot(int dev) { return (int)(g_sched_next[dev].fetch_add(1u) % (unsigned)kSchedSlots); }
+
 // ===========================================================================
 // TMA tensor maps
 // ===========================================================================

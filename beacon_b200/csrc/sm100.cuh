@@ -34,6 +34,29 @@ __device__ __forceinline__ void record_fault(unsigned int code, unsigned int sit
   atomicAdd(&g_beacon_status[2], 1u);
 }
 
+// Dynamic work distribution for the persistent kernels.  A launch takes one of kSchedSlots
+// counter pairs (the host rotates them launch by launch); a CTA's first work item is its
+// block index and every further one comes from the slot's counter (gridDim.x + the count
+// handed out so far), so a CTA that finishes early takes more work -- causal work items
+// differ in cost by up to the number of key tiles.  The last CTA of the launch to finish
+// resets the pair for the next launch that takes the slot.  Launches that share a slot must
+// not overlap on the GPU: with the slots rotating, up to kSchedSlots persistent launches
+// may be in flight at once on one device.
+constexpr int kSchedSlots = 64;
+__device__ unsigned int g_sched[kSchedSlots][2];  // {items handed out beyond the grid, CTAs done}
+
+__device__ __forceinline__ int sched_fetch(int slot) {
+  return (int)gridDim.x + (int)atomicAdd(&g_sched[slot][0], 1u);
+}
+// One thread per CTA, after every fetch of the CTA.
+__device__ __forceinline__ void sched_finish(int slot) {
+  __threadfence();
+  if (atomicAdd(&g_sched[slot][1], 1u) == gridDim.x - 1) {
+    atomicExch(&g_sched[slot][0], 0u);
+    atomicExch(&g_sched[slot][1], 0u);
+  }
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
