@@ -16,18 +16,18 @@
 //               barrier, the fp8 staging tile on this CTA's `stg_full`.
 //   warp 1      (leader) MMA issuer: the whole warp runs the loop, one elected lane issues.
 //   warps 2-5   epilogue (both CTAs), as in the bf16 GEMM.
-//   warps 6-13  converters (both CTAs): wait stg_full, decode, fence the generic-proxy
-//               stores for the tensor core, arrive on the leader's `full` barrier.
-// The leader's full[s] completes when both CTAs' A bytes have landed and all converter
+//   warps 6-15  converters (both CTAs), one group of two warps per stage: wait stg_full,
+//               decode, fence the generic-proxy stores for the tensor core, arrive on the
+//               leader's `full` barrier.
+// The leader's full[s] completes when both CTAs' A bytes have landed and stage s's converter
 // warps of both CTAs have stored their B halves; the MMAs' commit to both CTAs' empty[s]
 // then frees A, B and the staging buffer of stage s for the next round.
 //
-// Measured on B200 (4096^3): 0.27 ms, about 510 TFLOP/s, with HBM reads of 1 byte per weight
-// element.  The kernel is bound by the decode: a timestamp trace of one CTA pair showed
-// the converters busy back to back, 0.7-0.9 us per K step against 0.26 us of MMA, and the
-// MMA waiting on them.  Doubling the converter warps from 4 to 8 gained 6%; placing the
-// loads, decodes and stores of a thread's items in three batches (instead of item by
-// item) gained 20%.
+// Measured on B200 (4096^3), with HBM reads of 1 byte per weight element: 0.35 ms with one
+// set of converter warps decoding item by item; 0.27 ms with loads, decodes and stores
+// batched per thread and eight warps; about 0.15 ms with every stage decoded at once by its
+// own group (a timestamp trace had shown the converters busy back to back at 0.7-0.9 us
+// per K step against 0.26 us of MMA, most of it the stores, fence and arrive of a stage).
 //
 // Decoding (restating F8E4M3::to_f32, crates/beacon-core/src/dtype.rs:138-161, without the
 // per-element branches): the byte's 7 exponent-mantissa bits are placed in a bf16 at bit 4
@@ -52,12 +52,20 @@ struct GemmFp8Cfg {
   static constexpr size_t SMEM_BYTES =
       1024 + (size_t)STAGES * (A_BYTES + B_BYTES + STG_BYTES) + 256;
   static constexpr int CONV_WARP0 = 6;
-#ifndef BEACON_FP8_CONV_WARPS
-#define BEACON_FP8_CONV_WARPS 8
-#endif
-  static constexpr int CONV_WARPS = BEACON_FP8_CONV_WARPS;
+  // The converter warps form one group per stage; group g decodes stage g's K steps (g,
+  // g + STAGES, ...), so all stages are decoded at once: a stage's decode is short, but its
+  // stores, the proxy fence and the cluster-scope arrive that hands it to the MMA take far
+  // longer, and converters working through the stages one after another bounded the kernel
+  // (0.26 ms at 4096^3 against 0.16 with four stages decoding at once).  A group owning its
+  // stage waits on that stage's barrier phases strictly in order: groups taking K steps in
+  // turn over more stages than groups could wait on a phase two ahead of the barrier's, which
+  // a parity wait cannot tell from the phase before.
+  static constexpr int GROUP_WARPS = 2;
+  static constexpr int CONV_GROUPS = STAGES;
+  static constexpr int CONV_WARPS = CONV_GROUPS * GROUP_WARPS;
   static constexpr int THREADS = (CONV_WARP0 + CONV_WARPS) * 32;
-  static constexpr int ITEMS = 1024 / (CONV_WARPS * 32);  // (K row, 8-column chunk) items per thread
+  static constexpr int ITEMS = 1024 / (GROUP_WARPS * 32);  // (K row, 8-column chunk) items per thread
+  static_assert(ITEMS % 8 == 0, "8-item batches");
 };
 
 enum : unsigned int {
@@ -110,7 +118,7 @@ __global__ void __launch_bounds__(GemmFp8Cfg::THREADS, 1)
   const int cluster = (int)(blockIdx.x >> 1), n_clusters = (int)(gridDim.x >> 1);
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1 + 2 * Cfg::CONV_WARPS);  // the leader's expect_tx arrive + converter warps x 2 CTAs
+      mbar_init(&full[s], 1 + 2 * Cfg::GROUP_WARPS);  // the leader's expect_tx arrive + a group's warps x 2 CTAs
       mbar_init(&empty[s], 1);
       mbar_init(&stg_full[s], 1);
     }
@@ -243,52 +251,50 @@ __global__ void __launch_bounds__(GemmFp8Cfg::THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ converters (warps 6.., both CTAs)
+    // Group g decodes stage g: K steps g, g + STAGES, ... of the CTA's whole sequence (all tiles).
     // Item (k, c): K row k (0..63) and 8-column chunk c (0..15) of this CTA's 128 columns.
-    // Thread ct takes items ct + NCT j: a warp reads two whole 128-byte staging rows and
-    // writes four whole 128-byte rows of the swizzled bf16 operand (no bank conflicts).
-    const int ct = (int)threadIdx.x - Cfg::CONV_WARP0 * 32;
-    int stage = 0;
+    // Thread ct of a group takes items ct + NCT j: a warp reads two whole 128-byte staging
+    // rows and writes four whole 128-byte rows of the swizzled bf16 operand (no bank
+    // conflicts).
+    constexpr int NCT = Cfg::GROUP_WARPS * 32;
+    const int cw = (int)warp - Cfg::CONV_WARP0;
+    const int grp = cw / Cfg::GROUP_WARPS;
+    const int ct = (cw % Cfg::GROUP_WARPS) * 32 + (int)lane;
+    const int n_steps = ((num_tiles - cluster + n_clusters - 1) / n_clusters) * ktiles;  // this cluster's K steps
+    const int stage = grp;
     uint32_t phase = 0;
-    bool ok = true;
-    for (int tile = cluster; tile < num_tiles && ok; tile += n_clusters) {
-      for (int kt = 0; kt < ktiles; ++kt) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&stg_full[stage], phase, abort_flag, kSiteFp8Stg))) {
-          ok = false;
-          break;
-        }
-        // all eight loads first, then the decodes, then the stores: the items are independent,
-        // so their latencies overlap (decoded one after another, a stage took ~4x longer)
-        const uint32_t stg = smem_u32(sStg + stage * Cfg::STG_BYTES);
-        const uint32_t b = smem_u32(sB + stage * Cfg::B_BYTES);
-        constexpr int NCT = Cfg::CONV_WARPS * 32;
-        uint2 w[Cfg::ITEMS];
+    for (int step = grp; step < n_steps; step += STAGES, phase ^= 1u) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&stg_full[stage], phase, abort_flag, kSiteFp8Stg))) break;
+      // loads, decodes and stores in batches of eight: the items are independent, so their
+      // latencies overlap (decoded one after another, a stage took ~4x longer)
+      const uint32_t stg = smem_u32(sStg + stage * Cfg::STG_BYTES);
+      const uint32_t b = smem_u32(sB + stage * Cfg::B_BYTES);
 #pragma unroll
-        for (int j = 0; j < Cfg::ITEMS; ++j) {
-          const int it = ct + NCT * j;
+      for (int j0 = 0; j0 < Cfg::ITEMS; j0 += 8) {
+        uint2 w[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int it = ct + NCT * (j0 + j);
           const int k = it >> 4, c = it & 15;
           asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(w[j].x), "=r"(w[j].y) : "r"(stg + k * 128 + c * 8)
                        : "memory");
         }
-        uint4 o[Cfg::ITEMS];
+        uint4 o[8];
 #pragma unroll
-        for (int j = 0; j < Cfg::ITEMS; ++j) o[j] = e4m3x8_to_bf16x8(w[j]);
+        for (int j = 0; j < 8; ++j) o[j] = e4m3x8_to_bf16x8(w[j]);
 #pragma unroll
-        for (int j = 0; j < Cfg::ITEMS; ++j) {
-          const int it = ct + NCT * j;
+        for (int j = 0; j < 8; ++j) {
+          const int it = ct + NCT * (j0 + j);
           const int k = it >> 4, c = it & 15;
           asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(b + (c >> 3) * 8192 + k * 128 +
                                                                         (((c & 7) ^ (k & 7)) << 4)),
                        "r"(o[j].x), "r"(o[j].y), "r"(o[j].z), "r"(o[j].w)
                        : "memory");
         }
-        fence_proxy_async_smem();  // generic-proxy stores -> the tensor core's async proxy
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(cluster_map(&full[stage], 0));
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
       }
+      fence_proxy_async_smem();  // generic-proxy stores -> the tensor core's async proxy
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(cluster_map(&full[stage], 0));
     }
   }
 

@@ -6,6 +6,8 @@
     python profile_cases.py layernorm_bwd --tokens 16384 --width 4096
     python profile_cases.py gemm_fp8 --m 4096 --n 4096 --k 4096
     python profile_cases.py swiglu_bwd --tokens 16384 --width 4096 --n 14336
+    python profile_cases.py block          (pre-norm block forward, batch 4 x seq 2048, d_model 4096)
+    python profile_cases.py block_folded   (the same with both RMSNorms folded into the GEMMs)
 
 Each case runs `--warmup` untimed launches and then `--iters` launches timed with
 CUDA events, printing the per-launch time and TFLOP/s (algorithmic FLOPs: causal
@@ -32,6 +34,7 @@ if ROOT not in sys.path:
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["attn_fwd", "attn_bwd", "attn_bwd_recompute", "gemm", "gemm_fp8", "swiglu_bwd",
+                                     "block", "block_folded",
                                      "layernorm_fwd", "layernorm_bwd", "rmsnorm_fwd", "rmsnorm_bwd"])
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--width", type=int, default=4096)
@@ -75,6 +78,25 @@ def main(argv=None):
         C = torch.empty(a.m, a.n, device=dev, dtype=torch.bfloat16)
         fn = lambda: ops.linear_fp8w_fwd_devscale(A, W8, scale, out=C)
         flops, kname = 2.0 * a.m * a.n * a.k, "k_gemm_fp8w_tc2"
+    elif a.case.startswith("block"):
+        # pre-norm Llama block forward: batch 4 x seq 2048, d_model 4096, 32 x 128 heads, SwiGLU 14336
+        Bb, Sb, dm, Hb, F = 4, 2048, 4096, 32, 14336
+        T = Bb * Sb
+        x = torch.randn(T, dm, device=dev).bfloat16()
+        w = lambda r, c: (torch.randn(r, c, device=dev) * 0.02).bfloat16()
+        n1, n2 = torch.ones(dm, device=dev).bfloat16(), torch.ones(dm, device=dev).bfloat16()
+        wqkv, wo, wg, wu, wd = w(dm, 3 * dm), w(dm, dm), w(dm, F), w(dm, F), w(F, dm)
+        out = torch.empty_like(x)
+        ws = torch.empty(ops.llama_block_workspace_bytes(Bb, Sb, dm, Hb, Hb, 128, F), dtype=torch.uint8, device=dev)
+        if a.case == "block":
+            fn = lambda: ops.llama_block_fwd(x, n1, wqkv, wo, n2, wg, wu, wd, Bb, Sb, Hb, Hb, out=out, workspace=ws)
+        else:
+            wqkv_f, wg_f, wu_f = ops.llama_block_fold_weights(n1, wqkv, n2, wg, wu)
+            fn = lambda: ops.llama_block_fwd_folded(x, wqkv_f, wo, wg_f, wu_f, wd, Bb, Sb, Hb, Hb, out=out,
+                                                    workspace=ws)
+        flops = (2.0 * T * dm * 3 * dm + 2.0 * T * dm * dm + 2.0 * T * dm * 2 * F + 2.0 * T * F * dm
+                 + 2.0 * Bb * Hb * Sb * Sb * 128)
+        kname = "k_gemm_bf16_tc"
     elif a.case == "swiglu_bwd":
         T, dm, F = a.tokens // 2, a.width, a.n
         x = torch.randn(T, dm, device=dev).bfloat16()
@@ -104,7 +126,7 @@ def main(argv=None):
     ms, n = ops.profile_read(kname)
     kms = ms / max(n, 1)
     call_ms = e0.elapsed_time(e1) / a.iters
-    if a.case == "swiglu_bwd":  # five GEMM launches per call: the whole call against the algorithmic FLOPs
+    if a.case == "swiglu_bwd" or a.case.startswith("block"):  # several launches per call: the whole call
         print(f"{a.case}: {call_ms:.4f} ms/call {flops / (call_ms * 1e-3) / 1e12:.1f} TFLOP/s algorithmic "
               f"({n // max(a.iters, 1)} GEMM launches per call, {kms:.4f} ms each on average)", flush=True)
     else:
