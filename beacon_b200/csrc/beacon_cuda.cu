@@ -310,11 +310,11 @@ int launch_gemm_tc_bn(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtenso
   return launch_gemm_tc_t<BN, true, false>(ta, tb, tb2, p, sms, st);
 }
 
-template <bool A_MN, bool B_MN>
+template <bool A_MN, bool B_MN, int BN>
 int launch_gemm_tc2_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb2, const GemmParams& p,
                       int sms, cudaStream_t st) {
-  using Cfg = GemmCfg2;
-  auto kern = k_gemm_bf16_tc2<A_MN, B_MN>;
+  using Cfg = GemmCfg2<BN>;
+  auto kern = k_gemm_bf16_tc2<A_MN, B_MN, BN>;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -345,12 +345,22 @@ int launch_gemm_tc2_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtens
   return check_launch("k_gemm_bf16_tc2");
 }
 
-// Kernel choice override for tests: BEACON_GEMM_PATH = "1sm" | "2sm" (default: by shape).
+template <int BN>
+int launch_gemm_tc2_bn(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb2,
+                       const GemmParams& p, int sms, cudaStream_t st) {
+  if (!a_mn && b_mn) return launch_gemm_tc2_t<false, true, BN>(ta, tb, tb2, p, sms, st);
+  if (!a_mn && !b_mn) return launch_gemm_tc2_t<false, false, BN>(ta, tb, tb2, p, sms, st);
+  if (a_mn && b_mn) return launch_gemm_tc2_t<true, true, BN>(ta, tb, tb2, p, sms, st);
+  return launch_gemm_tc2_t<true, false, BN>(ta, tb, tb2, p, sms, st);
+}
+
+// Kernel choice override for tests: BEACON_GEMM_PATH = "1sm" | "2sm" (256x256 pair tiles) |
+// "2sm128" (256x128 pair tiles); default: by shape.
 int gemm_path_override() {
   static int v = -1;
   if (v < 0) {
     const char* e = getenv("BEACON_GEMM_PATH");
-    v = (e && !strcmp(e, "1sm")) ? 1 : (e && !strcmp(e, "2sm")) ? 2 : 0;
+    v = (e && !strcmp(e, "1sm")) ? 1 : (e && !strcmp(e, "2sm")) ? 2 : (e && !strcmp(e, "2sm128")) ? 3 : 0;
   }
   return v;
 }
@@ -409,23 +419,38 @@ int gemm_bf16(const Operand& A, const Operand& B, const Operand* B2, GemmParams 
                                             reinterpret_cast<const bf16*>(B.ptr), sbk, sbn, p);
     return check_launch("k_gemm_simt<bf16>");
   }
-  // 2-SM 256x256 pair tiles halve each SM's operand stream; they win whenever their
-  // wave efficiency is close to the best 1-SM tile's.
-  bool pair = false;
+  // 2-SM pair tiles halve each SM's operand stream; they win whenever their wave
+  // efficiency is close to the best 1-SM tile's.  Per SM and 64-deep K step a 128x128 1-SM
+  // tile needs 32 KB for 71-cycle MMAs, more than TMA delivers to one SM (measured ~58 B per
+  // clock in that kernel); a 256x128 pair tile needs 24 KB and a 256x256 one 32 KB for MMAs
+  // twice as long.  Scores: wave efficiency x the rows the tiles cover (M padded to 128 or
+  // 256 rows) x a per-shape credit.
+  int pair_bn = 0;  // 0: 1-SM tiles
   {
     const int ov = gemm_path_override();
+    const double rows1 = (double)p.M / (double)(((p.M + 127) / 128) * 128);
+    const double rows2 = (double)p.M / (double)(((p.M + 255) / 256) * 256);
     const int64_t cols2 = swiglu ? 128 : 256;
     const int64_t tiles2 = ((p.M + 255) / 256) * ((p.N + cols2 - 1) / cols2);
-    const double score2 = wave_eff(tiles2, di->sms / 2) * 1.15;
+    const double score2 = wave_eff(tiles2, di->sms / 2) * rows2 * 1.15;
+    const int64_t tiles2n = ((p.M + 255) / 256) * ((p.N + 127) / 128);
+    const double score2n = swiglu ? 0.0 : wave_eff(tiles2n, di->sms / 2) * rows2 * 0.97;
     const int bn1 = choose_bn(p.M, p.N, swiglu, di->sms);
     const int64_t c1 = swiglu ? bn1 / 2 : bn1;
     const double cost1 = bn1 == 256 ? 1.0 : bn1 == 128 ? 0.93 : 0.80;
-    const double score1 = wave_eff(((p.M + 127) / 128) * ((p.N + c1 - 1) / c1), di->sms) * cost1;
-    pair = ov == 2 || (ov == 0 && !force_bn && score2 > score1);
+    const double score1 = wave_eff(((p.M + 127) / 128) * ((p.N + c1 - 1) / c1), di->sms) * rows1 * cost1;
+    if (ov == 2 || (ov == 3 && swiglu)) {
+      pair_bn = 256;
+    } else if (ov == 3) {
+      pair_bn = 128;
+    } else if (ov == 0 && !force_bn) {
+      if (score2 > score1 && score2 >= score2n) pair_bn = 256;
+      else if (score2n > score1) pair_bn = 128;
+    }
   }
-  if (pair) {
+  if (pair_bn) {
     p.tiles_m = (p.M + 255) / 256;
-    p.tiles_n = swiglu ? (p.N + 127) / 128 : (p.N + 255) / 256;
+    p.tiles_n = swiglu ? (p.N + 127) / 128 : (p.N + pair_bn - 1) / pair_bn;
     CUtensorMap ta, tb, tb2;
     if (!A.mn_major)
       BEACON_TRY(make_map_2d(&ta, A.ptr, (uint64_t)p.K, (uint64_t)p.M, (uint64_t)A.ld, 64, 128));
@@ -436,7 +461,7 @@ int gemm_bf16(const Operand& A, const Operand& B, const Operand* B2, GemmParams 
     const uint64_t k2 = p.k_split > 0 ? (uint64_t)(p.K - p.k_split) : (uint64_t)p.K;
     auto map_b2 = [&](CUtensorMap* m, const Operand& op, uint64_t kext) -> int {
       if (op.mn_major) return make_map_2d(m, op.ptr, (uint64_t)p.N, kext, (uint64_t)op.ld, 64, 64);
-      return make_map_2d(m, op.ptr, kext, (uint64_t)p.N, (uint64_t)op.ld, 64, 128);
+      return make_map_2d(m, op.ptr, kext, (uint64_t)p.N, (uint64_t)op.ld, 64, (uint32_t)(pair_bn / 2));
     };
     BEACON_TRY(map_b2(&tb, B, k1));
     if (two_b) {
@@ -445,10 +470,8 @@ int gemm_bf16(const Operand& A, const Operand& B, const Operand* B2, GemmParams 
     } else {
       tb2 = tb;
     }
-    if (!A.mn_major && B.mn_major) return launch_gemm_tc2_t<false, true>(ta, tb, tb2, p, di->sms, st);
-    if (!A.mn_major && !B.mn_major) return launch_gemm_tc2_t<false, false>(ta, tb, tb2, p, di->sms, st);
-    if (A.mn_major && B.mn_major) return launch_gemm_tc2_t<true, true>(ta, tb, tb2, p, di->sms, st);
-    return launch_gemm_tc2_t<true, false>(ta, tb, tb2, p, di->sms, st);
+    if (pair_bn == 128) return launch_gemm_tc2_bn<128>(A.mn_major, B.mn_major, ta, tb, tb2, p, di->sms, st);
+    return launch_gemm_tc2_bn<256>(A.mn_major, B.mn_major, ta, tb, tb2, p, di->sms, st);
   }
   const int bn = force_bn ? force_bn : choose_bn(p.M, p.N, swiglu, di->sms);
   const int cols = swiglu ? bn / 2 : bn;

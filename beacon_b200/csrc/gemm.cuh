@@ -519,16 +519,20 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // ---------------------------------------------------------------------------
-// 2-SM variant: a cluster of two CTAs computes a 256x256 tile with
+// 2-SM variant: a cluster of two CTAs computes a 256xBN tile with
 // tcgen05.mma.cta_group::2 (M = 256 over the pair).  Each CTA TMA-loads its own 128 rows
-// of A and its own 128-column half of B (for SwiGLU: CTA 0 the gate columns, CTA 1 the
-// up columns), so every SM streams half the B operand a 1-SM 128x256 tile would, and
-// the pair's loads complete on the leader CTA's barrier.  Only the leader issues MMAs;
+// of A and its own BN/2-column half of B (for SwiGLU, BN = 256: CTA 0 the gate columns,
+// CTA 1 the up columns), so every SM streams half the B operand a 1-SM 128xBN tile would,
+// and the pair's loads complete on the leader CTA's barrier.  Only the leader issues MMAs;
 // each CTA's TMEM receives its 128 accumulator rows and its own epilogue warps drain
-// them.  No load uses multicast.
+// them.  No load uses multicast.  BN = 256 is the general tile; BN = 128 (256x128 pair
+// tiles) serves narrow outputs such as a column shard of N = 512, where 256x256 tiles
+// would leave half the SMs idle and 1-SM 128x128 tiles need more operand bytes per clock
+// than TMA delivers to an SM.
 // ---------------------------------------------------------------------------
+template <int BN_>
 struct GemmCfg2 {
-  static constexpr int BM = 128, BN = 256, BK = 64, STAGES = 6;
+  static constexpr int BM = 128, BN = BN_, BK = 64, STAGES = BN_ == 256 ? 6 : 8;
   static constexpr uint32_t A_BYTES = BM * BK * 2;           // this CTA's 128 rows of A
   static constexpr uint32_t B_BYTES = (BN / 2) * BK * 2;     // this CTA's half of B
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
@@ -537,11 +541,12 @@ struct GemmCfg2 {
   static constexpr int THREADS = 192;
 };
 
-template <bool A_MN, bool B_MN>
+template <bool A_MN, bool B_MN, int BN = 256>
 __global__ void __launch_bounds__(192, 1)
     k_gemm_bf16_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmB2, const GemmParams p) {
-  using Cfg = GemmCfg2;
+  using Cfg = GemmCfg2<BN>;
+  static_assert(BN == 256 || BN == 128, "pair tiles of 256 x 256 or 256 x 128");
   constexpr int BK = Cfg::BK, STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -586,9 +591,9 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int num_tiles = p.tiles_m * p.tiles_n;  // tiles of 256 x 256 (SwiGLU: 256 x 128 outputs)
+  const int num_tiles = p.tiles_m * p.tiles_n;  // tiles of 256 x BN (SwiGLU: 256 x 128 outputs)
   const int ktiles = (p.K + BK - 1) / BK;
-  const bool swiglu = epi_tile_pairs(p.epi);
+  const bool swiglu = BN == 256 && epi_tile_pairs(p.epi);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer (both CTAs)
@@ -601,7 +606,7 @@ __global__ void __launch_bounds__(192, 1)
         const int tm = tile / p.tiles_n, tn = tile % p.tiles_n;
         const int m0 = tm * 256 + 128 * (int)rank;
         const CUtensorMap* mb_tile = (swiglu && rank == 1) ? &tmB2 : &tmB;
-        const int n0 = swiglu ? tn * 128 : tn * 256 + 128 * (int)rank;
+        const int n0 = swiglu ? tn * 128 : tn * BN + (BN / 2) * (int)rank;
         for (int kt = 0; kt < ktiles; ++kt) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteGemmEmpty)) {
             ok = false;
@@ -623,10 +628,10 @@ __global__ void __launch_bounds__(192, 1)
           const CUtensorMap* mb = second ? &tmB2 : mb_tile;
           const int kb = second ? k0 - p.k_split : k0;
           if constexpr (!B_MN) {
-            tma_load_2d_pair(b, mb, lb, kb, n0);
+            tma_load_2d_pair(b, mb, lb, kb, n0);  // BN/2 rows of B^T (the tensor map's box)
           } else {
-            tma_load_2d_pair(b, mb, lb, n0, kb);
-            tma_load_2d_pair(b + 64 * BK * 2, mb, lb, n0 + 64, kb);
+#pragma unroll
+            for (int h = 0; h < BN / 128; ++h) tma_load_2d_pair(b + h * 64 * BK * 2, mb, lb, n0 + 64 * h, kb);
           }
           issued |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);

@@ -18,6 +18,13 @@
  *  - `stream` is a cudaStream_t (NULL = legacy default stream).  Every call is
  *    asynchronous on that stream and never synchronises the device, except
  *    where a comment says it may grow the library's internal workspace.
+ *  - Concurrency: calls on different streams may overlap on the GPU, except that
+ *    calls which take their scratch from the library's per-device workspace
+ *    (workspace = NULL) share that one buffer: give each stream its own workspace
+ *    when such calls may overlap.  The persistent kernels (attention forward, dQ)
+ *    take their work items from one of 64 counter slots per device, rotating
+ *    launch by launch and reset by each launch's last CTA: up to 64 such
+ *    launches may be in flight on one device at once.
  *  - Return value: a beacon_status that maps 1:1 onto beacon-cuda's LaunchError
  *    variants (crates/beacon-cuda/src/error.rs:4-13); 0 is Ok.  The message of
  *    the last error on the calling thread is available from beacon_last_error().

@@ -212,3 +212,43 @@ def test_outputs_only_16_byte_aligned():
     check(rc)
     torch.cuda.synchronize()
     assert torch.equal(dq, rq) and torch.equal(dk, rk) and torch.equal(dv, rv)
+
+
+def test_work_counter_slots_rotate_and_reset():
+    """The persistent forward and dQ kernels draw their work items from per-launch counter
+    slots in device memory (64 per device, reset by each launch's last CTA).  150 forward +
+    backward calls in a row wrap the slots twice, and two streams running at once take
+    different slots: every call must give the same outputs as the first."""
+    import torch
+    ops = _ops()
+    B, H, S, D = 1, 3, 640, 128  # 3 heads x 3 query-tile pairs: fewer items than SMs, and more
+    q, k, v, do = _qkv(B, H, H, S, D, 12)
+    t = lambda a: to_dev(a, torch.bfloat16)
+    q, k, v, do = t(q), t(k), t(v), t(do)
+    out0, lse0 = ops.attention_fwd(q, k, v)
+    dq0, dk0, dv0 = ops.attention_bwd(do, q, k, v, lse0)
+    for _ in range(150):
+        out, lse = ops.attention_fwd(q, k, v)
+    dq, dk, dv = ops.attention_bwd(do, q, k, v, lse)
+    torch.cuda.synchronize()
+    assert torch.equal(out, out0) and torch.equal(lse, lse0)
+    assert torch.equal(dq, dq0) and torch.equal(dk, dk0) and torch.equal(dv, dv0)
+    # two streams at once, a larger problem on each (more items than SMs)
+    q2, k2, v2, do2 = (t(a) for a in _qkv(2, 16, 16, 1024, 128, 13))
+    ref2 = ops.attention_fwd(q2, k2, v2)
+    refg = ops.attention_bwd(do2, q2, k2, v2, ref2[1])
+    torch.cuda.synchronize()
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    ws_bytes = ops.attention_bwd_workspace_bytes(2, 16, 1024, 128)
+    wss = [torch.empty(ws_bytes, dtype=torch.uint8, device="cuda") for _ in range(2)]  # one per stream
+    res = []
+    for s, ws in zip((s1, s2), wss):
+        with torch.cuda.stream(s):
+            o, l = ops.attention_fwd(q2, k2, v2)
+            res.append((o, l, ops.attention_bwd(do2, q2, k2, v2, l, workspace=ws)))
+    torch.cuda.synchronize()
+    for o, l, g in res:
+        assert torch.equal(o, ref2[0]) and torch.equal(l, ref2[1])
+        for a, b in zip(g, refg):
+            assert torch.equal(a, b)
+    assert ops.device_status(0)[0] == 0

@@ -1,6 +1,6 @@
-"""Both GEMM kernels — 1-SM 128-row tiles and 2-SM (cta_group::2) 256x256 pair tiles —
-on every operand layout and epilogue, forced through BEACON_GEMM_PATH in a child
-process so the shape heuristic cannot hide either one."""
+"""Every GEMM kernel shape -- 1-SM 128-row tiles, 2-SM (cta_group::2) 256x256 pair tiles and
+256x128 pair tiles -- on every operand layout and epilogue, forced through BEACON_GEMM_PATH
+in a child process so the shape heuristic cannot hide any of them."""
 import os
 import subprocess
 import sys
@@ -40,7 +40,7 @@ sys.exit(1 if fails else 0)
 '''
 
 
-@pytest.mark.parametrize("path", ["1sm", "2sm"])
+@pytest.mark.parametrize("path", ["1sm", "2sm", "2sm128"])
 def test_gemm_kernel_path(path):
     env = dict(os.environ, BEACON_GEMM_PATH=path, PYTHONPATH=HERE + os.pathsep + os.path.dirname(HERE))
     r = subprocess.run([sys.executable, "-c", CHILD, HERE], env=env, capture_output=True, text=True, timeout=300)
