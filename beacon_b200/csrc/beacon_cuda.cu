@@ -1042,7 +1042,23 @@ extern "C" int beacon_rmsnorm_adjoint_fwd(void* out, const void* x, const void* 
   const int d = (int)dim;
 #define RMS_FWD(T, V) \
   k_rmsnorm_fwd<T, V><<<grid, 256, 0, st>>>((T*)out, rms, (const T*)x, (const T*)weight, tokens, d, eps)
-  if (dtype == BEACON_BF16) {
+  // an odd count of 256-column chunks above 8 does not split over two warps: the CTA-per-row kernel
+  if (dtype == BEACON_BF16 && vec && dim % 256 == 0 && dim <= 4096 && (dim / 256 <= 8 || (dim / 256) % 2 == 0)) {
+    // k_rmsnorm_fwd_warp: one warp per row up to 2048 columns, two warps per row above;
+    // 8-warp CTAs, at most two per SM by their register use
+    const int wpr = dim > 2048 ? 2 : 1;
+    const int slots = 8 / wpr;
+    const int wgrid = (int)std::min<int64_t>((tokens + slots - 1) / slots, (int64_t)di->sms * 2);
+    const bf16 *xb = (const bf16*)x, *wb = (const bf16*)weight;
+    bf16* yb = (bf16*)out;
+    switch (dim / 256) {
+#define RMS_WARP(N, W) \
+  case N: k_rmsnorm_fwd_warp<N / W, W><<<wgrid, 256, 0, st>>>(yb, rms, xb, wb, tokens, d, eps); break;
+      RMS_WARP(1, 1) RMS_WARP(2, 1) RMS_WARP(3, 1) RMS_WARP(4, 1) RMS_WARP(5, 1) RMS_WARP(6, 1) RMS_WARP(7, 1)
+      RMS_WARP(8, 1) RMS_WARP(10, 2) RMS_WARP(12, 2) RMS_WARP(14, 2) RMS_WARP(16, 2)
+#undef RMS_WARP
+    }
+  } else if (dtype == BEACON_BF16) {
     if (vec && dim <= 256 * 8 * 1) RMS_FWD(bf16, 1);
     else if (vec && dim <= 256 * 8 * 2) RMS_FWD(bf16, 2);
     else if (vec && dim <= 256 * 8 * 4) RMS_FWD(bf16, 4);
@@ -1230,7 +1246,23 @@ extern "C" int beacon_layernorm_adjoint_fwd(void* out, const void* x, const void
 #define LN_FWD_ANY(T)                                                                                         \
   k_layernorm_fwd_any<T><<<grid, 256, 0, st>>>((T*)out, mean, invstd, (const T*)x, (const T*)weight,          \
                                                (const T*)bias, tokens, d, eps)
-  if (dtype == BEACON_BF16) {
+  const bool warp_rows = dtype == BEACON_BF16 && vec && dim % 256 == 0 && dim <= 4096 && (dim / 256 <= 8 ||
+                                                                                            (dim / 256) % 2 == 0);
+  if (warp_rows) {
+    // k_layernorm_fwd_warp: one warp per row up to 2048 columns, two warps per row above
+    const int wpr = dim > 2048 ? 2 : 1;
+    const int slots = 8 / wpr;
+    const int wgrid = (int)std::min<int64_t>((tokens + slots - 1) / slots, (int64_t)di->sms * 2);
+    const bf16 *xb = (const bf16*)x, *wb = (const bf16*)weight, *bb = (const bf16*)bias;
+    bf16* yb = (bf16*)out;
+    switch (dim / 256) {
+#define LN_WARP(N, W) \
+  case N: k_layernorm_fwd_warp<N / W, W><<<wgrid, 256, 0, st>>>(yb, mean, invstd, xb, wb, bb, tokens, d, eps); break;
+      LN_WARP(1, 1) LN_WARP(2, 1) LN_WARP(3, 1) LN_WARP(4, 1) LN_WARP(5, 1) LN_WARP(6, 1) LN_WARP(7, 1)
+      LN_WARP(8, 1) LN_WARP(10, 2) LN_WARP(12, 2) LN_WARP(14, 2) LN_WARP(16, 2)
+#undef LN_WARP
+    }
+  } else if (dtype == BEACON_BF16) {
     if (vec && dim <= 256 * 8 * 1) LN_FWD(bf16, 1);
     else if (vec && dim <= 256 * 8 * 2) LN_FWD(bf16, 2);
     else if (vec && dim <= 256 * 8 * 4) LN_FWD(bf16, 4);

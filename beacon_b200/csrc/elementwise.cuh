@@ -355,6 +355,71 @@ __device__ __forceinline__ float block_sum_256(float v, float* red) {
   return t;
 }
 
+// WPR warps per bf16 row (norm.rs:20-31), each lane holding 8 x NCH values of the row from
+// 16-byte loads (512 bytes per warp instruction; a row is WPR x NCH x 256 elements), grid-
+// stride over rows in steps of the grid's row slots.  The sum of squares is a shuffle
+// reduction (plus, for two warps per row, one exchange through shared memory behind a
+// 64-thread named barrier), so no CTA-wide barrier holds the other rows back: every
+// resident warp can have its row's loads in flight, where a CTA per row keeps about eight
+// rows in flight per SM and none while it reduces.  x is read with the streaming
+// (evict-first) hint and y stored with it; the weight row stays cached.  Two warps per
+// 4096-wide row keep a lane at 8 chunks (one warp would need 16 and spill).
+template <int NCH, int WPR>
+__global__ void __launch_bounds__(256, 2) k_rmsnorm_fwd_warp(__nv_bfloat16* __restrict__ y, float* __restrict__ rms,
+                                                             const __nv_bfloat16* __restrict__ x,
+                                                             const __nv_bfloat16* __restrict__ w, long long rows,
+                                                             int dim, float eps) {
+  static_assert(WPR == 1 || WPR == 2, "one or two warps per row");
+  __shared__ float part[8];
+  const int lane = (int)(threadIdx.x & 31u), warp = (int)(threadIdx.x >> 5);
+  const int slot = warp / WPR, sub = warp % WPR;  // row slot of the CTA, this warp's share of the row
+  constexpr int SLOTS = 8 / WPR;
+  const long long ns = (long long)gridDim.x * SLOTS;
+  const uint4* wv = reinterpret_cast<const uint4*>(w);
+  for (long long r = (long long)blockIdx.x * SLOTS + slot; r < rows; r += ns) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + r * dim);
+    uint4 u[NCH];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) u[c] = __ldcs(xr + (c * WPR + sub) * 32 + lane);
+    float ss = 0.0f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[c]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]);
+        ss = fmaf(f.x, f.x, ss);
+        ss = fmaf(f.y, f.y, ss);
+      }
+    }
+    ss = warp_sum(ss);
+    if constexpr (WPR == 2) {
+      if (lane == 0) part[warp] = ss;
+      named_bar_sync(1 + slot, 64);
+      ss = part[2 * slot] + part[2 * slot + 1];
+      named_bar_sync(1 + slot, 64);  // both have read the pair's partials before the next row's
+    }
+    const float rr = sqrtf(ss / (float)dim + eps);
+    const float inv = 1.0f / rr;
+    if (lane == 0 && sub == 0) rms[r] = rr;
+    uint4* yr = reinterpret_cast<uint4*>(y + r * dim);
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int v = (c * WPR + sub) * 32 + lane;
+      const uint4 gu = __ldg(wv + v);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[c]);
+      const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&gu);
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]), g = __bfloat1622float2(gh[j]);
+        o[j] = pack_bf16x2(f.x * inv * g.x, f.y * inv * g.y);
+      }
+      __stcs(yr + v, make_uint4(o[0], o[1], o[2], o[3]));
+    }
+  }
+}
+
 // One CTA of 256 threads per row (norm.rs:5-9 `rowwise`), grid-stride over rows.
 // VEC: 8-element vectors per thread held in registers (dim <= 256*8*VEC).
 template <typename T, int VEC>
@@ -616,6 +681,91 @@ __device__ __forceinline__ void block_sum2_256(float& a, float& b, float* red) {
 // row's reductions, so each CTA keeps a row of loads in flight while it waits at
 // the barriers.  dim % 8 == 0, dim <= 256 * 8 * VEC and 16-byte aligned pointers
 // (the host picks k_layernorm_fwd_any otherwise).
+// LayerNorm forward with WPR warps per bf16 row (norm.rs:56-73), the layout and loads of
+// k_rmsnorm_fwd_warp: the row stays in registers as bf16 and is unpacked for each of the
+// three passes (sum; sum of squared deviations from the mean; output), each reduction a
+// warp shuffle plus, for two warps per row, one exchange through shared memory.  Same
+// arithmetic as k_layernorm_fwd (biased variance about the mean).
+template <int NCH, int WPR>
+__global__ void __launch_bounds__(256, 2) k_layernorm_fwd_warp(__nv_bfloat16* __restrict__ y, float* __restrict__ mean,
+                                                               float* __restrict__ invstd,
+                                                               const __nv_bfloat16* __restrict__ x,
+                                                               const __nv_bfloat16* __restrict__ w,
+                                                               const __nv_bfloat16* __restrict__ b, long long rows,
+                                                               int dim, float eps) {
+  static_assert(WPR == 1 || WPR == 2, "one or two warps per row");
+  __shared__ float part_s[8], part_q[8];
+  const int lane = (int)(threadIdx.x & 31u), warp = (int)(threadIdx.x >> 5);
+  const int slot = warp / WPR, sub = warp % WPR;
+  constexpr int SLOTS = 8 / WPR;
+  const long long ns = (long long)gridDim.x * SLOTS;
+  const uint4* wv = reinterpret_cast<const uint4*>(w);
+  const uint4* bv = reinterpret_cast<const uint4*>(b);
+  for (long long r = (long long)blockIdx.x * SLOTS + slot; r < rows; r += ns) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + r * dim);
+    uint4 u[NCH];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) u[c] = __ldcs(xr + (c * WPR + sub) * 32 + lane);
+    float s = 0.0f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[c]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(h[k]);
+        s += f.x;
+        s += f.y;
+      }
+    }
+    s = warp_sum(s);
+    if constexpr (WPR == 2) {
+      if (lane == 0) part_s[warp] = s;
+      named_bar_sync(1 + slot, 64);
+      s = part_s[2 * slot] + part_s[2 * slot + 1];
+    }
+    const float mu = s / (float)dim;
+    float ss = 0.0f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[c]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(h[k]);
+        const float d0 = f.x - mu, d1 = f.y - mu;
+        ss = fmaf(d0, d0, ss);
+        ss = fmaf(d1, d1, ss);
+      }
+    }
+    ss = warp_sum(ss);
+    if constexpr (WPR == 2) {
+      if (lane == 0) part_q[warp] = ss;
+      named_bar_sync(1 + slot, 64);  // also: both warps have read part_s before the next row's
+      ss = part_q[2 * slot] + part_q[2 * slot + 1];
+    }
+    const float is = 1.0f / sqrtf(ss / (float)dim + eps);
+    if (lane == 0 && sub == 0) {
+      mean[r] = mu;
+      invstd[r] = is;
+    }
+    uint4* yr = reinterpret_cast<uint4*>(y + r * dim);
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int v = (c * WPR + sub) * 32 + lane;
+      const uint4 gu = __ldg(wv + v), bu = __ldg(bv + v);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[c]);
+      const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&gu);
+      const __nv_bfloat162* bh = reinterpret_cast<const __nv_bfloat162*>(&bu);
+      uint32_t o[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(h[k]), g = __bfloat1622float2(gh[k]), c2 = __bfloat1622float2(bh[k]);
+        o[k] = pack_bf16x2(fmaf((f.x - mu) * is, g.x, c2.x), fmaf((f.y - mu) * is, g.y, c2.y));
+      }
+      __stcs(yr + v, make_uint4(o[0], o[1], o[2], o[3]));
+    }
+  }
+}
+
 template <typename T, int VEC>
 __global__ void __launch_bounds__(256) k_layernorm_fwd(T* __restrict__ y, float* __restrict__ mean,
                                                        float* __restrict__ invstd, const T* __restrict__ x,

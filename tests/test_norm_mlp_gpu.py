@@ -14,8 +14,13 @@ def _ops():
     return ops
 
 
+# bf16 rows that are whole multiples of 256 up to 4096 take the warp-per-row forward: one
+# warp per row up to 2048 (17 x 256, 300 x 768, 1000 x 2048: more rows than the grid's row
+# slots), two warps per row above (64 x 4096, 513 x 3072); 70 x 2304 (nine 256-column
+# chunks, odd) and the rest take the CTA-per-row kernels.
 @pytest.mark.parametrize("T,dim,dt", [(64, 4096, "bf16"), (8, 14336, "bf16"), (33, 1000, "f32"), (16, 256, "f32"),
-                                      (5, 100, "bf16"), (64, 4096, "f32")])
+                                      (5, 100, "bf16"), (64, 4096, "f32"), (17, 256, "bf16"), (300, 768, "bf16"),
+                                      (1000, 2048, "bf16"), (513, 3072, "bf16"), (70, 2304, "bf16")])
 def test_rmsnorm(T, dim, dt):
     import torch
     ops = _ops()
@@ -33,13 +38,16 @@ def test_rmsnorm(T, dim, dt):
     assert rel_err(to_np(dg), rdg) <= tol
 
 
+# The forward of bf16 rows that are whole multiples of 256 up to 4096 (and not an odd count
+# of chunks above 8) runs one or two warps per row: (2000, 768), (1000, 256), (64, 4096),
+# (513, 3072); (70, 2304) and the rest take the CTA-per-row kernels.
 # (2000, 768): more rows than CTAs, so each CTA's dweight / dbias partials cover several rows;
 # widths up to 8192 (bf16) / 4096 (f32) take the register-resident backward, (8, 14336) the
 # one with partials in global memory; (5, 100) and (7, 20) reach the any-dim forward and the
 # scalar backward loop.
 @pytest.mark.parametrize("T,dim,dt", [(64, 4096, "bf16"), (8, 14336, "bf16"), (2000, 768, "bf16"), (40, 6144, "bf16"),
                                       (33, 1000, "f32"), (16, 256, "f32"), (5, 100, "bf16"), (7, 20, "f32"),
-                                      (64, 4096, "f32")])
+                                      (64, 4096, "f32"), (513, 3072, "bf16"), (70, 2304, "bf16"), (1000, 256, "bf16")])
 def test_layernorm(T, dim, dt):
     import torch
     ops = _ops()
