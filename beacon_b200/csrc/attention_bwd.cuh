@@ -9,8 +9,9 @@
 //                       drop-in entry, which has no O, runs the forward kernel's recompute
 //                       form (k_attn_fwd_tc<D, true>: O stays in TMEM, its epilogue writes
 //                       Dt and nlse2); given O, k_attn_bwd_prep reads it.
-//   2. k_attn_bwd_dkdv  one CTA per (128-key tile, KV head): dK and dV accumulate in TMEM
-//                       over the query tiles (and grouped query heads) that see the keys.
+//   2. k_attn_bwd_dkdv  persistent, one CTA per SM over (128-key tile, KV head) items: dK
+//                       and dV accumulate in TMEM over the query tiles (and grouped query
+//                       heads) that see the keys.
 //   3. k_attn_bwd_dq    persistent, one CTA per SM over (128-query tile, query head)
 //                       items: dQ accumulates in TMEM over the key tiles the queries
 //                       see, and is stored once in bf16.
@@ -50,7 +51,8 @@ template <int D>
 struct AttnBwdCfg {
   static constexpr uint32_t TILE_BYTES = 128 * D * 2;   // one 128-row tile of Q, K, V or dO
   static constexpr uint32_t STATS_BYTES = 2 * 128 * 4;  // lse2 and Dt of one query tile
-  // dK/dV kernel: K, V, three stages of Q (with lse2), two of dO (with Dt), barriers.  The
+  // dK/dV kernel: K, V, three stages of Q (with lse2), two of dO (with Dt), barriers and the
+  // two-slot work-item ring.  The
   // 128-byte swizzled tiles need a 1024-byte aligned base; the window is allotted only 256
   // bytes of alignment slack (the whole 227 KB is in use), and the kernel reports
   // kFaultSmemAlign and does nothing if the window's placement needs more.
@@ -83,6 +85,7 @@ enum : unsigned int {
   kSiteQDrain = 0x319,
   kSiteQQd = 0x31a,
   kSiteQItem = 0x31b,
+  kSiteBwdItem = 0x31c,
 };
 
 // ---------------------------------------------------------------------------
@@ -198,7 +201,13 @@ __device__ __forceinline__ void dq_ds_chunk(const uint32_t (&sc)[32], const uint
 }
 
 // ---------------------------------------------------------------------------
-// 2. dK / dV.  Per query tile n of the CTA's 128 keys (M=128 keys x N=128 queries):
+// 2. dK / dV.  Persistent: one CTA per SM walks work items (128-key tile, KV head), the first
+//    its block index and the next ones from the launch's work counter, published by the
+//    producer in a two-slot ring.  Query tiles are counted over all of the CTA's items (n),
+//    so the Q / dO rings, the TMEM regions and the barrier phases run on across items: the
+//    next item's K / V load once the current item's last S^T / dP^T have read K / V, and its
+//    first S^T / dP^T run while the warps write the current item's dK / dV rows.
+//    Per query tile n of the item's 128 keys (M=128 keys x N=128 queries):
 //     S^T(n)  = K Q(n)^T  -> TMEM region R_S(n)      dP^T(n) = V dO(n)^T -> region R_P(n)
 //   The two 128-column regions X = [0,128) and Y = [128,256) swap roles every tile
 //   (R_S(n) = X for even n, Y for odd n; R_P(n) is the other one), so the next tile's
@@ -217,6 +226,31 @@ __device__ __forceinline__ void dq_ds_chunk(const uint32_t (&sc)[32], const uint
 //   and dV / dK read them as the A operand from TMEM.
 // TMEM: X [0,128) | Y [128,256) | dV [256,256+D) | dK [256+D,256+2D).
 // ---------------------------------------------------------------------------
+// Work items of the persistent dK/dV kernel: (128-key tile, KV head) in the grouped head
+// order, key tile 0 (the most causal work) first.  The producer publishes them in a
+// two-slot ring in shared memory (the kernel's shared memory has no room for more).
+constexpr int kDkvItemRing = 2;
+struct DkvItem {
+  bool valid;
+  int jt, kvz, b, hk;
+  int it0, per_head, n_iter;  // first query tile, query tiles per query head, tiles of the item
+};
+__device__ __forceinline__ DkvItem dkv_item(const AttnBwdParams& p, int w) {
+  DkvItem x;
+  const int n_kvh = p.B * p.Hkv, n_kt = (p.S + 127) / 128;
+  x.valid = w < n_kt * n_kvh;
+  int jt = 0, kvz = 0;
+  if (x.valid) grouped_order(w, n_kvh, n_kt, jt, kvz);
+  x.jt = jt;
+  x.kvz = kvz;
+  x.b = kvz / p.Hkv;
+  x.hk = kvz % p.Hkv;
+  x.it0 = p.causal ? jt : 0;
+  x.per_head = n_kt - x.it0;
+  x.n_iter = x.valid ? (p.Hq / p.Hkv) * x.per_head : 0;
+  return x;
+}
+
 template <int D>
 __global__ void __launch_bounds__(384, 1)
     k_attn_bwd_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -226,8 +260,11 @@ __global__ void __launch_bounds__(384, 1)
   constexpr uint32_t TILE = Cfg::TILE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  if ((uint32_t)(smem - smem_raw) > Cfg::DKDV_SLACK) {  // uniform over the CTA: nothing has started
-    if (threadIdx.x == 0) record_fault(kFaultSmemAlign, kSiteBwdKV);
+  if ((uint32_t)(smem - smem_raw) > Cfg::DKDV_SLACK) {  // uniform over the grid: nothing has started
+    if (threadIdx.x == 0) {
+      record_fault(kFaultSmemAlign, kSiteBwdKV);
+      sched_finish(p.sched_slot);
+    }
     return;
   }
   uint8_t* sK = smem;
@@ -239,7 +276,7 @@ __global__ void __launch_bounds__(384, 1)
   float* sDt = sLse + QST * 128;                            // [2][128] Dt, with dO
   uint64_t* bars = reinterpret_cast<uint64_t*>(sDt + 2 * 128);
   constexpr int NB = D / 64;        // 64-column blocks of a tile
-  uint64_t* kv_full = bars + 0;
+  uint64_t* kv_full = bars + 0;     // an item's K and V
   // [3][2] per Q stage and column block (the last block's barrier also carries lse2): the
   // score MMAs of block 0 start while block 1 is still landing
   uint64_t* q_full = bars + 1;
@@ -251,27 +288,23 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* p_ready = bars + 16;   // P^T(n) stored by all 8 warps
   uint64_t* rp_free = bars + 17;   // dP^T(n) read by all 8 warps: R_P(n) may take S^T(n+1)
   uint64_t* ds_ready = bars + 18;  // dS^T(n) stored by all 8 warps
-  uint64_t* dkv_full = bars + 19;
+  uint64_t* dkv_full = bars + 19;  // an item's dK, dV complete in TMEM
   uint64_t* drain = bars + 20;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
+  uint64_t* kv_empty = bars + 21;  // an item's last S^T and dP^T have read K and V
+  uint64_t* item_full = bars + 22;                  // [2] item published by the producer
+  uint64_t* item_empty = item_full + kDkvItemRing;  // [2] read by the MMA warp and the 8 softmax warps
+  int* s_item = reinterpret_cast<int*>(item_empty + kDkvItemRing);  // [2] item indices
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_item + kDkvItemRing);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   constexpr uint32_t T_DV = 256, T_DK = 256 + D;
 
   const uint32_t warp = warp_id(), lane = lane_id();
-  const int n_kvh = p.B * p.Hkv;
-  // grouped head order (Q/dO tiles re-read from L2), key tile 0 (the most causal work) first
-  int jt, kvz;
-  grouped_order((int)blockIdx.x, n_kvh, (p.S + 127) / 128, jt, kvz);
-  const int b = kvz / p.Hkv, hk = kvz % p.Hkv;
   const int group = p.Hq / p.Hkv;
-  const int j0 = jt * 128;
-  const int n_q = (p.S + 127) / 128;
-  const int it0 = p.causal ? jt : 0;
-  const int iters_per_head = n_q - it0;
-  const int n_iter = group * iters_per_head;
+  const int n_items = ((p.S + 127) / 128) * p.B * p.Hkv;
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
+    mbar_init(kv_empty, 1);
     for (int i = 0; i < QST; ++i) {
       mbar_init(&q_full[2 * i], 1);
       mbar_init(&q_full[2 * i + 1], 1);
@@ -288,6 +321,10 @@ __global__ void __launch_bounds__(384, 1)
     mbar_init(ds_ready, 8);
     mbar_init(dkv_full, 1);
     mbar_init(drain, 1);
+    for (int i = 0; i < kDkvItemRing; ++i) {
+      mbar_init(&item_full[i], 1);
+      mbar_init(&item_empty[i], 9);
+    }
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -300,6 +337,17 @@ __global__ void __launch_bounds__(384, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // The ci-th item of this CTA from the ring (every role but the producer); `valid` false at
+  // the end of the CTA's work or when the wait gave up (then `ok` is cleared).
+  auto read_item = [&](int ci, bool& ok) -> DkvItem {
+    const int slot = ci % kDkvItemRing;
+    if (!mbar_wait(&item_full[slot], (uint32_t)(ci / kDkvItemRing) & 1u, abort_flag, kSiteBwdItem)) {
+      ok = false;
+      return dkv_item(p, INT32_MAX);
+    }
+    return dkv_item(p, s_item[slot]);
+  };
+
   if (warp < 4) {
     warpgroup_reg_dealloc<120>();
     if (warp == 0 && lane == 0) {
@@ -308,44 +356,65 @@ __global__ void __launch_bounds__(384, 1)
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       tma_prefetch_desc(&tmdO);
-      mbar_arrive_expect_tx(kv_full, 2 * TILE);
-      tma_load_rows<D>(sK, &tmK, kv_full, j0, kvz);
-      tma_load_rows<D>(sV, &tmV, kv_full, j0, kvz);
-      // Q (with lse2) and dO (with Dt) have rings of their own, Q three deep: Q(n+3) loads
-      // once dK(n) has read Q(n), a whole tile before S^T(n+3) needs it.
-      uint32_t qiss = 0, qpar = 0, diss = 0, dpar = 0;
+      // per item: K and V (once the previous item's last S^T and dP^T have read them), then
+      // Q (with lse2) and dO (with Dt) of its query tiles into rings that run on across
+      // items, Q three deep: Q(n+3) loads once dK(n) has read Q(n), a whole tile before
+      // S^T(n+3) needs it.  n counts query tiles over all of the CTA's items.
+      uint32_t n = 0, kviss = 0, kvpar = 0, qiss = 0, qpar = 0, diss = 0, dpar = 0;
       bool ok = true;
-      for (int n = 0; n < n_iter && ok; ++n) {
-        const int g = n / iters_per_head, it = it0 + n % iters_per_head;
-        const int bh = b * p.Hq + hk * group + g;
-        const int st = n & 1, qs = n % QST;
-        const uint32_t ph = (n >> 1) & 1, qph = (uint32_t)(n / QST) & 1u;
-        const long long srow = (long long)bh * p.S_pad + it * 128;
-        if (!mbar_wait(&q_empty[qs], qph ^ 1u, abort_flag, kSiteBwdQDEmpty)) {
+      for (int ci = 0; ok; ++ci) {
+        // fetch the CTA's next item and publish it (an index >= n_items ends every role)
+        const int w = ci == 0 ? (int)blockIdx.x : sched_fetch(p.sched_slot);
+        const int slot = ci % kDkvItemRing;
+        if (!mbar_wait(&item_empty[slot], ((uint32_t)(ci / kDkvItemRing) & 1u) ^ 1u, abort_flag, kSiteBwdItem)) {
           ok = false;
           break;
         }
+        s_item[slot] = w < n_items ? w : n_items;
+        mbar_arrive(&item_full[slot]);
+        const DkvItem x = dkv_item(p, w);
+        if (!x.valid) break;
+        if (!mbar_wait(kv_empty, ((uint32_t)ci & 1u) ^ 1u, abort_flag, kSiteBwdKV)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(kv_full, 2 * TILE);
+        tma_load_rows<D>(sK, &tmK, kv_full, x.jt * 128, x.kvz);
+        tma_load_rows<D>(sV, &tmV, kv_full, x.jt * 128, x.kvz);
+        kviss = 1;
+        kvpar = (uint32_t)ci & 1u;
+        for (int m = 0; m < x.n_iter; ++m, ++n) {
+          const int g = m / x.per_head, it = x.it0 + m % x.per_head;
+          const int bh = x.b * p.Hq + x.hk * group + g;
+          const int st = (int)(n & 1u), qs = (int)(n % QST);
+          const uint32_t ph = (n >> 1) & 1u, qph = (n / QST) & 1u;
+          const long long srow = (long long)bh * p.S_pad + it * 128;
+          if (!mbar_wait(&q_empty[qs], qph ^ 1u, abort_flag, kSiteBwdQDEmpty)) {
+            ok = false;
+            break;
+          }
 #pragma unroll
-        for (int cb = 0; cb < NB; ++cb) {
-          mbar_arrive_expect_tx(&q_full[2 * qs + cb], 128 * 128 + (cb == NB - 1 ? Cfg::STATS_BYTES / 2 : 0));
-          tma_load_3d(sQ + qs * TILE + cb * 128 * 128, &tmQ, &q_full[2 * qs + cb], cb * 64, it * 128, bh);
+          for (int cb = 0; cb < NB; ++cb) {
+            mbar_arrive_expect_tx(&q_full[2 * qs + cb], 128 * 128 + (cb == NB - 1 ? Cfg::STATS_BYTES / 2 : 0));
+            tma_load_3d(sQ + qs * TILE + cb * 128 * 128, &tmQ, &q_full[2 * qs + cb], cb * 64, it * 128, bh);
+          }
+          bulk_load(sLse + qs * 128, p.lse2 + srow, 512, &q_full[2 * qs + NB - 1]);
+          qiss |= 1u << qs;
+          qpar = (qpar & ~(1u << qs)) | (qph << qs);
+          if (!mbar_wait(&do_empty[st], ph ^ 1u, abort_flag, kSiteBwdQDEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&do_full[st], TILE + Cfg::STATS_BYTES / 2);
+          tma_load_rows<D>(sdO + st * TILE, &tmdO, &do_full[st], it * 128, bh);
+          bulk_load(sDt + st * 128, p.dt + srow, 512, &do_full[st]);
+          diss |= 1u << st;
+          dpar = (dpar & ~(1u << st)) | (ph << st);
         }
-        bulk_load(sLse + qs * 128, p.lse2 + srow, 512, &q_full[2 * qs + NB - 1]);
-        qiss |= 1u << qs;
-        qpar = (qpar & ~(1u << qs)) | (qph << qs);
-        if (!mbar_wait(&do_empty[st], ph ^ 1u, abort_flag, kSiteBwdQDEmpty)) {
-          ok = false;
-          break;
-        }
-        mbar_arrive_expect_tx(&do_full[st], TILE + Cfg::STATS_BYTES / 2);
-        tma_load_rows<D>(sdO + st * TILE, &tmdO, &do_full[st], it * 128, bh);
-        bulk_load(sDt + st * 128, p.dt + srow, 512, &do_full[st]);
-        diss |= 1u << st;
-        dpar = (dpar & ~(1u << st)) | (ph << st);
       }
       if (!ok) {
         volatile int no_abort = 0;
-        mbar_wait(kv_full, 0, &no_abort, kSiteBwdDrain);
+        if (kviss) mbar_wait(kv_full, kvpar, &no_abort, kSiteBwdDrain);
         for (int s = 0; s < QST; ++s)
           if (qiss & (1u << s))
             for (int cb = 0; cb < NB; ++cb) mbar_wait(&q_full[2 * s + cb], (qpar >> s) & 1u, &no_abort, kSiteBwdDrain);
@@ -385,37 +454,60 @@ __global__ void __launch_bounds__(384, 1)
         }
         return true;
       };
-      bool ok = warp_wait(kv_full, 0, abort_flag, kSiteBwdKV);
-      if (ok && n_iter > 0) {
-        if (!issue_st(0, 0, 0) || !warp_wait(&do_full[0], 0, abort_flag, kSiteBwdQDFull)) {
+      bool ok = true;
+      // Tile cursors over the CTA's whole sequence of query tiles: `cur` is tile n, `nxt`
+      // tile n + 1, possibly the first of the next item (read from the ring).
+      int cur_ci = 0, cur_m = 0, nxt_ci = 0, nxt_m = 0;
+      DkvItem cur = read_item(0, ok), nxt;
+      auto advance = [&]() {  // nxt := the tile after cur
+        nxt_ci = cur_ci;
+        nxt_m = cur_m + 1;
+        nxt = cur;
+        if (nxt_m >= cur.n_iter) {
+          nxt_ci = cur_ci + 1;
+          nxt_m = 0;
+          nxt = read_item(nxt_ci, ok);
+        }
+      };
+      cur.valid = __all_sync(0xffffffffu, cur.valid && ok);
+      if (cur.valid) {
+        if (!warp_wait(kv_full, 0, abort_flag, kSiteBwdKV) || !issue_st(0, 0, 0) ||
+            !warp_wait(&do_full[0], 0, abort_flag, kSiteBwdQDFull)) {
           ok = false;
         } else {
           tc_fence_after();
           if (leader) umma_commit(s_full);
           issue_score_tile<D>(leader, tmem + 128, v_desc, do_desc);
           if (leader) umma_commit(dp_full);
+          if (cur.n_iter == 1 && leader) umma_commit(kv_empty);  // the item's last S^T / dP^T issued
+          advance();
         }
       }
-      for (int n = 0; n < n_iter && ok; ++n) {
-        const int st = n & 1, st1 = (n + 1) & 1;
-        const uint32_t par = (uint32_t)n & 1u;
-        const bool more = n + 1 < n_iter;
-        const uint32_t rs = (n & 1) ? 128u : 0u, rp = 128u - rs;  // R_S(n), R_P(n)
-        const int qs = n % QST, qs1 = (n + 1) % QST;
+      for (uint32_t n = 0; cur.valid && ok; ++n) {
+        const int st = (int)(n & 1u), st1 = (int)((n + 1) & 1u);
+        const uint32_t par = n & 1u;
+        const bool more = __all_sync(0xffffffffu, nxt.valid);
+        const bool first = cur_m == 0;  // the item's first tile: dV and dK start afresh
+        const bool last = cur_m == cur.n_iter - 1;
+        const uint32_t rs = (n & 1u) ? 128u : 0u, rp = 128u - rs;  // R_S(n), R_P(n)
+        const int qs = (int)(n % QST), qs1 = (int)((n + 1) % QST);
         const uint64_t q_mn = sdesc_adv(q_desc_mn, qs * TILE), do_mn = sdesc_adv(do_desc_mn, st * TILE);
         // dV(n) as soon as P^T(n) is stored (the warps then wait for dP^T(n) and read it);
         // S^T(n+1) as soon as R_P(n) is free (the warps' next P phase waits for it); dK(n)
         // and dP^T(n+1) once dS^T(n) is stored, so dP^T(n+1) is done early in the next P phase.
         // (dV(n) in two halves around S^T(n+1): the issuing warp, which blocks while the
-        // tensor pipe's queue is full, gets to S^T(n+1) sooner.  The tensor pipe queues about
-        // five MMAs; S^T(n+1) before all of dV(n) measured 7% slower, and moving a quarter
-        // to a half of the exponentials to the FMA pipe made no difference.)
+        // tensor pipe's queue is full, gets to S^T(n+1) sooner.)  Tile n+1 may be the next
+        // item's first: its S^T / dP^T read the next item's K / V, which load once this
+        // item's last S^T / dP^T have read K / V, and run while the warps write this item's
+        // dK / dV; its dV / dK MMAs, which start the accumulators afresh, wait for P^T / dS^T,
+        // which the warps store only after those rows have left TMEM.
         if (!warp_wait(p_ready, par, abort_flag, kSiteBwdDsFull)) break;
         tc_fence_after();
-        issue_kv(T_DV, rs, do_mn, n == 0, 0, 4);
+        issue_kv(T_DV, rs, do_mn, first, 0, 4);
         if (!warp_wait(rp_free, par, abort_flag, kSiteBwdDsFull)) break;
         if (more) {
-          if (!issue_st(rp, qs1, (uint32_t)((n + 1) / QST) & 1u)) break;
+          if (nxt_m == 0 && !warp_wait(kv_full, (uint32_t)nxt_ci & 1u, abort_flag, kSiteBwdKV)) break;
+          if (!issue_st(rp, qs1, ((n + 1) / QST) & 1u)) break;
           if (leader) umma_commit(s_full);
         }
         issue_kv(T_DV, rs, do_mn, false, 4, 8);
@@ -424,15 +516,22 @@ __global__ void __launch_bounds__(384, 1)
         // dO(n) read by dP^T(n) and dV(n), and Dt(n), which shares its stage, by the warps'
         // dS phase: the stage may take dO(n+2)
         if (leader) umma_commit(&do_empty[st]);
-        issue_kv(T_DK, rs + 32, q_mn, n == 0);
+        issue_kv(T_DK, rs + 32, q_mn, first);
         if (leader) umma_commit(&q_empty[qs]);  // Q(n) read by S^T(n) and dK(n)
+        if (last && leader) umma_commit(dkv_full);
         if (more) {  // into R_S(n), behind dV(n) and dK(n), which read P^T / dS^T(n) from it
-          if (!warp_wait(&do_full[st1], ((n + 1) >> 1) & 1, abort_flag, kSiteBwdQDFull)) break;
+          if (!warp_wait(&do_full[st1], ((n + 1) >> 1) & 1u, abort_flag, kSiteBwdQDFull)) break;
           tc_fence_after();
           issue_score_tile<D>(leader, tmem + rs, v_desc, sdesc_adv(do_desc, st1 * TILE));
           if (leader) umma_commit(dp_full);
+          if (nxt_m == nxt.n_iter - 1 && leader) umma_commit(kv_empty);  // that item's last S^T / dP^T
         }
-        if (!more && leader) umma_commit(dkv_full);
+        if (last && leader) mbar_arrive(&item_empty[cur_ci % kDkvItemRing]);
+        if (!more) break;
+        cur = nxt;
+        cur_ci = nxt_ci;
+        cur_m = nxt_m;
+        advance();
       }
       if (leader) umma_commit(drain);
       volatile int no_abort = 0;
@@ -444,122 +543,134 @@ __global__ void __launch_bounds__(384, 1)
     const uint32_t quarter = warp & 3u;
     const int g = (int)(warp - 4) >> 2;        // 64-query group / dV or dK (epilogue)
     const int r = (int)(quarter * 32 + lane);  // TMEM lane = key row
-    const int kj = j0 + r;
     const uint32_t lane_base = (quarter * 32u) << 16;
-    const bool key_ok = kj < p.S;
-    const bool keys_full = j0 + 128 <= p.S;
     bool ok = true;
-    for (int n = 0; n < n_iter && ok; ++n) {
-      const int it = it0 + n % iters_per_head;
-      const int q0 = it * 128;
-      const int st = n & 1;
-      const uint32_t par = (uint32_t)n & 1u;
-      const uint32_t rs = (n & 1) ? 128u : 0u, rp = 128u - rs;
-      // off-diagonal tiles need no mask: every key < S and every query >= every key
-      const bool masked = !keys_full || (p.causal && it == jt);
-      const int qmin = p.causal ? kj - q0 : -1;
-      const int qs = n % QST;
-      const uint32_t lse2_addr = smem_u32(sLse + qs * 128 + 64 * g), dt_addr = smem_u32(sDt + st * 128 + 64 * g);
-      // first of this warp's 64 query columns that the key sees (64: none)
-      const int first_ok = key_ok ? max(qmin - 64 * g, 0) : 64;
-      // s_full: the scores; q_full: makes the TMA-written lse2 visible to this thread
-      if (!__all_sync(0xffffffffu, mbar_wait(s_full, par, abort_flag, kSiteBwdStFull) &&
-                                       mbar_wait(&q_full[2 * qs + NB - 1], (uint32_t)(n / QST) & 1u, abort_flag,
-                                                 kSiteBwdQDFull))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t cs = rs + 64 * g;  // this warp's 64 S^T columns
-      float pe[64];
-      {
-        uint32_t sv[64];
-        tmem_ld32(tmem + lane_base + cs, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-        tmem_ld32(tmem + lane_base + cs + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-        tmem_wait_ld();
-        if (masked)
-          bwd_p_cols<true>(sv, lse2_addr, p.scale_log2, first_ok, pe);
-        else
-          bwd_p_cols<false>(sv, lse2_addr, p.scale_log2, first_ok, pe);
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) pk[i] = pack_bf16x2(pe[2 * i], pe[2 * i + 1]);
-        tmem_st32(tmem + lane_base + cs, pk);  // P^T over the S^T columns just read
-      }
-      tmem_wait_st();
-      tc_fence_before();
+    uint32_t n = 0;  // query tiles over all of the CTA's items
+    for (int ci = 0; ok; ++ci) {
+      const DkvItem x = read_item(ci, ok);
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_ready);
-      // dp_full: dP^T(n); do_full: makes the TMA-written Dt visible to this thread
-      if (!__all_sync(0xffffffffu, mbar_wait(dp_full, par, abort_flag, kSiteBwdStFull) &&
-                                       mbar_wait(&do_full[st], (n >> 1) & 1, abort_flag, kSiteBwdQDFull))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t dpv[64];
-      tmem_ld32(tmem + lane_base + rp + 64 * g, *reinterpret_cast<uint32_t(*)[32]>(&dpv[0]));
-      tmem_ld32(tmem + lane_base + rp + 64 * g + 32, *reinterpret_cast<uint32_t(*)[32]>(&dpv[32]));
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(rp_free);  // R_P(n) may take S^T(n+1)
-      uint32_t dk[32];
-#pragma unroll
-      for (int e4 = 0; e4 < 16; ++e4) {
-        const float4 d4 = lds_f4(dt_addr + 16 * e4);
-        const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
-#pragma unroll
-        for (int u = 0; u < 4; u += 2) {
-          const int e = 4 * e4 + u;
-          float t0, t1, d0, d1;
-          fma2(t0, t1, dv[u], dv[u + 1], -1.0f, -1.0f, __uint_as_float(dpv[e]), __uint_as_float(dpv[e + 1]));
-          mul2(d0, d1, pe[e], pe[e + 1], t0, t1);
-          dk[e >> 1] = pack_bf16x2(d0, d1);
+      if (lane == 0) mbar_arrive(&item_empty[ci % kDkvItemRing]);
+      if (!__all_sync(0xffffffffu, ok && x.valid)) break;
+      const int j0 = x.jt * 128;
+      const int kj = j0 + r;
+      const bool key_ok = kj < p.S;
+      const bool keys_full = j0 + 128 <= p.S;
+      for (int m = 0; m < x.n_iter && ok; ++m, ++n) {
+        const int it = x.it0 + m % x.per_head;
+        const int q0 = it * 128;
+        const int st = (int)(n & 1u);
+        const uint32_t par = n & 1u;
+        const uint32_t rs = (n & 1u) ? 128u : 0u, rp = 128u - rs;
+        // off-diagonal tiles need no mask: every key < S and every query >= every key
+        const bool masked = !keys_full || (p.causal && it == x.jt);
+        const int qmin = p.causal ? kj - q0 : -1;
+        const int qs = (int)(n % QST);
+        const uint32_t lse2_addr = smem_u32(sLse + qs * 128 + 64 * g), dt_addr = smem_u32(sDt + st * 128 + 64 * g);
+        // first of this warp's 64 query columns that the key sees (64: none)
+        const int first_ok = key_ok ? max(qmin - 64 * g, 0) : 64;
+        // s_full: the scores; q_full: makes the TMA-written lse2 visible to this thread
+        if (!__all_sync(0xffffffffu, mbar_wait(s_full, par, abort_flag, kSiteBwdStFull) &&
+                                         mbar_wait(&q_full[2 * qs + NB - 1], (n / QST) & 1u, abort_flag,
+                                                   kSiteBwdQDFull))) {
+          ok = false;
+          break;
         }
+        tc_fence_after();
+        const uint32_t cs = rs + 64 * g;  // this warp's 64 S^T columns
+        float pe[64];
+        {
+          uint32_t sv[64];
+          tmem_ld32(tmem + lane_base + cs, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+          tmem_ld32(tmem + lane_base + cs + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+          tmem_wait_ld();
+          if (masked)
+            bwd_p_cols<true>(sv, lse2_addr, p.scale_log2, first_ok, pe);
+          else
+            bwd_p_cols<false>(sv, lse2_addr, p.scale_log2, first_ok, pe);
+          uint32_t pk[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) pk[i] = pack_bf16x2(pe[2 * i], pe[2 * i + 1]);
+          tmem_st32(tmem + lane_base + cs, pk);  // P^T over the S^T columns just read
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_ready);
+        // dp_full: dP^T(n); do_full: makes the TMA-written Dt visible to this thread
+        if (!__all_sync(0xffffffffu, mbar_wait(dp_full, par, abort_flag, kSiteBwdStFull) &&
+                                         mbar_wait(&do_full[st], (n >> 1) & 1u, abort_flag, kSiteBwdQDFull))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t dpv[64];
+        tmem_ld32(tmem + lane_base + rp + 64 * g, *reinterpret_cast<uint32_t(*)[32]>(&dpv[0]));
+        tmem_ld32(tmem + lane_base + rp + 64 * g + 32, *reinterpret_cast<uint32_t(*)[32]>(&dpv[32]));
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(rp_free);  // R_P(n) may take S^T(n+1)
+        uint32_t dk[32];
+#pragma unroll
+        for (int e4 = 0; e4 < 16; ++e4) {
+          const float4 d4 = lds_f4(dt_addr + 16 * e4);
+          const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+          for (int u = 0; u < 4; u += 2) {
+            const int e = 4 * e4 + u;
+            float t0, t1, d0, d1;
+            fma2(t0, t1, dv[u], dv[u + 1], -1.0f, -1.0f, __uint_as_float(dpv[e]), __uint_as_float(dpv[e + 1]));
+            mul2(d0, d1, pe[e], pe[e + 1], t0, t1);
+            dk[e >> 1] = pack_bf16x2(d0, d1);
+          }
+        }
+        tmem_st32(tmem + lane_base + cs + 32, dk);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ds_ready);
       }
-      tmem_st32(tmem + lane_base + cs + 32, dk);
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(ds_ready);
-    }
-    // final dV (g = 0) / dK (g = 1) rows, staged in the idle Q ring (272-byte row stride:
-    // conflict-free 16-byte stores) and written with one 256-byte bulk copy per row.
-    // Stored straight from registers, a warp's 16-byte stores hit 32 rows 256 bytes apart,
-    // half a sector each, and the epilogue took ~5k cycles per CTA.
-    if (ok && __all_sync(0xffffffffu, mbar_wait(dkv_full, 0, abort_flag, kSiteBwdDkvFull))) {
+      if (!ok) break;
+      // the item's dV (g = 0) / dK (g = 1) rows, 32-byte stores where the output allows (each
+      // a whole sector of the row); the MMA warp meanwhile runs the next item's first S^T and
+      // dP^T, and these warps store its first P^T only after the rows have left TMEM
+      if (!__all_sync(0xffffffffu, mbar_wait(dkv_full, (uint32_t)ci & 1u, abort_flag, kSiteBwdDkvFull))) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
-      constexpr uint32_t kRowStage = D * 2 + 16;
-      uint8_t* srow = sQ + (uint32_t)g * 128u * kRowStage + (uint32_t)r * kRowStage;
       const float sc = g == 0 ? 1.0f : p.scale;
       const uint32_t col = g == 0 ? T_DV : T_DK;
+      __nv_bfloat16* orow = (g == 0 ? p.dv : p.dk) + ((long long)x.kvz * p.S + (key_ok ? kj : 0)) * D;
+      const bool o32 = (reinterpret_cast<uintptr_t>(g == 0 ? p.dv : p.dk) & 31u) == 0;
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         uint32_t a[32];
         tmem_ld32(tmem + lane_base + col + c * 32, a);
         tmem_wait_ld();
+        if (key_ok) {
 #pragma unroll
-        for (int e = 0; e < 32; e += 8) {
-          uint4 w;
-          w.x = pack_bf16x2(__uint_as_float(a[e + 0]) * sc, __uint_as_float(a[e + 1]) * sc);
-          w.y = pack_bf16x2(__uint_as_float(a[e + 2]) * sc, __uint_as_float(a[e + 3]) * sc);
-          w.z = pack_bf16x2(__uint_as_float(a[e + 4]) * sc, __uint_as_float(a[e + 5]) * sc);
-          w.w = pack_bf16x2(__uint_as_float(a[e + 6]) * sc, __uint_as_float(a[e + 7]) * sc);
-          *reinterpret_cast<uint4*>(srow + (c * 32 + e) * 2) = w;
+          for (int e = 0; e < 32; e += 16) {
+            uint32_t wv[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              wv[i] = pack_bf16x2(__uint_as_float(a[e + 2 * i]) * sc, __uint_as_float(a[e + 2 * i + 1]) * sc);
+            if (o32) {
+              stg256(orow + c * 32 + e, wv[0], wv[1], wv[2], wv[3], wv[4], wv[5], wv[6], wv[7]);
+            } else {  // only 16-byte aligned
+              *reinterpret_cast<uint4*>(orow + c * 32 + e) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+              *reinterpret_cast<uint4*>(orow + c * 32 + e + 8) = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+            }
+          }
         }
       }
-      fence_proxy_async_smem();  // generic-proxy stores -> the bulk copy's async proxy
-      if (key_ok) {
-        bulk_store((g == 0 ? p.dv : p.dk) + ((long long)kvz * p.S + kj) * D, srow, D * 2);
-        bulk_commit_group();
-        bulk_wait_group_read0();  // the stage must outlive the copy's reads
-      }
+      tc_fence_before();
     }
   }
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) sched_finish(p.sched_slot);  // every fetch of this CTA is done
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::TMEM_COLS);
