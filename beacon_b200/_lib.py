@@ -33,7 +33,7 @@ EXPORTS = (
     "beacon_version", "beacon_last_error", "beacon_device_status", "beacon_launch_count",
     "beacon_diag_wait_timeout", "beacon_diag_exp2_poly",
     "beacon_profile_enable", "beacon_profile_read",
-    "beacon_matmul_fwd", "beacon_matmul_bwd", "beacon_linear_fwd", "beacon_linear_bwd",
+    "beacon_matmul_plan", "beacon_matmul_fwd", "beacon_matmul_bwd", "beacon_linear_fwd", "beacon_linear_bwd",
     "beacon_matmul_fp8w_fwd", "beacon_linear_fp8w_fwd", "beacon_linear_fp8w_fwd_devscale",
     "beacon_quantize_fp8e4m3",
     "beacon_attention_adjoint_fwd", "beacon_attention_adjoint_bwd", "beacon_attention_bwd_workspace_size",
@@ -96,6 +96,7 @@ def lib():
     _sig(L, "beacon_profile_enable", None, [_int])
     _sig(L, "beacon_profile_read", _int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_double),
                                           ctypes.POINTER(ctypes.c_uint64)])
+    _sig(L, "beacon_matmul_plan", _int, [_i64, _i64, _i64, ctypes.POINTER(ctypes.c_int32)])
     _sig(L, "beacon_matmul_fwd", _int, [_vp, _vp, _vp, _i64, _i64, _i64, _int, _vp])
     _sig(L, "beacon_matmul_bwd", _int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp])
     _sig(L, "beacon_linear_fwd", _int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp])

@@ -394,6 +394,45 @@ int choose_bn(int64_t M, int64_t Nout, bool swiglu, int sms) {
   return best;
 }
 
+// The tile shape of a bf16 GEMM: 2-SM pair tiles of 256 x pair_bn, or (pair_bn = 0) 1-SM
+// tiles of 128 x bn.
+struct GemmPlan {
+  int pair_bn = 0, bn = 0;
+};
+GemmPlan gemm_plan(int64_t M, int64_t N, bool swiglu, int sms, int force_bn) {
+  // 2-SM pair tiles halve each SM's operand stream; they win whenever their wave
+  // efficiency is close to the best 1-SM tile's.  Per SM and 64-deep K step a 128x128 1-SM
+  // tile needs 32 KB for 71-cycle MMAs, more than TMA delivers to one SM (measured ~58 B per
+  // clock in that kernel); a 256x128 pair tile needs 24 KB and a 256x256 one 32 KB for MMAs
+  // twice as long.  Scores: wave efficiency x the rows the tiles cover (M padded to 128 or
+  // 256 rows) x a per-shape credit.
+  GemmPlan plan;
+  {
+    const int ov = gemm_path_override();
+    const double rows1 = (double)M / (double)(((M + 127) / 128) * 128);
+    const double rows2 = (double)M / (double)(((M + 255) / 256) * 256);
+    const int64_t cols2 = swiglu ? 128 : 256;
+    const int64_t tiles2 = ((M + 255) / 256) * ((N + cols2 - 1) / cols2);
+    const double score2 = wave_eff(tiles2, sms / 2) * rows2 * 1.15;
+    const int64_t tiles2n = ((M + 255) / 256) * ((N + 127) / 128);
+    const double score2n = swiglu ? 0.0 : wave_eff(tiles2n, sms / 2) * rows2 * 0.97;
+    const int bn1 = choose_bn(M, N, swiglu, sms);
+    const int64_t c1 = swiglu ? bn1 / 2 : bn1;
+    const double cost1 = bn1 == 256 ? 1.0 : bn1 == 128 ? 0.93 : 0.80;
+    const double score1 = wave_eff(((M + 127) / 128) * ((N + c1 - 1) / c1), sms) * rows1 * cost1;
+    if (ov == 2 || (ov == 3 && swiglu)) {
+      plan.pair_bn = 256;
+    } else if (ov == 3) {
+      plan.pair_bn = 128;
+    } else if (ov == 0 && !force_bn) {
+      if (score2 > score1 && score2 >= score2n) plan.pair_bn = 256;
+      else if (score2n > score1) plan.pair_bn = 128;
+    }
+    plan.bn = plan.pair_bn ? plan.pair_bn : (force_bn ? force_bn : bn1);
+  }
+  return plan;
+}
+
 // C[M,N] = A . B (+ epilogue) with bf16 operands.  `B2` is the up-projection for the tile-pair
 // (SwiGLU) epilogues, or the second K range of B when p.k_split > 0 (C = A . [B ; B2]).
 int gemm_bf16(const Operand& A, const Operand& B, const Operand* B2, GemmParams p, cudaStream_t st, int force_bn = 0) {
@@ -419,35 +458,7 @@ int gemm_bf16(const Operand& A, const Operand& B, const Operand* B2, GemmParams 
                                             reinterpret_cast<const bf16*>(B.ptr), sbk, sbn, p);
     return check_launch("k_gemm_simt<bf16>");
   }
-  // 2-SM pair tiles halve each SM's operand stream; they win whenever their wave
-  // efficiency is close to the best 1-SM tile's.  Per SM and 64-deep K step a 128x128 1-SM
-  // tile needs 32 KB for 71-cycle MMAs, more than TMA delivers to one SM (measured ~58 B per
-  // clock in that kernel); a 256x128 pair tile needs 24 KB and a 256x256 one 32 KB for MMAs
-  // twice as long.  Scores: wave efficiency x the rows the tiles cover (M padded to 128 or
-  // 256 rows) x a per-shape credit.
-  int pair_bn = 0;  // 0: 1-SM tiles
-  {
-    const int ov = gemm_path_override();
-    const double rows1 = (double)p.M / (double)(((p.M + 127) / 128) * 128);
-    const double rows2 = (double)p.M / (double)(((p.M + 255) / 256) * 256);
-    const int64_t cols2 = swiglu ? 128 : 256;
-    const int64_t tiles2 = ((p.M + 255) / 256) * ((p.N + cols2 - 1) / cols2);
-    const double score2 = wave_eff(tiles2, di->sms / 2) * rows2 * 1.15;
-    const int64_t tiles2n = ((p.M + 255) / 256) * ((p.N + 127) / 128);
-    const double score2n = swiglu ? 0.0 : wave_eff(tiles2n, di->sms / 2) * rows2 * 0.97;
-    const int bn1 = choose_bn(p.M, p.N, swiglu, di->sms);
-    const int64_t c1 = swiglu ? bn1 / 2 : bn1;
-    const double cost1 = bn1 == 256 ? 1.0 : bn1 == 128 ? 0.93 : 0.80;
-    const double score1 = wave_eff(((p.M + 127) / 128) * ((p.N + c1 - 1) / c1), di->sms) * rows1 * cost1;
-    if (ov == 2 || (ov == 3 && swiglu)) {
-      pair_bn = 256;
-    } else if (ov == 3) {
-      pair_bn = 128;
-    } else if (ov == 0 && !force_bn) {
-      if (score2 > score1 && score2 >= score2n) pair_bn = 256;
-      else if (score2n > score1) pair_bn = 128;
-    }
-  }
+  const int pair_bn = gemm_plan(p.M, p.N, swiglu, di->sms, force_bn).pair_bn;  // 0: 1-SM tiles
   if (pair_bn) {
     p.tiles_m = (p.M + 255) / 256;
     p.tiles_n = swiglu ? (p.N + 127) / 128 : (p.N + pair_bn - 1) / pair_bn;
@@ -796,6 +807,24 @@ extern "C" int beacon_quantize_fp8e4m3(void* out_fp8, float* scale, float* amax,
   k_quantize_fp8<<<grid_for(std::max<int64_t>(n, 1), 256, di->sms), 256, 0, st>>>(
       reinterpret_cast<uint8_t*>(out_fp8), scale, amax, src, n);
   return check_launch("k_quantize_fp8");
+}
+
+extern "C" int beacon_matmul_plan(int64_t m, int64_t k, int64_t n, int32_t* out) {
+  if (!out) return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "matmul_plan: null output");
+  if (m <= 0 || n <= 0 || k < 0 || m > INT32_MAX || n > INT32_MAX)
+    return fail(BEACON_ERR_INVALID_LAUNCH_CONFIG, "matmul_plan: bad shape m=%lld k=%lld n=%lld", (long long)m,
+                (long long)k, (long long)n);
+  int dev;
+  DeviceInfo* di;
+  BEACON_TRY(current_device(&dev, &di));
+  const GemmPlan pl = gemm_plan(m, n, false, di->sms, 0);
+  const int64_t tm = pl.pair_bn ? 256 : 128, tn = pl.pair_bn ? pl.pair_bn : pl.bn;
+  out[0] = (int32_t)tm;
+  out[1] = (int32_t)tn;
+  out[2] = (int32_t)(((m + tm - 1) / tm) * ((n + tn - 1) / tn));
+  out[3] = pl.pair_bn ? 2 : 1;
+  out[4] = di->sms;
+  return BEACON_OK;
 }
 
 extern "C" int beacon_matmul_fwd(void* out, const void* lhs, const void* rhs, int64_t m, int64_t k, int64_t n,

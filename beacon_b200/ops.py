@@ -45,6 +45,18 @@ def _dtype(*ts) -> int:
 
 # ---------------------------------------------------------------- matmul / linear
 
+def matmul_plan(m, k, n):
+    """The bf16 GEMM's tile shape for [m, k] x [k, n] on the current device, with its wave
+    efficiency: {tile_m, tile_n, tiles, sms_per_tile, sms, wave_efficiency}."""
+    out = (ctypes.c_int32 * 5)()
+    check(_lib.lib().beacon_matmul_plan(m, k, n, out))
+    tile_m, tile_n, tiles, per, sms = (int(v) for v in out)
+    slots = max(sms // per, 1)
+    waves = -(-tiles // slots)
+    return {"tile_m": tile_m, "tile_n": tile_n, "tiles": tiles, "sms_per_tile": per, "sms": sms,
+            "wave_efficiency": tiles / (waves * slots)}
+
+
 def matmul_fwd(lhs, rhs, out=None):
     """out[m,n] = lhs[m,k] . rhs[k,n]  (matmul.rs:18-29)."""
     m, k = lhs.shape

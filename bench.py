@@ -22,7 +22,9 @@ Also reported on the same JSON line:
   "block":     one pre-norm Llama block forward (batch 4 x seq 2048, d_model 4096,
                32 x 128 heads, SwiGLU hidden 14336), one replica per rank;
   "gqa":       long-context grouped-query causal forward (64 query heads, 8 KV heads,
-               S=32768, D=128), KV groups sharded across ranks.
+               S=32768, D=128), KV groups sharded across ranks;
+  "block_backward": the backward operators at the block's shapes (SwiGLU MLP, the QKV
+               linear, RMSNorm), one replica per rank.
 
 After timing, rank 0 checks the timed runs' outputs against the oracle (the CPU
 restatement of the path, used here only as the checker): sampled heads of the
@@ -68,7 +70,7 @@ DKDV_FLOPS = 2.0 * FWD_FLOPS
 DQ_FLOPS = 1.5 * FWD_FLOPS
 # k_attn_bwd_dkdv DRAM traffic per launch from the ncu capture summarised in
 # profiles/k_attn_bwd_dkdv_h32s4096.md (B*H=32 heads captured, scaled by the head count).
-DKDV_TRAFFIC_PER_HEAD = (135.5e6 + 39.7e6) / 32
+DKDV_TRAFFIC_PER_HEAD = (135.5e6 + 39.3e6) / 32
 
 # pre-norm Llama block forward
 BLK_B, BLK_S, BLK_DM, BLK_H, BLK_D, BLK_F = 4, 2048, 4096, 32, 128, 14336
@@ -254,7 +256,7 @@ def run_reference(args, rank, world):
 
 # --------------------------------------------------------------------------- inputs and checks
 
-ATTN_SEED, GEMM_SEED, BLOCK_SEED, GQA_SEED = 2, 1, 3, 4
+ATTN_SEED, GEMM_SEED, BLOCK_SEED, GQA_SEED, BLOCK_BWD_SEED = 2, 1, 3, 4, 5
 CHECK_TOL = 2e-2  # bf16 inputs, fp32 accumulation, gradients included (norm-wise)
 
 
@@ -506,7 +508,10 @@ def run_beacon(args, rank, world, local):
         gt = 2.0 * GEMM_N ** 3 / (gms * 1e-3) / 1e12
         gemm = {"value": gt, "unit": "TFLOP/s", "ms": gms, "frac_of_burst_peak": gt / burst / world,
                 "config": f"bf16 {GEMM_N}^3, B columns sharded {world}-way, L2 flushed between iterations",
-                "per_gpu_tflops": gt / world}
+                "per_gpu_tflops": gt / world,
+                # the shard's tile shape as the library chose it: at 8 ranks the 4096 x 512 shard
+                # has too few tiles to fill the SMs, and the launch's fixed cost weighs more
+                "shard_plan": dict(ops.matmul_plan(GEMM_N, GEMM_N, ncols), shard=[GEMM_N, ncols, GEMM_N])}
         # 16 sampled rows of C: every rank's column block gathered to rank 0
         rows = torch.arange(0, GEMM_N, GEMM_N // 16, device=dev)
         c_rows = gather_rows(c[rows].t().contiguous(), world).t()  # [16, GEMM_N]
@@ -542,13 +547,15 @@ def run_beacon(args, rank, world, local):
 
     block, check_block = (None, None) if args.no_block else bench_block(args, rank, world, dev, stream)
     gqa, check_gqa = (None, None) if args.no_gqa else bench_gqa(args, rank, world, dev, stream)
+    block_bwd, check_block_bwd = (None, None) if args.no_block else bench_block_bwd(args, rank, world, dev, stream)
 
     if rank != 0:
         return
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         cpu, _ = cpu_attention_sample()
-    checks = {"attention": check_attn, "gemm": check_gemm, "gqa": check_gqa, "block": check_block}
+    checks = {"attention": check_attn, "gemm": check_gemm, "gqa": check_gqa, "block": check_block,
+              "block_backward": check_block_bwd}
     worst = 0.0
     for c in checks.values():
         if c:
@@ -561,7 +568,7 @@ def run_beacon(args, rank, world, local):
             "config": CONFIG, "frac_of_peak": value / (burst * world),
             "frac_of_sustained_peak": value / (sustained * world),
             "roofline": roofline, "max_rel_err": max_rel_err, "cpu_baseline": cpu, "e2e": e2e,
-            "with_out": with_out, "gemm": gemm, "block": block, "gqa": gqa,
+            "with_out": with_out, "gemm": gemm, "block": block, "block_backward": block_bwd, "gqa": gqa,
             "clocks": clk, "gpu_launches": int(n_launch), "impl": "beacon"}
     print(json.dumps(line), flush=True)
 
@@ -611,14 +618,15 @@ def bench_block(args, rank, world, dev, stream):
         ops.llama_block_fwd_folded(x, wqkv_f, wo, wg_f, wu_f, wd, BLK_B, BLK_S, BLK_H, BLK_H, out=out_f,
                                    workspace=ws)
 
-    # the two forms alternate over three rounds and each keeps its fastest round: under the
-    # 1 kW power cap the clock drifts by 10-20% over a few seconds, more than the forms differ
+    # the two forms alternate over four rounds, each round in the other order, and each keeps
+    # its fastest round: under the 1 kW power cap the clock drifts by 10-20% over a few
+    # seconds, more than the forms differ
     iters = max(10, args.steps // 2)
     barrier(world)
     t_un, t_fo = [], []
-    for _ in range(3):
-        t_un.append(_time_calls(fn, stream, iters, 2))
-        t_fo.append(_time_calls(fn_folded, stream, iters, 2))
+    for i in range(4):
+        for f in ((fn, fn_folded) if i % 2 == 0 else (fn_folded, fn)):
+            (t_un if f is fn else t_fo).append(_time_calls(f, stream, iters, 2))
     ms = max_over_ranks(min(t_un), world)
     ms_f = max_over_ranks(min(t_fo), world)
     torch.cuda.synchronize()
@@ -646,6 +654,83 @@ def bench_block(args, rank, world, dev, stream):
             "api": "beacon_llama_block_fwd_folded (RMSNorms folded into the GEMMs: 6 launches + a memset)",
             "unfused": {"ms": ms, "per_gpu_tflops": BLK_FLOPS / (ms * 1e-3) / 1e12,
                         "api": "beacon_llama_block_fwd (RMSNorm kernels write normalised rows: 7 launches)"}}, check
+
+
+def bench_block_bwd(args, rank, world, dev, stream):
+    """The backward operators at the block's shapes, one replica per rank: swiglu_bwd
+    (mlp.rs:31-52), linear_bwd of the QKV projection (matmul.rs:60-78) and rmsnorm_bwd
+    (norm.rs:33-50) at tokens 8192, d_model 4096, SwiGLU hidden 14336, QKV width 12288.
+    Algorithmic FLOPs: the SwiGLU backward 12 T d F (dWd, dh, dWg, dWu, dx; its recompute of
+    gate and up is not counted), the linear backward 4 T d N; the RMSNorm backward is
+    reported in GB/s of x, dy read and dx written."""
+    import torch
+    from beacon_b200 import ops
+    from beacon_b200.shard import unit_generator
+    T, dm, F, N = BLK_T, BLK_DM, BLK_F, 3 * BLK_H * BLK_D
+
+    def w(unit, *shape, std=0.02):
+        return (torch.randn(*shape, generator=unit_generator(BLOCK_BWD_SEED, unit, dev), device=dev) * std
+                ).to(torch.bfloat16)
+
+    x, dy = w(0, T, dm, std=1.0), w(1, T, dm, std=1.0)
+    wg, wu, wd = w(2, dm, F), w(3, dm, F), w(4, F, dm)
+    wqkv, dqkv = w(5, dm, N), w(6, T, N, std=1.0)
+    g = (1.0 + w(7, dm, std=0.1).float()).to(torch.bfloat16)
+    _, rms = ops.rmsnorm_fwd(x, g)
+    L, sp, P, bf = ops._lib.lib(), ops._stream(), ops._p, ops._lib.BF16
+    sdx, sdg, sdu, sdd = torch.empty_like(x), torch.empty_like(wg), torch.empty_like(wu), torch.empty_like(wd)
+    sw_ws = torch.empty(ops._lib.lib().beacon_swiglu_workspace_size(T, dm, F, bf, 1), dtype=torch.uint8, device=dev)
+    ldx, ldw, ldb = torch.empty_like(x), torch.empty_like(wqkv), torch.empty(N, dtype=torch.bfloat16, device=dev)
+    rdx, rdg = torch.empty_like(x), torch.empty_like(g)
+
+    def swiglu():
+        ops.check(L.beacon_swiglu_adjoint_bwd(P(sdx), P(sdg), P(sdu), P(sdd), P(dy), P(x), P(wg), P(wu), P(wd), T, dm,
+                                              F, bf, P(sw_ws), sw_ws.numel(), sp))
+
+    def linear():
+        ops.check(L.beacon_linear_bwd(P(ldx), P(ldw), P(ldb), P(dqkv), P(x), P(wqkv), T, dm, N, bf, sp))
+
+    def rmsnorm():
+        ops.check(L.beacon_rmsnorm_adjoint_bwd(P(rdx), P(rdg), P(dy), P(x), P(rms), P(g), T, dm, bf, None, 0, sp))
+
+    iters = max(10, args.steps // 2)
+    barrier(world)
+    res = {}
+    for name, fn in (("swiglu", swiglu), ("linear", linear), ("rmsnorm", rmsnorm)):
+        res[name] = max_over_ranks(min(_time_calls(fn, stream, iters, 2) for _ in range(2)), world)
+    torch.cuda.synchronize()
+    check = None
+    if rank == 0:  # sampled rows of dx and columns of the weight gradients against the oracle
+        import numpy as np
+        import oracle as O
+        rng = np.random.default_rng(BLOCK_BWD_SEED)
+        rows = np.sort(rng.choice(T, 16, replace=False))
+        cols = np.sort(rng.choice(F, 16, replace=False))
+        h = lambda t: t.float().cpu().numpy()
+        hx, hdy = h(x), h(dy)
+        rs = O.swiglu_bwd_sampled(hdy, hx, h(wg), h(wu), h(wd), rows, cols)
+        f64 = lambda a: np.asarray(a, dtype=np.float64)
+        lcols = np.sort(rng.choice(N, 16, replace=False))
+        hdq, hw = h(dqkv), h(wqkv)
+        rr = torch.from_numpy(rows).to(dev)
+        ndx, ndg = O.rmsnorm_bwd(hdy, hx, h(rms), h(g))
+        check = {"rows": rows.tolist(), "swiglu_dx": O.rel_err(h(sdx[rr]), rs[0]),
+                 "swiglu_dwg": O.rel_err(h(sdg)[:, cols], rs[1]), "swiglu_dwu": O.rel_err(h(sdu)[:, cols], rs[2]),
+                 "swiglu_dwd": O.rel_err(h(sdd)[cols, :], rs[3]),
+                 "linear_dx": O.rel_err(h(ldx[rr]), f64(hdq[rows]) @ f64(hw).T),
+                 "linear_dw": O.rel_err(h(ldw)[:, lcols], f64(hx).T @ f64(hdq[:, lcols])),
+                 "linear_db": O.rel_err(h(ldb), f64(hdq).sum(axis=0)),
+                 "rmsnorm_dx": O.rel_err(h(rdx), ndx), "rmsnorm_dweight": O.rel_err(h(rdg), ndg)}
+    del x, dy, wg, wu, wd, wqkv, dqkv, sdx, sdg, sdu, sdd, sw_ws, ldx, ldw, ldb, rdx, rdg
+    torch.cuda.empty_cache()
+    sw_fl, li_fl, rn_b = 12.0 * T * dm * F, 4.0 * T * dm * N, 3.0 * T * dm * 2 + 4.0 * T
+    return {"config": f"tokens {T}, d_model {dm}, SwiGLU hidden {F}, QKV width {N}, bf16; one replica per rank",
+            "swiglu_bwd": {"ms": res["swiglu"], "per_gpu_tflops": sw_fl / (res["swiglu"] * 1e-3) / 1e12,
+                           "api": "beacon_swiglu_adjoint_bwd (5 GEMMs)"},
+            "linear_bwd": {"ms": res["linear"], "per_gpu_tflops": li_fl / (res["linear"] * 1e-3) / 1e12,
+                           "api": "beacon_linear_bwd (dx, dW, dbias)"},
+            "rmsnorm_bwd": {"ms": res["rmsnorm"], "per_gpu_gbs": rn_b / (res["rmsnorm"] * 1e-3) / 1e9,
+                            "api": "beacon_rmsnorm_adjoint_bwd (row kernel + column sum)"}}, check
 
 
 def bench_gqa(args, rank, world, dev, stream):

@@ -112,6 +112,14 @@ int beacon_profile_read(const char* kernel, double* total_ms, uint64_t* count);
 
 /* ---- matmul / linear: crates/beacon-cuda/src/matmul.rs ---------------------- */
 
+/* The tile shape the bf16 GEMM entry points choose for an [m, k] x [k, n] product with
+ * 16-byte aligned rows on the current device: out[0] rows per tile (128, or 256 for an SM
+ * pair), out[1] columns per tile, out[2] tiles, out[3] SMs per tile (1 or 2), out[4] the
+ * device's SM count.  No counterpart in the reference: a planning query for launch
+ * configuration and benchmarks (wave efficiency = tiles / (ceil(tiles / slots) x slots),
+ * slots = SMs / SMs per tile). */
+int beacon_matmul_plan(int64_t m, int64_t k, int64_t n, int32_t* out);
+
 /* matmul_fwd (matmul.rs:18-29): out[m,n] = lhs[m,k] . rhs[k,n] */
 int beacon_matmul_fwd(void* out, const void* lhs, const void* rhs, int64_t m, int64_t k, int64_t n,
                       int dtype, void* stream);

@@ -169,3 +169,11 @@ def test_arena_dispatch_checks_access_modes():
     if not torch.cuda.is_available():
         rc = _launch_access(b"matmul_fwd", [(0, 128, W), (128, 64, R), (256, 64, RW)], mm)
         assert rc not in (_lib.OK, _lib.ERR_INVALID_LAUNCH_CONFIG, _lib.ERR_SHAPE_MISMATCH), _lib.last_error()
+
+
+def test_matmul_plan_rejects_null_output_and_bad_shapes_before_any_device_call():
+    L = _lib.lib()
+    assert L.beacon_matmul_plan(64, 64, 64, None) == _lib.ERR_INVALID_LAUNCH_CONFIG
+    out = (ctypes.c_int32 * 5)()
+    assert L.beacon_matmul_plan(0, 64, 64, out) == _lib.ERR_INVALID_LAUNCH_CONFIG
+    assert "bad shape" in _lib.last_error()

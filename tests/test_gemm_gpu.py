@@ -198,3 +198,17 @@ def test_fp8_quantizer_is_bit_exact_and_feeds_the_gemm():
     # all zeros: scale 1, codes 0
     q0, s0, a0 = ops.quantize_fp8e4m3(torch.zeros(64, device="cuda"))
     assert not q0.any() and float(s0.item()) == 1.0 and float(a0.item()) == 0.0
+
+
+def test_matmul_plan_reports_the_tile_shapes():
+    """beacon_matmul_plan reports the shape the GEMM entries pick: 256x256 SM-pair tiles for
+    4096^3, 256x128 pair tiles for the 8-way column shard 4096 x 512, 1-SM 128-row tiles when
+    M = 128 would leave half of a pair's rows empty."""
+    from beacon_b200 import ops
+    big = ops.matmul_plan(4096, 4096, 4096)
+    assert (big["tile_m"], big["tile_n"], big["sms_per_tile"], big["tiles"]) == (256, 256, 2, 256)
+    shard = ops.matmul_plan(4096, 4096, 512)
+    assert (shard["tile_m"], shard["tile_n"], shard["sms_per_tile"], shard["tiles"]) == (256, 128, 2, 64)
+    small = ops.matmul_plan(128, 4096, 4096)
+    assert small["tile_m"] == 128 and small["sms_per_tile"] == 1
+    assert 0.0 < shard["wave_efficiency"] <= 1.0
