@@ -252,3 +252,26 @@ def test_work_counter_slots_rotate_and_reset():
         for a, b in zip(g, refg):
             assert torch.equal(a, b)
     assert ops.device_status(0)[0] == 0
+
+
+@pytest.mark.parametrize("B,H,Hkv,S,D,causal", [
+    (2, 96, 96, 256, 128, True),    # 192 heads: more items than SMs in all three kernels, 1-2 tiles each
+    (2, 96, 48, 384, 64, True),     # GQA groups of 2 at head_dim 64, ragged causal items
+    (1, 160, 160, 200, 128, False),  # one tile per item, a tail inside it
+])
+def test_persistent_kernels_many_short_items(B, H, Hkv, S, D, causal):
+    """The persistent forward, dK/dV and dQ kernels with more (and much shorter) work items
+    than SMs: the item rings wrap many times and consecutive items overlap.  Every head is
+    checked against the oracle."""
+    import torch
+    ops = _ops()
+    q, k, v, do = _qkv(B, H, Hkv, S, D, 14)
+    t = lambda a: to_dev(a, torch.bfloat16)
+    out, lse = ops.attention_fwd(t(q), t(k), t(v), causal=causal)
+    dq, dk, dv = ops.attention_bwd(t(do), t(q), t(k), t(v), lse, causal=causal)
+    ro, rl = O.attention_fwd(q, k, v, causal=causal)
+    assert rel_err(to_np(out), ro) <= BF16_TOL
+    assert rel_err(to_np(lse), rl) <= 1e-3
+    for a, r in zip((dq, dk, dv), O.attention_bwd(do, q, k, v, rl, causal=causal)):
+        assert rel_err(to_np(a), r) <= BF16_TOL
+    assert ops.device_status(0)[0] == 0
