@@ -1024,6 +1024,16 @@ extern "C" int beacon_dropout_fwd(void* out, const void* input, void* mask, int6
   int dev;
   DeviceInfo* di;
   BEACON_TRY(current_device(&dev, &di));
+  if (aligned16(out) && aligned16(mask) && aligned16(input)) {  // eight elements per thread
+    const int grid = grid_for((n + 7) / 8, 256, di->sms);
+    if (dtype == BEACON_BF16)
+      k_dropout_fwd_vec<bf16><<<grid, 256, 0, as_stream(stream)>>>((bf16*)out, (bf16*)mask, (const bf16*)input, n, p,
+                                                                   seed);
+    else
+      k_dropout_fwd_vec<float><<<grid, 256, 0, as_stream(stream)>>>((float*)out, (float*)mask, (const float*)input, n,
+                                                                    p, seed);
+    return check_launch("k_dropout_fwd_vec");
+  }
   const int grid = grid_for(n, 256, di->sms);
   if (dtype == BEACON_BF16)
     k_dropout_fwd<bf16><<<grid, 256, 0, as_stream(stream)>>>((bf16*)out, (bf16*)mask, (const bf16*)input, n, p, seed);
@@ -1042,6 +1052,16 @@ extern "C" int beacon_dropout_bwd(void* d_in, const void* d_out, const void* mas
   int dev;
   DeviceInfo* di;
   BEACON_TRY(current_device(&dev, &di));
+  if (aligned16(d_in) && aligned16(d_out) && aligned16(mask)) {  // eight elements per thread
+    const int grid = grid_for((n + 7) / 8, 256, di->sms);
+    if (dtype == BEACON_BF16)
+      k_dropout_bwd_vec<bf16><<<grid, 256, 0, as_stream(stream)>>>((bf16*)d_in, (const bf16*)d_out,
+                                                                   (const bf16*)mask, n);
+    else
+      k_dropout_bwd_vec<float><<<grid, 256, 0, as_stream(stream)>>>((float*)d_in, (const float*)d_out,
+                                                                    (const float*)mask, n);
+    return check_launch("k_dropout_bwd_vec");
+  }
   const int grid = grid_for(n, 256, di->sms);
   if (dtype == BEACON_BF16)
     k_dropout_bwd<bf16><<<grid, 256, 0, as_stream(stream)>>>((bf16*)d_in, (const bf16*)d_out, (const bf16*)mask, n);

@@ -337,6 +337,60 @@ __device__ __forceinline__ float ldf(const float* p) { return *p; }
 __device__ __forceinline__ void stf(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
 __device__ __forceinline__ void stf(float* p, float v) { *p = v; }
 
+// Dropout (the draw and arithmetic of k_dropout_fwd / k_dropout_bwd above).
+// The same draw and arithmetic, eight elements per thread with 16-byte loads and stores (the
+// scalar kernel's 2-byte accesses and one hash per thread kept it at half of HBM speed);
+// pointers 16-byte aligned.  The n % 8 tail is done by the first threads of CTA 0.
+template <typename T>
+__global__ void __launch_bounds__(256) k_dropout_fwd_vec(T* __restrict__ out, T* __restrict__ mask,
+                                                         const T* __restrict__ in, long long n, float p,
+                                                         unsigned long long seed) {
+  const float keep_scale = p < 1.0f ? 1.0f / (1.0f - p) : 0.0f;
+  const T m_keep = T(keep_scale);
+  const float mk = elem_ld(&m_keep);
+  const long long n8 = n / 8, stride = (long long)gridDim.x * blockDim.x;
+  for (long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x; g < n8; g += stride) {
+    const long long i0 = g * 8;
+    float x[8], o[8], m[8];
+    load8(in + i0, x);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float u = (float)(splitmix64_at(seed, (uint64_t)(i0 + j)) >> 40) * (1.0f / 16777216.0f);
+      const bool keep = p < 1.0f && u >= p;
+      m[j] = keep ? mk : 0.0f;
+      o[j] = keep ? x[j] * mk : 0.0f;
+    }
+    store8(mask + i0, m);
+    store8(out + i0, o);
+  }
+  if (blockIdx.x == 0 && threadIdx.x < n - n8 * 8) {
+    const long long i = n8 * 8 + threadIdx.x;
+    const float u = (float)(splitmix64_at(seed, (uint64_t)i) >> 40) * (1.0f / 16777216.0f);
+    const bool keep = p < 1.0f && u >= p;
+    mask[i] = keep ? m_keep : T(0.0f);
+    elem_st(out + i, keep ? elem_ld(in + i) * mk : 0.0f);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) k_dropout_bwd_vec(T* __restrict__ d_in, const T* __restrict__ d_out,
+                                                         const T* __restrict__ mask, long long n) {
+  const long long n8 = n / 8, stride = (long long)gridDim.x * blockDim.x;
+  for (long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x; g < n8; g += stride) {
+    float a[8], b[8], o[8];
+    load8(d_out + g * 8, a);
+    load8(mask + g * 8, b);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = a[j] * b[j];
+    store8(d_in + g * 8, o);
+  }
+  if (blockIdx.x == 0 && threadIdx.x < n - n8 * 8) {
+    const long long i = n8 * 8 + threadIdx.x;
+    elem_st(d_in + i, elem_ld(d_out + i) * elem_ld(mask + i));
+  }
+}
+
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

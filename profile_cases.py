@@ -6,6 +6,8 @@
     python profile_cases.py layernorm_bwd --tokens 16384 --width 4096
     python profile_cases.py gemm_fp8 --m 4096 --n 4096 --k 4096
     python profile_cases.py swiglu_bwd --tokens 16384 --width 4096 --n 14336
+    python profile_cases.py swiglu_fwd --tokens 4096 --width 4096 --n 14336
+    python profile_cases.py residual_add | cast_f32_bf16 | dropout_fwd   (16384 x 4096 elements)
     python profile_cases.py block          (pre-norm block forward, batch 4 x seq 2048, d_model 4096)
     python profile_cases.py block_folded   (the same with both RMSNorms folded into the GEMMs)
 
@@ -16,7 +18,10 @@ and RMSNorm backward cases are HBM-bound and print GB/s of algorithmic bytes ins
 (RMSNorm backward: x, dy in, dx out, 4 B of rms per row): the LayerNorm forward reads x
 and writes out (2 * tokens * width * 2 B, bf16) plus 8 B of statistics per row; the
 backward reads x and dy and writes dx (3 * tokens * width * 2 B) plus the statistics
-read, timed over the whole call (row kernel and the two column sums).  Sizes default to
+read, timed over the whole call (row kernel and the two column sums).  The elementwise
+cases count their operands once: residual add and dropout 3 x 2 B per element (two bf16
+tensors in and one out, or one in and out plus the mask), the f32 -> bf16 cast 4 + 2 B.
+Sizes default to
 a case larger than the 126 MB L2 but a few hundred MB on the device, the size an
 ncu capture of a single launch (-k <kernel> -s <warmup launches> -c 1) should use.
 """
@@ -34,7 +39,8 @@ if ROOT not in sys.path:
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["attn_fwd", "attn_bwd", "attn_bwd_recompute", "gemm", "gemm_fp8", "swiglu_bwd",
-                                     "block", "block_folded",
+                                     "swiglu_fwd", "block", "block_folded", "residual_add", "cast_f32_bf16",
+                                     "dropout_fwd",
                                      "layernorm_fwd", "layernorm_bwd", "rmsnorm_fwd", "rmsnorm_bwd"])
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--width", type=int, default=4096)
@@ -55,8 +61,8 @@ def main(argv=None):
 
     torch.manual_seed(0)
     dev = torch.device("cuda", 0)
-    if a.case.startswith(("layernorm", "rmsnorm")):
-        return _layernorm(a, torch, ops, dev)
+    if a.case.startswith(("layernorm", "rmsnorm", "residual", "cast", "dropout")):
+        return _hbm_case(a, torch, ops, dev)
     if a.case.startswith("attn"):
         H, S, D = a.heads, a.seq, a.dim
         Hkv = a.kv_heads or H
@@ -97,6 +103,13 @@ def main(argv=None):
         flops = (2.0 * T * dm * 3 * dm + 2.0 * T * dm * dm + 2.0 * T * dm * 2 * F + 2.0 * T * F * dm
                  + 2.0 * Bb * Hb * Sb * Sb * 128)
         kname = "k_gemm_bf16_tc"
+    elif a.case == "swiglu_fwd":
+        T, dm, F = a.tokens // 2, a.width, a.n
+        x = torch.randn(T, dm, device=dev).bfloat16()
+        wg, wu = ((torch.randn(dm, F, device=dev) * 0.02).bfloat16() for _ in range(2))
+        wd = (torch.randn(F, dm, device=dev) * 0.02).bfloat16()
+        fn = lambda: ops.swiglu_fwd(x, wg, wu, wd)  # gate/up GEMM with the SwiGLU epilogue, then down
+        flops, kname = 6.0 * T * dm * F, "k_gemm_bf16_tc"
     elif a.case == "swiglu_bwd":
         T, dm, F = a.tokens // 2, a.width, a.n
         x = torch.randn(T, dm, device=dev).bfloat16()
@@ -126,7 +139,7 @@ def main(argv=None):
     ms, n = ops.profile_read(kname)
     kms = ms / max(n, 1)
     call_ms = e0.elapsed_time(e1) / a.iters
-    if a.case == "swiglu_bwd" or a.case.startswith("block"):  # several launches per call: the whole call
+    if a.case.startswith(("swiglu", "block")):  # several launches per call: the whole call
         print(f"{a.case}: {call_ms:.4f} ms/call {flops / (call_ms * 1e-3) / 1e12:.1f} TFLOP/s algorithmic "
               f"({n // max(a.iters, 1)} GEMM launches per call, {kms:.4f} ms each on average)", flush=True)
     else:
@@ -141,7 +154,7 @@ def main(argv=None):
     return 0
 
 
-def _layernorm(a, torch, ops, dev):
+def _hbm_case(a, torch, ops, dev):
     T, W = a.tokens, a.width
     x = torch.randn(T, W, device=dev).bfloat16()
     dy = torch.randn(T, W, device=dev).bfloat16()
@@ -155,6 +168,13 @@ def _layernorm(a, torch, ops, dev):
     elif a.case == "rmsnorm_bwd":
         _, rms = ops.rmsnorm_fwd(x, g)
         fn, nbytes = (lambda: ops.rmsnorm_bwd(dy, x, rms, g)), 3.0 * T * W * 2 + 4.0 * T
+    elif a.case == "residual_add":  # a, b in, out: bf16
+        fn, nbytes = (lambda: ops.residual_add(x, dy)), 3.0 * T * W * 2
+    elif a.case == "cast_f32_bf16":  # f32 in, bf16 out with the reference's rounding
+        xf = x.float()
+        fn, nbytes = (lambda: ops.cast(xf, 2)), 6.0 * T * W
+    elif a.case == "dropout_fwd":  # x in, out and the mask out: bf16
+        fn, nbytes = (lambda: ops.dropout_fwd(x, 0.1, 7)), 3.0 * T * W * 2
     else:
         fn, nbytes = (lambda: ops.layernorm_bwd(dy, x, mean, invstd, g)), 3.0 * T * W * 2 + 8.0 * T
     for _ in range(a.warmup):
@@ -167,7 +187,7 @@ def _layernorm(a, torch, ops, dev):
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / a.iters
-    print(f"{a.case}: tokens {T} width {W} bf16 {ms:.4f} ms/call {nbytes / (ms * 1e-3) / 1e9:.0f} GB/s algorithmic",
+    print(f"{a.case}: tokens {T} width {W} {ms:.4f} ms/call {nbytes / (ms * 1e-3) / 1e9:.0f} GB/s algorithmic",
           flush=True)
     ops.device_status(0)
     return 0

@@ -70,3 +70,17 @@ def test_dropout_mask_is_bit_exact(n, p, dt):
     d_in = ops.dropout_bwd(to_dev(dy, tdt), mask)
     ref = dy * rmask
     assert np.array_equal(to_np(d_in), as_bf16(ref) if dt == "bf16" else ref)
+
+
+def test_dropout_scalar_path_for_unaligned_input():
+    """An input that is not 16-byte aligned takes the one-element-per-thread kernels, with
+    the same draw: masks and outputs bit-exact as on the vectorised path."""
+    import torch
+    from beacon_b200 import ops
+    x = as_bf16(normal((5001,), 57))
+    dev = to_dev(np.concatenate([np.zeros(1, dtype=np.float32), x]), torch.bfloat16)[1:]  # 2-byte offset
+    assert dev.data_ptr() % 16 != 0
+    out, mask = ops.dropout_fwd(dev, 0.3, seed=99)
+    rout, rmask = O.dropout_fwd(x, 0.3, 99, bf16=True)
+    assert np.array_equal(to_np(mask), rmask)
+    assert np.array_equal(to_np(out), rout)
