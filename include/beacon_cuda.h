@@ -21,7 +21,7 @@
  *  - Concurrency: calls on different streams may overlap on the GPU, except that
  *    calls which take their scratch from the library's per-device workspace
  *    (workspace = NULL) share that one buffer: give each stream its own workspace
- *    when such calls may overlap.  The persistent kernels (attention forward, dQ)
+ *    when such calls may overlap.  The persistent kernels (attention forward, dK/dV, dQ)
  *    take their work items from one of 64 counter slots per device, rotating
  *    launch by launch and reset by each launch's last CTA: up to 64 such
  *    launches may be in flight on one device at once.

@@ -48,6 +48,7 @@ def main(argv=None):
     ap.add_argument("--kv-heads", type=int, default=0)
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--dim", type=int, default=128)
+    ap.add_argument("--non-causal", action="store_true", help="attention cases: every key for every query")
     ap.add_argument("--m", type=int, default=4096)
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--k", type=int, default=4096)
@@ -70,14 +71,16 @@ def main(argv=None):
         k = torch.randn(1, Hkv, S, D, device=dev).bfloat16()
         v = torch.randn(1, Hkv, S, D, device=dev).bfloat16()
         do = torch.randn(1, H, S, D, device=dev).bfloat16()
-        out, lse = ops.attention_fwd(q, k, v)
-        fwd = 2.0 * H * S * S * D
+        c = not a.non_causal
+        out, lse = ops.attention_fwd(q, k, v, causal=c)
+        fwd = 2.0 * H * S * S * D * (1 if c else 2)
         if a.case == "attn_fwd":
-            fn, flops, kname = (lambda: ops.attention_fwd(q, k, v, out=out, lse=lse)), fwd, "k_attn_fwd_tc"
+            fn, flops, kname = (lambda: ops.attention_fwd(q, k, v, causal=c, out=out, lse=lse)), fwd, "k_attn_fwd_tc"
         elif a.case == "attn_bwd":
-            fn, flops, kname = (lambda: ops.attention_bwd(do, q, k, v, lse, out=out)), 2.5 * fwd, "k_attn_bwd_dkdv"
+            fn, flops, kname = ((lambda: ops.attention_bwd(do, q, k, v, lse, causal=c, out=out)), 2.5 * fwd,
+                                "k_attn_bwd_dkdv")
         else:
-            fn, flops, kname = (lambda: ops.attention_bwd(do, q, k, v, lse)), 2.5 * fwd, "k_attn_bwd_dkdv"
+            fn, flops, kname = (lambda: ops.attention_bwd(do, q, k, v, lse, causal=c)), 2.5 * fwd, "k_attn_bwd_dkdv"
     elif a.case == "gemm_fp8":
         A = (torch.rand(a.m, a.k, device=dev) * 2 - 1).bfloat16()
         W8, scale, _ = ops.quantize_fp8e4m3(torch.randn(a.k, a.n, device=dev))
