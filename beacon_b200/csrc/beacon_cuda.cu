@@ -1144,6 +1144,54 @@ extern "C" int beacon_rmsnorm_adjoint_bwd(void* dx, void* dweight, const void* d
     if (dweight) return zero_fill(dweight, (size_t)dim * es, st);
     return BEACON_OK;
   }
+  // bf16 rows of 256 x NCH x WPR columns (NCH <= 4; WPR 1, 2 or 4 warps per row, the
+  // fewest that fit) up to 4096: one to four warps per row (k_rmsnorm_bwd_warp).
+  if (dtype == BEACON_BF16 && dim % 256 == 0 && dim <= 4096) {
+    const int nch = (int)(dim / 256);
+    const void* fn = nullptr;
+    int wpr = 0;
+#define RMS_BWD_WARP_PICK(N, W)                                \
+  if (!fn && nch == (N) * (W)) {                               \
+    fn = (const void*)k_rmsnorm_bwd_warp<N, W>;                \
+    wpr = W;                                                   \
+  }
+    RMS_BWD_WARP_PICK(1, 1) RMS_BWD_WARP_PICK(2, 1) RMS_BWD_WARP_PICK(3, 1) RMS_BWD_WARP_PICK(4, 1)
+    RMS_BWD_WARP_PICK(3, 2) RMS_BWD_WARP_PICK(4, 2)
+    RMS_BWD_WARP_PICK(3, 4) RMS_BWD_WARP_PICK(4, 4)
+#undef RMS_BWD_WARP_PICK
+    if (fn) {
+      int nb = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fn, 256, 0) != cudaSuccess || nb <= 0) nb = 2;
+      cudaGetLastError();
+      const int slots = 8 / wpr;
+      const int grid = (int)std::min<int64_t>((tokens + slots - 1) / slots, (int64_t)di->sms * nb);
+      float* part = nullptr;
+      bool ok = true;
+      if (dweight) {
+        void* ws = nullptr;
+        BEACON_TRY(get_workspace(dev, (size_t)grid * dim * 4, workspace, workspace_bytes, &ws));
+        ok = aligned16(ws);
+        part = reinterpret_cast<float*>(ws);
+      }
+      if (ok) {
+#define RMS_BWD_WARP(N, W)                                                                                       \
+  if (fn == (const void*)k_rmsnorm_bwd_warp<N, W>)                                                               \
+    k_rmsnorm_bwd_warp<N, W><<<grid, 256, 0, st>>>((bf16*)dx, part, (const bf16*)dy, (const bf16*)x, rms,        \
+                                                   (const bf16*)weight, tokens, (int)dim);
+        RMS_BWD_WARP(1, 1) RMS_BWD_WARP(2, 1) RMS_BWD_WARP(3, 1) RMS_BWD_WARP(4, 1)
+        RMS_BWD_WARP(3, 2) RMS_BWD_WARP(4, 2)
+        RMS_BWD_WARP(3, 4) RMS_BWD_WARP(4, 4)
+#undef RMS_BWD_WARP
+        BEACON_TRY(check_launch("rmsnorm_bwd"));
+        if (dweight) {
+          k_colsum_split2<bf16><<<dim3((unsigned)((dim + 31) / 32), 1), 256, 0, st>>>((bf16*)dweight, part, nullptr,
+                                                                                      nullptr, grid, (int)dim);
+          BEACON_TRY(check_launch("rmsnorm_bwd colsum"));
+        }
+        return BEACON_OK;
+      }
+    }
+  }
   // Register-resident rows (k_rmsnorm_bwd_rows) up to 8192 bf16 / 4096 f32 columns;
   // beyond that, for dim % 8 != 0 or with a misaligned workspace, k_rmsnorm_bwd.
   int rows_vec = 0;

@@ -1212,6 +1212,121 @@ __global__ void __launch_bounds__(256, VEC <= 2 ? 2 : 1)
   }
 }
 
+// RMSNorm backward with WPR warps per bf16 row (norm.rs:33-50), the row layout of
+// k_rmsnorm_fwd_warp: a lane holds 8 x NCH columns of the row (dim = 256 x NCH x WPR),
+// loaded with 16-byte streaming loads, so every resident warp has its row's x and dy in
+// flight and no CTA-wide barrier holds the other rows back.  The arithmetic is
+// k_rmsnorm_bwd_rows' (dot = sum w dy x; dx = w dy / rms - x dot / (rms^3 dim)); each lane
+// keeps its weight columns and its dweight partials (sum dy x / rms) in registers across
+// the rows it visits, and at the end the CTA's row slots add their partials in shared
+// memory in slot order and write one partial row per CTA for k_colsum_split2.
+template <int NCH, int WPR>
+__global__ void __launch_bounds__(256, 2) k_rmsnorm_bwd_warp(__nv_bfloat16* __restrict__ dx, float* __restrict__ part,
+                                                             const __nv_bfloat16* __restrict__ dy,
+                                                             const __nv_bfloat16* __restrict__ x,
+                                                             const float* __restrict__ rms,
+                                                             const __nv_bfloat16* __restrict__ w, long long rows,
+                                                             int dim) {
+  static_assert(WPR == 1 || WPR == 2 || WPR == 4, "one, two or four warps per row");
+  static_assert(NCH >= 1 && NCH <= 4, "at most 32 columns per lane");
+  constexpr int SLOTS = 8 / WPR;
+  __shared__ float dots[8];
+  __shared__ __align__(16) float acc[256 * 4 * 4];  // the CTA's dweight partial row (dim <= 4096)
+  const int lane = (int)(threadIdx.x & 31u), warp = (int)(threadIdx.x >> 5);
+  const int slot = warp / WPR, sub = warp % WPR;
+  const long long ns = (long long)gridDim.x * SLOTS;
+  const uint4* wv = reinterpret_cast<const uint4*>(w);
+  uint4 gu[NCH];
+  float aw[NCH][8];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    gu[c] = __ldg(wv + (c * WPR + sub) * 32 + lane);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) aw[c][j] = 0.0f;
+  }
+  for (long long r = (long long)blockIdx.x * SLOTS + slot; r < rows; r += ns) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + r * dim);
+    const uint4* dr = reinterpret_cast<const uint4*>(dy + r * dim);
+    uint4 ux[NCH], ud[NCH];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      ux[c] = __ldcs(xr + (c * WPR + sub) * 32 + lane);
+      ud[c] = __ldcs(dr + (c * WPR + sub) * 32 + lane);
+    }
+    const float inv = 1.0f / __ldg(rms + r);
+    float dot = 0.0f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const __nv_bfloat162* hx = reinterpret_cast<const __nv_bfloat162*>(&ux[c]);
+      const __nv_bfloat162* hd = reinterpret_cast<const __nv_bfloat162*>(&ud[c]);
+      const __nv_bfloat162* hg = reinterpret_cast<const __nv_bfloat162*>(&gu[c]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 a = __bfloat1622float2(hx[j]), d = __bfloat1622float2(hd[j]), g = __bfloat1622float2(hg[j]);
+        dot = fmaf(g.x * d.x, a.x, dot);
+        dot = fmaf(g.y * d.y, a.y, dot);
+      }
+    }
+    dot = warp_sum(dot);
+    if constexpr (WPR > 1) {
+      if (lane == 0) dots[warp] = dot;
+      named_bar_sync(1 + slot, 32 * WPR);
+      dot = 0.0f;
+#pragma unroll
+      for (int i = 0; i < WPR; ++i) dot += dots[slot * WPR + i];
+      named_bar_sync(1 + slot, 32 * WPR);  // every warp of the slot has read the partials
+    }
+    // the rows stay packed across the reduction: the unpacked floats are formed again below
+    // rather than held (64 more registers at NCH = 4, which spilled)
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      asm volatile("" : "+r"(ux[c].x), "+r"(ux[c].y), "+r"(ux[c].z), "+r"(ux[c].w));
+      asm volatile("" : "+r"(ud[c].x), "+r"(ud[c].y), "+r"(ud[c].z), "+r"(ud[c].w));
+      asm volatile("" : "+r"(gu[c].x), "+r"(gu[c].y), "+r"(gu[c].z), "+r"(gu[c].w));
+    }
+    const float cc = dot * inv * inv * inv / (float)dim;
+    uint4* xo = reinterpret_cast<uint4*>(dx + r * dim);
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const __nv_bfloat162* hx = reinterpret_cast<const __nv_bfloat162*>(&ux[c]);
+      const __nv_bfloat162* hd = reinterpret_cast<const __nv_bfloat162*>(&ud[c]);
+      const __nv_bfloat162* hg = reinterpret_cast<const __nv_bfloat162*>(&gu[c]);
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 a = __bfloat1622float2(hx[j]), d = __bfloat1622float2(hd[j]), g = __bfloat1622float2(hg[j]);
+        o[j] = pack_bf16x2(g.x * d.x * inv - a.x * cc, g.y * d.y * inv - a.y * cc);
+        aw[c][2 * j] += d.x * a.x * inv;
+        aw[c][2 * j + 1] += d.y * a.y * inv;
+      }
+      __stcs(xo + (c * WPR + sub) * 32 + lane, make_uint4(o[0], o[1], o[2], o[3]));
+    }
+  }
+  if (part == nullptr) return;  // uniform over the grid
+#pragma unroll 1
+  for (int s = 0; s < SLOTS; ++s) {
+    if (slot == s) {
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        float4* p4 = reinterpret_cast<float4*>(acc + ((c * WPR + sub) * 32 + lane) * 8);
+        float4 lo = make_float4(aw[c][0], aw[c][1], aw[c][2], aw[c][3]);
+        float4 hi = make_float4(aw[c][4], aw[c][5], aw[c][6], aw[c][7]);
+        if (s > 0) {
+          const float4 plo = p4[0], phi = p4[1];
+          lo = make_float4(plo.x + lo.x, plo.y + lo.y, plo.z + lo.z, plo.w + lo.w);
+          hi = make_float4(phi.x + hi.x, phi.y + hi.y, phi.z + hi.z, phi.w + hi.w);
+        }
+        p4[0] = lo;
+        p4[1] = hi;
+      }
+    }
+    __syncthreads();
+  }
+  float4* prow = reinterpret_cast<float4*>(part + (long long)blockIdx.x * dim);
+  const float4* a4 = reinterpret_cast<const float4*>(acc);
+  for (int i = (int)threadIdx.x; i < dim / 4; i += 256) prow[i] = a4[i];
+}
+
 // ---------------------------------------------------------------------------
 // SwiGLU elementwise pieces (mlp.rs:12-52); silu(z) = z * sigmoid(z)
 // ---------------------------------------------------------------------------

@@ -17,10 +17,14 @@ def _ops():
 # bf16 rows that are whole multiples of 256 up to 4096 take the warp-per-row forward: one
 # warp per row up to 2048 (17 x 256, 300 x 768, 1000 x 2048: more rows than the grid's row
 # slots), two warps per row above (64 x 4096, 513 x 3072); 70 x 2304 (nine 256-column
-# chunks, odd) and the rest take the CTA-per-row kernels.
+# chunks, odd) and the rest take the CTA-per-row kernels.  The backward of bf16 rows of
+# 256 x (1-4) x (1, 2 or 4 warps) columns runs one to four warps per row: 17 x 256, 40 x 512,
+# 300 x 768 and 129 x 1024 one warp; 7 x 1536 and 1000 x 2048 two; 513 x 3072, 64 x 4096
+# and 3 x 4096 (fewer rows than one CTA's row slots on the second CTA) four.
 @pytest.mark.parametrize("T,dim,dt", [(64, 4096, "bf16"), (8, 14336, "bf16"), (33, 1000, "f32"), (16, 256, "f32"),
                                       (5, 100, "bf16"), (64, 4096, "f32"), (17, 256, "bf16"), (300, 768, "bf16"),
-                                      (1000, 2048, "bf16"), (513, 3072, "bf16"), (70, 2304, "bf16")])
+                                      (1000, 2048, "bf16"), (513, 3072, "bf16"), (70, 2304, "bf16"),
+                                      (40, 512, "bf16"), (129, 1024, "bf16"), (7, 1536, "bf16"), (3, 4096, "bf16")])
 def test_rmsnorm(T, dim, dt):
     import torch
     ops = _ops()
@@ -36,6 +40,28 @@ def test_rmsnorm(T, dim, dt):
     rdx, rdg = O.rmsnorm_bwd(dy, x, rr, g)
     assert rel_err(to_np(dx), rdx) <= tol
     assert rel_err(to_np(dg), rdg) <= tol
+
+
+# dweight not wanted (null): dx alone, on the warp-per-row backward (4096) and the row kernel
+# (2304)
+@pytest.mark.parametrize("T,dim", [(100, 4096), (70, 2304)])
+def test_rmsnorm_bwd_dx_only(T, dim):
+    import ctypes
+    import torch
+    from beacon_b200 import _lib
+    from beacon_b200.errors import check
+    ops = _ops()
+    x, g, dy = (as_bf16(normal(s, 30 + i)) for i, s in enumerate([(T, dim), (dim,), (T, dim)]))
+    t = lambda a: to_dev(a, torch.bfloat16)
+    xt, gt, dyt = t(x), t(g), t(dy)
+    _, rms = ops.rmsnorm_fwd(xt, gt)
+    rdx, _ = O.rmsnorm_bwd(dy, x, to_np(rms), g)
+    dx = torch.empty(T, dim, dtype=torch.bfloat16, device="cuda")
+    p = lambda a: ctypes.c_void_p(a.data_ptr())
+    check(_lib.lib().beacon_rmsnorm_adjoint_bwd(p(dx), None, p(dyt), p(xt), p(rms), p(gt), T, dim, _lib.BF16, None, 0,
+                                                ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    torch.cuda.synchronize()
+    assert rel_err(to_np(dx), rdx) <= BF16_TOL
 
 
 # The forward of bf16 rows that are whole multiples of 256 up to 4096 (and not an odd count
