@@ -174,19 +174,54 @@ class ClockSampler:
 
 # --------------------------------------------------------------------------- distributed
 
+def parse_cpulist(text):
+    """'0-3,8,10-11' -> {0, 1, 2, 3, 8, 10, 11}."""
+    cpus = set()
+    for part in text.strip().split(","):
+        if "-" in part:
+            a, b = part.split("-")
+            cpus.update(range(int(a), int(b) + 1))
+        elif part:
+            cpus.add(int(part))
+    return cpus
+
+
+def bind_host_threads(local):
+    """With several ranks on one host, keeps this rank's threads on the CPUs that the host
+    lists as local to its GPU (the PCI device's local_cpulist), so the pinned host buffers
+    it allocates afterwards sit in the memory the GPU's copy engines reach without crossing
+    between sockets.  Returns the CPU list used, or None where there is nothing to narrow."""
+    import torch
+    try:
+        p = torch.cuda.get_device_properties(local)
+        bus = "%04x:%02x:%02x.0" % (p.pci_domain_id, p.pci_bus_id, p.pci_device_id)
+        with open(f"/sys/bus/pci/devices/{bus}/local_cpulist") as f:
+            text = f.read().strip()
+        cur = os.sched_getaffinity(0)
+        use = parse_cpulist(text) & cur
+    except Exception:  # no CUDA device, no sysfs entry, an unparsable list: leave the threads as they are
+        return None
+    if not use or use == cur:
+        return None
+    os.sched_setaffinity(0, use)
+    return text
+
+
 def dist_setup(n_gpus):
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    cpus = None
     if world > 1:
         import torch.distributed as dist
         torch.cuda.set_device(local)
+        cpus = bind_host_threads(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device("cuda", local))
     else:
         torch.cuda.set_device(0)
-    return rank, world, local
+    return rank, world, local, cpus
 
 
 def barrier(world):
@@ -297,7 +332,7 @@ def check_attention(world, h0, nh, out, lse, dq, dk, dv, dev):
 
 # --------------------------------------------------------------------------- GPU arm
 
-def run_beacon(args, rank, world, local):
+def run_beacon(args, rank, world, local, cpus=None):
     import torch
     from beacon_b200 import ops
 
@@ -470,7 +505,9 @@ def run_beacon(args, rank, world, local):
                "h2d_bytes_per_step": int(sum_over_ranks(h2d, world)),
                "d2h_bytes_per_step": int(sum_over_ranks(d2h, world)),
                "api": f"beacon_attention_adjoint_fwd + beacon_attention_adjoint_bwd on {n_chunks} head chunks, "
-                      "copies in, compute and copies out overlapped on three streams"}
+                      "copies in, compute and copies out overlapped on three streams",
+               "host_cpus": (f"each rank's threads on its GPU's local CPUs (rank 0: {cpus})" if cpus
+                             else "not narrowed")}
 
     del q, k, v, do, out, dq, dk, dv, host
     torch.cuda.empty_cache()
@@ -803,9 +840,9 @@ def main():
         world = int(os.environ.get("WORLD_SIZE", "1"))
         run_reference(args, rank, world)
         return
-    rank, world, local = dist_setup(args.gpus)
+    rank, world, local, cpus = dist_setup(args.gpus)
     try:
-        run_beacon(args, rank, world, local)
+        run_beacon(args, rank, world, local, cpus)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -114,3 +114,17 @@ def test_two_gloo_ranks_gather_sampled_units_from_their_owners():
         p.join(timeout=120)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert q.get(timeout=5) is True
+
+
+def test_bench_cpulist_parsing():
+    import importlib.util
+    import pathlib
+    spec = importlib.util.spec_from_file_location("bench_mod", pathlib.Path(__file__).resolve().parents[1] / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    assert bench.parse_cpulist("0-3,8,10-11") == {0, 1, 2, 3, 8, 10, 11}
+    assert bench.parse_cpulist("5\n") == {5}
+    assert bench.parse_cpulist("") == set()
+    before = os.sched_getaffinity(0)
+    assert bench.bind_host_threads(0) is None  # no GPU here: the threads stay where they are
+    assert os.sched_getaffinity(0) == before
