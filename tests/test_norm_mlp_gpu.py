@@ -70,10 +70,13 @@ def test_rmsnorm_bwd_dx_only(T, dim):
 # (2000, 768): more rows than CTAs, so each CTA's dweight / dbias partials cover several rows;
 # widths up to 8192 (bf16) / 4096 (f32) take the register-resident backward, (8, 14336) the
 # one with partials in global memory; (5, 100) and (7, 20) reach the any-dim forward and the
-# scalar backward loop.
+# scalar backward loop; 40 x 512, 129 x 1024, 7 x 1536, 300 x 2048 and 3 x 4096 (fewer rows
+# than CTAs) cover the register-resident backward's one- and two-vector widths.
 @pytest.mark.parametrize("T,dim,dt", [(64, 4096, "bf16"), (8, 14336, "bf16"), (2000, 768, "bf16"), (40, 6144, "bf16"),
                                       (33, 1000, "f32"), (16, 256, "f32"), (5, 100, "bf16"), (7, 20, "f32"),
-                                      (64, 4096, "f32"), (513, 3072, "bf16"), (70, 2304, "bf16"), (1000, 256, "bf16")])
+                                      (64, 4096, "f32"), (513, 3072, "bf16"), (70, 2304, "bf16"), (1000, 256, "bf16"),
+                                      (40, 512, "bf16"), (129, 1024, "bf16"), (7, 1536, "bf16"), (300, 2048, "bf16"),
+                                      (3, 4096, "bf16")])
 def test_layernorm(T, dim, dt):
     import torch
     ops = _ops()
@@ -92,9 +95,10 @@ def test_layernorm(T, dim, dt):
     assert rel_err(to_np(db), rdb) <= tol
 
 
-@pytest.mark.parametrize("skip", ["dweight", "dbias"])
+@pytest.mark.parametrize("skip", ["dweight", "dbias", "both"])
 def test_layernorm_bwd_one_parameter_gradient(skip):
-    """dweight or dbias alone (the other NULL): the column-sum kernel writes only the one asked for."""
+    """dweight or dbias alone (the other NULL): the column-sum kernel writes only the one asked
+    for; both NULL: dx alone."""
     import ctypes
     import torch
     from beacon_b200 import _lib
@@ -110,13 +114,15 @@ def test_layernorm_bwd_one_parameter_gradient(skip):
     db = torch.full((dim,), float("nan"), dtype=torch.bfloat16, device="cuda")
     p = lambda a: None if a is None else ctypes.c_void_p(a.data_ptr())
     dyt, xt, gt = t(dy), t(x), t(g)
-    check(_lib.lib().beacon_layernorm_adjoint_bwd(p(dx), None if skip == "dweight" else p(dw),
-                                                  None if skip == "dbias" else p(db), p(dyt), p(xt), p(mu), p(inv),
-                                                  p(gt), T, dim, _lib.BF16, None, 0,
+    check(_lib.lib().beacon_layernorm_adjoint_bwd(p(dx), None if skip in ("dweight", "both") else p(dw),
+                                                  None if skip in ("dbias", "both") else p(db), p(dyt), p(xt), p(mu),
+                                                  p(inv), p(gt), T, dim, _lib.BF16, None, 0,
                                                   ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
     torch.cuda.synchronize()
     assert rel_err(to_np(dx), rdx) <= BF16_TOL
-    if skip == "dweight":
+    if skip == "both":
+        assert torch.isnan(dw.float()).all() and torch.isnan(db.float()).all()
+    elif skip == "dweight":
         assert torch.isnan(dw.float()).all() and rel_err(to_np(db), rdb) <= BF16_TOL
     else:
         assert torch.isnan(db.float()).all() and rel_err(to_np(dw), rdg) <= BF16_TOL
