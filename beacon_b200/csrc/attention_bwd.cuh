@@ -205,8 +205,10 @@ __device__ __forceinline__ void dq_ds_chunk(const uint32_t (&sc)[32], const uint
 //    its block index and the next ones from the launch's work counter, published by the
 //    producer in a two-slot ring.  Query tiles are counted over all of the CTA's items (n),
 //    so the Q / dO rings, the TMEM regions and the barrier phases run on across items: the
-//    next item's K / V load once the current item's last S^T / dP^T have read K / V, and its
-//    first S^T / dP^T run while the warps write the current item's dK / dV rows.
+//    next item's K / V load once the current item's last S^T / dP^T have read K / V, its
+//    first S^T / dP^T run behind the current item's last dK, and the warps write the
+//    current item's dK / dV rows after the next item's first P and dS phases, while the
+//    tensor core computes that item's second S^T; its first dV / dK MMAs wait for them.
 //    Per query tile n of the item's 128 keys (M=128 keys x N=128 queries):
 //     S^T(n)  = K Q(n)^T  -> TMEM region R_S(n)      dP^T(n) = V dO(n)^T -> region R_P(n)
 //   The two 128-column regions X = [0,128) and Y = [128,256) swap roles every tile
@@ -293,7 +295,8 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* kv_empty = bars + 21;  // an item's last S^T and dP^T have read K and V
   uint64_t* item_full = bars + 22;                  // [2] item published by the producer
   uint64_t* item_empty = item_full + kDkvItemRing;  // [2] read by the MMA warp and the 8 softmax warps
-  int* s_item = reinterpret_cast<int*>(item_empty + kDkvItemRing);  // [2] item indices
+  uint64_t* acc_free = item_empty + kDkvItemRing;   // an item's dV, dK read out of TMEM by the 8 warps
+  int* s_item = reinterpret_cast<int*>(acc_free + 1);  // [2] item indices
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_item + kDkvItemRing);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   constexpr uint32_t T_DV = 256, T_DK = 256 + D;
@@ -325,6 +328,7 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(&item_full[i], 1);
       mbar_init(&item_empty[i], 9);
     }
+    mbar_init(acc_free, 8);
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -488,6 +492,9 @@ __global__ void __launch_bounds__(384, 1)
         const uint32_t par = n & 1u;
         const bool more = __all_sync(0xffffffffu, nxt.valid);
         const bool first = cur_m == 0;  // the item's first tile: dV and dK start afresh
+        // ... in accumulators that may still hold the previous item's dV / dK: its dV / dK
+        // MMAs then wait until the warps have read those out (acc_free)
+        const bool defer = first && cur_ci > 0;
         const bool last = cur_m == cur.n_iter - 1;
         const uint32_t rs = (n & 1u) ? 128u : 0u, rp = 128u - rs;  // R_S(n), R_P(n)
         const int qs = (int)(n % QST), qs1 = (int)((n + 1) % QST);
@@ -498,19 +505,26 @@ __global__ void __launch_bounds__(384, 1)
         // (dV(n) in two halves around S^T(n+1): the issuing warp, which blocks while the
         // tensor pipe's queue is full, gets to S^T(n+1) sooner.)  Tile n+1 may be the next
         // item's first: its S^T / dP^T read the next item's K / V, which load once this
-        // item's last S^T / dP^T have read K / V, and run while the warps write this item's
-        // dK / dV; its dV / dK MMAs, which start the accumulators afresh, wait for P^T / dS^T,
-        // which the warps store only after those rows have left TMEM.
+        // item's last S^T / dP^T have read K / V.  On an item's first tile the warps run the
+        // P and dS phases before they write the previous item's dK / dV rows, so S^T(n+1) is
+        // issued ahead of dV(n), which waits for acc_free; meanwhile the tensor core computes
+        // S^T(n+1), and the warps' next P phase finds it ready.
         if (!warp_wait(p_ready, par, abort_flag, kSiteBwdDsFull)) break;
         tc_fence_after();
-        issue_kv(T_DV, rs, do_mn, first, 0, 4);
+        if (!defer) issue_kv(T_DV, rs, do_mn, first, 0, 4);
         if (!warp_wait(rp_free, par, abort_flag, kSiteBwdDsFull)) break;
         if (more) {
           if (nxt_m == 0 && !warp_wait(kv_full, (uint32_t)nxt_ci & 1u, abort_flag, kSiteBwdKV)) break;
           if (!issue_st(rp, qs1, ((n + 1) / QST) & 1u)) break;
           if (leader) umma_commit(s_full);
         }
-        issue_kv(T_DV, rs, do_mn, false, 4, 8);
+        if (defer) {
+          if (!warp_wait(acc_free, (uint32_t)(cur_ci - 1) & 1u, abort_flag, kSiteBwdDkvFull)) break;
+          tc_fence_after();
+          issue_kv(T_DV, rs, do_mn, true, 0, 8);
+        } else {
+          issue_kv(T_DV, rs, do_mn, false, 4, 8);
+        }
         if (!warp_wait(ds_ready, par, abort_flag, kSiteBwdDsFull)) break;
         tc_fence_after();
         // dO(n) read by dP^T(n) and dV(n), and Dt(n), which shares its stage, by the warps'
@@ -546,6 +560,47 @@ __global__ void __launch_bounds__(384, 1)
     const uint32_t lane_base = (quarter * 32u) << 16;
     bool ok = true;
     uint32_t n = 0;  // query tiles over all of the CTA's items
+    // An item's dV (g = 0) / dK (g = 1) rows, 32-byte stores where the output allows (each a
+    // whole sector of the row).  They are written after the next item's first P and dS
+    // phases (the tensor core meanwhile computes that item's second S^T), and acc_free then
+    // lets that item's dV / dK MMAs start the accumulators afresh.
+    auto write_dkv = [&](const DkvItem& e, int eci) -> bool {
+      if (!__all_sync(0xffffffffu, mbar_wait(dkv_full, (uint32_t)eci & 1u, abort_flag, kSiteBwdDkvFull)))
+        return false;
+      tc_fence_after();
+      const int ekj = e.jt * 128 + r;
+      const bool ekey_ok = ekj < p.S;
+      const float sc = g == 0 ? 1.0f : p.scale;
+      const uint32_t col = g == 0 ? T_DV : T_DK;
+      __nv_bfloat16* orow = (g == 0 ? p.dv : p.dk) + ((long long)e.kvz * p.S + (ekey_ok ? ekj : 0)) * D;
+      const bool o32 = (reinterpret_cast<uintptr_t>(g == 0 ? p.dv : p.dk) & 31u) == 0;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t a[32];
+        tmem_ld32(tmem + lane_base + col + c * 32, a);
+        tmem_wait_ld();
+        if (ekey_ok) {
+#pragma unroll
+          for (int q = 0; q < 32; q += 16) {
+            uint32_t wv[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              wv[i] = pack_bf16x2(__uint_as_float(a[q + 2 * i]) * sc, __uint_as_float(a[q + 2 * i + 1]) * sc);
+            if (o32) {
+              stg256(orow + c * 32 + q, wv[0], wv[1], wv[2], wv[3], wv[4], wv[5], wv[6], wv[7]);
+            } else {  // only 16-byte aligned
+              *reinterpret_cast<uint4*>(orow + c * 32 + q) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+              *reinterpret_cast<uint4*>(orow + c * 32 + q + 8) = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      return true;
+    };
+    DkvItem prev;
+    prev.valid = false;
+    int prev_ci = 0;
     for (int ci = 0; ok; ++ci) {
       const DkvItem x = read_item(ci, ok);
       __syncwarp();
@@ -629,43 +684,22 @@ __global__ void __launch_bounds__(384, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(ds_ready);
-      }
-      if (!ok) break;
-      // the item's dV (g = 0) / dK (g = 1) rows, 32-byte stores where the output allows (each
-      // a whole sector of the row); the MMA warp meanwhile runs the next item's first S^T and
-      // dP^T, and these warps store its first P^T only after the rows have left TMEM
-      if (!__all_sync(0xffffffffu, mbar_wait(dkv_full, (uint32_t)ci & 1u, abort_flag, kSiteBwdDkvFull))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const float sc = g == 0 ? 1.0f : p.scale;
-      const uint32_t col = g == 0 ? T_DV : T_DK;
-      __nv_bfloat16* orow = (g == 0 ? p.dv : p.dk) + ((long long)x.kvz * p.S + (key_ok ? kj : 0)) * D;
-      const bool o32 = (reinterpret_cast<uintptr_t>(g == 0 ? p.dv : p.dk) & 31u) == 0;
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t a[32];
-        tmem_ld32(tmem + lane_base + col + c * 32, a);
-        tmem_wait_ld();
-        if (key_ok) {
-#pragma unroll
-          for (int e = 0; e < 32; e += 16) {
-            uint32_t wv[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              wv[i] = pack_bf16x2(__uint_as_float(a[e + 2 * i]) * sc, __uint_as_float(a[e + 2 * i + 1]) * sc);
-            if (o32) {
-              stg256(orow + c * 32 + e, wv[0], wv[1], wv[2], wv[3], wv[4], wv[5], wv[6], wv[7]);
-            } else {  // only 16-byte aligned
-              *reinterpret_cast<uint4*>(orow + c * 32 + e) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-              *reinterpret_cast<uint4*>(orow + c * 32 + e + 8) = make_uint4(wv[4], wv[5], wv[6], wv[7]);
-            }
+        if (m == 0 && prev.valid) {  // the previous item's rows, then its accumulators are free
+          if (!write_dkv(prev, prev_ci)) {
+            ok = false;
+            break;
           }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(acc_free);
+          prev.valid = false;
         }
       }
-      tc_fence_before();
+      if (!ok) break;
+      prev = x;
+      prev_ci = ci;
     }
+    // the CTA's last item
+    if (ok && prev.valid) write_dkv(prev, prev_ci);
   }
 
   tc_fence_before();
