@@ -655,17 +655,30 @@ def bench_block(args, rank, world, dev, stream):
         ops.llama_block_fwd_folded(x, wqkv_f, wo, wg_f, wu_f, wd, BLK_B, BLK_S, BLK_H, BLK_H, out=out_f,
                                    workspace=ws)
 
-    # the two forms alternate over four rounds, each round in the other order, and each keeps
-    # its fastest round: under the 1 kW power cap the clock drifts by 10-20% over a few
-    # seconds, more than the forms differ
-    iters = max(10, args.steps // 2)
+    # the two forms alternate call by call (each pair in the other order than the one
+    # before), every call timed by its own events, and each form keeps its median: under the
+    # 1 kW power cap the clock falls by 10-20% as the GPU warms over the few seconds of the
+    # run, more than the forms differ, and this way both forms see the same trend (timing
+    # them in alternating rounds and keeping each one's fastest round favoured whichever form
+    # came first in the first round)
+    pairs = max(10, args.steps // 2)
+    for f in (fn, fn_folded, fn, fn_folded):
+        f()
+    torch.cuda.synchronize()
     barrier(world)
-    t_un, t_fo = [], []
-    for i in range(4):
-        for f in ((fn, fn_folded) if i % 2 == 0 else (fn_folded, fn)):
-            (t_un if f is fn else t_fo).append(_time_calls(f, stream, iters, 2))
-    ms = max_over_ranks(min(t_un), world)
-    ms_f = max_over_ranks(min(t_fo), world)
+    ev = {"un": [], "fo": []}
+    for i in range(pairs):
+        for name, f in ((("un", fn), ("fo", fn_folded)) if i % 2 == 0 else (("fo", fn_folded), ("un", fn))):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            f()
+            e1.record(stream)
+            ev[name].append((e0, e1))
+    torch.cuda.synchronize()
+    t_un = [a.elapsed_time(b) for a, b in ev["un"]]
+    t_fo = [a.elapsed_time(b) for a, b in ev["fo"]]
+    ms = max_over_ranks(statistics.median(t_un), world)
+    ms_f = max_over_ranks(statistics.median(t_fo), world)
     torch.cuda.synchronize()
     check = None
     if rank == 0:  # rows of sequence 1 of both timed replicas against the sampled-row block oracle
