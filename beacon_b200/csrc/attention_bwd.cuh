@@ -448,7 +448,7 @@ __global__ void __launch_bounds__(384, 1)
         const uint64_t qd = sdesc_adv(q_desc, qs * TILE);
 #pragma unroll
         for (int cb = 0; cb < NB; ++cb) {
-          if (!warp_wait(&q_full[2 * qs + cb], par, abort_flag, kSiteBwdQDFull)) return false;
+          if (!lane_wait(&q_full[2 * qs + cb], par, abort_flag, kSiteBwdQDFull)) return false;
           tc_fence_after();
 #pragma unroll
           for (int k4 = 0; k4 < 4; ++k4) {
@@ -490,7 +490,7 @@ __global__ void __launch_bounds__(384, 1)
       for (uint32_t n = 0; cur.valid && ok; ++n) {
         const int st = (int)(n & 1u), st1 = (int)((n + 1) & 1u);
         const uint32_t par = n & 1u;
-        const bool more = __all_sync(0xffffffffu, nxt.valid);
+        const bool more = nxt.valid;  // the same on every lane: all read the same item
         const bool first = cur_m == 0;  // the item's first tile: dV and dK start afresh
         // ... in accumulators that may still hold the previous item's dV / dK: its dV / dK
         // MMAs then wait until the warps have read those out (acc_free)
@@ -509,23 +509,23 @@ __global__ void __launch_bounds__(384, 1)
         // P and dS phases before they write the previous item's dK / dV rows, so S^T(n+1) is
         // issued ahead of dV(n), which waits for acc_free; meanwhile the tensor core computes
         // S^T(n+1), and the warps' next P phase finds it ready.
-        if (!warp_wait(p_ready, par, abort_flag, kSiteBwdDsFull)) break;
+        if (!lane_wait(p_ready, par, abort_flag, kSiteBwdDsFull)) break;
         tc_fence_after();
         if (!defer) issue_kv(T_DV, rs, do_mn, first, 0, 4);
-        if (!warp_wait(rp_free, par, abort_flag, kSiteBwdDsFull)) break;
+        if (!lane_wait(rp_free, par, abort_flag, kSiteBwdDsFull)) break;
         if (more) {
-          if (nxt_m == 0 && !warp_wait(kv_full, (uint32_t)nxt_ci & 1u, abort_flag, kSiteBwdKV)) break;
+          if (nxt_m == 0 && !lane_wait(kv_full, (uint32_t)nxt_ci & 1u, abort_flag, kSiteBwdKV)) break;
           if (!issue_st(rp, qs1, ((n + 1) / QST) & 1u)) break;
           if (leader) umma_commit(s_full);
         }
         if (defer) {
-          if (!warp_wait(acc_free, (uint32_t)(cur_ci - 1) & 1u, abort_flag, kSiteBwdDkvFull)) break;
+          if (!lane_wait(acc_free, (uint32_t)(cur_ci - 1) & 1u, abort_flag, kSiteBwdDkvFull)) break;
           tc_fence_after();
           issue_kv(T_DV, rs, do_mn, true, 0, 8);
         } else {
           issue_kv(T_DV, rs, do_mn, false, 4, 8);
         }
-        if (!warp_wait(ds_ready, par, abort_flag, kSiteBwdDsFull)) break;
+        if (!lane_wait(ds_ready, par, abort_flag, kSiteBwdDsFull)) break;
         tc_fence_after();
         // dO(n) read by dP^T(n) and dV(n), and Dt(n), which shares its stage, by the warps'
         // dS phase: the stage may take dO(n+2)
@@ -534,7 +534,7 @@ __global__ void __launch_bounds__(384, 1)
         if (leader) umma_commit(&q_empty[qs]);  // Q(n) read by S^T(n) and dK(n)
         if (last && leader) umma_commit(dkv_full);
         if (more) {  // into R_S(n), behind dV(n) and dK(n), which read P^T / dS^T(n) from it
-          if (!warp_wait(&do_full[st1], ((n + 1) >> 1) & 1u, abort_flag, kSiteBwdQDFull)) break;
+          if (!lane_wait(&do_full[st1], ((n + 1) >> 1) & 1u, abort_flag, kSiteBwdQDFull)) break;
           tc_fence_after();
           issue_score_tile<D>(leader, tmem + rs, v_desc, sdesc_adv(do_desc, st1 * TILE));
           if (leader) umma_commit(dp_full);
@@ -931,16 +931,16 @@ __global__ void __launch_bounds__(384, 1)
       const uint64_t k_desc = tile_desc_k(smem_u32(sK)), k_desc_mn = tile_desc_mn(smem_u32(sK));
       const uint64_t v_desc = tile_desc_k(smem_u32(sV));
       auto issue_s = [&](const DqItem& x, uint32_t t) -> bool {  // S(t) into buffer t&1
-        if (x.j == 0 && !warp_wait(q_full, (uint32_t)x.ci & 1u, abort_flag, kSiteQQd)) return false;
-        if (!warp_wait(&k_full[t % KST], (t / KST) & 1u, abort_flag, kSiteQKFull)) return false;
+        if (x.j == 0 && !lane_wait(q_full, (uint32_t)x.ci & 1u, abort_flag, kSiteQQd)) return false;
+        if (!lane_wait(&k_full[t % KST], (t / KST) & 1u, abort_flag, kSiteQKFull)) return false;
         tc_fence_after();
         issue_score_tile<D>(leader, tmem + T_S + 128 * (t & 1), q_desc, sdesc_adv(k_desc, (t % KST) * TILE));
         if (x.j == x.n_kt - 1 && leader) umma_commit(q_empty);  // the item's last S has read Q
         return true;
       };
       auto issue_dp = [&](const DqItem& x, uint32_t t) -> bool {  // dP(t); then S(t) and dP(t) are announced
-        if (x.j == 0 && !warp_wait(do_full, (uint32_t)x.ci & 1u, abort_flag, kSiteQQd)) return false;
-        if (!warp_wait(&v_full[t & 1], (t >> 1) & 1u, abort_flag, kSiteQVFull)) return false;
+        if (x.j == 0 && !lane_wait(do_full, (uint32_t)x.ci & 1u, abort_flag, kSiteQQd)) return false;
+        if (!lane_wait(&v_full[t & 1], (t >> 1) & 1u, abort_flag, kSiteQVFull)) return false;
         tc_fence_after();
         issue_score_tile<D>(leader, tmem + T_DP, do_desc, sdesc_adv(v_desc, (t & 1) * TILE));
         if (leader) umma_commit(&v_empty[t & 1]);
@@ -968,7 +968,7 @@ __global__ void __launch_bounds__(384, 1)
       for (uint32_t t = 0; xq.valid && ok; ++t) {
         const uint32_t sb = T_S + 128 * (t & 1);
         const uint64_t k_mn = sdesc_adv(k_desc_mn, (t % KST) * TILE);
-        if (!warp_wait(dp_free, t & 1u, abort_flag, kSiteQDpFree)) {
+        if (!lane_wait(dp_free, t & 1u, abort_flag, kSiteQDpFree)) {
           ok = false;
           break;
         }
@@ -981,12 +981,12 @@ __global__ void __launch_bounds__(384, 1)
           xp = dq_next(xp);
         }
         // the item's first dQ MMA overwrites the accumulator: the previous item's dQ must be out
-        if (xq.j == 0 && xq.ci > 0 && !warp_wait(dq_free, (uint32_t)(xq.ci - 1) & 1u, abort_flag, kSiteQDqFull)) {
+        if (xq.j == 0 && xq.ci > 0 && !lane_wait(dq_free, (uint32_t)(xq.ci - 1) & 1u, abort_flag, kSiteQDqFull)) {
           ok = false;
           break;
         }
         for (int c = 0; c < 2 && ok; ++c) {
-          if (!warp_wait(&ds_chunk[2 * c + (t & 1)], (t >> 1) & 1u, abort_flag, kSiteQDsFull)) {
+          if (!lane_wait(&ds_chunk[2 * c + (t & 1)], (t >> 1) & 1u, abort_flag, kSiteQDsFull)) {
             ok = false;
             break;
           }
