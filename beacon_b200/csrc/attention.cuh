@@ -368,25 +368,32 @@ __global__ void __launch_bounds__(384, 1)
         uint32_t ns[2] = {0u, 0u};  // S tiles issued per tile slot over all items (P barrier phases)
         bool ok = true;
         FwdItem x;
-        for (int ci = 0; ok && __all_sync(0xffffffffu, read_item(ci, x)); ++ci) {
-          if (!warp_wait(q_full, (uint32_t)ci & 1u, abort_flag, kSiteAttnQ)) { ok = false; break; }
-          if (!warp_wait(&k_full[tk & 1u], (tk >> 1) & 1u, abort_flag, kSiteAttnKFull)) { ok = false; break; }
-          tc_fence_after();
-          for (int t = 0; t < 2; ++t)
-            if (x.nkv[t] > 0) issue_s(t, tk);
-          if (leader) umma_commit(&k_empty[tk & 1u]);
-          if (x.n_j == 1 && leader) umma_commit(q_empty);  // the item's last S has read Q
-          for (int j = 0; j < x.n_j && ok; ++j) {
+        // Per-lane waits (lane_wait) inside an item: a lane whose wait gives up skips the rest of
+        // the item's work and meets the others at the item's __syncwarp and the next vote, so
+        // every lane runs the same warp collectives.
+        for (int ci = 0;; ++ci) {
+          const bool got = ok && read_item(ci, x);
+          if (!__all_sync(0xffffffffu, got)) break;
+          bool iok = lane_wait(q_full, (uint32_t)ci & 1u, abort_flag, kSiteAttnQ) &&
+                     lane_wait(&k_full[tk & 1u], (tk >> 1) & 1u, abort_flag, kSiteAttnKFull);
+          if (iok) {
+            tc_fence_after();
+            for (int t = 0; t < 2; ++t)
+              if (x.nkv[t] > 0) issue_s(t, tk);
+            if (leader) umma_commit(&k_empty[tk & 1u]);
+            if (x.n_j == 1 && leader) umma_commit(q_empty);  // the item's last S has read Q
+          }
+          for (int j = 0; j < x.n_j && iok; ++j) {
             const uint32_t tv = tk + (uint32_t)j, tn = tv + 1u;  // V_j, K_{j+1} ring counts
             bool k_next = false;  // K_{j+1} has landed
-            if (!warp_wait(&v_full[tv & 1u], (tv >> 1) & 1u, abort_flag, kSiteAttnVFull)) { ok = false; break; }
+            if (!lane_wait(&v_full[tv & 1u], (tv >> 1) & 1u, abort_flag, kSiteAttnVFull)) { iok = false; break; }
             const uint64_t vd = sdesc_adv(v_desc, (tv & 1u) * Cfg::KV_BYTES);
-            for (int t = 0; t < 2 && ok; ++t) {
+            for (int t = 0; t < 2 && iok; ++t) {
               if (j >= x.nkv[t]) continue;
               // O_t += P_t V_j, P_t from TMEM (K = 128 keys), each 64-key half as soon as it is stored
-              for (int hf = 0; hf < 2 && ok; ++hf) {
-                if (!warp_wait(&p_full[2 * t + hf], (ns[t] + (uint32_t)j) & 1u, abort_flag, kSiteAttnPFull)) {
-                  ok = false;
+              for (int hf = 0; hf < 2 && iok; ++hf) {
+                if (!lane_wait(&p_full[2 * t + hf], (ns[t] + (uint32_t)j) & 1u, abort_flag, kSiteAttnPFull)) {
+                  iok = false;
                   break;
                 }
                 tc_fence_after();
@@ -397,12 +404,12 @@ __global__ void __launch_bounds__(384, 1)
                                           sdesc_adv(vd, kk * 2048), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
                 }
               }
-              if (!ok) break;
+              if (!iok) break;
               if (j == x.nkv[t] - 1 && leader) umma_commit(&o_full[t]);
               if (j + 1 < x.nkv[t]) {
                 if (!k_next) {
-                  if (!warp_wait(&k_full[tn & 1u], (tn >> 1) & 1u, abort_flag, kSiteAttnKFull)) {
-                    ok = false;
+                  if (!lane_wait(&k_full[tn & 1u], (tn >> 1) & 1u, abort_flag, kSiteAttnKFull)) {
+                    iok = false;
                     break;
                   }
                   tc_fence_after();
@@ -411,17 +418,17 @@ __global__ void __launch_bounds__(384, 1)
                 issue_s(t, tn);
               }
             }
-            if (!ok) break;
+            if (!iok) break;
             if (leader) umma_commit(&v_empty[tv & 1u]);
             if (k_next && leader) umma_commit(&k_empty[tn & 1u]);
             if (j + 2 == x.n_j && leader) umma_commit(q_empty);  // S(n_j - 1) were the item's last S
           }
-          if (!ok) break;
+          ok = iok;
           tk += (uint32_t)x.n_j;
           ns[0] += (uint32_t)x.nkv[0];
           ns[1] += (uint32_t)x.nkv[1];
           __syncwarp();
-          if (leader) mbar_arrive(&item_empty[ci % kFwdItemRing]);
+          if (ok && leader) mbar_arrive(&item_empty[ci % kFwdItemRing]);
         }
         if (leader) umma_commit(drain);
         volatile int no_abort = 0;

@@ -165,13 +165,14 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
                                           unsigned int site) {
   return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, site));
 }
-// The backward MMA-issuing warps' waits in their per-tile loops: every lane polls the barrier
-// on its own and no vote follows.  Inside the dK/dV kernel, whose softmax warps keep the
-// issuing warp's SM sub-partition busy, a warp vote in the MMA warp measured ~400 cycles
+// The attention MMA-issuing warps' waits in their per-tile loops: every lane polls the
+// barrier on its own and no vote follows.  Inside the dK/dV kernel, whose softmax warps keep
+// the issuing warp's SM sub-partition busy, a warp vote in the MMA warp measured ~400 cycles
 // (clock64 trace, six or seven votes per tile); without them the dK/dV and dQ kernels
-// measured 1.5% and 3% faster at 32 heads and the same at 256.  The outcome is the same on
-// every lane except on a timeout or an abort, after which each lane leaves its loop on its
-// own and meets the others at the drain wait (every wait still ends within its limit).
+// measured 1.5% and 3% faster at 32 heads (the same at 256) and the forward 2-2.5% faster.
+// The outcome is the same on every lane except on a timeout or an abort, after which each
+// lane leaves its work on its own and meets the others at the loop's next warp collective or
+// the drain wait (every wait still ends within its limit).
 __device__ __forceinline__ bool lane_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           unsigned int site) {
   return mbar_wait(bar, parity, abort_flag, site);
